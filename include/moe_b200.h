@@ -1,0 +1,181 @@
+/*
+ * moe_b200.h -- C ABI of the B200 (sm_100a) MoE-layer hot path.
+ *
+ * This library replaces the Vulkan MoE dispatch of moe-680m (paths below are relative to the
+ * moe-680m source tree).  The reference binds its compute through ash/Vulkan
+ * (src/device.rs, src/pipeline.rs) and records the MoE layer in
+ * InferenceEngine::record_and_submit_moe (src/inference.rs:663-766), with routing from
+ * do_route (src/inference.rs:622-659) and the router tail of record_and_submit_layer
+ * (src/inference.rs:598-616).  Every argument of those kernels is a u64 byte offset into one
+ * device arena (PushConstants, src/inference.rs:15-51), offset 0 meaning "missing tensor"
+ * (src/memory.rs:33, :234).  This ABI keeps that model: a context owns (or wraps) one device
+ * arena and every tensor argument is a byte offset into it; offset 0 is invalid.
+ *
+ * Conventions
+ *  - Every call returns MOE_OK (0) or a negative MOE_E* status; moe_last_error() gives text.
+ *  - Calls are stream-ordered on the context's stream (moe_set_stream) and asynchronous
+ *    unless stated otherwise; moe_sync() is the fence wait of the reference
+ *    (src/inference.rs:169-182).  A context is not thread-safe (the reference serialises its
+ *    engine behind a Mutex, src/server.rs:95).
+ *  - Weights are GGUF IQ4_XS (ggml type 23): rows of 136-byte blocks of 256 weights, row-major
+ *    [out_features][in_features], blocks along in_features.
+ *  - Activations are f32 row-major [M][hidden].
+ */
+#ifndef MOE_B200_H
+#define MOE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MOE_B200_ABI_VERSION 1
+
+/* status codes */
+#define MOE_OK 0
+#define MOE_E_INVALID (-1)     /* bad argument (offset 0, out of arena, bad shape) */
+#define MOE_E_CUDA (-2)        /* a CUDA runtime call failed */
+#define MOE_E_OOM (-3)         /* device allocation failed */
+#define MOE_E_UNSUPPORTED (-4) /* shape or device outside what this build supports */
+#define MOE_E_DEVICE (-5)      /* a kernel reported an error status (bounds / bad index) */
+
+typedef struct moe_ctx moe_ctx;
+
+/* Layer flags */
+#define MOE_F_SHARED 1u      /* layer has a shared expert (always active, own bucket) */
+#define MOE_F_SHARED_GATE 2u /* shared expert weighted by sigmoid(g . x); else weight 1.0 */
+
+/* Per-layer description: the scalar half of LayerWeights (src/memory.rs:201-223) plus the
+ * ModelConfig fields the MoE kernels read.  Offsets are arena byte offsets. */
+typedef struct moe_layer_spec {
+    uint32_t hidden;      /* H, multiple of 256 */
+    uint32_t inter;       /* I (expert and shared intermediate), multiple of 256 */
+    uint32_t n_experts;   /* E, 1..256 */
+    uint32_t top_k;       /* k, 1..8 */
+    uint32_t flags;       /* MOE_F_* */
+    float scale;          /* global combine scale (1.0; 1/9 reproduces the reference) */
+    uint64_t router_w;    /* f32 [E][H]  (ffn_gate; src/memory.rs:212) */
+    uint64_t router_bias; /* f32 [E] added to the logits, or 0 */
+    uint64_t shared_gate; /* f32 [H] (MOE_F_SHARED_GATE), else 0 */
+    uint64_t shared_w1;   /* IQ4_XS [I][H] (shared_expert.w1; src/memory.rs:251) */
+    uint64_t shared_w3;   /* IQ4_XS [I][H] */
+    uint64_t shared_w2;   /* IQ4_XS [H][I] */
+} moe_layer_spec;
+
+/* ---- context and arena (replaces DeviceContext::init / allocate_uma, src/device.rs:20,217) */
+
+/* Create a context on CUDA device `device` owning a fresh arena of `arena_bytes`. */
+int moe_ctx_create(int device, uint64_t arena_bytes, moe_ctx** out);
+/* Create a context over caller-owned device memory [base, base+bytes) (not freed by us). */
+int moe_ctx_create_external(int device, void* base, uint64_t bytes, moe_ctx** out);
+void moe_ctx_destroy(moe_ctx* ctx);
+/* Copy into / out of the arena (replaces the host memcpy of load_weights_from_tensors,
+ * src/memory.rs:297-321, and the coherent-mapping writes of src/inference.rs:685-699).
+ * Upload is stream-ordered; download waits for the stream and the copy. */
+int moe_arena_upload(moe_ctx* ctx, uint64_t off, const void* host, uint64_t n);
+int moe_arena_download(moe_ctx* ctx, uint64_t off, void* host, uint64_t n);
+/* Device address of arena offset `off` (for interop; no ownership transfer). */
+int moe_arena_ptr(moe_ctx* ctx, uint64_t off, void** dptr);
+/* Use `stream` (a cudaStream_t, or NULL for the context's own stream) for later calls. */
+int moe_set_stream(moe_ctx* ctx, void* stream);
+/* Wait for all work queued on the context's stream (the reference's fence wait). */
+int moe_sync(moe_ctx* ctx);
+/* Copy the last error message of this context (or of context creation if ctx is NULL). */
+int moe_last_error(const moe_ctx* ctx, char* buf, size_t n);
+int moe_abi_version(void);
+
+/* ---- layers (replaces LayerWeights::from_registry, src/memory.rs:227-290) ---------------- */
+
+/* Register one MoE layer.  w1/w3/w2 are host arrays of E arena offsets (the flat
+ * expert_w{1,2,3}[layer*E + e] tables of LayerWeights, one layer's slice).  Every offset is
+ * validated (non-zero, 256-byte aligned, inside the arena).  Returns a layer id >= 0. */
+int moe_layer_create(moe_ctx* ctx, const moe_layer_spec* spec, const uint64_t* w1,
+                     const uint64_t* w3, const uint64_t* w2, uint32_t* layer_id);
+
+/* Pre-size the internal workspace for batches of up to max_tokens tokens (call before CUDA
+ * graph capture; forward calls otherwise grow it on demand). */
+int moe_reserve(moe_ctx* ctx, uint32_t layer_id, uint32_t max_tokens);
+
+/* ---- routing (router.comp + router_topk.comp + router.rs::route_single) ------------------ */
+
+/* Router projection, 256-way softmax and top-k for M tokens of x (f32 [M][H] at x_off).
+ * Writes M records of (k+1) x {u32 expert_id, f32 weight} at topk_off: entry 0 is the shared
+ * expert {E, gate} (gate = sigmoid(g.x), or 1.0), entries 1..k the routed experts by
+ * descending probability, ties to the lower expert index (the 72-byte record of
+ * shaders/router_topk.comp:87-92 with the shared id made distinct from expert 0). */
+int moe_route(moe_ctx* ctx, uint32_t layer_id, uint64_t x_off, uint32_t M, uint64_t topk_off);
+
+/* do_route (src/inference.rs:622-659): moe_route into the workspace, wait, and return
+ * RoutingOutput rows on the host: routed[M][k] expert ids and weights[M][k]
+ * (src/router.rs:4-8).  `shared_gate` (M floats) may be NULL. */
+int moe_do_route(moe_ctx* ctx, uint32_t layer_id, uint64_t x_off, uint32_t M,
+                 uint16_t* routed, float* weights, float* shared_gate);
+
+/* ---- bucketing (src/router.rs:55-97 build_expert_batches) -------------------------------- */
+
+/* Bucket M routing records (format of moe_route) by expert.  Outputs (arena offsets):
+ *   ranges   i32 [E+2]  bucket e = [ranges[e], ranges[e+1]); bucket E is the shared expert
+ *   tokens   i32 [S]    token index per slot, ascending inside each bucket (stable)
+ *   weights  f32 [S]    routing weight per slot (shared: the gate)
+ *   slot_pos i32 [M][k+1] sorted position of each token's slot (slot k = shared)
+ * with S = M*(k + has_shared). */
+int moe_bucket(moe_ctx* ctx, uint32_t n_experts, uint32_t top_k, int has_shared,
+               uint64_t topk_off, uint32_t M, uint64_t ranges_off, uint64_t tokens_off,
+               uint64_t weights_off, uint64_t slot_pos_off);
+
+/* ---- the MoE layer (record_and_submit_moe, src/inference.rs:663-766) --------------------- */
+
+/* out = resid + scale * (sum_j w_j * E_j(x) + gate * S(x)), E_j(x) = W2 (silu(W1 x) * W3 x),
+ * for M tokens: router, top-k, bucketing, grouped experts and combine, all on the device.
+ * resid_off may equal x_off; out_off may equal resid_off (in-place residual update). */
+int moe_forward(moe_ctx* ctx, uint32_t layer_id, uint64_t x_off, uint64_t resid_off,
+                uint64_t out_off, uint32_t M);
+
+/* record_and_submit_moe with host routing (RoutingOutput rows as returned by moe_do_route):
+ * experts and combine only; routed[M][k] ids, weights[M][k], shared_gate[M] (NULL: 1.0). */
+int moe_forward_routed(moe_ctx* ctx, uint32_t layer_id, uint64_t x_off, uint64_t resid_off,
+                       uint64_t out_off, uint32_t M, const uint16_t* routed,
+                       const float* weights, const float* shared_gate);
+
+/* ---- stack glue (rms_norm.comp + residual_add.comp, src/inference.rs:474-482, :588-596) -- */
+
+/* y = x / sqrt(mean(x^2) + eps), per token, no gain (shaders/rms_norm.comp:36-58). */
+int moe_rms_norm(moe_ctx* ctx, uint64_t x_off, uint64_t y_off, uint32_t M, uint32_t H, float eps);
+
+/* ---- tracing ----------------------------------------------------------------------------- */
+
+/* Per-stage device time of the MoE calls, from CUDA events recorded on the context's stream
+ * around every kernel stage (the reference has no timing; its only trace is MOE_DEBUG logging,
+ * src/main.rs:21-28).  While enabled, each moe_forward / moe_forward_routed waits for its own
+ * completion to read its events, so enable it only for measurement runs. */
+typedef struct moe_stage_stat {
+    char name[24];       /* "router", "topk", "bucket", "gemv13", "gemv2", "combine", ... */
+    uint32_t calls;      /* launches of this stage since the last reset */
+    float total_ms;      /* summed device time */
+} moe_stage_stat;
+
+/* Enable (1) or disable (0) stage timing; either resets the accumulated statistics. */
+int moe_profile(moe_ctx* ctx, int enable);
+/* Copy up to `max` stage statistics; *n receives the number of stages. */
+int moe_profile_read(moe_ctx* ctx, moe_stage_stat* out, int max, int* n);
+/* Number of kernels this context has launched since creation. */
+int moe_launch_count(moe_ctx* ctx, uint64_t* n);
+
+/* ---- weight utilities ------------------------------------------------------------------ */
+
+/* Decode n_blocks IQ4_XS blocks at src_off into f32 [n_blocks*256] at dst_off (exact; the
+ * dequant_iq4_xs primitive of shaders/common.glsl:59-86 for the GGUF block format). */
+int moe_dequant_iq4xs(moe_ctx* ctx, uint64_t src_off, uint64_t n_blocks, uint64_t dst_off);
+
+/* Fill n_blocks synthetic IQ4_XS blocks at dst_off (seeded counter-based generator: block b
+ * is 17 little-endian words splitmix64(key + 17*(block_start+b) + i), then its f16 d is
+ * replaced by f16(0.005 + 0.015*u), u = (word0 >> 40) * 2^-24).  Benchmark/test input only. */
+int moe_synth_iq4xs(moe_ctx* ctx, uint64_t dst_off, uint64_t key, uint64_t block_start,
+                    uint64_t n_blocks);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* MOE_B200_H */

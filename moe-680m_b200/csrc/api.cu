@@ -1,0 +1,626 @@
+// C ABI entry points (include/moe_b200.h): context, arena, layers, routing, bucketing and the
+// MoE layer forward.  Host-side validation happens here, before any launch: offsets must be
+// non-zero (offset 0 is the reference's "missing tensor" sentinel, src/memory.rs:33,234),
+// aligned and inside the arena; shapes must be ones the kernels support.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "moe_common.cuh"
+#include "moe_internal.h"
+
+using moe::Ctx;
+using moe::Layer;
+using moe::Workspace;
+
+struct moe_ctx : public Ctx {};
+
+namespace {
+
+thread_local std::string g_create_error;
+
+int fail(Ctx* c, int code, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    if (c) c->err = buf; else g_create_error = buf;
+    return code;
+}
+
+int cuda_fail(Ctx* c, cudaError_t e, const char* what) {
+    return fail(c, MOE_E_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+#define MOE_CUDA(c, call)                                   \
+    do {                                                    \
+        cudaError_t e_ = (call);                            \
+        if (e_ != cudaSuccess) return cuda_fail(c, e_, #call); \
+    } while (0)
+
+bool off_ok(const Ctx* c, uint64_t off, uint64_t bytes, uint64_t align) {
+    if (off == 0 || off % align != 0) return false;
+    if (off > c->bytes || bytes > c->bytes - off) return false;
+    return true;
+}
+
+template <typename T>
+T* at(const Ctx* c, uint64_t off) {
+    return reinterpret_cast<T*>(c->base + off);
+}
+
+size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+void free_ws(Workspace& ws) {
+    if (ws.base) cudaFree(ws.base);
+    ws = Workspace{};
+}
+
+// Grow the workspace to hold a forward of M tokens for (E, k, slots, H, I).
+int ensure_ws(Ctx* c, uint32_t M, uint32_t E, uint32_t k, uint32_t slots, uint32_t H,
+              uint32_t I) {
+    Workspace& ws = c->ws;
+    if (ws.base && M <= ws.cap_tokens && E <= ws.cap_experts && slots <= ws.cap_slots &&
+        H <= ws.cap_hidden && I <= ws.cap_inter)
+        return MOE_OK;
+    M = std::max(M, ws.cap_tokens);
+    E = std::max(E, ws.cap_experts);
+    slots = std::max(std::max(slots, k + 1), ws.cap_slots);
+    H = std::max(H, ws.cap_hidden);
+    I = std::max(I, ws.cap_inter);
+    const size_t S = static_cast<size_t>(M) * slots;
+    const int tiles = (M + 255) / 256;
+    const int max_chunks = moe::max_chunks_for(M, slots, E);
+    size_t off = 0;
+    auto take = [&](size_t bytes) { const size_t o = off; off = align_up(off + bytes, 256); return o; };
+    const size_t o_logits = take(sizeof(float) * 4 * M * (E + 1));
+    const size_t o_topk = take(sizeof(uint2) * M * (slots + 1));
+    const size_t o_tile = take(sizeof(int) * tiles * (E + 1));
+    const size_t o_ranges = take(sizeof(int) * (E + 2));
+    const size_t o_stok = take(sizeof(int) * S);
+    const size_t o_sw = take(sizeof(float) * S);
+    const size_t o_pos = take(sizeof(int) * M * slots);
+    const size_t o_chunks = take(sizeof(moe::Chunk) * max_chunks);
+    const size_t o_cnt = take(sizeof(int) * 8);
+    const size_t o_h = take(sizeof(float) * S * I);
+    const size_t o_y = take(sizeof(float) * S * H);
+    const size_t total = off;
+    int* status = ws.status;
+    ws.status = nullptr;
+    cudaStreamSynchronize(c->stream);
+    free_ws(ws);
+    void* p = nullptr;
+    cudaError_t e = cudaMalloc(&p, total);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        ws.status = status;
+        return fail(c, MOE_E_OOM, "workspace of %zu bytes for %u tokens: %s", total, M,
+                    cudaGetErrorString(e));
+    }
+    uint8_t* b = static_cast<uint8_t*>(p);
+    ws.base = b;
+    ws.bytes = total;
+    ws.cap_tokens = M; ws.cap_experts = E; ws.cap_slots = slots; ws.cap_hidden = H; ws.cap_inter = I;
+    ws.logits = reinterpret_cast<float*>(b + o_logits);
+    ws.topk = reinterpret_cast<uint2*>(b + o_topk);
+    ws.tilecnt = reinterpret_cast<int*>(b + o_tile);
+    ws.ranges = reinterpret_cast<int*>(b + o_ranges);
+    ws.sorted_tok = reinterpret_cast<int*>(b + o_stok);
+    ws.sorted_w = reinterpret_cast<float*>(b + o_sw);
+    ws.slot_pos = reinterpret_cast<int*>(b + o_pos);
+    ws.chunks = reinterpret_cast<moe::Chunk*>(b + o_chunks);
+    ws.counters = reinterpret_cast<int*>(b + o_cnt);
+    ws.h = reinterpret_cast<float*>(b + o_h);
+    ws.ypart = reinterpret_cast<float*>(b + o_y);
+    ws.max_chunks = static_cast<uint32_t>(max_chunks);
+    ws.status = status;
+    return MOE_OK;
+}
+
+int ensure_layer_ws(Ctx* c, const Layer& L, uint32_t M) {
+    return ensure_ws(c, M, L.spec.n_experts, L.spec.top_k, static_cast<uint32_t>(L.slots()),
+                     L.spec.hidden, L.spec.inter);
+}
+
+struct DeviceGuard {
+    explicit DeviceGuard(int dev) { cudaSetDevice(dev); }
+};
+
+int check_launch(Ctx* c, const char* what) {
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(c, e, what);
+    return MOE_OK;
+}
+
+int get_layer(Ctx* c, uint32_t id, Layer** L) {
+    if (id >= c->layers.size()) return fail(c, MOE_E_INVALID, "unknown layer id %u", id);
+    *L = &c->layers[id];
+    return MOE_OK;
+}
+
+int check_tokens(Ctx* c, const Layer& L, uint64_t off, uint32_t M, const char* name) {
+    if (!off_ok(c, off, static_cast<uint64_t>(M) * L.spec.hidden * 4, 16))
+        return fail(c, MOE_E_INVALID, "%s offset %llu invalid for %u tokens", name,
+                    static_cast<unsigned long long>(off), M);
+    return MOE_OK;
+}
+
+// ---- tracing: one event per stage boundary of the current call --------------------------
+void prof_begin(Ctx* c) {
+    if (!c->prof) return;
+    c->ev_names.clear();
+    if (c->ev.empty()) {
+        cudaEvent_t e;
+        cudaEventCreate(&e);
+        c->ev.push_back(e);
+    }
+    cudaEventRecord(c->ev[0], c->stream);
+}
+
+// Marks the end of a stage of `n_launch` kernels.
+void stage(Ctx* c, const char* name, int n_launch) {
+    c->launches += static_cast<uint64_t>(n_launch);
+    if (!c->prof) return;
+    c->ev_names.push_back(name);
+    const size_t i = c->ev_names.size();
+    while (c->ev.size() <= i) {
+        cudaEvent_t e;
+        cudaEventCreate(&e);
+        c->ev.push_back(e);
+    }
+    cudaEventRecord(c->ev[i], c->stream);
+}
+
+void prof_end(Ctx* c) {
+    if (!c->prof || c->ev_names.empty()) return;
+    cudaEventSynchronize(c->ev[c->ev_names.size()]);
+    for (size_t i = 0; i < c->ev_names.size(); ++i) {
+        float ms = 0.f;
+        cudaEventElapsedTime(&ms, c->ev[i], c->ev[i + 1]);
+        moe::StageStat* st = nullptr;
+        for (auto& s : c->stats)
+            if (s.name == c->ev_names[i]) st = &s;
+        if (!st) {
+            c->stats.push_back(moe::StageStat{c->ev_names[i], 0, 0.0});
+            st = &c->stats.back();
+        }
+        st->calls += 1;
+        st->total_ms += ms;
+    }
+    c->ev_names.clear();
+}
+
+// Routing of M tokens into ws.topk.
+int run_route(Ctx* c, const Layer& L, const float* x, uint32_t M) {
+    moe::launch_router_logits(L, x, static_cast<int>(M), c->ws.logits, c->stream);
+    stage(c, "router", 1);
+    moe::launch_topk(L, c->ws.logits, static_cast<int>(M), c->ws.topk, c->ws.status, c->stream);
+    stage(c, "topk", 1);
+    return check_launch(c, "router");
+}
+
+int run_experts(Ctx* c, const Layer& L, const float* x, const float* resid, float* out,
+                uint32_t M) {
+    Workspace& ws = c->ws;
+    const int slots = L.slots();
+    moe::launch_bucket(static_cast<int>(L.spec.n_experts), static_cast<int>(L.spec.top_k),
+                       L.has_shared(), ws.topk, static_cast<int>(M), ws, ws.ranges,
+                       ws.sorted_tok, ws.sorted_w, ws.slot_pos, ws.status, c->stream);
+    stage(c, "bucket", 3);
+    const int max_chunks = moe::max_chunks_for(static_cast<int>(M), slots,
+                                               static_cast<int>(L.spec.n_experts));
+    moe::launch_gemv13(L, x, ws, static_cast<int>(M), max_chunks, c->sm_count, c->stream);
+    stage(c, "gemv13", 1);
+    moe::launch_gemv2(L, ws, static_cast<int>(M), max_chunks, c->sm_count, c->stream);
+    stage(c, "gemv2", 1);
+    moe::launch_combine(L, ws, resid, out, static_cast<int>(M), c->stream);
+    stage(c, "combine", 1);
+    return check_launch(c, "experts");
+}
+
+}  // namespace
+
+extern "C" {
+
+int moe_abi_version(void) { return MOE_B200_ABI_VERSION; }
+
+static int ctx_init(int device, moe_ctx* c) {
+    c->device = device;
+    cudaDeviceProp prop;
+    MOE_CUDA(c, cudaGetDeviceProperties(&prop, device));
+    if (prop.major != 10)
+        return fail(c, MOE_E_UNSUPPORTED, "device %d is sm_%d%d; this build targets sm_100a",
+                    device, prop.major, prop.minor);
+    c->sm_count = prop.multiProcessorCount;
+    MOE_CUDA(c, cudaStreamCreateWithFlags(&c->own_stream, cudaStreamNonBlocking));
+    c->stream = c->own_stream;
+    void* st = nullptr;
+    MOE_CUDA(c, cudaMalloc(&st, 256));
+    MOE_CUDA(c, cudaMemset(st, 0, 256));
+    c->ws.status = static_cast<int*>(st);
+    return MOE_OK;
+}
+
+int moe_ctx_create(int device, uint64_t arena_bytes, moe_ctx** out) {
+    if (!out) return fail(nullptr, MOE_E_INVALID, "out is NULL");
+    *out = nullptr;
+    if (arena_bytes < 256) return fail(nullptr, MOE_E_INVALID, "arena too small");
+    int n = 0;
+    cudaError_t e = cudaGetDeviceCount(&n);
+    if (e != cudaSuccess || device < 0 || device >= n)
+        return fail(nullptr, MOE_E_CUDA, "no CUDA device %d (%s)", device,
+                    e == cudaSuccess ? "out of range" : cudaGetErrorString(e));
+    cudaSetDevice(device);
+    moe_ctx* c = new moe_ctx();
+    int rc = ctx_init(device, c);
+    if (rc != MOE_OK) { g_create_error = c->err; moe_ctx_destroy(c); return rc; }
+    void* p = nullptr;
+    e = cudaMalloc(&p, arena_bytes);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        fail(nullptr, MOE_E_OOM, "arena of %llu bytes: %s",
+             static_cast<unsigned long long>(arena_bytes), cudaGetErrorString(e));
+        moe_ctx_destroy(c);
+        return MOE_E_OOM;
+    }
+    c->base = static_cast<uint8_t*>(p);
+    c->bytes = arena_bytes;
+    c->owns = true;
+    *out = c;
+    return MOE_OK;
+}
+
+int moe_ctx_create_external(int device, void* base, uint64_t bytes, moe_ctx** out) {
+    if (!out || !base) return fail(nullptr, MOE_E_INVALID, "out/base is NULL");
+    *out = nullptr;
+    if (reinterpret_cast<uintptr_t>(base) % 256 != 0)
+        return fail(nullptr, MOE_E_INVALID, "external arena must be 256-byte aligned");
+    int n = 0;
+    cudaError_t e = cudaGetDeviceCount(&n);
+    if (e != cudaSuccess || device < 0 || device >= n)
+        return fail(nullptr, MOE_E_CUDA, "no CUDA device %d", device);
+    cudaSetDevice(device);
+    moe_ctx* c = new moe_ctx();
+    int rc = ctx_init(device, c);
+    if (rc != MOE_OK) { g_create_error = c->err; moe_ctx_destroy(c); return rc; }
+    c->base = static_cast<uint8_t*>(base);
+    c->bytes = bytes;
+    c->owns = false;
+    *out = c;
+    return MOE_OK;
+}
+
+void moe_ctx_destroy(moe_ctx* c) {
+    if (!c) return;
+    cudaSetDevice(c->device);
+    if (c->stream) cudaStreamSynchronize(c->stream);
+    for (auto& L : c->layers)
+        if (L.tab) cudaFree(const_cast<uint8_t**>(L.tab));
+    int* status = c->ws.status;
+    free_ws(c->ws);
+    if (status) cudaFree(status);
+    if (c->owns && c->base) cudaFree(c->base);
+    for (cudaEvent_t e : c->ev) cudaEventDestroy(e);
+    if (c->own_stream) cudaStreamDestroy(c->own_stream);
+    delete c;
+}
+
+int moe_last_error(const moe_ctx* c, char* buf, size_t n) {
+    if (!buf || n == 0) return MOE_E_INVALID;
+    const std::string& s = c ? c->err : g_create_error;
+    std::snprintf(buf, n, "%s", s.c_str());
+    return MOE_OK;
+}
+
+int moe_arena_upload(moe_ctx* c, uint64_t off, const void* host, uint64_t n) {
+    if (!c || !host) return fail(c, MOE_E_INVALID, "NULL argument");
+    if (n == 0) return MOE_OK;
+    if (!off_ok(c, off, n, 1)) return fail(c, MOE_E_INVALID, "upload [%llu, +%llu) outside arena",
+                                          (unsigned long long)off, (unsigned long long)n);
+    DeviceGuard g(c->device);
+    MOE_CUDA(c, cudaMemcpyAsync(c->base + off, host, n, cudaMemcpyHostToDevice, c->stream));
+    return MOE_OK;
+}
+
+int moe_arena_download(moe_ctx* c, uint64_t off, void* host, uint64_t n) {
+    if (!c || !host) return fail(c, MOE_E_INVALID, "NULL argument");
+    if (n == 0) return MOE_OK;
+    if (!off_ok(c, off, n, 1)) return fail(c, MOE_E_INVALID, "download [%llu, +%llu) outside arena",
+                                          (unsigned long long)off, (unsigned long long)n);
+    DeviceGuard g(c->device);
+    MOE_CUDA(c, cudaMemcpyAsync(host, c->base + off, n, cudaMemcpyDeviceToHost, c->stream));
+    MOE_CUDA(c, cudaStreamSynchronize(c->stream));
+    return MOE_OK;
+}
+
+int moe_arena_ptr(moe_ctx* c, uint64_t off, void** dptr) {
+    if (!c || !dptr) return fail(c, MOE_E_INVALID, "NULL argument");
+    if (off >= c->bytes) return fail(c, MOE_E_INVALID, "offset outside arena");
+    *dptr = c->base + off;
+    return MOE_OK;
+}
+
+int moe_set_stream(moe_ctx* c, void* stream) {
+    if (!c) return fail(c, MOE_E_INVALID, "NULL context");
+    c->stream = stream ? static_cast<cudaStream_t>(stream) : c->own_stream;
+    return MOE_OK;
+}
+
+int moe_sync(moe_ctx* c) {
+    if (!c) return fail(c, MOE_E_INVALID, "NULL context");
+    DeviceGuard g(c->device);
+    MOE_CUDA(c, cudaStreamSynchronize(c->stream));
+    int st = 0;
+    MOE_CUDA(c, cudaMemcpy(&st, c->ws.status, sizeof(int), cudaMemcpyDeviceToHost));
+    if (st != 0) {
+        cudaMemset(c->ws.status, 0, sizeof(int));
+        const char* what = st == moe::kDevBadExpert ? "expert id out of range"
+                         : st == moe::kDevBadToken ? "token index out of range"
+                         : st == moe::kDevOverflow ? "chunk list overflow" : "device error";
+        return fail(c, MOE_E_DEVICE, "kernel reported status %d (%s)", st, what);
+    }
+    return MOE_OK;
+}
+
+int moe_layer_create(moe_ctx* c, const moe_layer_spec* spec, const uint64_t* w1,
+                     const uint64_t* w3, const uint64_t* w2, uint32_t* layer_id) {
+    if (!c || !spec || !w1 || !w3 || !w2 || !layer_id) return fail(c, MOE_E_INVALID, "NULL argument");
+    const moe_layer_spec& s = *spec;
+    if (s.hidden == 0 || s.hidden % 256 != 0 || s.hidden > 16384)
+        return fail(c, MOE_E_UNSUPPORTED, "hidden %u: must be a multiple of 256, <= 16384", s.hidden);
+    if (s.inter != 256 && s.inter != 512 && s.inter != 1024)
+        return fail(c, MOE_E_UNSUPPORTED, "inter %u: supported 256, 512, 1024", s.inter);
+    if (s.n_experts == 0 || s.n_experts > moe::kMaxExperts)
+        return fail(c, MOE_E_UNSUPPORTED, "n_experts %u: supported 1..256", s.n_experts);
+    if (s.top_k == 0 || s.top_k > moe::kMaxTopK || s.top_k > s.n_experts)
+        return fail(c, MOE_E_UNSUPPORTED, "top_k %u: supported 1..min(8, n_experts)", s.top_k);
+    if ((s.flags & MOE_F_SHARED_GATE) && !(s.flags & MOE_F_SHARED))
+        return fail(c, MOE_E_INVALID, "MOE_F_SHARED_GATE needs MOE_F_SHARED");
+    const uint64_t H = s.hidden, I = s.inter, E = s.n_experts;
+    if (!off_ok(c, s.router_w, E * H * 4, 16)) return fail(c, MOE_E_INVALID, "router_w offset invalid");
+    if (s.router_bias && !off_ok(c, s.router_bias, E * 4, 4))
+        return fail(c, MOE_E_INVALID, "router_bias offset invalid");
+    if (s.flags & MOE_F_SHARED_GATE) {
+        if (!off_ok(c, s.shared_gate, H * 4, 16)) return fail(c, MOE_E_INVALID, "shared_gate offset invalid");
+    }
+    const uint64_t b13 = I * (H / 256) * 136, b2 = H * (I / 256) * 136;
+    std::vector<const uint8_t*> tab(3 * (E + 1), nullptr);
+    for (uint64_t e = 0; e < E; ++e) {
+        if (!off_ok(c, w1[e], b13, 256) || !off_ok(c, w3[e], b13, 256) || !off_ok(c, w2[e], b2, 256))
+            return fail(c, MOE_E_INVALID, "expert %llu: weight offset missing, misaligned or outside arena",
+                        static_cast<unsigned long long>(e));
+        tab[e] = c->base + w1[e];
+        tab[(E + 1) + e] = c->base + w3[e];
+        tab[2 * (E + 1) + e] = c->base + w2[e];
+    }
+    if (s.flags & MOE_F_SHARED) {
+        if (!off_ok(c, s.shared_w1, b13, 256) || !off_ok(c, s.shared_w3, b13, 256) ||
+            !off_ok(c, s.shared_w2, b2, 256))
+            return fail(c, MOE_E_INVALID, "shared expert weight offset missing, misaligned or outside arena");
+        tab[E] = c->base + s.shared_w1;
+        tab[(E + 1) + E] = c->base + s.shared_w3;
+        tab[2 * (E + 1) + E] = c->base + s.shared_w2;
+    }
+    DeviceGuard g(c->device);
+    void* d = nullptr;
+    MOE_CUDA(c, cudaMalloc(&d, tab.size() * sizeof(void*)));
+    MOE_CUDA(c, cudaMemcpy(d, tab.data(), tab.size() * sizeof(void*), cudaMemcpyHostToDevice));
+    Layer L;
+    L.spec = s;
+    L.tab = static_cast<const uint8_t**>(d);
+    L.router_w_ptr = c->base + s.router_w;
+    L.bias_ptr = s.router_bias ? c->base + s.router_bias : nullptr;
+    L.gate_ptr = (s.flags & MOE_F_SHARED_GATE) ? c->base + s.shared_gate : nullptr;
+    c->layers.push_back(L);
+    *layer_id = static_cast<uint32_t>(c->layers.size() - 1);
+    return MOE_OK;
+}
+
+int moe_reserve(moe_ctx* c, uint32_t layer_id, uint32_t max_tokens) {
+    if (!c) return fail(c, MOE_E_INVALID, "NULL context");
+    Layer* L;
+    int rc = get_layer(c, layer_id, &L);
+    if (rc) return rc;
+    DeviceGuard g(c->device);
+    return ensure_layer_ws(c, *L, std::max(max_tokens, 1u));
+}
+
+int moe_route(moe_ctx* c, uint32_t layer_id, uint64_t x_off, uint32_t M, uint64_t topk_off) {
+    if (!c) return fail(c, MOE_E_INVALID, "NULL context");
+    Layer* L;
+    int rc = get_layer(c, layer_id, &L);
+    if (rc) return rc;
+    if (M == 0) return MOE_OK;
+    if ((rc = check_tokens(c, *L, x_off, M, "x"))) return rc;
+    const uint64_t rec = static_cast<uint64_t>(M) * (L->spec.top_k + 1) * 8;
+    if (!off_ok(c, topk_off, rec, 8)) return fail(c, MOE_E_INVALID, "topk offset invalid");
+    DeviceGuard g(c->device);
+    if ((rc = ensure_layer_ws(c, *L, M))) return rc;
+    if ((rc = run_route(c, *L, at<float>(c, x_off), M))) return rc;
+    MOE_CUDA(c, cudaMemcpyAsync(c->base + topk_off, c->ws.topk, rec, cudaMemcpyDeviceToDevice, c->stream));
+    return MOE_OK;
+}
+
+int moe_do_route(moe_ctx* c, uint32_t layer_id, uint64_t x_off, uint32_t M, uint16_t* routed,
+                 float* weights, float* shared_gate) {
+    if (!c || !routed || !weights) return fail(c, MOE_E_INVALID, "NULL argument");
+    Layer* L;
+    int rc = get_layer(c, layer_id, &L);
+    if (rc) return rc;
+    if (M == 0) return MOE_OK;
+    if ((rc = check_tokens(c, *L, x_off, M, "x"))) return rc;
+    DeviceGuard g(c->device);
+    if ((rc = ensure_layer_ws(c, *L, M))) return rc;
+    if ((rc = run_route(c, *L, at<float>(c, x_off), M))) return rc;
+    const int k = static_cast<int>(L->spec.top_k);
+    std::vector<uint2> rec(static_cast<size_t>(M) * (k + 1));
+    MOE_CUDA(c, cudaMemcpyAsync(rec.data(), c->ws.topk, rec.size() * sizeof(uint2),
+                                cudaMemcpyDeviceToHost, c->stream));
+    if ((rc = moe_sync(c))) return rc;
+    for (uint32_t t = 0; t < M; ++t) {
+        const uint2* r = &rec[static_cast<size_t>(t) * (k + 1)];
+        for (int s = 0; s < k; ++s) {
+            routed[static_cast<size_t>(t) * k + s] = static_cast<uint16_t>(r[1 + s].x);
+            float w;
+            std::memcpy(&w, &r[1 + s].y, 4);
+            weights[static_cast<size_t>(t) * k + s] = w;
+        }
+        if (shared_gate) std::memcpy(&shared_gate[t], &r[0].y, 4);
+    }
+    return MOE_OK;
+}
+
+int moe_bucket(moe_ctx* c, uint32_t n_experts, uint32_t top_k, int has_shared, uint64_t topk_off,
+               uint32_t M, uint64_t ranges_off, uint64_t tokens_off, uint64_t weights_off,
+               uint64_t slot_pos_off) {
+    if (!c) return fail(c, MOE_E_INVALID, "NULL context");
+    if (n_experts == 0 || n_experts > moe::kMaxExperts || top_k == 0 || top_k > moe::kMaxTopK ||
+        top_k > n_experts)
+        return fail(c, MOE_E_UNSUPPORTED, "n_experts %u / top_k %u unsupported", n_experts, top_k);
+    if (M == 0) return MOE_OK;
+    const uint64_t slots = top_k + (has_shared ? 1 : 0);
+    const uint64_t S = static_cast<uint64_t>(M) * slots;
+    if (!off_ok(c, topk_off, static_cast<uint64_t>(M) * (top_k + 1) * 8, 8) ||
+        !off_ok(c, ranges_off, (n_experts + 2) * 4ull, 4) || !off_ok(c, tokens_off, S * 4, 4) ||
+        !off_ok(c, weights_off, S * 4, 4) || !off_ok(c, slot_pos_off, S * 4, 4))
+        return fail(c, MOE_E_INVALID, "bucket buffer offsets invalid");
+    DeviceGuard g(c->device);
+    int rc = ensure_ws(c, M, n_experts, top_k, static_cast<uint32_t>(slots), 0, 0);
+    if (rc) return rc;
+    moe::launch_bucket(static_cast<int>(n_experts), static_cast<int>(top_k), has_shared != 0,
+                       at<uint2>(c, topk_off), static_cast<int>(M), c->ws, at<int>(c, ranges_off),
+                       at<int>(c, tokens_off), at<float>(c, weights_off), at<int>(c, slot_pos_off),
+                       c->ws.status, c->stream);
+    stage(c, "bucket", 3);
+    return check_launch(c, "bucket");
+}
+
+int moe_forward(moe_ctx* c, uint32_t layer_id, uint64_t x_off, uint64_t resid_off,
+                uint64_t out_off, uint32_t M) {
+    if (!c) return fail(c, MOE_E_INVALID, "NULL context");
+    Layer* L;
+    int rc = get_layer(c, layer_id, &L);
+    if (rc) return rc;
+    if (M == 0) return MOE_OK;
+    if ((rc = check_tokens(c, *L, x_off, M, "x"))) return rc;
+    if (resid_off && (rc = check_tokens(c, *L, resid_off, M, "resid"))) return rc;
+    if ((rc = check_tokens(c, *L, out_off, M, "out"))) return rc;
+    DeviceGuard g(c->device);
+    if ((rc = ensure_layer_ws(c, *L, M))) return rc;
+    const float* x = at<float>(c, x_off);
+    prof_begin(c);
+    if ((rc = run_route(c, *L, x, M))) return rc;
+    rc = run_experts(c, *L, x, resid_off ? at<float>(c, resid_off) : nullptr, at<float>(c, out_off), M);
+    prof_end(c);
+    return rc;
+}
+
+int moe_forward_routed(moe_ctx* c, uint32_t layer_id, uint64_t x_off, uint64_t resid_off,
+                       uint64_t out_off, uint32_t M, const uint16_t* routed, const float* weights,
+                       const float* shared_gate) {
+    if (!c || !routed || !weights) return fail(c, MOE_E_INVALID, "NULL argument");
+    Layer* L;
+    int rc = get_layer(c, layer_id, &L);
+    if (rc) return rc;
+    if (M == 0) return MOE_OK;
+    if ((rc = check_tokens(c, *L, x_off, M, "x"))) return rc;
+    if (resid_off && (rc = check_tokens(c, *L, resid_off, M, "resid"))) return rc;
+    if ((rc = check_tokens(c, *L, out_off, M, "out"))) return rc;
+    const int k = static_cast<int>(L->spec.top_k);
+    const uint32_t E = L->spec.n_experts;
+    std::vector<uint2> rec(static_cast<size_t>(M) * (k + 1));
+    for (uint32_t t = 0; t < M; ++t) {
+        uint2* r = &rec[static_cast<size_t>(t) * (k + 1)];
+        float g = shared_gate ? shared_gate[t] : 1.0f;
+        uint32_t gb;
+        std::memcpy(&gb, &g, 4);
+        r[0] = make_uint2(E, gb);
+        for (int s = 0; s < k; ++s) {
+            const uint16_t e = routed[static_cast<size_t>(t) * k + s];
+            if (e >= E) return fail(c, MOE_E_INVALID, "token %u slot %d: expert %u >= %u", t, s, e, E);
+            for (int s2 = 0; s2 < s; ++s2)
+                if (routed[static_cast<size_t>(t) * k + s2] == e)
+                    return fail(c, MOE_E_INVALID, "token %u: expert %u routed twice", t, e);
+            uint32_t wb;
+            std::memcpy(&wb, &weights[static_cast<size_t>(t) * k + s], 4);
+            r[1 + s] = make_uint2(e, wb);
+        }
+    }
+    DeviceGuard g(c->device);
+    if ((rc = ensure_layer_ws(c, *L, M))) return rc;
+    // Pageable source: the copy has left `rec` when cudaMemcpyAsync returns.
+    MOE_CUDA(c, cudaMemcpyAsync(c->ws.topk, rec.data(), rec.size() * sizeof(uint2),
+                                cudaMemcpyHostToDevice, c->stream));
+    const float* x = at<float>(c, x_off);
+    prof_begin(c);
+    rc = run_experts(c, *L, x, resid_off ? at<float>(c, resid_off) : nullptr, at<float>(c, out_off), M);
+    prof_end(c);
+    return rc;
+}
+
+int moe_profile(moe_ctx* c, int enable) {
+    if (!c) return fail(c, MOE_E_INVALID, "NULL context");
+    c->prof = enable != 0;
+    c->stats.clear();
+    c->ev_names.clear();
+    return MOE_OK;
+}
+
+int moe_profile_read(moe_ctx* c, moe_stage_stat* out, int max, int* n) {
+    if (!c || !n) return fail(c, MOE_E_INVALID, "NULL argument");
+    *n = static_cast<int>(c->stats.size());
+    for (int i = 0; i < *n && i < max && out; ++i) {
+        std::memset(&out[i], 0, sizeof(out[i]));
+        std::snprintf(out[i].name, sizeof(out[i].name), "%s", c->stats[i].name.c_str());
+        out[i].calls = c->stats[i].calls;
+        out[i].total_ms = static_cast<float>(c->stats[i].total_ms);
+    }
+    return MOE_OK;
+}
+
+int moe_launch_count(moe_ctx* c, uint64_t* n) {
+    if (!c || !n) return fail(c, MOE_E_INVALID, "NULL argument");
+    *n = c->launches;
+    return MOE_OK;
+}
+
+int moe_rms_norm(moe_ctx* c, uint64_t x_off, uint64_t y_off, uint32_t M, uint32_t H, float eps) {
+    if (!c) return fail(c, MOE_E_INVALID, "NULL context");
+    if (M == 0) return MOE_OK;
+    if (H == 0 || H % 4 != 0) return fail(c, MOE_E_INVALID, "H must be a positive multiple of 4");
+    const uint64_t n = static_cast<uint64_t>(M) * H * 4;
+    if (!off_ok(c, x_off, n, 16) || !off_ok(c, y_off, n, 16)) return fail(c, MOE_E_INVALID, "rms_norm offsets invalid");
+    DeviceGuard g(c->device);
+    moe::launch_rms_norm(at<float>(c, x_off), at<float>(c, y_off), static_cast<int>(M),
+                         static_cast<int>(H), eps, c->stream);
+    stage(c, "rms_norm", 1);
+    return check_launch(c, "rms_norm");
+}
+
+int moe_dequant_iq4xs(moe_ctx* c, uint64_t src_off, uint64_t n_blocks, uint64_t dst_off) {
+    if (!c) return fail(c, MOE_E_INVALID, "NULL context");
+    if (n_blocks == 0) return MOE_OK;
+    if (!off_ok(c, src_off, n_blocks * 136, 4) || !off_ok(c, dst_off, n_blocks * 1024, 4))
+        return fail(c, MOE_E_INVALID, "dequant offsets invalid");
+    DeviceGuard g(c->device);
+    moe::launch_dequant(c->base + src_off, n_blocks, at<float>(c, dst_off), c->stream);
+    return check_launch(c, "dequant");
+}
+
+int moe_synth_iq4xs(moe_ctx* c, uint64_t dst_off, uint64_t key, uint64_t block_start,
+                    uint64_t n_blocks) {
+    if (!c) return fail(c, MOE_E_INVALID, "NULL context");
+    if (n_blocks == 0) return MOE_OK;
+    if (!off_ok(c, dst_off, n_blocks * 136, 8)) return fail(c, MOE_E_INVALID, "synth offset invalid");
+    DeviceGuard g(c->device);
+    moe::launch_synth(c->base + dst_off, key, block_start, n_blocks, c->stream);
+    return check_launch(c, "synth");
+}
+
+}  // extern "C"

@@ -1,0 +1,125 @@
+// Host-side internals shared by the library's translation units.
+#pragma once
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <string>
+#include <vector>
+
+#include "../../include/moe_b200.h"
+
+namespace moe {
+
+// Tokens per chunk of the CUDA-core grouped GEMV kernels.
+constexpr int kGemvTok = 8;
+
+// Device copies of one layer's per-expert weight pointers; index E is the shared expert.
+struct ExpertTables {
+    const uint8_t* const* w1;  // [E+1]
+    const uint8_t* const* w3;  // [E+1]
+    const uint8_t* const* w2;  // [E+1]
+};
+
+struct Layer {
+    moe_layer_spec spec;
+    const uint8_t** tab = nullptr;  // device [3][E+1]
+    const uint8_t* router_w_ptr = nullptr;
+    const uint8_t* bias_ptr = nullptr;  // may be null
+    const uint8_t* gate_ptr = nullptr;  // may be null
+    ExpertTables tables() const {
+        const uint32_t n = spec.n_experts + 1;
+        return ExpertTables{tab, tab + n, tab + 2 * n};
+    }
+    bool has_shared() const { return (spec.flags & MOE_F_SHARED) != 0; }
+    int slots() const { return static_cast<int>(spec.top_k) + (has_shared() ? 1 : 0); }
+};
+
+// Chunk of one bucket handled by the grouped kernels: tokens [start, start+n) of the sorted
+// order, all routed to expert `bucket` (bucket == E: shared expert).
+struct Chunk {
+    int bucket;
+    int start;
+    int n;
+    int pad;
+};
+
+// Workspace carve-up for one forward of up to `cap_tokens` tokens.
+struct Workspace {
+    uint8_t* base = nullptr;
+    size_t bytes = 0;
+    uint32_t cap_tokens = 0;
+    uint32_t cap_experts = 0;
+    uint32_t cap_slots = 0;
+    uint32_t cap_hidden = 0;
+    uint32_t cap_inter = 0;
+    // regions
+    float* logits = nullptr;      // [M][E+1]
+    uint2* topk = nullptr;        // [M][k+1] {id, f32 bits}
+    int* tilecnt = nullptr;       // [tiles][E+1]
+    int* ranges = nullptr;        // [E+2]
+    int* sorted_tok = nullptr;    // [S]
+    float* sorted_w = nullptr;    // [S]
+    int* slot_pos = nullptr;      // [M][k+1]
+    Chunk* chunks = nullptr;      // [max_chunks]
+    int* counters = nullptr;      // [8] device counters (n_chunks, ...)
+    int* status = nullptr;        // device error status
+    float* h = nullptr;           // [S][I]
+    float* ypart = nullptr;       // [S][H]
+    uint2* host_topk = nullptr;   // pinned staging for moe_forward_routed
+    uint32_t max_chunks = 0;
+};
+
+struct StageStat {
+    std::string name;
+    uint32_t calls = 0;
+    double total_ms = 0.0;
+};
+
+struct Ctx {
+    // tracing: events of the current call and accumulated per-stage statistics
+    bool prof = false;
+    std::vector<cudaEvent_t> ev;
+    std::vector<std::string> ev_names;
+    std::vector<StageStat> stats;
+    uint64_t launches = 0;
+    int device = 0;
+    uint8_t* base = nullptr;
+    uint64_t bytes = 0;
+    bool owns = false;
+    cudaStream_t own_stream = nullptr;
+    cudaStream_t stream = nullptr;
+    int sm_count = 148;
+    std::string err;
+    std::vector<Layer> layers;
+    Workspace ws;
+};
+
+// Kernel launchers (stream-ordered, no synchronisation).
+int router_split_for(int M, int H);
+void launch_router_logits(const Layer& L, const float* x, int M, float* logits, cudaStream_t s);
+void launch_topk(const Layer& L, const float* logits, int M, uint2* topk, int* status,
+                 cudaStream_t s);
+void launch_bucket(int E, int k, bool has_shared, const uint2* topk, int M, Workspace& ws,
+                   int* ranges, int* sorted_tok, float* sorted_w, int* slot_pos, int* status,
+                   cudaStream_t s);
+void launch_gemv13(const Layer& L, const float* x, const Workspace& ws, int M, int max_chunks,
+                   int sm_count, cudaStream_t s);
+void launch_gemv2(const Layer& L, const Workspace& ws, int M, int max_chunks, int sm_count,
+                  cudaStream_t s);
+void launch_combine(const Layer& L, const Workspace& ws, const float* resid, float* out, int M,
+                    cudaStream_t s);
+void launch_rms_norm(const float* x, float* y, int M, int H, float eps, cudaStream_t s);
+void launch_dequant(const uint8_t* src, uint64_t n_blocks, float* dst, cudaStream_t s);
+void launch_synth(uint8_t* dst, uint64_t key, uint64_t block_start, uint64_t n_blocks,
+                  cudaStream_t s);
+
+// Upper bound on the chunk count: every non-empty bucket adds at most one partial chunk, and
+// every chunk holds at least one slot.
+inline int max_chunks_for(int M, int slots, int E) {
+    const int S = M * slots;
+    const int nonempty = S < E + 1 ? S : E + 1;
+    const int bound = (S + kGemvTok - 1) / kGemvTok + nonempty;
+    return bound < S ? bound : S;
+}
+
+}  // namespace moe

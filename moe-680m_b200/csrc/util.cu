@@ -1,0 +1,107 @@
+// Utility kernels: f32 IQ4_XS decode (dequant check), synthetic IQ4_XS weights, RMSNorm glue.
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include "moe_common.cuh"
+#include "moe_internal.h"
+
+namespace moe {
+
+namespace {
+
+// One warp per block: lane l decodes weights 8l..8l+7 of the 256 (sub-block l/4).
+__global__ void dequant_kernel(const uint8_t* __restrict__ src, uint64_t n_blocks,
+                               float* __restrict__ dst) {
+    const uint64_t warp = (static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (warp >= n_blocks) return;
+    const uint8_t* blk = src + warp * kBlockBytes;
+    const uint32_t h0 = *reinterpret_cast<const uint32_t*>(blk);
+    const uint32_t h1 = *reinterpret_cast<const uint32_t*>(blk + 4);
+    const int ib = lane >> 2, w = lane & 3;  // sub-block, word inside its 16 qs bytes
+    const uint32_t q = *reinterpret_cast<const uint32_t*>(blk + 8 + ib * 16 + w * 4);
+    const float dl = iq4_subscale(h0, h1, ib);
+    uint32_t r0, r1;
+    kv_lookup8(q, r0, r1);
+    float* o = dst + warp * kQK + ib * 32;
+    const int j0 = w * 4;
+    o[j0 + 0] = dl * kv_float<0>(r0);
+    o[j0 + 16] = dl * kv_float<1>(r0);
+    o[j0 + 1] = dl * kv_float<2>(r0);
+    o[j0 + 17] = dl * kv_float<3>(r0);
+    o[j0 + 2] = dl * kv_float<0>(r1);
+    o[j0 + 18] = dl * kv_float<1>(r1);
+    o[j0 + 3] = dl * kv_float<2>(r1);
+    o[j0 + 19] = dl * kv_float<3>(r1);
+}
+
+// splitmix64 (Steele, Lea & Flood 2014): the published finaliser constants.
+__device__ __forceinline__ uint64_t splitmix64(uint64_t z) {
+    z += 0x9E3779B97F4A7C15ull;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}
+
+// Thread per 8-byte word of the output; word i of block b = splitmix64(key + 17*b + i).
+__global__ void synth_kernel(uint8_t* __restrict__ dst, uint64_t key, uint64_t block_start,
+                             uint64_t n_blocks) {
+    const uint64_t i = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const uint64_t n_words = n_blocks * 17;
+    if (i >= n_words) return;
+    const uint64_t b = i / 17, w = i - b * 17;
+    uint64_t v = splitmix64(key + (block_start + b) * 17 + w);
+    if (w == 0) {
+        const float u = static_cast<float>(static_cast<uint32_t>(v >> 40)) * (1.0f / 16777216.0f);
+        const float d = __fadd_rn(0.005f, __fmul_rn(0.015f, u));
+        const uint64_t hb = __half_as_ushort(__float2half_rn(d));
+        v = (v & ~0xFFFFull) | hb;
+    }
+    // 136-byte blocks are 8-byte aligned: store as two 4-byte halves (alignment 8 holds too).
+    reinterpret_cast<uint64_t*>(dst)[i] = v;
+}
+
+// One CTA per token: y = x * rsqrt(mean(x^2) + eps) (shaders/rms_norm.comp:36-58, no gain).
+__global__ void __launch_bounds__(256)
+rms_norm_kernel(const float* __restrict__ x, float* __restrict__ y, int H, float eps) {
+    __shared__ float red[8];
+    const float* xr = x + static_cast<size_t>(blockIdx.x) * H;
+    float* yr = y + static_cast<size_t>(blockIdx.x) * H;
+    float ss = 0.f;
+    for (int i = threadIdx.x * 4; i < H; i += blockDim.x * 4) {
+        const float4 v = *reinterpret_cast<const float4*>(xr + i);
+        ss = fmaf(v.x, v.x, ss); ss = fmaf(v.y, v.y, ss);
+        ss = fmaf(v.z, v.z, ss); ss = fmaf(v.w, v.w, ss);
+    }
+    ss = warp_sum(ss);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    float tot = 0.f;
+    for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) tot += red[w];
+    const float r = 1.0f / sqrtf(tot / static_cast<float>(H) + eps);
+    for (int i = threadIdx.x * 4; i < H; i += blockDim.x * 4) {
+        float4 v = *reinterpret_cast<const float4*>(xr + i);
+        v.x *= r; v.y *= r; v.z *= r; v.w *= r;
+        *reinterpret_cast<float4*>(yr + i) = v;
+    }
+}
+
+}  // namespace
+
+void launch_dequant(const uint8_t* src, uint64_t n_blocks, float* dst, cudaStream_t s) {
+    const uint64_t threads = n_blocks * 32;
+    dequant_kernel<<<static_cast<unsigned>((threads + 255) / 256), 256, 0, s>>>(src, n_blocks, dst);
+}
+
+void launch_synth(uint8_t* dst, uint64_t key, uint64_t block_start, uint64_t n_blocks,
+                  cudaStream_t s) {
+    const uint64_t words = n_blocks * 17;
+    synth_kernel<<<static_cast<unsigned>((words + 255) / 256), 256, 0, s>>>(dst, key, block_start,
+                                                                           n_blocks);
+}
+
+void launch_rms_norm(const float* x, float* y, int M, int H, float eps, cudaStream_t s) {
+    rms_norm_kernel<<<M, 256, 0, s>>>(x, y, H, eps);
+}
+
+}  // namespace moe
