@@ -102,17 +102,22 @@ def distinct_experts(routed: np.ndarray) -> int:
     return len(np.unique(routed))
 
 
-def cpu_baseline(shapes, sample_tokens: int, x: np.ndarray, threads: int = 0):
-    """C restatement of the reference's MoE layer (f32 accumulation) on the host cores."""
+def cpu_baseline(shapes, x: np.ndarray, min_seconds: float = 10.0, threads: int = 0):
+    """C restatement of the reference's MoE layer (f32 accumulation) on the host cores: whole
+    512-token prefills repeated until ``min_seconds`` of CPU time have passed."""
     sys.path.insert(0, str(ROOT / "oracle"))
     import coracle
     layer = coracle.synthetic_layer(SEED, 0, shapes, ZIPF)
-    xs = np.ascontiguousarray(x[:sample_tokens])
+    xs = np.ascontiguousarray(x)
     coracle.moe_forward(layer, xs[:4], xs[:4], acc64=False, nthreads=threads)  # warm
-    t0 = time.perf_counter()
-    coracle.moe_forward(layer, xs, xs, acc64=False, nthreads=threads)
-    dt = time.perf_counter() - t0
-    return layer, sample_tokens / dt, dt
+    n, t0 = 0, time.perf_counter()
+    while True:
+        coracle.moe_forward(layer, xs, xs, acc64=False, nthreads=threads)
+        n += xs.shape[0]
+        dt = time.perf_counter() - t0
+        if dt >= min_seconds:
+            break
+    return layer, n / dt, dt, n
 
 
 def run_reference(args):
@@ -178,7 +183,8 @@ def main():
     n_dec_layers = 16  # decode cycles through 16 layers (6.9 GB) so no step hits in L2
     arena = (n_dec_layers + 1) * sh.expert_bytes * (sh.n_experts + 1) + (256 << 20)
     ctx = host.Context(local, arena)
-    stream = torch.cuda.current_stream()
+    stream = torch.cuda.Stream()  # a real stream: torch events and the library share it
+    torch.cuda.set_stream(stream)
     ctx.set_stream(stream.cuda_stream)
     _, _, pre_ids = host.build_synthetic_model(ctx, SEED, 1, sh, ZIPF)
     pre = pre_ids[0]
@@ -296,9 +302,9 @@ def main():
     # ---- CPU baseline (rank 0, N=1 only) ------------------------------------------------------
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
-        _, v, dt = cpu_baseline(sh, CPU_SAMPLE_TOKENS, xs[0])
+        _, v, dt, n = cpu_baseline(sh, xs[0])
         cpu = {"value": v, "unit": "tok/s", "cores": os.cpu_count(), "kind": "port",
-               "sample": f"{CPU_SAMPLE_TOKENS} tokens of the config-1 prefill ({dt:.1f} s), C "
+               "sample": f"{n} tokens = repeated config-1 512-token prefills ({dt:.1f} s), C "
                          "restatement of the reference MoE layer (oracle/, f32, OpenMP all cores)"}
 
     if rank == 0:

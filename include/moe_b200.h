@@ -139,6 +139,15 @@ int moe_forward_routed(moe_ctx* ctx, uint32_t layer_id, uint64_t x_off, uint64_t
                        uint64_t out_off, uint32_t M, const uint16_t* routed,
                        const float* weights, const float* shared_gate);
 
+/* Expert-product kernels used by moe_forward / moe_forward_routed (a tuning and diagnostic
+ * knob; the default picks by batch size: CUDA-core grouped GEMV for M <= 8, tcgen05 grouped
+ * GEMM otherwise). */
+#define MOE_PATH_AUTO 0
+#define MOE_PATH_GEMV 1        /* CUDA cores, exact f32 dequantisation and accumulation */
+#define MOE_PATH_TC_SMEM_A 2   /* tcgen05, fp16 operands, dequantised weights in shared memory */
+#define MOE_PATH_TC_TMEM_A 3   /* tcgen05, fp16 operands, dequantised weights in tensor memory */
+int moe_set_path(moe_ctx* ctx, int path);
+
 /* ---- stack glue (rms_norm.comp + residual_add.comp, src/inference.rs:474-482, :588-596) -- */
 
 /* y = x / sqrt(mean(x^2) + eps), per token, no gain (shaders/rms_norm.comp:36-58). */

@@ -90,6 +90,14 @@ int ensure_ws(Ctx* c, uint32_t M, uint32_t E, uint32_t k, uint32_t slots, uint32
     const size_t o_cnt = take(sizeof(int) * 8);
     const size_t o_h = take(sizeof(float) * S * I);
     const size_t o_y = take(sizeof(float) * S * H);
+    const int max13 = moe::max_tiles_for(M, slots, E, moe::tc_max_n(13));
+    const int max2 = moe::max_tiles_for(M, slots, E, moe::tc_max_n(2));
+    const size_t o_t13 = take(sizeof(moe::TcTile) * max13);
+    const size_t o_t2 = take(sizeof(moe::TcTile) * max2);
+    const size_t o_x16 = take(sizeof(__half) * S * H);
+    const size_t o_h16 = take(sizeof(__half) * S * I);
+    const size_t o_xe = take(sizeof(int) * S);
+    const size_t o_he = take(sizeof(int) * S);
     const size_t total = off;
     int* status = ws.status;
     ws.status = nullptr;
@@ -118,6 +126,14 @@ int ensure_ws(Ctx* c, uint32_t M, uint32_t E, uint32_t k, uint32_t slots, uint32
     ws.counters = reinterpret_cast<int*>(b + o_cnt);
     ws.h = reinterpret_cast<float*>(b + o_h);
     ws.ypart = reinterpret_cast<float*>(b + o_y);
+    ws.tiles13 = reinterpret_cast<moe::TcTile*>(b + o_t13);
+    ws.tiles2 = reinterpret_cast<moe::TcTile*>(b + o_t2);
+    ws.max_tiles13 = static_cast<uint32_t>(max13);
+    ws.max_tiles2 = static_cast<uint32_t>(max2);
+    ws.x16 = reinterpret_cast<__half*>(b + o_x16);
+    ws.h16 = reinterpret_cast<__half*>(b + o_h16);
+    ws.xexp = reinterpret_cast<int*>(b + o_xe);
+    ws.hexp = reinterpret_cast<int*>(b + o_he);
     ws.max_chunks = static_cast<uint32_t>(max_chunks);
     ws.status = status;
     return MOE_OK;
@@ -205,20 +221,58 @@ int run_route(Ctx* c, const Layer& L, const float* x, uint32_t M) {
     return check_launch(c, "router");
 }
 
+// Expert path for a batch of M tokens: CUDA-core grouped GEMV for decode-sized batches,
+// tcgen05 grouped GEMM otherwise (or as forced by moe_set_path).
+int choose_path(const Ctx* c, uint32_t M) {
+    if (c->path != moe::kPathAuto) return c->path;
+    return M <= 8 ? moe::kPathGemv : moe::kPathTcSmemA;
+}
+
+int ensure_tmap(Ctx* c, CUtensorMap* m, const void** base, uint64_t* rows, uint64_t* cols,
+                const void* p, uint64_t r, uint64_t cl) {
+    if (*base == p && *rows == r && *cols == cl) return MOE_OK;
+    if (!moe::make_fp16_tmap(m, p, r, cl))
+        return fail(c, MOE_E_CUDA, "cuTensorMapEncodeTiled failed (rows %llu, cols %llu)",
+                    static_cast<unsigned long long>(r), static_cast<unsigned long long>(cl));
+    *base = p; *rows = r; *cols = cl;
+    return MOE_OK;
+}
+
 int run_experts(Ctx* c, const Layer& L, const float* x, const float* resid, float* out,
                 uint32_t M) {
     Workspace& ws = c->ws;
     const int slots = L.slots();
-    moe::launch_bucket(static_cast<int>(L.spec.n_experts), static_cast<int>(L.spec.top_k),
-                       L.has_shared(), ws.topk, static_cast<int>(M), ws, ws.ranges,
-                       ws.sorted_tok, ws.sorted_w, ws.slot_pos, ws.status, c->stream);
+    const int E = static_cast<int>(L.spec.n_experts);
+    moe::launch_bucket(E, static_cast<int>(L.spec.top_k), L.has_shared(), ws.topk,
+                       static_cast<int>(M), ws, ws.ranges, ws.sorted_tok, ws.sorted_w,
+                       ws.slot_pos, ws.status, c->stream);
     stage(c, "bucket", 3);
-    const int max_chunks = moe::max_chunks_for(static_cast<int>(M), slots,
-                                               static_cast<int>(L.spec.n_experts));
-    moe::launch_gemv13(L, x, ws, static_cast<int>(M), max_chunks, c->sm_count, c->stream);
-    stage(c, "gemv13", 1);
-    moe::launch_gemv2(L, ws, static_cast<int>(M), max_chunks, c->sm_count, c->stream);
-    stage(c, "gemv2", 1);
+    const int path = choose_path(c, M);
+    if (path == moe::kPathGemv) {
+        const int max_chunks = moe::max_chunks_for(static_cast<int>(M), slots, E);
+        moe::launch_gemv13(L, x, ws, static_cast<int>(M), max_chunks, c->sm_count, c->stream);
+        stage(c, "gemv13", 1);
+        moe::launch_gemv2(L, ws, static_cast<int>(M), max_chunks, c->sm_count, c->stream);
+        stage(c, "gemv2", 1);
+    } else {
+        const bool a_tmem = path == moe::kPathTcTmemA;
+        const uint64_t S = static_cast<uint64_t>(M) * slots;
+        const int H = static_cast<int>(L.spec.hidden), I = static_cast<int>(L.spec.inter);
+        int rc = ensure_tmap(c, &ws.xmap, &ws.xmap_base, &ws.xmap_rows, &ws.xmap_cols, ws.x16, S, H);
+        if (rc) return rc;
+        rc = ensure_tmap(c, &ws.hmap, &ws.hmap_base, &ws.hmap_rows, &ws.hmap_cols, ws.h16, S, I);
+        if (rc) return rc;
+        moe::launch_convert_rows(x, ws.sorted_tok, static_cast<int>(S), H, ws.x16, ws.xexp, c->stream);
+        stage(c, "convert_x", 1);
+        const int items13 = moe::max_tiles_for(static_cast<int>(M), slots, E, moe::tc_max_n(13)) * (I / 128);
+        moe::launch_tc13(L, ws.xmap, ws, items13, c->sm_count, a_tmem, c->stream);
+        stage(c, "tc13", 1);
+        moe::launch_convert_rows(ws.h, nullptr, static_cast<int>(S), I, ws.h16, ws.hexp, c->stream);
+        stage(c, "convert_h", 1);
+        const int items2 = moe::max_tiles_for(static_cast<int>(M), slots, E, moe::tc_max_n(2)) * (H / 128);
+        moe::launch_tc2(L, ws.hmap, ws, items2, c->sm_count, a_tmem, c->stream);
+        stage(c, "tc2", 1);
+    }
     moe::launch_combine(L, ws, resid, out, static_cast<int>(M), c->stream);
     stage(c, "combine", 1);
     return check_launch(c, "experts");
@@ -562,6 +616,14 @@ int moe_forward_routed(moe_ctx* c, uint32_t layer_id, uint64_t x_off, uint64_t r
     rc = run_experts(c, *L, x, resid_off ? at<float>(c, resid_off) : nullptr, at<float>(c, out_off), M);
     prof_end(c);
     return rc;
+}
+
+int moe_set_path(moe_ctx* c, int path) {
+    if (!c) return fail(c, MOE_E_INVALID, "NULL context");
+    if (path < moe::kPathAuto || path > moe::kPathTcTmemA)
+        return fail(c, MOE_E_INVALID, "unknown path %d", path);
+    c->path = path;
+    return MOE_OK;
 }
 
 int moe_profile(moe_ctx* c, int enable) {

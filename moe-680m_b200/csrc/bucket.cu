@@ -56,13 +56,23 @@ bucket_count_kernel(const uint2* __restrict__ topk, int M, int E, int k, int has
 }
 
 // One CTA.  tilecnt[tile][e] -> absolute offset of tile's first slot in bucket e (in place);
-// ranges[0..E+1]; chunks of at most kGemvTok tokens per bucket.
+// ranges[0..E+1]; chunks of at most kGemvTok tokens per bucket; tensor-core token tiles.
+struct TileLists {
+    TcTile* t13;
+    int max13;
+    TcTile* t2;
+    int max2;
+    int n13, n2;  // tokens per tile
+};
+
 __global__ void __launch_bounds__(1024)
 bucket_scan_kernel(int* __restrict__ tilecnt, int n_tiles, int E, int* __restrict__ ranges,
-                   Chunk* __restrict__ chunks, int max_chunks, int* __restrict__ counters,
-                   int* status) {
+                   Chunk* __restrict__ chunks, int max_chunks, TileLists lists,
+                   int* __restrict__ counters, int* status) {
     __shared__ int tot[kMaxExperts + 2];
     __shared__ int nch[kMaxExperts + 2];
+    __shared__ int f13[kMaxExperts + 2];
+    __shared__ int f2[kMaxExperts + 2];
     const int nb = E + 1;
     for (int e = threadIdx.x; e < nb; e += blockDim.x) {
         int run = 0;
@@ -76,18 +86,27 @@ bucket_scan_kernel(int* __restrict__ tilecnt, int n_tiles, int E, int* __restric
     }
     __syncthreads();
     if (threadIdx.x == 0) {
-        int r = 0, c = 0;
+        int r = 0, c = 0, a13 = 0, a2 = 0;
         for (int e = 0; e < nb; ++e) {
             ranges[e] = r;
-            r += tot[e];
+            const int cnt = tot[e];
+            r += cnt;
             const int n = nch[e];
             nch[e] = c;  // first chunk index of bucket e
             c += n;
+            f13[e] = a13;
+            a13 += (cnt + lists.n13 - 1) / lists.n13;
+            f2[e] = a2;
+            a2 += (cnt + lists.n2 - 1) / lists.n2;
             tot[e] = ranges[e];
         }
         ranges[nb] = r;
         if (c > max_chunks) { set_dev_error(status, kDevOverflow); c = max_chunks; }
+        if (a13 > lists.max13) { set_dev_error(status, kDevOverflow); a13 = lists.max13; }
+        if (a2 > lists.max2) { set_dev_error(status, kDevOverflow); a2 = lists.max2; }
         counters[0] = c;
+        counters[1] = a13;
+        counters[2] = a2;
     }
     __syncthreads();
     for (int e = threadIdx.x; e < nb; e += blockDim.x) {
@@ -98,6 +117,14 @@ bucket_scan_kernel(int* __restrict__ tilecnt, int n_tiles, int E, int* __restric
         for (int s = 0; s < cnt; s += kGemvTok, ++ci) {
             if (ci >= max_chunks) break;
             chunks[ci] = Chunk{e, ranges[e] + s, min(kGemvTok, cnt - s), 0};
+        }
+        if (lists.t13) {
+            int ti = f13[e];
+            for (int s = 0; s < cnt && ti < lists.max13; s += lists.n13, ++ti)
+                lists.t13[ti] = TcTile{e, ranges[e] + s, min(lists.n13, cnt - s), 0};
+            ti = f2[e];
+            for (int s = 0; s < cnt && ti < lists.max2; s += lists.n2, ++ti)
+                lists.t2[ti] = TcTile{e, ranges[e] + s, min(lists.n2, cnt - s), 0};
         }
     }
 }
@@ -143,8 +170,10 @@ void launch_bucket(int E, int k, bool has_shared, const uint2* topk, int M, Work
     const size_t smem = 8 * (E + 1) * sizeof(uint32_t);
     bucket_count_kernel<<<n_tiles, kTile, smem, s>>>(topk, M, E, k, has_shared ? 1 : 0,
                                                      ws.tilecnt, status);
+    TileLists tl{ws.tiles13, static_cast<int>(ws.max_tiles13), ws.tiles2,
+                 static_cast<int>(ws.max_tiles2), tc_max_n(13), tc_max_n(2)};
     bucket_scan_kernel<<<1, 1024, 0, s>>>(ws.tilecnt, n_tiles, E, ranges, ws.chunks,
-                                          static_cast<int>(ws.max_chunks), ws.counters, status);
+                                          static_cast<int>(ws.max_chunks), tl, ws.counters, status);
     bucket_scatter_kernel<<<n_tiles, kTile, smem, s>>>(topk, M, E, k, has_shared ? 1 : 0,
                                                        ws.tilecnt, sorted_tok, sorted_w, slot_pos,
                                                        status);

@@ -139,7 +139,7 @@ __host__ __device__ constexpr int padded_len(int n) { return (n / 32) * 36; }
 __device__ __forceinline__ int padded_idx(int k) { return (k >> 5) * 36 + (k & 31); }
 
 // Device-side error codes written to the status word.
-enum DevErr : int { kDevOk = 0, kDevBadExpert = 1, kDevBadToken = 2, kDevOverflow = 3 };
+enum DevErr : int { kDevOk = 0, kDevBadExpert = 1, kDevBadToken = 2, kDevOverflow = 3, kDevTimeout = 4 };
 
 __device__ __forceinline__ void set_dev_error(int* status, int code) {
     if (status) atomicCAS(status, 0, code);

@@ -1,5 +1,7 @@
 // Host-side internals shared by the library's translation units.
 #pragma once
+#include <cuda.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -43,6 +45,17 @@ struct Chunk {
     int pad;
 };
 
+// Token tile of one bucket for the tensor-core kernels: slots [p0, p0+n) of the sorted order.
+struct TcTile {
+    int bucket;
+    int p0;
+    int n;
+    int pad;
+};
+
+// Expert-path selection (moe_set_path).
+enum Path : int { kPathAuto = 0, kPathGemv = 1, kPathTcSmemA = 2, kPathTcTmemA = 3 };
+
 // Workspace carve-up for one forward of up to `cap_tokens` tokens.
 struct Workspace {
     uint8_t* base = nullptr;
@@ -65,6 +78,18 @@ struct Workspace {
     int* status = nullptr;        // device error status
     float* h = nullptr;           // [S][I]
     float* ypart = nullptr;       // [S][H]
+    TcTile* tiles13 = nullptr;    // tensor-core token tiles of <= 64 tokens
+    TcTile* tiles2 = nullptr;     // tensor-core token tiles of <= 128 tokens
+    uint32_t max_tiles13 = 0, max_tiles2 = 0;
+    __half* x16 = nullptr;        // [S][H] gathered, scaled, K-permuted activations
+    __half* h16 = nullptr;        // [S][I]
+    int* xexp = nullptr;          // [S] power-of-two exponent of x16's scale
+    int* hexp = nullptr;          // [S]
+    // tensor maps (re-encoded when the buffers or the slot count change)
+    CUtensorMap xmap, hmap;
+    const void* xmap_base = nullptr;
+    const void* hmap_base = nullptr;
+    uint64_t xmap_rows = 0, hmap_rows = 0, xmap_cols = 0, hmap_cols = 0;
     uint2* host_topk = nullptr;   // pinned staging for moe_forward_routed
     uint32_t max_chunks = 0;
 };
@@ -89,6 +114,7 @@ struct Ctx {
     cudaStream_t own_stream = nullptr;
     cudaStream_t stream = nullptr;
     int sm_count = 148;
+    int path = kPathAuto;
     std::string err;
     std::vector<Layer> layers;
     Workspace ws;
@@ -106,6 +132,14 @@ void launch_gemv13(const Layer& L, const float* x, const Workspace& ws, int M, i
                    int sm_count, cudaStream_t s);
 void launch_gemv2(const Layer& L, const Workspace& ws, int M, int max_chunks, int sm_count,
                   cudaStream_t s);
+int tc_max_n(int mode);
+void launch_convert_rows(const float* src, const int* gather, int n_rows, int len, __half* dst,
+                         int* sexp, cudaStream_t s);
+void launch_tc13(const Layer& L, const CUtensorMap& xmap, const Workspace& ws, int max_items,
+                 int sm_count, bool a_tmem, cudaStream_t s);
+void launch_tc2(const Layer& L, const CUtensorMap& hmap, const Workspace& ws, int max_items,
+                int sm_count, bool a_tmem, cudaStream_t s);
+bool make_fp16_tmap(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols);
 void launch_combine(const Layer& L, const Workspace& ws, const float* resid, float* out, int M,
                     cudaStream_t s);
 void launch_rms_norm(const float* x, float* y, int M, int H, float eps, cudaStream_t s);
@@ -115,6 +149,13 @@ void launch_synth(uint8_t* dst, uint64_t key, uint64_t block_start, uint64_t n_b
 
 // Upper bound on the chunk count: every non-empty bucket adds at most one partial chunk, and
 // every chunk holds at least one slot.
+inline int max_tiles_for(int M, int slots, int E, int nmax) {
+    const int S = M * slots;
+    const int nonempty = S < E + 1 ? S : E + 1;
+    const int bound = (S + nmax - 1) / nmax + nonempty;
+    return bound < S ? bound : S;
+}
+
 inline int max_chunks_for(int M, int slots, int E) {
     const int S = M * slots;
     const int nonempty = S < E + 1 ? S : E + 1;

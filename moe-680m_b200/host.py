@@ -29,8 +29,10 @@ EXPORTS = (
     "moe_arena_upload", "moe_arena_download", "moe_arena_ptr", "moe_set_stream", "moe_sync",
     "moe_last_error", "moe_layer_create", "moe_reserve", "moe_route", "moe_do_route",
     "moe_bucket", "moe_forward", "moe_forward_routed", "moe_rms_norm", "moe_dequant_iq4xs",
-    "moe_synth_iq4xs", "moe_profile", "moe_profile_read", "moe_launch_count",
+    "moe_synth_iq4xs", "moe_profile", "moe_profile_read", "moe_launch_count", "moe_set_path",
 )
+
+PATH_AUTO, PATH_GEMV, PATH_TC_SMEM_A, PATH_TC_TMEM_A = 0, 1, 2, 3
 
 
 class MoeError(RuntimeError):
@@ -95,6 +97,7 @@ def lib():
         "moe_profile": (i32, [vp, i32]),
         "moe_profile_read": (i32, [vp, P(StageStatC), i32, P(i32)]),
         "moe_launch_count": (i32, [vp, P(u64)]),
+        "moe_set_path": (i32, [vp, i32]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -257,6 +260,9 @@ class Context:
         n = C.c_int()
         self._check(lib().moe_profile_read(self.h, arr, 32, C.byref(n)))
         return {arr[i].name.decode(): (arr[i].calls, arr[i].total_ms) for i in range(min(n.value, 32))}
+
+    def set_path(self, path: int):
+        self._check(lib().moe_set_path(self.h, path))
 
     def launch_count(self) -> int:
         n = C.c_uint64()

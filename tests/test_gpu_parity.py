@@ -146,7 +146,7 @@ def test_exact_ties_pick_lower_index(ctx):
     spec = host.LayerSpec(256, 256, 16, 4, 0, 1.0, lw_off)
     e_off = [ctx.alloc(synth.matrix_bytes(256, 256)) for _ in range(3)]
     lid2 = ctx.layer_create(spec, [e_off[0]] * 16, [e_off[1]] * 16, [e_off[2]] * 16)
-    x = synth.tokens(77, 0, 32, 256) + 4.0 * wr[3] / np.linalg.norm(wr[3])
+    x = synth.tokens(77, 0, 32, 256) + 40.0 * wr[3] / np.linalg.norm(wr[3])
     xo = ctx.put(x.astype(np.float32))
     routed, w, _ = ctx.do_route(lid2, xo, 32, 4)
     assert (routed[:, :3] == np.array([3, 9, 12])).all()
