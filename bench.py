@@ -33,7 +33,7 @@ METRIC = "MoE-layer tok/s at M=1 and 512-tok prefill; % of HBM / tensor-core roo
 SEED = 20240601
 PREFILL_M = 512
 ZIPF = 1.1
-CPU_SAMPLE_TOKENS = 64
+CPU_SAMPLE_TOKENS = 512
 
 
 def load_pkg():
@@ -164,6 +164,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--path", type=int, default=0,
+                    help="expert kernels: 0 auto, 1 CUDA-core GEMV, 2 tcgen05 (A in smem), 3 tcgen05 (A in TMEM)")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
@@ -186,6 +188,7 @@ def main():
     stream = torch.cuda.Stream()  # a real stream: torch events and the library share it
     torch.cuda.set_stream(stream)
     ctx.set_stream(stream.cuda_stream)
+    ctx.set_path(args.path)
     _, _, pre_ids = host.build_synthetic_model(ctx, SEED, 1, sh, ZIPF)
     pre = pre_ids[0]
     _, _, dec_ids = host.build_synthetic_model(ctx, SEED + 1, n_dec_layers, sh, None)
@@ -240,6 +243,7 @@ def main():
     hbm, tfl, peak_kind = peaks()
     stage_ms = {k: v[1] / max(v[0], 1) for k, v in stages.items()}
     alg_bytes = {"gemv13": n_mats * 2 * sh.w13_bytes, "gemv2": n_mats * sh.w2_bytes,
+                 "tc13": n_mats * 2 * sh.w13_bytes, "tc2": n_mats * sh.w2_bytes,
                  "router": sh.n_experts * H * 4 + H * 4 + PREFILL_M * H * 4}
     dom = max(stage_ms, key=stage_ms.get)
     layer_bytes = n_mats * sh.expert_bytes
@@ -310,11 +314,14 @@ def main():
     if rank == 0:
         line = {"metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": K,
                 "warmup": W, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
-                "vs_baseline": None, "dtype": "f32",
+                "vs_baseline": None, "dtype": "f32" if args.path == 1 else "f16 (f32 accumulate)",
                 "data": "synthetic (seeded IQ4_XS weights generated on device, N(0,1) tokens)",
                 "config": {"workload": "config1: prefill 512 tok, Zipf(1.1) router bias, 1 MoE layer "
                                        "(H=2048, I=512, E=256, top-8 + gated shared, IQ4_XS)",
                            "tokens_per_step": PREFILL_M, "parallelism": f"replicas x{world}",
+                           "expert_kernels": {0: "auto (tcgen05, A in TMEM)", 1: "CUDA-core GEMV",
+                                              2: "tcgen05, A in smem", 3: "tcgen05, A in TMEM"}[args.path],
+                           "distinct_experts": round(statistics.mean(distinct), 1),
                            "l2": "weights 430 MB per layer exceed the 126 MB L2; fresh tokens per step"},
                 "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches,
                 "clocks": clk.summary(), "decode": decode}

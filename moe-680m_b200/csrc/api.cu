@@ -88,7 +88,7 @@ int ensure_ws(Ctx* c, uint32_t M, uint32_t E, uint32_t k, uint32_t slots, uint32
     const size_t o_pos = take(sizeof(int) * M * slots);
     const size_t o_chunks = take(sizeof(moe::Chunk) * max_chunks);
     const size_t o_cnt = take(sizeof(int) * 8);
-    const size_t o_h = take(sizeof(float) * S * I);
+    const size_t o_h = take(sizeof(float) * S * 2 * I);
     const size_t o_y = take(sizeof(float) * S * H);
     const int max13 = moe::max_tiles_for(M, slots, E, moe::tc_max_n(13));
     const int max2 = moe::max_tiles_for(M, slots, E, moe::tc_max_n(2));
@@ -223,9 +223,9 @@ int run_route(Ctx* c, const Layer& L, const float* x, uint32_t M) {
 
 // Expert path for a batch of M tokens: CUDA-core grouped GEMV for decode-sized batches,
 // tcgen05 grouped GEMM otherwise (or as forced by moe_set_path).
-int choose_path(const Ctx* c, uint32_t M) {
+int choose_path(const Ctx* c, const Layer& L, uint32_t M) {
     if (c->path != moe::kPathAuto) return c->path;
-    return M <= 8 ? moe::kPathGemv : moe::kPathTcSmemA;
+    return (M <= 8 || !L.wmaps) ? moe::kPathGemv : moe::kPathTcTmemA;
 }
 
 int ensure_tmap(Ctx* c, CUtensorMap* m, const void** base, uint64_t* rows, uint64_t* cols,
@@ -247,7 +247,9 @@ int run_experts(Ctx* c, const Layer& L, const float* x, const float* resid, floa
                        static_cast<int>(M), ws, ws.ranges, ws.sorted_tok, ws.sorted_w,
                        ws.slot_pos, ws.status, c->stream);
     stage(c, "bucket", 3);
-    const int path = choose_path(c, M);
+    const int path = choose_path(c, L, M);
+    if (path != moe::kPathGemv && !L.wmaps)
+        return fail(c, MOE_E_UNSUPPORTED, "tensor-core path needs hidden and inter multiples of 512");
     if (path == moe::kPathGemv) {
         const int max_chunks = moe::max_chunks_for(static_cast<int>(M), slots, E);
         moe::launch_gemv13(L, x, ws, static_cast<int>(M), max_chunks, c->sm_count, c->stream);
@@ -262,12 +264,12 @@ int run_experts(Ctx* c, const Layer& L, const float* x, const float* resid, floa
         if (rc) return rc;
         rc = ensure_tmap(c, &ws.hmap, &ws.hmap_base, &ws.hmap_rows, &ws.hmap_cols, ws.h16, S, I);
         if (rc) return rc;
-        moe::launch_convert_rows(x, ws.sorted_tok, static_cast<int>(S), H, ws.x16, ws.xexp, c->stream);
+        moe::launch_convert_x(x, ws.sorted_tok, static_cast<int>(S), H, ws.x16, ws.xexp, c->stream);
         stage(c, "convert_x", 1);
-        const int items13 = moe::max_tiles_for(static_cast<int>(M), slots, E, moe::tc_max_n(13)) * (I / 128);
+        const int items13 = moe::max_tiles_for(static_cast<int>(M), slots, E, moe::tc_max_n(13)) * (2 * I / 128);
         moe::launch_tc13(L, ws.xmap, ws, items13, c->sm_count, a_tmem, c->stream);
         stage(c, "tc13", 1);
-        moe::launch_convert_rows(ws.h, nullptr, static_cast<int>(S), I, ws.h16, ws.hexp, c->stream);
+        moe::launch_convert_h(ws.h, static_cast<int>(S), I, ws.h16, ws.hexp, c->stream);
         stage(c, "convert_h", 1);
         const int items2 = moe::max_tiles_for(static_cast<int>(M), slots, E, moe::tc_max_n(2)) * (H / 128);
         moe::launch_tc2(L, ws.hmap, ws, items2, c->sm_count, a_tmem, c->stream);
@@ -354,8 +356,10 @@ void moe_ctx_destroy(moe_ctx* c) {
     if (!c) return;
     cudaSetDevice(c->device);
     if (c->stream) cudaStreamSynchronize(c->stream);
-    for (auto& L : c->layers)
+    for (auto& L : c->layers) {
         if (L.tab) cudaFree(const_cast<uint8_t**>(L.tab));
+        if (L.wmaps) cudaFree(L.wmaps);
+    }
     int* status = c->ws.status;
     free_ws(c->ws);
     if (status) cudaFree(status);
@@ -468,6 +472,27 @@ int moe_layer_create(moe_ctx* c, const moe_layer_spec* spec, const uint64_t* w1,
     Layer L;
     L.spec = s;
     L.tab = static_cast<const uint8_t**>(d);
+    if (moe::tc_supported(static_cast<int>(H), static_cast<int>(I))) {
+        // raw IQ4_XS tensor maps for the tensor-core path: [W1 | W3 | W2][E+1]
+        std::vector<CUtensorMap> maps(3 * (E + 1));
+        bool ok = true;
+        const uint64_t nb = E + 1;
+        for (uint64_t e = 0; e <= E && ok; ++e) {
+            if (e == E && !(s.flags & MOE_F_SHARED)) {
+                maps[e] = maps[0]; maps[nb + e] = maps[nb]; maps[2 * nb + e] = maps[2 * nb];
+                continue;
+            }
+            ok = moe::make_iq4_tmap(&maps[e], tab[e], I, b13 / I) &&
+                 moe::make_iq4_tmap(&maps[nb + e], tab[nb + e], I, b13 / I) &&
+                 moe::make_iq4_tmap(&maps[2 * nb + e], tab[2 * nb + e], H, b2 / H);
+        }
+        if (ok) {
+            void* dm = nullptr;
+            MOE_CUDA(c, cudaMalloc(&dm, maps.size() * sizeof(CUtensorMap)));
+            MOE_CUDA(c, cudaMemcpy(dm, maps.data(), maps.size() * sizeof(CUtensorMap), cudaMemcpyHostToDevice));
+            L.wmaps = static_cast<CUtensorMap*>(dm);
+        }
+    }
     L.router_w_ptr = c->base + s.router_w;
     L.bias_ptr = s.router_bias ? c->base + s.router_bias : nullptr;
     L.gate_ptr = (s.flags & MOE_F_SHARED_GATE) ? c->base + s.shared_gate : nullptr;

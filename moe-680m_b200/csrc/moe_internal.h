@@ -28,6 +28,8 @@ struct Layer {
     const uint8_t* router_w_ptr = nullptr;
     const uint8_t* bias_ptr = nullptr;  // may be null
     const uint8_t* gate_ptr = nullptr;  // may be null
+    CUtensorMap* wmaps = nullptr;       // device [3][E+1] raw IQ4_XS maps (W1, W3, W2), or null
+                                        // when the shapes do not suit the tensor-core path
     ExpertTables tables() const {
         const uint32_t n = spec.n_experts + 1;
         return ExpertTables{tab, tab + n, tab + 2 * n};
@@ -76,7 +78,7 @@ struct Workspace {
     Chunk* chunks = nullptr;      // [max_chunks]
     int* counters = nullptr;      // [8] device counters (n_chunks, ...)
     int* status = nullptr;        // device error status
-    float* h = nullptr;           // [S][I]
+    float* h = nullptr;           // [S][2I]: GEMV path h [S][I]; tensor-core path [g | u]
     float* ypart = nullptr;       // [S][H]
     TcTile* tiles13 = nullptr;    // tensor-core token tiles of <= 64 tokens
     TcTile* tiles2 = nullptr;     // tensor-core token tiles of <= 128 tokens
@@ -133,8 +135,12 @@ void launch_gemv13(const Layer& L, const float* x, const Workspace& ws, int M, i
 void launch_gemv2(const Layer& L, const Workspace& ws, int M, int max_chunks, int sm_count,
                   cudaStream_t s);
 int tc_max_n(int mode);
-void launch_convert_rows(const float* src, const int* gather, int n_rows, int len, __half* dst,
-                         int* sexp, cudaStream_t s);
+bool tc_supported(int hidden, int inter);
+void launch_convert_x(const float* x, const int* gather, int n_rows, int len, __half* dst,
+                      int* sexp, cudaStream_t s);
+void launch_convert_h(const float* gu, int n_rows, int inter, __half* dst, int* sexp,
+                      cudaStream_t s);
+bool make_iq4_tmap(CUtensorMap* m, const void* base, uint64_t rows, uint64_t row_bytes);
 void launch_tc13(const Layer& L, const CUtensorMap& xmap, const Workspace& ws, int max_items,
                  int sm_count, bool a_tmem, cudaStream_t s);
 void launch_tc2(const Layer& L, const CUtensorMap& hmap, const Workspace& ws, int max_items,
