@@ -7,6 +7,7 @@
 #include <algorithm>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <string>
 #include <vector>
@@ -98,11 +99,13 @@ int ensure_ws(Ctx* c, uint32_t M, uint32_t E, uint32_t k, uint32_t slots, uint32
     const size_t o_h16 = take(sizeof(__half) * S * I);
     const size_t o_xe = take(sizeof(int) * S);
     const size_t o_he = take(sizeof(int) * S);
+    const size_t o_io = take(sizeof(moe::IoArgs));
     const size_t total = off;
     int* status = ws.status;
     ws.status = nullptr;
     cudaStreamSynchronize(c->stream);
     free_ws(ws);
+    c->ws_gen += 1;  // captured graphs refer to the old buffers
     void* p = nullptr;
     cudaError_t e = cudaMalloc(&p, total);
     if (e != cudaSuccess) {
@@ -134,6 +137,7 @@ int ensure_ws(Ctx* c, uint32_t M, uint32_t E, uint32_t k, uint32_t slots, uint32
     ws.h16 = reinterpret_cast<__half*>(b + o_h16);
     ws.xexp = reinterpret_cast<int*>(b + o_xe);
     ws.hexp = reinterpret_cast<int*>(b + o_he);
+    ws.io = reinterpret_cast<moe::IoArgs*>(b + o_io);
     ws.max_chunks = static_cast<uint32_t>(max_chunks);
     ws.status = status;
     return MOE_OK;
@@ -212,9 +216,14 @@ void prof_end(Ctx* c) {
     c->ev_names.clear();
 }
 
-// Routing of M tokens into ws.topk.
-int run_route(Ctx* c, const Layer& L, const float* x, uint32_t M) {
-    moe::launch_router_logits(L, x, static_cast<int>(M), c->ws.logits, c->stream);
+void run_set_io(Ctx* c, const float* x, const float* resid, float* out) {
+    moe::launch_set_io(c->ws.io, x, resid, out, c->stream);
+    stage(c, "set_io", 1);
+}
+
+// Routing of M tokens (activations from ws.io) into ws.topk.
+int run_route(Ctx* c, const Layer& L, uint32_t M) {
+    moe::launch_router_logits(L, c->ws.io, static_cast<int>(M), c->ws.logits, c->stream);
     stage(c, "router", 1);
     moe::launch_topk(L, c->ws.logits, static_cast<int>(M), c->ws.topk, c->ws.status, c->stream);
     stage(c, "topk", 1);
@@ -238,8 +247,7 @@ int ensure_tmap(Ctx* c, CUtensorMap* m, const void** base, uint64_t* rows, uint6
     return MOE_OK;
 }
 
-int run_experts(Ctx* c, const Layer& L, const float* x, const float* resid, float* out,
-                uint32_t M) {
+int run_experts(Ctx* c, const Layer& L, uint32_t M) {
     Workspace& ws = c->ws;
     const int slots = L.slots();
     const int E = static_cast<int>(L.spec.n_experts);
@@ -252,7 +260,7 @@ int run_experts(Ctx* c, const Layer& L, const float* x, const float* resid, floa
         return fail(c, MOE_E_UNSUPPORTED, "tensor-core path needs hidden and inter multiples of 512");
     if (path == moe::kPathGemv) {
         const int max_chunks = moe::max_chunks_for(static_cast<int>(M), slots, E);
-        moe::launch_gemv13(L, x, ws, static_cast<int>(M), max_chunks, c->sm_count, c->stream);
+        moe::launch_gemv13(L, ws.io, ws, static_cast<int>(M), max_chunks, c->sm_count, c->stream);
         stage(c, "gemv13", 1);
         moe::launch_gemv2(L, ws, static_cast<int>(M), max_chunks, c->sm_count, c->stream);
         stage(c, "gemv2", 1);
@@ -264,7 +272,7 @@ int run_experts(Ctx* c, const Layer& L, const float* x, const float* resid, floa
         if (rc) return rc;
         rc = ensure_tmap(c, &ws.hmap, &ws.hmap_base, &ws.hmap_rows, &ws.hmap_cols, ws.h16, S, I);
         if (rc) return rc;
-        moe::launch_convert_x(x, ws.sorted_tok, static_cast<int>(S), H, ws.x16, ws.xexp, c->stream);
+        moe::launch_convert_x(ws.io, ws.sorted_tok, static_cast<int>(S), H, ws.x16, ws.xexp, c->stream);
         stage(c, "convert_x", 1);
         const int items13 = moe::max_tiles_for(static_cast<int>(M), slots, E, moe::tc_max_n(13)) * (2 * I / 128);
         moe::launch_tc13(L, ws.xmap, ws, items13, c->sm_count, a_tmem, c->stream);
@@ -275,9 +283,93 @@ int run_experts(Ctx* c, const Layer& L, const float* x, const float* resid, floa
         moe::launch_tc2(L, ws.hmap, ws, items2, c->sm_count, a_tmem, c->stream);
         stage(c, "tc2", 1);
     }
-    moe::launch_combine(L, ws, resid, out, static_cast<int>(M), c->stream);
+    moe::launch_combine(L, ws, ws.io, static_cast<int>(M), c->stream);
     stage(c, "combine", 1);
     return check_launch(c, "experts");
+}
+
+// ---- CUDA graphs of moe_forward ------------------------------------------------------------
+constexpr size_t kMaxGraphs = 64;
+
+void destroy_graph(moe::GraphEntry& g) {
+    if (g.exec) cudaGraphExecDestroy(g.exec);
+    if (g.graph) cudaGraphDestroy(g.graph);
+    g.exec = nullptr;
+    g.graph = nullptr;
+}
+
+int record_forward(Ctx* c, const Layer& L, uint32_t M, const float* x, const float* resid, float* out) {
+    run_set_io(c, x, resid, out);
+    int rc = run_route(c, L, M);
+    if (rc) return rc;
+    return run_experts(c, L, M);
+}
+
+// Replay (capturing on first use) the forward of (layer, M, path) with new activation pointers:
+// only the set_io node's arguments change between replays.
+int graph_forward(Ctx* c, uint32_t layer, const Layer& L, uint32_t M, const float* x,
+                  const float* resid, float* out) {
+    const int path = choose_path(c, L, M);
+    moe::GraphEntry* e = nullptr;
+    for (auto& g : c->graphs)
+        if (g.layer == layer && g.M == M && g.path == path && g.stream == c->stream && g.ws_gen == c->ws_gen)
+            e = &g;
+    if (!e) {
+        // drop stale entries, then the least recently used one if the cache is full
+        for (size_t i = 0; i < c->graphs.size();) {
+            if (c->graphs[i].ws_gen != c->ws_gen) {
+                destroy_graph(c->graphs[i]);
+                c->graphs.erase(c->graphs.begin() + static_cast<long>(i));
+            } else {
+                ++i;
+            }
+        }
+        if (c->graphs.size() >= kMaxGraphs) {
+            size_t lru = 0;
+            for (size_t i = 1; i < c->graphs.size(); ++i)
+                if (c->graphs[i].last_use < c->graphs[lru].last_use) lru = i;
+            destroy_graph(c->graphs[lru]);
+            c->graphs.erase(c->graphs.begin() + static_cast<long>(lru));
+        }
+        moe::GraphEntry g;
+        g.layer = layer; g.M = M; g.path = path; g.stream = c->stream; g.ws_gen = c->ws_gen;
+        const uint64_t l0 = c->launches;
+        MOE_CUDA(c, cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal));
+        int rc = record_forward(c, L, M, x, resid, out);
+        cudaGraph_t graph = nullptr;
+        cudaError_t ce = cudaStreamEndCapture(c->stream, &graph);
+        g.n_kernels = c->launches - l0;
+        c->launches = l0;
+        if (rc != MOE_OK) { if (graph) cudaGraphDestroy(graph); return rc; }
+        if (ce != cudaSuccess) return cuda_fail(c, ce, "cudaStreamEndCapture");
+        g.graph = graph;
+        size_t n_root = 0;
+        cudaGraphGetRootNodes(graph, nullptr, &n_root);
+        if (n_root != 1) { destroy_graph(g); return fail(c, MOE_E_CUDA, "captured forward has %zu roots", n_root); }
+        cudaGraphGetRootNodes(graph, &g.io_node, &n_root);
+        ce = cudaGraphInstantiate(&g.exec, graph, 0);
+        if (ce != cudaSuccess) { destroy_graph(g); return cuda_fail(c, ce, "cudaGraphInstantiate"); }
+        c->graphs.push_back(g);
+        e = &c->graphs.back();
+    }
+    e->last_use = ++c->graph_clock;
+    moe::IoArgs* io = c->ws.io;
+    void* args[4] = {&io, const_cast<float**>(&x), const_cast<float**>(&resid), &out};
+    cudaKernelNodeParams p{};
+    p.func = const_cast<void*>(moe::set_io_func());
+    p.gridDim = dim3(1);
+    p.blockDim = dim3(1);
+    p.kernelParams = args;
+    MOE_CUDA(c, cudaGraphExecKernelNodeSetParams(e->exec, e->io_node, &p));
+    MOE_CUDA(c, cudaGraphLaunch(e->exec, c->stream));
+    c->launches += e->n_kernels;
+    return MOE_OK;
+}
+
+bool stream_capturing(Ctx* c) {
+    cudaStreamCaptureStatus st = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(c->stream, &st) != cudaSuccess) return true;
+    return st != cudaStreamCaptureStatusNone;
 }
 
 }  // namespace
@@ -296,6 +388,8 @@ static int ctx_init(int device, moe_ctx* c) {
     c->sm_count = prop.multiProcessorCount;
     MOE_CUDA(c, cudaStreamCreateWithFlags(&c->own_stream, cudaStreamNonBlocking));
     c->stream = c->own_stream;
+    const char* ng = std::getenv("MOE_B200_NO_GRAPHS");
+    c->use_graphs = !(ng && ng[0] == '1');
     void* st = nullptr;
     MOE_CUDA(c, cudaMalloc(&st, 256));
     MOE_CUDA(c, cudaMemset(st, 0, 256));
@@ -360,6 +454,7 @@ void moe_ctx_destroy(moe_ctx* c) {
         if (L.tab) cudaFree(const_cast<uint8_t**>(L.tab));
         if (L.wmaps) cudaFree(L.wmaps);
     }
+    for (auto& g : c->graphs) destroy_graph(g);
     int* status = c->ws.status;
     free_ws(c->ws);
     if (status) cudaFree(status);
@@ -521,7 +616,8 @@ int moe_route(moe_ctx* c, uint32_t layer_id, uint64_t x_off, uint32_t M, uint64_
     if (!off_ok(c, topk_off, rec, 8)) return fail(c, MOE_E_INVALID, "topk offset invalid");
     DeviceGuard g(c->device);
     if ((rc = ensure_layer_ws(c, *L, M))) return rc;
-    if ((rc = run_route(c, *L, at<float>(c, x_off), M))) return rc;
+    run_set_io(c, at<float>(c, x_off), nullptr, nullptr);
+    if ((rc = run_route(c, *L, M))) return rc;
     MOE_CUDA(c, cudaMemcpyAsync(c->base + topk_off, c->ws.topk, rec, cudaMemcpyDeviceToDevice, c->stream));
     return MOE_OK;
 }
@@ -536,7 +632,8 @@ int moe_do_route(moe_ctx* c, uint32_t layer_id, uint64_t x_off, uint32_t M, uint
     if ((rc = check_tokens(c, *L, x_off, M, "x"))) return rc;
     DeviceGuard g(c->device);
     if ((rc = ensure_layer_ws(c, *L, M))) return rc;
-    if ((rc = run_route(c, *L, at<float>(c, x_off), M))) return rc;
+    run_set_io(c, at<float>(c, x_off), nullptr, nullptr);
+    if ((rc = run_route(c, *L, M))) return rc;
     const int k = static_cast<int>(L->spec.top_k);
     std::vector<uint2> rec(static_cast<size_t>(M) * (k + 1));
     MOE_CUDA(c, cudaMemcpyAsync(rec.data(), c->ws.topk, rec.size() * sizeof(uint2),
@@ -593,9 +690,12 @@ int moe_forward(moe_ctx* c, uint32_t layer_id, uint64_t x_off, uint64_t resid_of
     DeviceGuard g(c->device);
     if ((rc = ensure_layer_ws(c, *L, M))) return rc;
     const float* x = at<float>(c, x_off);
+    const float* resid = resid_off ? at<float>(c, resid_off) : nullptr;
+    float* out = at<float>(c, out_off);
+    if (c->use_graphs && !c->prof && !stream_capturing(c))
+        return graph_forward(c, layer_id, *L, M, x, resid, out);
     prof_begin(c);
-    if ((rc = run_route(c, *L, x, M))) return rc;
-    rc = run_experts(c, *L, x, resid_off ? at<float>(c, resid_off) : nullptr, at<float>(c, out_off), M);
+    rc = record_forward(c, *L, M, x, resid, out);
     prof_end(c);
     return rc;
 }
@@ -636,9 +736,9 @@ int moe_forward_routed(moe_ctx* c, uint32_t layer_id, uint64_t x_off, uint64_t r
     // Pageable source: the copy has left `rec` when cudaMemcpyAsync returns.
     MOE_CUDA(c, cudaMemcpyAsync(c->ws.topk, rec.data(), rec.size() * sizeof(uint2),
                                 cudaMemcpyHostToDevice, c->stream));
-    const float* x = at<float>(c, x_off);
     prof_begin(c);
-    rc = run_experts(c, *L, x, resid_off ? at<float>(c, resid_off) : nullptr, at<float>(c, out_off), M);
+    run_set_io(c, at<float>(c, x_off), resid_off ? at<float>(c, resid_off) : nullptr, at<float>(c, out_off));
+    rc = run_experts(c, *L, M);
     prof_end(c);
     return rc;
 }

@@ -85,9 +85,10 @@ __device__ __forceinline__ void stage_rows(float* dst, int stride, const float* 
 
 template <int TOK>
 __global__ void __launch_bounds__(32 * kWarps)
-gemv13_kernel(const float* __restrict__ x, int H, int I, ExpertTables tabs,
+gemv13_kernel(const IoArgs* __restrict__ io, int H, int I, ExpertTables tabs,
               const int* __restrict__ sorted_tok, const Chunk* __restrict__ chunks,
               const int* __restrict__ counters, float* __restrict__ h) {
+    const float* __restrict__ x = io->x;
     extern __shared__ __align__(16) float xs[];
     const int stride = padded_len(H);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -194,7 +195,9 @@ gemv2_kernel(int H, int I, ExpertTables tabs, const Chunk* __restrict__ chunks,
 __global__ void __launch_bounds__(256)
 combine_kernel(const float* __restrict__ ypart, const int* __restrict__ slot_pos,
                const float* __restrict__ sorted_w, int ns, int H, float scale,
-               const float* __restrict__ resid, float* __restrict__ out) {
+               const IoArgs* __restrict__ io) {
+    const float* __restrict__ resid = io->resid;
+    float* __restrict__ out = io->out;
     const int t = blockIdx.x;
     const int c = (blockIdx.y * blockDim.x + threadIdx.x) * 4;
     if (c >= H) return;
@@ -221,9 +224,21 @@ void set_smem(K kern, size_t bytes) {
                                                 static_cast<int>(bytes));
 }
 
+__global__ void set_io_kernel(IoArgs* dst, const float* x, const float* resid, float* out) {
+    dst->x = x;
+    dst->resid = resid;
+    dst->out = out;
+}
+
 }  // namespace
 
-void launch_gemv13(const Layer& L, const float* x, const Workspace& ws, int M, int max_chunks,
+void launch_set_io(IoArgs* dst, const float* x, const float* resid, float* out, cudaStream_t s) {
+    set_io_kernel<<<1, 1, 0, s>>>(dst, x, resid, out);
+}
+
+const void* set_io_func() { return reinterpret_cast<const void*>(&set_io_kernel); }
+
+void launch_gemv13(const Layer& L, const IoArgs* x, const Workspace& ws, int M, int max_chunks,
                    int sm_count, cudaStream_t s) {
     const int H = L.spec.hidden, I = L.spec.inter;
     const int items = max_chunks * (I / kRows13);
@@ -260,12 +275,11 @@ void launch_gemv2(const Layer& L, const Workspace& ws, int M, int max_chunks, in
     }
 }
 
-void launch_combine(const Layer& L, const Workspace& ws, const float* resid, float* out, int M,
-                    cudaStream_t s) {
+void launch_combine(const Layer& L, const Workspace& ws, const IoArgs* io, int M, cudaStream_t s) {
     const int H = L.spec.hidden;
     dim3 grid(M, (H / 4 + 255) / 256);
     combine_kernel<<<grid, 256, 0, s>>>(ws.ypart, ws.slot_pos, ws.sorted_w,
-                                        L.slots(), H, L.spec.scale, resid, out);
+                                        L.slots(), H, L.spec.scale, io);
 }
 
 }  // namespace moe

@@ -17,7 +17,8 @@
 //               store the fp16 A operand, 64 K per stage, into TMEM (tcgen05.st) or into
 //               128-byte-swizzled shared memory;
 //   warp 9      TMA: B operand (fp16 activations of the tile's slots, pre-scaled per slot by a
-//               power of two, K permuted as below), 16-row boxes, 4-deep ring;
+//               power of two, K permuted as below), 16-row boxes, 8-deep (A in TMEM) or
+//               4-deep (A in shared memory) ring;
 //   warp 8      allocates TMEM; lane 0 issues tcgen05.mma (M=128, N=16..kNMax, K=16) and
 //               tcgen05.commit;
 //   warps 11-14 epilogue: TMEM -> registers, undo the activation scale, store f32
@@ -44,7 +45,6 @@ namespace {
 
 using namespace tc;
 
-constexpr int kStages = 4;          // MMA stages (64 K each) in flight
 constexpr int kProdWarps = 8;
 constexpr int kThreads = 15 * 32;
 constexpr int kMmaWarp = 8, kTmaBWarp = 9, kTmaAWarp = 10;  // warps 11-14: epilogue
@@ -59,9 +59,12 @@ constexpr int kStagesPerChunk = 8;                 // 512 K / 64 K
 constexpr int kBStageBytes = kNMax * 128;
 constexpr int kAStageBytes = 128 * 128;            // smem-A variant
 
+// MMA stages (64 K each) in flight: 8 with A in TMEM (TMEM columns 256..511), 4 with A in
+// shared memory; the raw A ring holds two 512-K chunks (16 stages of look-ahead).
 template <bool A_TMEM>
 struct Layout {
-    static constexpr int kRaw = A_TMEM ? 3 : 2;  // raw ring depth
+    static constexpr int kStages = A_TMEM ? 8 : 4;
+    static constexpr int kRaw = 2;
     static constexpr size_t kB = 0;
     static constexpr size_t kA = kB + static_cast<size_t>(kStages) * kBStageBytes;
     static constexpr size_t kR = kA + (A_TMEM ? 0 : static_cast<size_t>(kStages) * kAStageBytes);
@@ -130,6 +133,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 expert_tc_kernel(const __grid_constant__ CUtensorMap bmap, const TcArgs a) {
     using Lay = Layout<A_TMEM>;
     constexpr int kRaw = Lay::kRaw;
+    constexpr int kStages = Lay::kStages;
     extern __shared__ uint8_t smem_raw[];
     // 128-byte-swizzled operand tiles need 1024-byte aligned shared-memory addresses
     uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
@@ -360,10 +364,11 @@ __device__ __forceinline__ int chunk_k(int c) { return 64 * (c >> 3) + 32 * ((c 
 
 // dst[p][perm(k)] = fp16(src[gather[p]][k] * 2^-e); sexp[p] = e.
 __global__ void __launch_bounds__(256)
-convert_x_kernel(const float* __restrict__ src, const int* __restrict__ gather, int n_rows,
+convert_x_kernel(const IoArgs* __restrict__ io, const int* __restrict__ gather, int n_rows,
                  int len, __half* __restrict__ dst, int* __restrict__ sexp) {
     const int p = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
     if (p >= n_rows) return;
+    const float* __restrict__ src = io->x;
     const float* s = src + static_cast<size_t>(gather[p]) * len;
     float mx = 0.f;
     for (int i = lane * 4; i < len; i += 128) {
@@ -430,7 +435,7 @@ int tc_max_n(int) { return kNMax; }
 
 bool tc_supported(int hidden, int inter) { return hidden % 512 == 0 && inter % 512 == 0; }
 
-void launch_convert_x(const float* x, const int* gather, int n_rows, int len, __half* dst,
+void launch_convert_x(const IoArgs* x, const int* gather, int n_rows, int len, __half* dst,
                       int* sexp, cudaStream_t s) {
     convert_x_kernel<<<(n_rows * 32 + 255) / 256, 256, 0, s>>>(x, gather, n_rows, len, dst, sexp);
 }

@@ -47,6 +47,15 @@ struct Chunk {
     int pad;
 };
 
+// Per-call activation pointers, read by the kernels from device memory so that one captured
+// CUDA graph serves every call with the same (layer, M, path): only the tiny kernel that writes
+// this block changes between replays.
+struct IoArgs {
+    const float* x;      // [M][H] MoE input (router and experts)
+    const float* resid;  // [M][H] residual added to the output, or null
+    float* out;          // [M][H]
+};
+
 // Token tile of one bucket for the tensor-core kernels: slots [p0, p0+n) of the sorted order.
 struct TcTile {
     int bucket;
@@ -92,7 +101,7 @@ struct Workspace {
     const void* xmap_base = nullptr;
     const void* hmap_base = nullptr;
     uint64_t xmap_rows = 0, hmap_rows = 0, xmap_cols = 0, hmap_cols = 0;
-    uint2* host_topk = nullptr;   // pinned staging for moe_forward_routed
+    IoArgs* io = nullptr;         // device IoArgs of the current call
     uint32_t max_chunks = 0;
 };
 
@@ -102,7 +111,25 @@ struct StageStat {
     double total_ms = 0.0;
 };
 
+// One captured forward (set_io + routing + experts + combine) for a (layer, M, path, stream).
+struct GraphEntry {
+    uint32_t layer = 0;
+    uint32_t M = 0;
+    int path = 0;
+    cudaStream_t stream = nullptr;
+    uint64_t ws_gen = 0;
+    cudaGraph_t graph = nullptr;
+    cudaGraphExec_t exec = nullptr;
+    cudaGraphNode_t io_node = nullptr;
+    uint64_t n_kernels = 0;
+    uint64_t last_use = 0;
+};
+
 struct Ctx {
+    // CUDA graphs of moe_forward, keyed by (layer, M, path, stream)
+    bool use_graphs = true;
+    std::vector<GraphEntry> graphs;
+    uint64_t ws_gen = 0, graph_clock = 0;
     // tracing: events of the current call and accumulated per-stage statistics
     bool prof = false;
     std::vector<cudaEvent_t> ev;
@@ -124,19 +151,21 @@ struct Ctx {
 
 // Kernel launchers (stream-ordered, no synchronisation).
 int router_split_for(int M, int H);
-void launch_router_logits(const Layer& L, const float* x, int M, float* logits, cudaStream_t s);
+void launch_set_io(IoArgs* dst, const float* x, const float* resid, float* out, cudaStream_t s);
+const void* set_io_func();
+void launch_router_logits(const Layer& L, const IoArgs* io, int M, float* logits, cudaStream_t s);
 void launch_topk(const Layer& L, const float* logits, int M, uint2* topk, int* status,
                  cudaStream_t s);
 void launch_bucket(int E, int k, bool has_shared, const uint2* topk, int M, Workspace& ws,
                    int* ranges, int* sorted_tok, float* sorted_w, int* slot_pos, int* status,
                    cudaStream_t s);
-void launch_gemv13(const Layer& L, const float* x, const Workspace& ws, int M, int max_chunks,
+void launch_gemv13(const Layer& L, const IoArgs* io, const Workspace& ws, int M, int max_chunks,
                    int sm_count, cudaStream_t s);
 void launch_gemv2(const Layer& L, const Workspace& ws, int M, int max_chunks, int sm_count,
                   cudaStream_t s);
 int tc_max_n(int mode);
 bool tc_supported(int hidden, int inter);
-void launch_convert_x(const float* x, const int* gather, int n_rows, int len, __half* dst,
+void launch_convert_x(const IoArgs* io, const int* gather, int n_rows, int len, __half* dst,
                       int* sexp, cudaStream_t s);
 void launch_convert_h(const float* gu, int n_rows, int inter, __half* dst, int* sexp,
                       cudaStream_t s);
@@ -146,7 +175,7 @@ void launch_tc13(const Layer& L, const CUtensorMap& xmap, const Workspace& ws, i
 void launch_tc2(const Layer& L, const CUtensorMap& hmap, const Workspace& ws, int max_items,
                 int sm_count, bool a_tmem, cudaStream_t s);
 bool make_fp16_tmap(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols);
-void launch_combine(const Layer& L, const Workspace& ws, const float* resid, float* out, int M,
+void launch_combine(const Layer& L, const Workspace& ws, const IoArgs* io, int M,
                     cudaStream_t s);
 void launch_rms_norm(const float* x, float* y, int M, int H, float eps, cudaStream_t s);
 void launch_dequant(const uint8_t* src, uint64_t n_blocks, float* dst, cudaStream_t s);

@@ -19,9 +19,10 @@ constexpr int kRowsPerCta = 4;  // warps per CTA
 
 template <int TOK>
 __global__ void __launch_bounds__(32 * kRowsPerCta)
-router_gemv_kernel(const float* __restrict__ x, int M, int H, const float* __restrict__ wr,
+router_gemv_kernel(const IoArgs* __restrict__ io, int M, int H, const float* __restrict__ wr,
                    const float* __restrict__ gate_w, int E, int n_rows,
                    float* __restrict__ logits) {
+    const float* __restrict__ x = io->x;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int row = blockIdx.x * kRowsPerCta + warp;
     const int t0 = blockIdx.y * TOK;
@@ -58,9 +59,10 @@ router_gemv_kernel(const float* __restrict__ x, int M, int H, const float* __res
 constexpr int kTM = 64, kTE = 64, kTK = 16;
 
 __global__ void __launch_bounds__(256)
-router_gemm_kernel(const float* __restrict__ x, int M, int H, const float* __restrict__ wr,
+router_gemm_kernel(const IoArgs* __restrict__ io, int M, int H, const float* __restrict__ wr,
                    const float* __restrict__ gate_w, int E, int n_rows, int k_len,
                    float* __restrict__ partial) {
+    const float* __restrict__ x = io->x;
     __shared__ __align__(16) float xs[kTK][kTM + 4];
     __shared__ __align__(16) float ws[kTK][kTE + 4];
     const int tid = threadIdx.x;
@@ -192,7 +194,7 @@ int router_split_for(int M, int H) {
     return (H % (kGemmSplit * kTK) == 0) ? kGemmSplit : 1;
 }
 
-void launch_router_logits(const Layer& L, const float* x, int M, float* logits, cudaStream_t s) {
+void launch_router_logits(const Layer& L, const IoArgs* x, int M, float* logits, cudaStream_t s) {
     const int E = L.spec.n_experts, H = L.spec.hidden;
     const bool gate = (L.spec.flags & MOE_F_SHARED_GATE) != 0;
     const int n_rows = E + (gate ? 1 : 0);

@@ -233,3 +233,15 @@ def test_invalid_arguments(ctx):
     spec = host.LayerSpec(2048, 768, 256, 8, 0, 1.0, 256)
     with pytest.raises(host.MoeError):
         ctx.layer_create(spec, [256] * 256, [256] * 256, [256] * 256)  # unsupported inter
+
+
+def test_graph_replay_new_pointers(ctx):
+    """Repeated forwards of one (layer, M) replay one captured CUDA graph; each call's own
+    input/residual/output buffers must be used."""
+    lid, hl = model(ctx, 1234, FULL, None)
+    m = 24
+    xs = [synth.tokens(77, i, m, FULL.hidden) for i in range(3)]
+    outs = [run_forward(ctx, lid, x, x)[0] for x in xs]
+    for x, out in zip(xs, outs):
+        ref = coracle.moe_forward(hl, x, x, acc64=True)
+        check_close(out, ref["out64"], "graph replay")
