@@ -164,6 +164,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--only", default="all", choices=["all", "prefill"],
+                    help="prefill: skip the decode, end-to-end and CPU legs (profiling runs)")
     ap.add_argument("--path", type=int, default=0,
                     help="expert kernels: 0 auto, 1 CUDA-core GEMV, 2 tcgen05 (A in smem), 3 tcgen05 (A in TMEM)")
     args = ap.parse_args()
@@ -182,7 +184,8 @@ def main():
     from moe680m_b200 import host, synth
 
     sh = synth.LayerShapes()
-    n_dec_layers = 16  # decode cycles through 16 layers (6.9 GB) so no step hits in L2
+    only_prefill = args.only == "prefill"
+    n_dec_layers = 0 if only_prefill else 16  # decode cycles through 16 layers (6.9 GB): no L2 hits
     arena = (n_dec_layers + 1) * sh.expert_bytes * (sh.n_experts + 1) + (256 << 20)
     ctx = host.Context(local, arena)
     stream = torch.cuda.Stream()  # a real stream: torch events and the library share it
@@ -191,7 +194,7 @@ def main():
     ctx.set_path(args.path)
     _, _, pre_ids = host.build_synthetic_model(ctx, SEED, 1, sh, ZIPF)
     pre = pre_ids[0]
-    _, _, dec_ids = host.build_synthetic_model(ctx, SEED + 1, n_dec_layers, sh, None)
+    dec_ids = host.build_synthetic_model(ctx, SEED + 1, n_dec_layers, sh, None)[2] if n_dec_layers else []
     K, W = args.steps, args.warmup
     n_x = K + W
     H = sh.hidden
@@ -255,61 +258,62 @@ def main():
                 "layer_frac": layer_bytes / (ms / 1e3) / 1e9 / hbm,
                 "stage_ms": {k: round(v, 4) for k, v in stage_ms.items()}}
 
-    # ---- end to end through the public API: pinned host buffers, copies inside --------------
-    hx = [torch.from_numpy(x).pin_memory() for x in xs[:4]]
-    hout = torch.empty((PREFILL_M, H), dtype=torch.float32).pin_memory()
-    xin = ctx.alloc(PREFILL_M * H * 4)
-    nbytes = PREFILL_M * H * 4
-    for i in range(2):
-        ctx.upload_ptr(xin, hx[i].data_ptr(), nbytes)
-        ctx.forward(pre, xin, xin, out_off, PREFILL_M)
-        ctx.download_ptr(out_off, hout.data_ptr(), nbytes)
-    torch.cuda.synchronize()
-    t0 = time.perf_counter()
-    for i in range(K):
-        ctx.upload_ptr(xin, hx[i % 4].data_ptr(), nbytes)
-        ctx.forward(pre, xin, xin, out_off, PREFILL_M)
-        ctx.download_ptr(out_off, hout.data_ptr(), nbytes)
-    e2e_s = (time.perf_counter() - t0) / K
-    if world > 1:
-        t = torch.tensor([e2e_s], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_s = float(t.item())
-    e2e = {"value": world * PREFILL_M / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": nbytes,
-           "d2h_bytes_per_step": nbytes}
+    e2e, decode, cpu = None, None, None
+    if not only_prefill:
+        # ---- end to end through the public API: pinned host buffers, copies inside --------------
+        hx = [torch.from_numpy(x).pin_memory() for x in xs[:4]]
+        hout = torch.empty((PREFILL_M, H), dtype=torch.float32).pin_memory()
+        xin = ctx.alloc(PREFILL_M * H * 4)
+        nbytes = PREFILL_M * H * 4
+        for i in range(2):
+            ctx.upload_ptr(xin, hx[i].data_ptr(), nbytes)
+            ctx.forward(pre, xin, xin, out_off, PREFILL_M)
+            ctx.download_ptr(out_off, hout.data_ptr(), nbytes)
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for i in range(K):
+            ctx.upload_ptr(xin, hx[i % 4].data_ptr(), nbytes)
+            ctx.forward(pre, xin, xin, out_off, PREFILL_M)
+            ctx.download_ptr(out_off, hout.data_ptr(), nbytes)
+        e2e_s = (time.perf_counter() - t0) / K
+        if world > 1:
+            t = torch.tensor([e2e_s], device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            e2e_s = float(t.item())
+        e2e = {"value": world * PREFILL_M / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": nbytes,
+               "d2h_bytes_per_step": nbytes}
 
-    # ---- decode (config 0): M=1, cycling through 16 layers ----------------------------------
-    kd = max(K, 64)
-    xd = [ctx.put(synth.tokens(SEED + 7, rank * 1000 + i, 1, H)) for i in range(kd)]
-    od = ctx.alloc(H * 4)
-    for i in range(8):
-        ctx.forward(dec_ids[i % n_dec_layers], xd[i], xd[i], od, 1)
-    torch.cuda.synchronize()
-    ev0.record(stream)
-    for i in range(kd):
-        ctx.forward(dec_ids[i % n_dec_layers], xd[i], xd[i], od, 1)
-    ev1.record(stream)
-    torch.cuda.synchronize()
-    dms = ev0.elapsed_time(ev1) / kd
-    ctx.profile(True)
-    for i in range(kd):
-        ctx.forward(dec_ids[i % n_dec_layers], xd[i], xd[i], od, 1)
-    dstages = {k: v[1] / max(v[0], 1) for k, v in ctx.profile_read().items()}
-    ctx.profile(False)
-    dec_bytes = (sh.top_k + 1) * sh.expert_bytes
-    decode = {"tok_s": 1e3 / dms, "us_per_token": dms * 1e3,
-              "layer_achieved_gbs": dec_bytes / (dms / 1e3) / 1e9,
-              "layer_frac": dec_bytes / (dms / 1e3) / 1e9 / hbm,
-              "alg_bytes_per_token": dec_bytes, "stage_us": {k: round(v * 1e3, 2) for k, v in dstages.items()},
-              "l2": "16 layers (6.9 GB) cycled, a fresh token per step"}
+        # ---- decode (config 0): M=1, cycling through 16 layers ----------------------------------
+        kd = max(K, 64)
+        xd = [ctx.put(synth.tokens(SEED + 7, rank * 1000 + i, 1, H)) for i in range(kd)]
+        od = ctx.alloc(H * 4)
+        for i in range(2 * n_dec_layers):  # capture every layer's graph before timing
+            ctx.forward(dec_ids[i % n_dec_layers], xd[i % kd], xd[i % kd], od, 1)
+        torch.cuda.synchronize()
+        ev0.record(stream)
+        for i in range(kd):
+            ctx.forward(dec_ids[i % n_dec_layers], xd[i], xd[i], od, 1)
+        ev1.record(stream)
+        torch.cuda.synchronize()
+        dms = ev0.elapsed_time(ev1) / kd
+        ctx.profile(True)
+        for i in range(kd):
+            ctx.forward(dec_ids[i % n_dec_layers], xd[i], xd[i], od, 1)
+        dstages = {k: v[1] / max(v[0], 1) for k, v in ctx.profile_read().items()}
+        ctx.profile(False)
+        dec_bytes = (sh.top_k + 1) * sh.expert_bytes
+        decode = {"tok_s": 1e3 / dms, "us_per_token": dms * 1e3,
+                  "layer_achieved_gbs": dec_bytes / (dms / 1e3) / 1e9,
+                  "layer_frac": dec_bytes / (dms / 1e3) / 1e9 / hbm,
+                  "alg_bytes_per_token": dec_bytes, "stage_us": {k: round(v * 1e3, 2) for k, v in dstages.items()},
+                  "l2": "16 layers (6.9 GB) cycled, a fresh token per step"}
 
-    # ---- CPU baseline (rank 0, N=1 only) ------------------------------------------------------
-    cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu:
-        _, v, dt, n = cpu_baseline(sh, xs[0])
-        cpu = {"value": v, "unit": "tok/s", "cores": os.cpu_count(), "kind": "port",
-               "sample": f"{n} tokens = repeated config-1 512-token prefills ({dt:.1f} s), C "
-                         "restatement of the reference MoE layer (oracle/, f32, OpenMP all cores)"}
+        # ---- CPU baseline (rank 0, N=1 only) ------------------------------------------------------
+        if rank == 0 and world == 1 and not args.no_cpu:
+            _, v, dt, n = cpu_baseline(sh, xs[0])
+            cpu = {"value": v, "unit": "tok/s", "cores": os.cpu_count(), "kind": "port",
+                   "sample": f"{n} tokens = repeated config-1 512-token prefills ({dt:.1f} s), C "
+                             "restatement of the reference MoE layer (oracle/, f32, OpenMP all cores)"}
 
     if rank == 0:
         line = {"metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": K,
