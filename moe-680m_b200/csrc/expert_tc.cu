@@ -35,6 +35,8 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include <cstdlib>
+
 #include "moe_common.cuh"
 #include "moe_internal.h"
 #include "tc_ptx.cuh"
@@ -45,9 +47,15 @@ namespace {
 
 using namespace tc;
 
-constexpr int kProdWarps = 8;
-constexpr int kThreads = 15 * 32;
-constexpr int kMmaWarp = 8, kTmaBWarp = 9, kTmaAWarp = 10;  // warps 11-14: epilogue
+// Warp roles: producers 0..PW-1, then MMA, TMA-B, TMA-A, and four epilogue warps.
+template <int PW>
+struct Roles {
+    static constexpr int kProd = PW;
+    static constexpr int kMma = PW, kTmaB = PW + 1, kTmaA = PW + 2, kEpi0 = PW + 3;
+    static constexpr int kThreads = (PW + 7) * 32;
+    static constexpr int kParts = PW / 4;          // producer warps per 32-row quarter
+    static constexpr int kWordsPerPart = 8 / kParts;  // qs words (8 weights) per row per stage
+};
 constexpr int kTmemCols = 512;
 constexpr int kBoxRows = 16;        // B TMA box: 16 rows x 64 fp16
 constexpr int kNMax = 128;          // tokens per tile
@@ -128,9 +136,17 @@ __device__ __forceinline__ Item get_item(const TcArgs& a, int item) {
     return Item{tl.bucket, tl.p0, tl.n, item - t * a.n_rt};
 }
 
-template <bool A_TMEM>
-__global__ void __launch_bounds__(kThreads, 1)
+template <int NW>
+__device__ __forceinline__ void tmem_store_words(uint32_t taddr, const uint32_t (&v)[NW * 4]) {
+    if constexpr (NW == 4) tmem_st16(taddr, v);
+    else tmem_st8(taddr, v);
+}
+
+template <bool A_TMEM, int PW>
+__global__ void __launch_bounds__(Roles<PW>::kThreads, 1)
 expert_tc_kernel(const __grid_constant__ CUtensorMap bmap, const TcArgs a) {
+    using R = Roles<PW>;
+    constexpr int kProdWarps = R::kProd, kMmaWarp = R::kMma, kTmaBWarp = R::kTmaB, kTmaAWarp = R::kTmaA;
     using Lay = Layout<A_TMEM>;
     constexpr int kRaw = Lay::kRaw;
     constexpr int kStages = Lay::kStages;
@@ -180,8 +196,12 @@ expert_tc_kernel(const __grid_constant__ CUtensorMap bmap, const TcArgs a) {
 
     if (warp < kProdWarps) {
         // ---------------- producers: raw IQ4_XS (smem) -> fp16 A operand ----------------
+        constexpr int NW = R::kWordsPerPart;
         const int q = warp & 3;
-        const int half = warp >> 2;  // which sub-block of each 64-K stage
+        const int part = warp >> 2;  // which qs words of each row's 64-K stage
+        const int half = (part * NW) >> 2;           // sub-block of the stage
+        const int w0 = (part * NW) & 3;              // first word inside the sub-block
+        const int col = half * 16 + w0 * 4;          // first TMEM column / 4-byte pair
         const int row = q * 32 + lane;
         int g = 0, rc = 0;
         for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
@@ -195,24 +215,27 @@ expert_tc_kernel(const __grid_constant__ CUtensorMap bmap, const TcArgs a) {
                     const uint8_t* blk = raw + (sc >> 2) * kBlockBytes;
                     const int ib = (sc & 3) * 2 + half;
                     const uint2 hdr = lds64(blk);
-                    const uint2 q01 = lds64(blk + 8 + ib * 16);
-                    const uint2 q23 = lds64(blk + 16 + ib * 16);
-                    uint32_t v[16];
+                    uint32_t qw[NW];
+#pragma unroll
+                    for (int i = 0; i < NW; i += 2) {
+                        const uint2 qq = lds64(blk + 8 + ib * 16 + (w0 + i) * 4);
+                        qw[i] = qq.x;
+                        qw[i + 1] = qq.y;
+                    }
+                    uint32_t v[NW * 4];
                     const __half2 scl = subscale_h2(hdr.x, hdr.y, ib);
-                    word_f16(q01.x, scl, v + 0);
-                    word_f16(q01.y, scl, v + 4);
-                    word_f16(q23.x, scl, v + 8);
-                    word_f16(q23.y, scl, v + 12);
+#pragma unroll
+                    for (int i = 0; i < NW; ++i) word_f16(qw[i], scl, v + 4 * i);
                     if (!mbar_wait(&empty[slot], ((g / kStages) & 1) ^ 1, abort)) { ok = false; break; }
                     if constexpr (A_TMEM) {
-                        tmem_st16(tmem + (static_cast<uint32_t>(q * 32) << 16) + kACol0 + slot * 32 + half * 16, v);
+                        tmem_store_words<NW>(tmem + (static_cast<uint32_t>(q * 32) << 16) + kACol0 + slot * 32 + col, v);
                         tmem_wait_st();
                         tc_fence_before();
                     } else {
                         uint8_t* rowp = ast + slot * kAStageBytes + row * 128;
 #pragma unroll
-                        for (int c = 0; c < 4; ++c) {
-                            const int cc = half * 4 + c;
+                        for (int c = 0; c < NW; ++c) {
+                            const int cc = (col >> 2) + c;   // 16-byte chunk of the 128-byte row
                             *reinterpret_cast<uint4*>(rowp + ((cc ^ (row & 7)) << 4)) =
                                 make_uint4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
                         }
@@ -416,12 +439,26 @@ convert_h_kernel(const float* __restrict__ gu, int n_rows, int I, __half* __rest
     }
 }
 
+template <bool A_TMEM, int PW>
+void launch_tc_pw(const CUtensorMap& bmap, const TcArgs& args, int n_cta, cudaStream_t s) {
+    const size_t smem = Layout<A_TMEM>::kTotal;
+    cudaFuncSetAttribute(expert_tc_kernel<A_TMEM, PW>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         static_cast<int>(smem));
+    expert_tc_kernel<A_TMEM, PW><<<n_cta, Roles<PW>::kThreads, smem, s>>>(bmap, args);
+}
+
+int producer_warps() {
+    static int pw = [] {
+        const char* e = std::getenv("MOE_B200_TC_PRODUCER_WARPS");
+        return (e && std::atoi(e) == 8) ? 8 : 16;
+    }();
+    return pw;
+}
+
 template <bool A_TMEM>
 void launch_tc(const CUtensorMap& bmap, const TcArgs& args, int n_cta, cudaStream_t s) {
-    const size_t smem = Layout<A_TMEM>::kTotal;
-    cudaFuncSetAttribute(expert_tc_kernel<A_TMEM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         static_cast<int>(smem));
-    expert_tc_kernel<A_TMEM><<<n_cta, kThreads, smem, s>>>(bmap, args);
+    if (producer_warps() == 8) launch_tc_pw<A_TMEM, 8>(bmap, args, n_cta, s);
+    else launch_tc_pw<A_TMEM, 16>(bmap, args, n_cta, s);
 }
 
 static_assert(Layout<true>::kTotal <= 227 * 1024, "smem budget (A in TMEM)");
