@@ -52,7 +52,8 @@ template <int PW>
 struct Roles {
     static constexpr int kProd = PW;
     static constexpr int kMma = PW, kTmaB = PW + 1, kTmaA = PW + 2, kEpi0 = PW + 3;
-    static constexpr int kThreads = (PW + 7) * 32;
+    static constexpr int kEpiWarps = 8;               // two per 32-lane TMEM quarter
+    static constexpr int kThreads = (PW + 3 + kEpiWarps) * 32;
     static constexpr int kParts = PW / 4;          // producer warps per 32-row quarter
     static constexpr int kWordsPerPart = 8 / kParts;  // qs words (8 weights) per row per stage
 };
@@ -182,7 +183,7 @@ expert_tc_kernel(const __grid_constant__ CUtensorMap bmap, const TcArgs a) {
         }
         for (int i = 0; i < 2; ++i) {
             mbar_init(&accf[i], 1);
-            mbar_init(&acce[i], 128);
+            mbar_init(&acce[i], R::kEpiWarps * 32);
         }
         *abort = 0;
         fence_mbar_init();
@@ -324,7 +325,10 @@ expert_tc_kernel(const __grid_constant__ CUtensorMap bmap, const TcArgs a) {
         __syncwarp();
     } else {
         // ---------------- epilogue ----------------
+        // Two warps per TMEM lane quarter, each taking alternate 16-column chunks.
+        const int ew = warp - R::kEpi0;
         const int q = warp & 3;
+        const int sub = ew >> 2;
         const int row = q * 32 + lane;
         int it = 0;
         for (int item = blockIdx.x; item < n_items; item += gridDim.x, ++it) {
@@ -334,17 +338,19 @@ expert_tc_kernel(const __grid_constant__ CUtensorMap bmap, const TcArgs a) {
             tc_fence_after();
             const int feat = x.rt * 128 + row;
             const uint32_t tl = tmem + (static_cast<uint32_t>(q * 32) << 16) + b * kAccStride;
-            for (int c0 = 0; c0 < x.n; c0 += 16) {
+            float* __restrict__ out = a.out + feat;
+            for (int c0 = sub * 16; c0 < x.n; c0 += 32) {
                 uint32_t v[16];
                 tmem_ld16(tl + c0, v);
+                int e[16];
+#pragma unroll
+                for (int t = 0; t < 16; ++t) e[t] = c0 + t < x.n ? __ldg(a.sexp + x.p0 + c0 + t) : 0;
                 tmem_wait_ld();
 #pragma unroll
                 for (int t = 0; t < 16; ++t) {
-                    if (c0 + t < x.n) {
-                        const int p = x.p0 + c0 + t;
-                        const float sc = __int_as_float((127 + a.sexp[p]) << 23);  // 2^e, exact
-                        a.out[static_cast<size_t>(p) * a.out_ld + feat] = __uint_as_float(v[t]) * sc;
-                    }
+                    if (c0 + t < x.n)
+                        out[static_cast<size_t>(x.p0 + c0 + t) * a.out_ld] =
+                            __uint_as_float(v[t]) * __int_as_float((127 + e[t]) << 23);  // * 2^e
                 }
             }
             tc_fence_before();
