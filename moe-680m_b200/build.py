@@ -40,16 +40,21 @@ def needs_build() -> bool:
     return any(p.stat().st_mtime > t for p in _deps())
 
 
-def build(force: bool = False, verbose: bool = False, ptxas_v: bool = False) -> Path:
-    if not force and not needs_build():
+def build(force: bool = False, verbose: bool = False, ptxas_v: bool = False,
+          defines: tuple = (), out: Path | None = None) -> Path:
+    """Compile the library; ``defines``/``out`` produce a variant elsewhere (e.g. a debug build
+    with -DMOE_TC_TRACE) without touching the default library."""
+    lib = Path(out) if out else LIB
+    bdir = BUILD if not defines else BUILD.parent / ("_build_" + "_".join(d.lower() for d in defines))
+    if not force and not defines and not needs_build():
         return LIB
-    BUILD.mkdir(exist_ok=True)
-    LIB.parent.mkdir(exist_ok=True)
+    bdir.mkdir(exist_ok=True)
+    lib.parent.mkdir(parents=True, exist_ok=True)
     srcs = _sources()
-    extra = ["-Xptxas", "-v"] if ptxas_v else []
+    extra = (["-Xptxas", "-v"] if ptxas_v else []) + [f"-D{d}" for d in defines]
 
     def compile_one(src: Path):
-        obj = BUILD / (src.stem + ".o")
+        obj = bdir / (src.stem + ".o")
         cmd = [NVCC, *ARCH, *FLAGS, *extra, "-c", str(src), "-o", str(obj)]
         r = subprocess.run(cmd, capture_output=True, text=True)
         return src, obj, cmd, r
@@ -62,14 +67,14 @@ def build(force: bool = False, verbose: bool = False, ptxas_v: bool = False) -> 
             if r.returncode != 0:
                 raise RuntimeError(f"nvcc failed on {src.name}")
             objs.append(str(obj))
-    tmp = LIB.with_suffix(".so.tmp")
+    tmp = lib.with_suffix(".so.tmp")
     cmd = [NVCC, *ARCH, "-shared", "-Xcompiler", "-fPIC", "-o", str(tmp), *objs, "-cudart", "static"]
     r = subprocess.run(cmd, capture_output=True, text=True)
     if r.returncode != 0:
         sys.stderr.write(" ".join(cmd) + "\n" + r.stdout + r.stderr)
         raise RuntimeError("link failed")
-    os.replace(tmp, LIB)
-    return LIB
+    os.replace(tmp, lib)
+    return lib
 
 
 if __name__ == "__main__":
@@ -77,5 +82,7 @@ if __name__ == "__main__":
     ap.add_argument("--force", action="store_true")
     ap.add_argument("--verbose", action="store_true")
     ap.add_argument("--ptxas-v", action="store_true")
+    ap.add_argument("--define", action="append", default=[], help="extra -D for a variant build")
+    ap.add_argument("--out", default=None, help="output path of a variant build")
     a = ap.parse_args()
-    print(build(force=a.force, verbose=a.verbose, ptxas_v=a.ptxas_v))
+    print(build(force=a.force, verbose=a.verbose, ptxas_v=a.ptxas_v, defines=tuple(a.define), out=a.out))

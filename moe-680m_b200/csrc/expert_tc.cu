@@ -43,6 +43,22 @@
 
 namespace moe {
 
+#ifdef MOE_TC_TRACE
+// Debug timeline (builds with -DMOE_TC_TRACE only): %globaltimer stamps of CTA 0's roles.
+// Rows: 0 MMA full-wait done (per stage), 1 producer warp 0 empty-wait done (per stage),
+// 2 TMA-B empty-wait done (per stage), 3 TMA-A rempty-wait done (per chunk),
+// 4 epilogue accf-wait done (per item), 5 epilogue done (per item), 6 MMA acce-wait done.
+// Bank 0: gate/up launch, bank 1: down launch.
+__device__ unsigned long long g_tc_trace[2][8][1024];
+#define TC_TRACE(row, idx)                                                                     \
+    do {                                                                                       \
+        if (blockIdx.x == 0 && (idx) < 1024)                                                   \
+            g_tc_trace[a.counter_idx == 1 ? 0 : 1][row][idx] = tc::globaltimer_ns();          \
+    } while (0)
+#else
+#define TC_TRACE(row, idx) do {} while (0)
+#endif
+
 namespace {
 
 using namespace tc;
@@ -228,6 +244,7 @@ expert_tc_kernel(const __grid_constant__ CUtensorMap bmap, const TcArgs a) {
 #pragma unroll
                     for (int i = 0; i < NW; ++i) word_f16(qw[i], scl, v + 4 * i);
                     if (!mbar_wait(&empty[slot], ((g / kStages) & 1) ^ 1, abort)) { ok = false; break; }
+                    if (warp == 0 && lane == 0) TC_TRACE(1, g);
                     if constexpr (A_TMEM) {
                         tmem_store_words<NW>(tmem + (static_cast<uint32_t>(q * 32) << 16) + kACol0 + slot * 32 + col, v);
                         tmem_wait_st();
@@ -257,12 +274,14 @@ expert_tc_kernel(const __grid_constant__ CUtensorMap bmap, const TcArgs a) {
                 const uint32_t idesc = idesc_f16(128, (x.n + 15) & ~15);
                 const int b = it & 1;
                 if (!mbar_wait(&acce[b], ((it >> 1) & 1) ^ 1, abort)) break;
+                TC_TRACE(6, it);
                 tc_fence_after();
                 const uint32_t d = tmem + b * kAccStride;
                 bool ok = true;
                 for (int s = 0; s < nst; ++s, ++g) {
                     const int slot = g % kStages;
                     if (!mbar_wait(&full[slot], (g / kStages) & 1, abort)) { ok = false; break; }
+                    TC_TRACE(0, g);
                     tc_fence_after();
                     const uint32_t bbase = smem_u32(bst + slot * kBStageBytes);
 #pragma unroll
@@ -294,6 +313,7 @@ expert_tc_kernel(const __grid_constant__ CUtensorMap bmap, const TcArgs a) {
                 for (int s = 0; s < nst; ++s, ++g) {
                     const int slot = g % kStages;
                     if (!mbar_wait(&empty[slot], ((g / kStages) & 1) ^ 1, abort)) { ok = false; break; }
+                    TC_TRACE(2, g);
                     mbar_arrive_expect_tx(&full[slot], nbox * kBoxRows * 128);
                     for (int i = 0; i < nbox; ++i)
                         tma_load_2d(bst + slot * kBStageBytes + i * kBoxRows * 128, &bmap, s * 64,
@@ -316,6 +336,7 @@ expert_tc_kernel(const __grid_constant__ CUtensorMap bmap, const TcArgs a) {
                 for (int kc = 0; kc < nchunk; ++kc, ++rc) {
                     const int rs = rc % kRaw;
                     if (!mbar_wait(&rempty[rs], ((rc / kRaw) & 1) ^ 1, abort)) { ok = false; break; }
+                    TC_TRACE(3, rc);
                     mbar_arrive_expect_tx(&rfull[rs], kRawBytes);
                     tma_load_2d(rst + rs * kRawBytes, wm, kc * (kRawRowBytes / 2), row0, &rfull[rs]);
                 }
@@ -335,6 +356,7 @@ expert_tc_kernel(const __grid_constant__ CUtensorMap bmap, const TcArgs a) {
             const Item x = get_item(a, item);
             const int b = it & 1;
             if (!mbar_wait(&accf[b], (it >> 1) & 1, abort)) break;
+            if (ew == 0 && lane == 0) TC_TRACE(4, it);
             tc_fence_after();
             const int feat = x.rt * 128 + row;
             const uint32_t tl = tmem + (static_cast<uint32_t>(q * 32) << 16) + b * kAccStride;
@@ -355,6 +377,7 @@ expert_tc_kernel(const __grid_constant__ CUtensorMap bmap, const TcArgs a) {
             }
             tc_fence_before();
             mbar_arrive(&acce[b]);
+            if (ew == 0 && lane == 0) TC_TRACE(5, it);
         }
     }
 
@@ -547,5 +570,15 @@ bool make_iq4_tmap(CUtensorMap* m, const void* base, uint64_t rows, uint64_t row
                   estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
+
+#ifdef MOE_TC_TRACE
+extern "C" int moe_debug_tc_trace(unsigned long long* out) {
+    return cudaMemcpyFromSymbol(out, g_tc_trace, sizeof(g_tc_trace)) == cudaSuccess ? 0 : -2;
+}
+extern "C" int moe_debug_tc_trace_clear() {
+    static unsigned long long zero[2][8][1024];
+    return cudaMemcpyToSymbol(g_tc_trace, zero, sizeof(zero)) == cudaSuccess ? 0 : -2;
+}
+#endif
 
 }  // namespace moe
