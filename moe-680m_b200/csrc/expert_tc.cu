@@ -12,10 +12,10 @@
 // (token tile of one bucket x 128-row feature tile):
 //   warp 10     TMA: raw IQ4_XS bytes of the item's 128 weight rows, 512 K (two 136-byte
 //               blocks per row) per load, into a 2- or 3-deep shared-memory ring;
-//   warps 0-7   dequantise from that ring (kvalues_iq4nl lookup by byte permutes, fp16 scale
-//               per 32-weight sub-block; two warps per 32-row quarter, one sub-block each) and
-//               store the fp16 A operand, 64 K per stage, into TMEM (tcgen05.st) or into
-//               128-byte-swizzled shared memory;
+//   producer warps (8 or 16) dequantise from that ring (kvalues_iq4nl lookup by byte
+//               permutes, fp16 scale per 32-weight sub-block) and store the fp16 A operand, 64 K
+//               per stage, into TMEM (tcgen05.st) or 128-byte-swizzled shared memory; the warps
+//               of one 32-row quarter take turns by stage;
 //   warp 9      TMA: B operand (fp16 activations of the tile's slots, pre-scaled per slot by a
 //               power of two, K permuted as below), 16-row boxes, 8-deep (A in TMEM) or
 //               4-deep (A in shared memory) ring;
@@ -71,7 +71,6 @@ struct Roles {
     static constexpr int kEpiWarps = 8;               // two per 32-lane TMEM quarter
     static constexpr int kThreads = (PW + 3 + kEpiWarps) * 32;
     static constexpr int kParts = PW / 4;          // producer warps per 32-row quarter
-    static constexpr int kWordsPerPart = 8 / kParts;  // qs words (8 weights) per row per stage
 };
 constexpr int kTmemCols = 512;
 constexpr int kBoxRows = 16;        // B TMA box: 16 rows x 64 fp16
@@ -153,12 +152,6 @@ __device__ __forceinline__ Item get_item(const TcArgs& a, int item) {
     return Item{tl.bucket, tl.p0, tl.n, item - t * a.n_rt};
 }
 
-template <int NW>
-__device__ __forceinline__ void tmem_store_words(uint32_t taddr, const uint32_t (&v)[NW * 4]) {
-    if constexpr (NW == 4) tmem_st16(taddr, v);
-    else tmem_st8(taddr, v);
-}
-
 template <bool A_TMEM, int PW>
 __global__ void __launch_bounds__(Roles<PW>::kThreads, 1)
 expert_tc_kernel(const __grid_constant__ CUtensorMap bmap, const TcArgs a) {
@@ -190,7 +183,7 @@ expert_tc_kernel(const __grid_constant__ CUtensorMap bmap, const TcArgs a) {
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < kStages; ++i) {
-            mbar_init(&full[i], kProdWarps * 32 + 1);
+            mbar_init(&full[i], 128 + 1);  // one producer warp per row quarter + TMA-B
             mbar_init(&empty[i], 1);
         }
         for (int i = 0; i < kRaw; ++i) {
@@ -213,12 +206,12 @@ expert_tc_kernel(const __grid_constant__ CUtensorMap bmap, const TcArgs a) {
 
     if (warp < kProdWarps) {
         // ---------------- producers: raw IQ4_XS (smem) -> fp16 A operand ----------------
-        constexpr int NW = R::kWordsPerPart;
+        // Warp (q, part) builds whole 64-K stages of rows 32q..32q+31 for the stages g with
+        // g % kParts == part, so kParts stages per row quarter are in flight at once and the
+        // fixed per-stage latency (store, completion wait, barrier) overlaps across warps.
+        constexpr int kParts = R::kParts;
         const int q = warp & 3;
-        const int part = warp >> 2;  // which qs words of each row's 64-K stage
-        const int half = (part * NW) >> 2;           // sub-block of the stage
-        const int w0 = (part * NW) & 3;              // first word inside the sub-block
-        const int col = half * 16 + w0 * 4;          // first TMEM column / 4-byte pair
+        const int part = warp >> 2;
         const int row = q * 32 + lane;
         int g = 0, rc = 0;
         for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
@@ -228,35 +221,35 @@ expert_tc_kernel(const __grid_constant__ CUtensorMap bmap, const TcArgs a) {
                 if (!mbar_wait(&rfull[rs], (rc / kRaw) & 1, abort)) { ok = false; break; }
                 const uint8_t* raw = rst + rs * kRawBytes + row * kRawRowBytes;
                 for (int sc = 0; sc < kStagesPerChunk; ++sc, ++g) {
+                    if (g % kParts != part) continue;
                     const int slot = g % kStages;
                     const uint8_t* blk = raw + (sc >> 2) * kBlockBytes;
-                    const int ib = (sc & 3) * 2 + half;
+                    const int ib0 = (sc & 3) * 2;
                     const uint2 hdr = lds64(blk);
-                    uint32_t qw[NW];
+                    uint32_t qw[8];
 #pragma unroll
-                    for (int i = 0; i < NW; i += 2) {
-                        const uint2 qq = lds64(blk + 8 + ib * 16 + (w0 + i) * 4);
+                    for (int i = 0; i < 8; i += 2) {
+                        const uint2 qq = lds64(blk + 8 + ib0 * 16 + i * 4);
                         qw[i] = qq.x;
                         qw[i + 1] = qq.y;
                     }
-                    uint32_t v[NW * 4];
-                    const __half2 scl = subscale_h2(hdr.x, hdr.y, ib);
+                    uint32_t v[32];
+                    const __half2 s0 = subscale_h2(hdr.x, hdr.y, ib0);
+                    const __half2 s1 = subscale_h2(hdr.x, hdr.y, ib0 + 1);
 #pragma unroll
-                    for (int i = 0; i < NW; ++i) word_f16(qw[i], scl, v + 4 * i);
+                    for (int i = 0; i < 8; ++i) word_f16(qw[i], i < 4 ? s0 : s1, v + 4 * i);
                     if (!mbar_wait(&empty[slot], ((g / kStages) & 1) ^ 1, abort)) { ok = false; break; }
                     if (warp == 0 && lane == 0) TC_TRACE(1, g);
                     if constexpr (A_TMEM) {
-                        tmem_store_words<NW>(tmem + (static_cast<uint32_t>(q * 32) << 16) + kACol0 + slot * 32 + col, v);
+                        tmem_st32(tmem + (static_cast<uint32_t>(q * 32) << 16) + kACol0 + slot * 32, v);
                         tmem_wait_st();
                         tc_fence_before();
                     } else {
                         uint8_t* rowp = ast + slot * kAStageBytes + row * 128;
 #pragma unroll
-                        for (int c = 0; c < NW; ++c) {
-                            const int cc = (col >> 2) + c;   // 16-byte chunk of the 128-byte row
-                            *reinterpret_cast<uint4*>(rowp + ((cc ^ (row & 7)) << 4)) =
+                        for (int c = 0; c < 8; ++c)
+                            *reinterpret_cast<uint4*>(rowp + ((c ^ (row & 7)) << 4)) =
                                 make_uint4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
-                        }
                         fence_proxy_async_smem();
                     }
                     mbar_arrive(&full[slot]);
