@@ -236,15 +236,25 @@ expert_tc_kernel(const __grid_constant__ CUtensorMap bmap, const TcArgs a) {
                     uint32_t v[32];
                     const __half2 s0 = subscale_h2(hdr.x, hdr.y, ib0);
                     const __half2 s1 = subscale_h2(hdr.x, hdr.y, ib0 + 1);
+#if defined(MOE_TC_DIAG) && MOE_TC_DIAG == 2
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) v[i] = qw[i & 7] ^ hdr.x;  // diagnostic: no dequant
+#else
 #pragma unroll
                     for (int i = 0; i < 8; ++i) word_f16(qw[i], i < 4 ? s0 : s1, v + 4 * i);
+#endif
                     if (!mbar_wait(&empty[slot], ((g / kStages) & 1) ^ 1, abort)) { ok = false; break; }
                     if (warp == 0 && lane == 0) TC_TRACE(1, g);
+#if defined(MOE_TC_DIAG) && MOE_TC_DIAG == 1
+                    if (v[0] == 0x12345678u && v[31] == 0x9abcdef0u) g_tc_trace[1][7][0] = v[5];  // keep work
+                    if constexpr (false) {
+#else
                     if constexpr (A_TMEM) {
+#endif
                         tmem_st32(tmem + (static_cast<uint32_t>(q * 32) << 16) + kACol0 + slot * 32, v);
                         tmem_wait_st();
                         tc_fence_before();
-                    } else {
+                    } else if constexpr (!A_TMEM) {
                         uint8_t* rowp = ast + slot * kAStageBytes + row * 128;
 #pragma unroll
                         for (int c = 0; c < 8; ++c)
