@@ -80,7 +80,7 @@ int ensure_ws(Ctx* c, uint32_t M, uint32_t E, uint32_t k, uint32_t slots, uint32
     const int max_chunks = moe::max_chunks_for(M, slots, E);
     size_t off = 0;
     auto take = [&](size_t bytes) { const size_t o = off; off = align_up(off + bytes, 256); return o; };
-    const size_t o_logits = take(sizeof(float) * 4 * M * (E + 1));
+    const size_t o_logits = take(sizeof(float) * 16 * M * (E + 1));  // up to 16 K splits
     const size_t o_topk = take(sizeof(uint2) * M * (slots + 1));
     const size_t o_tile = take(sizeof(int) * tiles * (E + 1));
     const size_t o_ranges = take(sizeof(int) * (E + 2));
@@ -100,6 +100,8 @@ int ensure_ws(Ctx* c, uint32_t M, uint32_t E, uint32_t k, uint32_t slots, uint32
     const size_t o_xe = take(sizeof(int) * S);
     const size_t o_he = take(sizeof(int) * S);
     const size_t o_io = take(sizeof(moe::IoArgs));
+    const size_t o_xh = take(sizeof(float) * M * H);
+    const size_t o_xl = take(sizeof(float) * M * H);
     const size_t total = off;
     int* status = ws.status;
     ws.status = nullptr;
@@ -138,6 +140,8 @@ int ensure_ws(Ctx* c, uint32_t M, uint32_t E, uint32_t k, uint32_t slots, uint32
     ws.xexp = reinterpret_cast<int*>(b + o_xe);
     ws.hexp = reinterpret_cast<int*>(b + o_he);
     ws.io = reinterpret_cast<moe::IoArgs*>(b + o_io);
+    ws.xh = reinterpret_cast<float*>(b + o_xh);
+    ws.xl = reinterpret_cast<float*>(b + o_xl);
     ws.max_chunks = static_cast<uint32_t>(max_chunks);
     ws.status = status;
     return MOE_OK;
@@ -221,11 +225,32 @@ void run_set_io(Ctx* c, const float* x, const float* resid, float* out) {
     stage(c, "set_io", 1);
 }
 
-// Routing of M tokens (activations from ws.io) into ws.topk.
+int ensure_tmap(Ctx* c, CUtensorMap* m, const void** base, uint64_t* rows, uint64_t* cols,
+                const void* p, uint64_t r, uint64_t cl);
+
+// Routing of M tokens (activations from ws.io) into ws.topk: tensor-core router (3xTF32) for
+// batches above 8 tokens when the layer supports it, CUDA-core f32 otherwise.
 int run_route(Ctx* c, const Layer& L, uint32_t M) {
-    moe::launch_router_logits(L, c->ws.io, static_cast<int>(M), c->ws.logits, c->stream);
-    stage(c, "router", 1);
-    moe::launch_topk(L, c->ws.logits, static_cast<int>(M), c->ws.topk, c->ws.status, c->stream);
+    Workspace& ws = c->ws;
+    const int E = static_cast<int>(L.spec.n_experts), H = static_cast<int>(L.spec.hidden);
+    if (M > 8 && L.wsplit) {
+        if (ws.xh_base != ws.xh || ws.xh_rows != M || ws.xh_cols != static_cast<uint64_t>(H)) {
+            if (!moe::make_f32_tmap(&ws.xhmap, ws.xh, M, H, 256) || !moe::make_f32_tmap(&ws.xlmap, ws.xl, M, H, 256))
+                return fail(c, MOE_E_CUDA, "cuTensorMapEncodeTiled failed for the router operands");
+            ws.xh_base = ws.xh; ws.xh_rows = M; ws.xh_cols = static_cast<uint64_t>(H);
+        }
+        moe::launch_split_x(ws.io, static_cast<size_t>(M) * H, ws.xh, ws.xl, c->stream);
+        stage(c, "router_split", 1);
+        moe::launch_router_tc(L, ws.xhmap, ws.xlmap, static_cast<int>(M), ws.logits, ws.status, c->stream);
+        stage(c, "router", 1);
+        moe::launch_topk(L, ws.logits, moe::router_tc_split(static_cast<int>(M), E, H), false, ws.io,
+                         static_cast<int>(M), ws.topk, ws.status, c->stream);
+    } else {
+        moe::launch_router_logits(L, ws.io, static_cast<int>(M), ws.logits, c->stream);
+        stage(c, "router", 1);
+        moe::launch_topk(L, ws.logits, moe::router_split_for(static_cast<int>(M), H), true, ws.io,
+                         static_cast<int>(M), ws.topk, ws.status, c->stream);
+    }
     stage(c, "topk", 1);
     return check_launch(c, "router");
 }
@@ -272,7 +297,7 @@ int run_experts(Ctx* c, const Layer& L, uint32_t M) {
         if (rc) return rc;
         rc = ensure_tmap(c, &ws.hmap, &ws.hmap_base, &ws.hmap_rows, &ws.hmap_cols, ws.h16, S, I);
         if (rc) return rc;
-        moe::launch_convert_x(ws.io, ws.sorted_tok, static_cast<int>(S), H, ws.x16, ws.xexp, c->stream);
+        moe::launch_convert_x(ws.io, ws.slot_pos, static_cast<int>(M), slots, H, ws.x16, ws.xexp, c->stream);
         stage(c, "convert_x", 1);
         const int items13 = moe::max_tiles_for(static_cast<int>(M), slots, E, moe::tc_max_n(13)) * (2 * I / 128);
         moe::launch_tc13(L, ws.xmap, ws, items13, c->sm_count, a_tmem, c->stream);
@@ -453,6 +478,7 @@ void moe_ctx_destroy(moe_ctx* c) {
     for (auto& L : c->layers) {
         if (L.tab) cudaFree(const_cast<uint8_t**>(L.tab));
         if (L.wmaps) cudaFree(L.wmaps);
+        if (L.wsplit) cudaFree(L.wsplit);
     }
     for (auto& g : c->graphs) destroy_graph(g);
     int* status = c->ws.status;
@@ -567,6 +593,19 @@ int moe_layer_create(moe_ctx* c, const moe_layer_spec* spec, const uint64_t* w1,
     Layer L;
     L.spec = s;
     L.tab = static_cast<const uint8_t**>(d);
+    if (H % 32 == 0) {
+        // router weight split for the tensor-core router: [Wh | Wl], each [E][H] f32
+        void* wsd = nullptr;
+        MOE_CUDA(c, cudaMalloc(&wsd, 2 * E * H * sizeof(float)));
+        float* whp = static_cast<float*>(wsd);
+        moe::launch_split_tf32(reinterpret_cast<const float*>(c->base + s.router_w), E * H, whp,
+                               whp + E * H, c->stream);
+        MOE_CUDA(c, cudaStreamSynchronize(c->stream));
+        if (moe::make_f32_tmap(&L.rmaps[0], whp, E, H, 128) && moe::make_f32_tmap(&L.rmaps[1], whp + E * H, E, H, 128))
+            L.wsplit = whp;
+        else
+            cudaFree(wsd);
+    }
     if (moe::tc_supported(static_cast<int>(H), static_cast<int>(I))) {
         // raw IQ4_XS tensor maps for the tensor-core path: [W1 | W3 | W2][E+1]
         std::vector<CUtensorMap> maps(3 * (E + 1));

@@ -21,6 +21,7 @@ namespace moe {
 namespace {
 
 constexpr int kTile = 256;  // tokens per tile (8 warps x 32)
+constexpr int kScanThreads = 288;  // >= kMaxExperts + 1, whole warps
 
 __device__ __forceinline__ void build_masks(uint32_t* masks, int nb, const uint2* topk, int M,
                                             int E, int k, int* status) {
@@ -65,67 +66,81 @@ struct TileLists {
     int n13, n2;  // tokens per tile
 };
 
-__global__ void __launch_bounds__(1024)
+// Block-wide exclusive scan of int4 values (one per thread), returns the block total.
+__device__ __forceinline__ int4 block_exscan4(int4 v, int4* warp_tot, int4& total) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    int4 inc = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int ax = __shfl_up_sync(0xffffffffu, inc.x, o), ay = __shfl_up_sync(0xffffffffu, inc.y, o);
+        const int az = __shfl_up_sync(0xffffffffu, inc.z, o), aw = __shfl_up_sync(0xffffffffu, inc.w, o);
+        if (lane >= o) { inc.x += ax; inc.y += ay; inc.z += az; inc.w += aw; }
+    }
+    if (lane == 31) warp_tot[warp] = inc;
+    __syncthreads();
+    if (warp == 0) {
+        int4 t = lane < nw ? warp_tot[lane] : make_int4(0, 0, 0, 0);
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int ax = __shfl_up_sync(0xffffffffu, t.x, o), ay = __shfl_up_sync(0xffffffffu, t.y, o);
+            const int az = __shfl_up_sync(0xffffffffu, t.z, o), aw = __shfl_up_sync(0xffffffffu, t.w, o);
+            if (lane >= o) { t.x += ax; t.y += ay; t.z += az; t.w += aw; }
+        }
+        if (lane < nw) warp_tot[lane] = t;  // inclusive over warps
+    }
+    __syncthreads();
+    const int4 before = warp > 0 ? warp_tot[warp - 1] : make_int4(0, 0, 0, 0);
+    total = warp_tot[nw - 1];
+    return make_int4(before.x + inc.x - v.x, before.y + inc.y - v.y, before.z + inc.z - v.z,
+                     before.w + inc.w - v.w);
+}
+
+// One CTA, one thread per bucket (blockDim >= E+1).  tilecnt[tile][e] -> absolute offset of
+// the tile's first slot in bucket e (in place); ranges[0..E+1]; the chunk list of the CUDA-core
+// kernels and the token-tile lists of the tensor-core kernels.
+__global__ void __launch_bounds__(kScanThreads)
 bucket_scan_kernel(int* __restrict__ tilecnt, int n_tiles, int E, int* __restrict__ ranges,
                    Chunk* __restrict__ chunks, int max_chunks, TileLists lists,
                    int* __restrict__ counters, int* status) {
-    __shared__ int tot[kMaxExperts + 2];
-    __shared__ int nch[kMaxExperts + 2];
-    __shared__ int f13[kMaxExperts + 2];
-    __shared__ int f2[kMaxExperts + 2];
+    __shared__ int4 warp_tot[32];
     const int nb = E + 1;
-    for (int e = threadIdx.x; e < nb; e += blockDim.x) {
-        int run = 0;
+    const int e = threadIdx.x;
+    int cnt = 0;
+    if (e < nb) {
         for (int tl = 0; tl < n_tiles; ++tl) {
             const int c = tilecnt[static_cast<size_t>(tl) * nb + e];
-            tilecnt[static_cast<size_t>(tl) * nb + e] = run;
-            run += c;
+            tilecnt[static_cast<size_t>(tl) * nb + e] = cnt;
+            cnt += c;
         }
-        tot[e] = run;
-        nch[e] = (run + kGemvTok - 1) / kGemvTok;
     }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        int r = 0, c = 0, a13 = 0, a2 = 0;
-        for (int e = 0; e < nb; ++e) {
-            ranges[e] = r;
-            const int cnt = tot[e];
-            r += cnt;
-            const int n = nch[e];
-            nch[e] = c;  // first chunk index of bucket e
-            c += n;
-            f13[e] = a13;
-            a13 += (cnt + lists.n13 - 1) / lists.n13;
-            f2[e] = a2;
-            a2 += (cnt + lists.n2 - 1) / lists.n2;
-            tot[e] = ranges[e];
+    const int4 v = make_int4(cnt, (cnt + kGemvTok - 1) / kGemvTok, (cnt + lists.n13 - 1) / lists.n13,
+                             (cnt + lists.n2 - 1) / lists.n2);
+    int4 total;
+    const int4 first = block_exscan4(v, warp_tot, total);
+    if (e < nb) {
+        ranges[e] = first.x;
+        for (int tl = 0; tl < n_tiles; ++tl) tilecnt[static_cast<size_t>(tl) * nb + e] += first.x;
+        int ci = first.y;
+        for (int s = 0; s < cnt && ci < max_chunks; s += kGemvTok, ++ci)
+            chunks[ci] = Chunk{e, first.x + s, min(kGemvTok, cnt - s), 0};
+        if (lists.t13) {
+            int ti = first.z;
+            for (int s = 0; s < cnt && ti < lists.max13; s += lists.n13, ++ti)
+                lists.t13[ti] = TcTile{e, first.x + s, min(lists.n13, cnt - s), 0};
+            ti = first.w;
+            for (int s = 0; s < cnt && ti < lists.max2; s += lists.n2, ++ti)
+                lists.t2[ti] = TcTile{e, first.x + s, min(lists.n2, cnt - s), 0};
         }
-        ranges[nb] = r;
+    }
+    if (threadIdx.x == 0) {
+        ranges[nb] = total.x;
+        int c = total.y, a13 = total.z, a2 = total.w;
         if (c > max_chunks) { set_dev_error(status, kDevOverflow); c = max_chunks; }
         if (a13 > lists.max13) { set_dev_error(status, kDevOverflow); a13 = lists.max13; }
         if (a2 > lists.max2) { set_dev_error(status, kDevOverflow); a2 = lists.max2; }
         counters[0] = c;
         counters[1] = a13;
         counters[2] = a2;
-    }
-    __syncthreads();
-    for (int e = threadIdx.x; e < nb; e += blockDim.x) {
-        const int base = tot[e];
-        for (int tl = 0; tl < n_tiles; ++tl) tilecnt[static_cast<size_t>(tl) * nb + e] += base;
-        const int cnt = ranges[e + 1] - ranges[e];
-        int ci = nch[e];
-        for (int s = 0; s < cnt; s += kGemvTok, ++ci) {
-            if (ci >= max_chunks) break;
-            chunks[ci] = Chunk{e, ranges[e] + s, min(kGemvTok, cnt - s), 0};
-        }
-        if (lists.t13) {
-            int ti = f13[e];
-            for (int s = 0; s < cnt && ti < lists.max13; s += lists.n13, ++ti)
-                lists.t13[ti] = TcTile{e, ranges[e] + s, min(lists.n13, cnt - s), 0};
-            ti = f2[e];
-            for (int s = 0; s < cnt && ti < lists.max2; s += lists.n2, ++ti)
-                lists.t2[ti] = TcTile{e, ranges[e] + s, min(lists.n2, cnt - s), 0};
-        }
     }
 }
 
@@ -172,7 +187,7 @@ void launch_bucket(int E, int k, bool has_shared, const uint2* topk, int M, Work
                                                      ws.tilecnt, status);
     TileLists tl{ws.tiles13, static_cast<int>(ws.max_tiles13), ws.tiles2,
                  static_cast<int>(ws.max_tiles2), tc_max_n(13), tc_max_n(2)};
-    bucket_scan_kernel<<<1, 1024, 0, s>>>(ws.tilecnt, n_tiles, E, ranges, ws.chunks,
+    bucket_scan_kernel<<<1, kScanThreads, 0, s>>>(ws.tilecnt, n_tiles, E, ranges, ws.chunks,
                                           static_cast<int>(ws.max_chunks), tl, ws.counters, status);
     bucket_scatter_kernel<<<n_tiles, kTile, smem, s>>>(topk, M, E, k, has_shared ? 1 : 0,
                                                        ws.tilecnt, sorted_tok, sorted_w, slot_pos,

@@ -417,57 +417,72 @@ __device__ __forceinline__ void put_chunk(__half* d, int c, float4 lo, float4 hi
 // chunk c (8 halves): stage c/8, sub-block (c%8)/4, word c%4 -> k = 64*(c/8)+32*((c%8)/4)+4*(c%4)
 __device__ __forceinline__ int chunk_k(int c) { return 64 * (c >> 3) + 32 * ((c & 7) >> 2) + 4 * (c & 3); }
 
-// dst[p][perm(k)] = fp16(src[gather[p]][k] * 2^-e); sexp[p] = e.
+__device__ __forceinline__ float4 swiglu4(float4 g, float4 u) {
+    return make_float4(silu_f(g.x) * u.x, silu_f(g.y) * u.y, silu_f(g.z) * u.z, silu_f(g.w) * u.w);
+}
+
+// One warp per token: x[t] -> fp16(x * 2^-e) in the permuted K order, written to the rows of
+// all the token's slots (slot_pos[t][0..ns)); sexp[p] = e for those slots.
 __global__ void __launch_bounds__(256)
-convert_x_kernel(const IoArgs* __restrict__ io, const int* __restrict__ gather, int n_rows,
+convert_x_kernel(const IoArgs* __restrict__ io, const int* __restrict__ slot_pos, int M, int ns,
                  int len, __half* __restrict__ dst, int* __restrict__ sexp) {
-    const int p = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
-    if (p >= n_rows) return;
-    const float* __restrict__ src = io->x;
-    const float* s = src + static_cast<size_t>(gather[p]) * len;
+    const int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    if (t >= M) return;
+    const float* s = io->x + static_cast<size_t>(t) * len;
     float mx = 0.f;
     for (int i = lane * 4; i < len; i += 128) {
         const float4 v = *reinterpret_cast<const float4*>(s + i);
         mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
     }
     const int e = row_exp(warp_max(mx));
-    if (lane == 0) sexp[p] = e;
     const float sc = pow2f(-e);
-    __half* d = dst + static_cast<size_t>(p) * len;
+    int pos[kMaxTopK + 1];
+#pragma unroll
+    for (int j = 0; j < kMaxTopK + 1; ++j) pos[j] = j < ns ? slot_pos[static_cast<size_t>(t) * ns + j] : -1;
+    if (lane < ns && pos[lane] >= 0) sexp[pos[lane]] = e;
     for (int c = lane; c < len / 8; c += 32) {
         const int kb = chunk_k(c);
-        put_chunk(d, c, *reinterpret_cast<const float4*>(s + kb),
-                  *reinterpret_cast<const float4*>(s + kb + 16), sc);
+        const float4 lo = *reinterpret_cast<const float4*>(s + kb);
+        const float4 hi = *reinterpret_cast<const float4*>(s + kb + 16);
+        __half2 o[4];
+        o[0] = __floats2half2_rn(lo.x * sc, hi.x * sc);
+        o[1] = __floats2half2_rn(lo.y * sc, hi.y * sc);
+        o[2] = __floats2half2_rn(lo.z * sc, hi.z * sc);
+        o[3] = __floats2half2_rn(lo.w * sc, hi.w * sc);
+        const uint4 val = *reinterpret_cast<uint4*>(o);
+#pragma unroll
+        for (int j = 0; j < kMaxTopK + 1; ++j)
+            if (j < ns && pos[j] >= 0)
+                *reinterpret_cast<uint4*>(dst + static_cast<size_t>(pos[j]) * len + 8 * c) = val;
     }
 }
 
-__device__ __forceinline__ float4 swiglu4(float4 g, float4 u) {
-    return make_float4(silu_f(g.x) * u.x, silu_f(g.y) * u.y, silu_f(g.z) * u.z, silu_f(g.w) * u.w);
-}
-
 // gu[p] = [g (I) | u (I)] f32 -> h = silu(g) * u -> dst[p][perm(k)] = fp16(h * 2^-e); sexp[p] = e.
+// One warp per slot; h is staged in shared memory (I <= 1024).
 __global__ void __launch_bounds__(256)
 convert_h_kernel(const float* __restrict__ gu, int n_rows, int I, __half* __restrict__ dst,
                  int* __restrict__ sexp) {
+    __shared__ __align__(16) float hs[8][1024];
+    const int wib = threadIdx.x >> 5;
     const int p = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
     if (p >= n_rows) return;
     const float* g = gu + static_cast<size_t>(p) * 2 * I;
     const float* u = g + I;
+    float* h = hs[wib];
     float mx = 0.f;
     for (int i = lane * 4; i < I; i += 128) {
-        const float4 h = swiglu4(*reinterpret_cast<const float4*>(g + i), *reinterpret_cast<const float4*>(u + i));
-        mx = fmaxf(mx, fmaxf(fmaxf(fabsf(h.x), fabsf(h.y)), fmaxf(fabsf(h.z), fabsf(h.w))));
+        const float4 v = swiglu4(*reinterpret_cast<const float4*>(g + i), *reinterpret_cast<const float4*>(u + i));
+        *reinterpret_cast<float4*>(h + i) = v;
+        mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
     }
+    __syncwarp();
     const int e = row_exp(warp_max(mx));
     if (lane == 0) sexp[p] = e;
     const float sc = pow2f(-e);
     __half* d = dst + static_cast<size_t>(p) * I;
     for (int c = lane; c < I / 8; c += 32) {
         const int kb = chunk_k(c);
-        const float4 lo = swiglu4(*reinterpret_cast<const float4*>(g + kb), *reinterpret_cast<const float4*>(u + kb));
-        const float4 hi = swiglu4(*reinterpret_cast<const float4*>(g + kb + 16),
-                                  *reinterpret_cast<const float4*>(u + kb + 16));
-        put_chunk(d, c, lo, hi, sc);
+        put_chunk(d, c, *reinterpret_cast<const float4*>(h + kb), *reinterpret_cast<const float4*>(h + kb + 16), sc);
     }
 }
 
@@ -504,9 +519,9 @@ int tc_max_n(int) { return kNMax; }
 
 bool tc_supported(int hidden, int inter) { return hidden % 512 == 0 && inter % 512 == 0; }
 
-void launch_convert_x(const IoArgs* x, const int* gather, int n_rows, int len, __half* dst,
+void launch_convert_x(const IoArgs* x, const int* slot_pos, int M, int ns, int len, __half* dst,
                       int* sexp, cudaStream_t s) {
-    convert_x_kernel<<<(n_rows * 32 + 255) / 256, 256, 0, s>>>(x, gather, n_rows, len, dst, sexp);
+    convert_x_kernel<<<(M * 32 + 255) / 256, 256, 0, s>>>(x, slot_pos, M, ns, len, dst, sexp);
 }
 
 void launch_convert_h(const float* gu, int n_rows, int inter, __half* dst, int* sexp,
@@ -556,6 +571,19 @@ bool make_fp16_tmap(CUtensorMap* m, const void* base, uint64_t rows, uint64_t co
     const cuuint32_t box[2] = {64, kBoxRows};
     const cuuint32_t estr[2] = {1, 1};
     return encode(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box,
+                  estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// 2D tensor map over an f32 [rows][cols] row-major matrix, box box_rows x 32 cols, 128B swizzle.
+bool make_f32_tmap(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows) {
+    auto encode = tmap_encoder();
+    if (!encode || (cols * 4) % 16 != 0) return false;
+    const cuuint64_t dims[2] = {cols, rows};
+    const cuuint64_t strides[1] = {cols * 4};
+    const cuuint32_t box[2] = {32, box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    return encode(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void*>(base), dims, strides, box,
                   estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }

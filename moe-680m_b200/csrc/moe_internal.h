@@ -30,6 +30,8 @@ struct Layer {
     const uint8_t* gate_ptr = nullptr;  // may be null
     CUtensorMap* wmaps = nullptr;       // device [3][E+1] raw IQ4_XS maps (W1, W3, W2), or null
                                         // when the shapes do not suit the tensor-core path
+    float* wsplit = nullptr;            // device [2][E][H]: router weight split (TF32 hi, rest)
+    CUtensorMap rmaps[2];               // maps over wsplit (valid when wsplit != null)
     ExpertTables tables() const {
         const uint32_t n = spec.n_experts + 1;
         return ExpertTables{tab, tab + n, tab + 2 * n};
@@ -95,6 +97,11 @@ struct Workspace {
     __half* x16 = nullptr;        // [S][H] gathered, scaled, K-permuted activations
     __half* h16 = nullptr;        // [S][I]
     int* xexp = nullptr;          // [S] power-of-two exponent of x16's scale
+    float* xh = nullptr;          // [M][H] TF32 part of x (tensor-core router)
+    float* xl = nullptr;          // [M][H] remainder
+    CUtensorMap xhmap, xlmap;
+    const void* xh_base = nullptr;
+    uint64_t xh_rows = 0, xh_cols = 0;
     int* hexp = nullptr;          // [S]
     // tensor maps (re-encoded when the buffers or the slot count change)
     CUtensorMap xmap, hmap;
@@ -154,8 +161,8 @@ int router_split_for(int M, int H);
 void launch_set_io(IoArgs* dst, const float* x, const float* resid, float* out, cudaStream_t s);
 const void* set_io_func();
 void launch_router_logits(const Layer& L, const IoArgs* io, int M, float* logits, cudaStream_t s);
-void launch_topk(const Layer& L, const float* logits, int M, uint2* topk, int* status,
-                 cudaStream_t s);
+void launch_topk(const Layer& L, const float* logits, int n_split, bool gate_in_logits,
+                 const IoArgs* io, int M, uint2* topk, int* status, cudaStream_t s);
 void launch_bucket(int E, int k, bool has_shared, const uint2* topk, int M, Workspace& ws,
                    int* ranges, int* sorted_tok, float* sorted_w, int* slot_pos, int* status,
                    cudaStream_t s);
@@ -165,11 +172,17 @@ void launch_gemv2(const Layer& L, const Workspace& ws, int M, int max_chunks, in
                   cudaStream_t s);
 int tc_max_n(int mode);
 bool tc_supported(int hidden, int inter);
-void launch_convert_x(const IoArgs* io, const int* gather, int n_rows, int len, __half* dst,
+void launch_convert_x(const IoArgs* io, const int* slot_pos, int M, int ns, int len, __half* dst,
                       int* sexp, cudaStream_t s);
 void launch_convert_h(const float* gu, int n_rows, int inter, __half* dst, int* sexp,
                       cudaStream_t s);
 bool make_iq4_tmap(CUtensorMap* m, const void* base, uint64_t rows, uint64_t row_bytes);
+bool make_f32_tmap(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows);
+void launch_split_tf32(const float* src, size_t n, float* hi, float* lo, cudaStream_t s);
+void launch_split_x(const IoArgs* io, size_t n, float* hi, float* lo, cudaStream_t s);
+int router_tc_split(int M, int E, int H);
+void launch_router_tc(const Layer& L, const CUtensorMap& xh, const CUtensorMap& xl, int M,
+                      float* partial, int* status, cudaStream_t s);
 void launch_tc13(const Layer& L, const CUtensorMap& xmap, const Workspace& ws, int max_items,
                  int sm_count, bool a_tmem, cudaStream_t s);
 void launch_tc2(const Layer& L, const CUtensorMap& hmap, const Workspace& ws, int max_items,

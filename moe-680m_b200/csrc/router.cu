@@ -118,8 +118,9 @@ router_gemm_kernel(const IoArgs* __restrict__ io, int M, int H, const float* __r
 // descending, ties toward the lower expert index (strict '>' insertion, router_topk.comp:67-85).
 __global__ void __launch_bounds__(256)
 topk_kernel(const float* __restrict__ partial, int n_split, int M, int E, int k,
-            const float* __restrict__ bias, int shared_mode, uint2* __restrict__ topk,
-            int* status) {
+            const float* __restrict__ bias, int shared_mode, int gate_in_logits,
+            const IoArgs* __restrict__ io, const float* __restrict__ gate_w, int H,
+            uint2* __restrict__ topk, int* status) {
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
     if (warp >= M) return;
     const int t = warp;
@@ -174,15 +175,23 @@ topk_kernel(const float* __restrict__ partial, int n_split, int M, int E, int k,
         }
         if (lane == 0) rec[1 + r] = make_uint2(static_cast<uint32_t>(bi), __float_as_uint(bv));
     }
-    if (lane == 0) {
-        float g = 1.0f;
-        if (shared_mode == 2) {
-            float z = 0.f;
+    float g = 1.0f;
+    if (shared_mode == 2) {
+        float z = 0.f;
+        if (gate_in_logits) {
             for (int s = 0; s < n_split; ++s) z += partial[(static_cast<size_t>(s) * M + t) * (E + 1) + E];
-            g = 1.0f / (1.0f + expf(-z));
+        } else {  // gate logit g . x[t], fixed-order warp reduction
+            const float* xr = io->x + static_cast<size_t>(t) * H;
+            for (int i = lane * 4; i < H; i += 128) {
+                const float4 a = *reinterpret_cast<const float4*>(xr + i);
+                const float4 b = *reinterpret_cast<const float4*>(gate_w + i);
+                z = fmaf(a.x, b.x, z); z = fmaf(a.y, b.y, z); z = fmaf(a.z, b.z, z); z = fmaf(a.w, b.w, z);
+            }
+            z = warp_sum(z);
         }
-        rec[0] = make_uint2(static_cast<uint32_t>(E), __float_as_uint(g));
+        g = 1.0f / (1.0f + expf(-z));
     }
+    if (lane == 0) rec[0] = make_uint2(static_cast<uint32_t>(E), __float_as_uint(g));
 }
 
 }  // namespace
@@ -213,15 +222,16 @@ void launch_router_logits(const Layer& L, const IoArgs* x, int M, float* logits,
     }
 }
 
-void launch_topk(const Layer& L, const float* logits, int M, uint2* topk, int* status,
-                 cudaStream_t s) {
+void launch_topk(const Layer& L, const float* logits, int n_split, bool gate_in_logits,
+                 const IoArgs* io, int M, uint2* topk, int* status, cudaStream_t s) {
     const int E = L.spec.n_experts;
-    const int split = router_split_for(M, L.spec.hidden);
     const int shared_mode = (L.spec.flags & MOE_F_SHARED_GATE) ? 2 : 1;
     const float* bias = reinterpret_cast<const float*>(L.bias_ptr);
-    const int warps_per_cta = 8;
+    const int warps_per_cta = 4;
     topk_kernel<<<(M + warps_per_cta - 1) / warps_per_cta, 32 * warps_per_cta, 0, s>>>(
-        logits, split, M, E, static_cast<int>(L.spec.top_k), bias, shared_mode, topk, status);
+        logits, n_split, M, E, static_cast<int>(L.spec.top_k), bias, shared_mode,
+        gate_in_logits ? 1 : 0, io, reinterpret_cast<const float*>(L.gate_ptr),
+        static_cast<int>(L.spec.hidden), topk, status);
 }
 
 }  // namespace moe
