@@ -116,14 +116,24 @@ router_gemm_kernel(const IoArgs* __restrict__ io, int M, int H, const float* __r
 // ---- softmax + top-k: one warp per token ----------------------------------------------------
 // Probabilities p = exp(l - max) / sum (router_topk.comp:36-60).  Top-k keeps the k largest p,
 // descending, ties toward the lower expert index (strict '>' insertion, router_topk.comp:67-85).
-__global__ void __launch_bounds__(256)
-topk_kernel(const float* __restrict__ partial, int n_split, int M, int E, int k,
+template <int NS>
+__global__ void __launch_bounds__(128)
+topk_kernel(const float* __restrict__ partial, int M, int E, int k,
             const float* __restrict__ bias, int shared_mode, int gate_in_logits,
             const IoArgs* __restrict__ io, const float* __restrict__ gate_w, int H,
             uint2* __restrict__ topk, int* status) {
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
     if (warp >= M) return;
     const int t = warp;
+    // all NS x 8 partial loads are independent; the splits are then added in a fixed order
+    float part[NS][8];
+#pragma unroll
+    for (int s = 0; s < NS; ++s)
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const int e = lane + 32 * i;
+            part[s][i] = e < E ? partial[(static_cast<size_t>(s) * M + t) * (E + 1) + e] : 0.f;
+        }
     float p[8];
     float mx = -INFINITY;
 #pragma unroll
@@ -132,8 +142,8 @@ topk_kernel(const float* __restrict__ partial, int n_split, int M, int E, int k,
         float l = -INFINITY;
         if (e < E) {
             l = 0.f;
-            for (int s = 0; s < n_split; ++s)
-                l += partial[(static_cast<size_t>(s) * M + t) * (E + 1) + e];
+#pragma unroll
+            for (int s = 0; s < NS; ++s) l += part[s][i];
             if (bias) l += bias[e];
         }
         p[i] = l;
@@ -179,7 +189,8 @@ topk_kernel(const float* __restrict__ partial, int n_split, int M, int E, int k,
     if (shared_mode == 2) {
         float z = 0.f;
         if (gate_in_logits) {
-            for (int s = 0; s < n_split; ++s) z += partial[(static_cast<size_t>(s) * M + t) * (E + 1) + E];
+#pragma unroll
+            for (int s = 0; s < NS; ++s) z += partial[(static_cast<size_t>(s) * M + t) * (E + 1) + E];
         } else {  // gate logit g . x[t], fixed-order warp reduction
             const float* xr = io->x + static_cast<size_t>(t) * H;
             for (int i = lane * 4; i < H; i += 128) {
@@ -227,11 +238,19 @@ void launch_topk(const Layer& L, const float* logits, int n_split, bool gate_in_
     const int E = L.spec.n_experts;
     const int shared_mode = (L.spec.flags & MOE_F_SHARED_GATE) ? 2 : 1;
     const float* bias = reinterpret_cast<const float*>(L.bias_ptr);
-    const int warps_per_cta = 4;
-    topk_kernel<<<(M + warps_per_cta - 1) / warps_per_cta, 32 * warps_per_cta, 0, s>>>(
-        logits, n_split, M, E, static_cast<int>(L.spec.top_k), bias, shared_mode,
-        gate_in_logits ? 1 : 0, io, reinterpret_cast<const float*>(L.gate_ptr),
-        static_cast<int>(L.spec.hidden), topk, status);
+    const int grid = (M + 3) / 4;
+    const float* gw = reinterpret_cast<const float*>(L.gate_ptr);
+    const int k = static_cast<int>(L.spec.top_k), H = static_cast<int>(L.spec.hidden);
+    const int gl = gate_in_logits ? 1 : 0;
+#define MOE_TOPK(NS) topk_kernel<NS><<<grid, 128, 0, s>>>(logits, M, E, k, bias, shared_mode, gl, io, gw, H, topk, status)
+    switch (n_split) {
+        case 1: MOE_TOPK(1); break;
+        case 2: MOE_TOPK(2); break;
+        case 4: MOE_TOPK(4); break;
+        case 8: MOE_TOPK(8); break;
+        default: MOE_TOPK(16); break;
+    }
+#undef MOE_TOPK
 }
 
 }  // namespace moe

@@ -127,7 +127,8 @@ def test_forward_full_shapes(ctx, m, zipf):
     ties = near_ties(hl, x, FULL.top_k)
     ok = np.array([t not in ties for t in range(m)])
     assert np.array_equal(routed.astype(np.int32)[ok], ref["ids"][ok])
-    assert np.allclose(w[ok], ref["w"][ok], rtol=2e-6, atol=1e-9)
+    # softmax weights from f32-accurate logits (f32 CUDA-core or 3xTF32 tensor-core router)
+    assert np.allclose(w[ok], ref["w"][ok], rtol=2e-5, atol=1e-9)
     assert np.allclose(g, ref["gate"], rtol=1e-5)
     if ok.all():
         check_close(out, ref["out64"], f"M={m}")
