@@ -19,7 +19,7 @@
 //   warp 9      TMA: B operand (fp16 activations of the tile's slots, pre-scaled per slot by a
 //               power of two, K permuted as below), 16-row boxes, 8-deep (A in TMEM) or
 //               4-deep (A in shared memory) ring;
-//   warp 8      allocates TMEM; lane 0 issues tcgen05.mma (M=128, N=16..kNMax, K=16) and
+//   warp 8      allocates TMEM; one elected lane issues tcgen05.mma (M=128, N=16..kNMax, K=16) and
 //               tcgen05.commit;
 //   warps 11-14 epilogue: TMEM -> registers, undo the activation scale, store f32
 //               out[slot][feature] (gate/up pre-activations, or the unweighted down output).
@@ -269,24 +269,24 @@ expert_tc_kernel(const __grid_constant__ CUtensorMap bmap, const TcArgs a) {
             if (!ok) break;
         }
     } else if (warp == kMmaWarp) {
-        // ---------------- MMA issuer ----------------
-        if (lane == 0) {
-            int g = 0, it = 0;
-            for (int item = blockIdx.x; item < n_items && !*abort; item += gridDim.x, ++it) {
-                const Item x = get_item(a, item);
-                const uint32_t idesc = idesc_f16(128, (x.n + 15) & ~15);
-                const int b = it & 1;
-                if (!mbar_wait(&acce[b], ((it >> 1) & 1) ^ 1, abort)) break;
-                TC_TRACE(6, it);
+        // ---------------- MMA issuer (whole warp loops, one elected lane issues) ----------------
+        int g = 0, it = 0;
+        for (int item = blockIdx.x; item < n_items; item += gridDim.x, ++it) {
+            const Item x = get_item(a, item);
+            const uint32_t idesc = idesc_f16(128, (x.n + 15) & ~15);
+            const int b = it & 1;
+            if (!mbar_wait_warp(&acce[b], ((it >> 1) & 1) ^ 1, abort)) break;
+            if (lane == 0) TC_TRACE(6, it);
+            tc_fence_after();
+            const uint32_t d = tmem + b * kAccStride;
+            bool ok = true;
+            for (int s = 0; s < nst; ++s, ++g) {
+                const int slot = g % kStages;
+                if (!mbar_wait_warp(&full[slot], (g / kStages) & 1, abort)) { ok = false; break; }
+                if (lane == 0) TC_TRACE(0, g);
                 tc_fence_after();
-                const uint32_t d = tmem + b * kAccStride;
-                bool ok = true;
-                for (int s = 0; s < nst; ++s, ++g) {
-                    const int slot = g % kStages;
-                    if (!mbar_wait(&full[slot], (g / kStages) & 1, abort)) { ok = false; break; }
-                    TC_TRACE(0, g);
-                    tc_fence_after();
-                    const uint32_t bbase = smem_u32(bst + slot * kBStageBytes);
+                const uint32_t bbase = smem_u32(bst + slot * kBStageBytes);
+                if (elect_one()) {
 #pragma unroll
                     for (int j = 0; j < 4; ++j) {
                         const uint64_t bdesc = sw128_desc(bbase + 32 * j);
@@ -300,11 +300,12 @@ expert_tc_kernel(const __grid_constant__ CUtensorMap bmap, const TcArgs a) {
                     }
                     mma_commit(&empty[slot]);
                 }
-                if (!ok) break;
-                mma_commit(&accf[b]);
+                __syncwarp();
             }
+            if (!ok) break;
+            if (elect_one()) mma_commit(&accf[b]);
+            __syncwarp();
         }
-        __syncwarp();
     } else if (warp == kTmaBWarp) {
         // ---------------- B operand loads ----------------
         if (lane == 0) {

@@ -5,7 +5,7 @@
 //
 // One CTA per (128-expert tile, <=256-token tile, K split): warp 0 lane 0 streams the four
 // operand tiles (Wh, Wl: 128 x 32; xh, xl: 256 x 32 f32, 128-byte swizzle) with TMA into a
-// 2-stage ring, warp 1 lane 0 issues tcgen05.mma kind::tf32 (M=128, N=tokens, K=8) into one
+// 2-stage ring, warp 1 (one elected lane) issues tcgen05.mma kind::tf32 (M=128, N=tokens, K=8) into one
 // TMEM accumulator, warps 2-5 write the f32 partial logits partial[split][token][expert]; the
 // top-k kernel sums the splits in a fixed order.  Identical router rows go through identical
 // operations, so they still produce identical logits.
@@ -86,28 +86,30 @@ router_tc_kernel(const __grid_constant__ CUtensorMap wh_map, const __grid_consta
         }
         __syncwarp();
     } else if (warp == 1) {
-        if (lane == 0) {
-            const uint32_t idesc = idesc_tf32(128, N);
-            bool ok = true;
-            for (int s = 0; s < nst; ++s) {
-                const int slot = s % kRStages;
-                if (!mbar_wait(&full[slot], (s / kRStages) & 1, abort)) { ok = false; break; }
-                tc_fence_after();
-                const uint32_t base = smem_u32(smem + slot * kRStage);
+        // whole warp loops; one elected lane issues (keeps the MMA operands warp-uniform)
+        const uint32_t idesc = idesc_tf32(128, N);
+        bool ok = true;
+        for (int s = 0; s < nst; ++s) {
+            const int slot = s % kRStages;
+            if (!mbar_wait_warp(&full[slot], (s / kRStages) & 1, abort)) { ok = false; break; }
+            tc_fence_after();
+            const uint32_t base = smem_u32(smem + slot * kRStage);
+            if (elect_one()) {
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
                     const uint64_t wh = sw128_desc(base + 32 * j);
                     const uint64_t wl = sw128_desc(base + kWTile + 32 * j);
                     const uint64_t xh = sw128_desc(base + 2 * kWTile + 32 * j);
                     const uint64_t xl = sw128_desc(base + 2 * kWTile + kXTile + 32 * j);
-                    mma_ss(tmem, wh, xh, idesc, (s | j) != 0);
-                    mma_ss(tmem, wh, xl, idesc, 1);
-                    mma_ss(tmem, wl, xh, idesc, 1);
+                    mma_tf32(tmem, wh, xh, idesc, (s | j) != 0);
+                    mma_tf32(tmem, wh, xl, idesc, 1);
+                    mma_tf32(tmem, wl, xh, idesc, 1);
                 }
                 mma_commit(&empty[slot]);
             }
-            if (ok) mma_commit(accf);
+            __syncwarp();
         }
+        if (ok && elect_one()) mma_commit(accf);
         __syncwarp();
     } else {
         const int q = warp & 3;
