@@ -83,12 +83,19 @@ constexpr int kStagesPerChunk = 8;                 // 512 K / 64 K
 constexpr int kBStageBytes = kNMax * 128;
 constexpr int kAStageBytes = 128 * 128;            // smem-A variant
 
-// MMA stages (64 K each) in flight: 8 with A in TMEM (TMEM columns 256..511), 4 with A in
-// shared memory; the raw A ring holds two 512-K chunks (16 stages of look-ahead).
+// MMA stages (64 K each) in flight and depth of the raw A ring (512-K chunks).  With A in TMEM
+// (TMEM columns 256..) the default is 4 stages and a 4-chunk raw ring: the raw weight stream
+// needs ~130 KB in flight per SM to cover HBM latency; with A in shared memory, 4 and 2.
+#ifndef MOE_TC_STAGES
+#define MOE_TC_STAGES 4
+#endif
+#ifndef MOE_TC_RAW
+#define MOE_TC_RAW 4
+#endif
 template <bool A_TMEM>
 struct Layout {
-    static constexpr int kStages = A_TMEM ? 8 : 4;
-    static constexpr int kRaw = 2;
+    static constexpr int kStages = A_TMEM ? MOE_TC_STAGES : 4;
+    static constexpr int kRaw = A_TMEM ? MOE_TC_RAW : 2;
     static constexpr size_t kB = 0;
     static constexpr size_t kA = kB + static_cast<size_t>(kStages) * kBStageBytes;
     static constexpr size_t kR = kA + (A_TMEM ? 0 : static_cast<size_t>(kStages) * kAStageBytes);
