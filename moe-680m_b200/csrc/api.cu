@@ -225,7 +225,7 @@ void run_set_io(Ctx* c, const float* x, const float* resid, float* out) {
     stage(c, "set_io", 1);
 }
 
-int ensure_tmap(Ctx* c, CUtensorMap* m, const void** base, uint64_t* rows, uint64_t* cols,
+int ensure_tmap(Ctx* c, moe::BMaps* m, const void** base, uint64_t* rows, uint64_t* cols,
                 const void* p, uint64_t r, uint64_t cl);
 
 // Routing of M tokens (activations from ws.io) into ws.topk: tensor-core router (3xTF32) for
@@ -262,10 +262,10 @@ int choose_path(const Ctx* c, const Layer& L, uint32_t M) {
     return (M <= 8 || !L.wmaps) ? moe::kPathGemv : moe::kPathTcTmemA;
 }
 
-int ensure_tmap(Ctx* c, CUtensorMap* m, const void** base, uint64_t* rows, uint64_t* cols,
+int ensure_tmap(Ctx* c, moe::BMaps* m, const void** base, uint64_t* rows, uint64_t* cols,
                 const void* p, uint64_t r, uint64_t cl) {
     if (*base == p && *rows == r && *cols == cl) return MOE_OK;
-    if (!moe::make_fp16_tmap(m, p, r, cl))
+    if (!moe::make_fp16_tmaps(m, p, r, cl))
         return fail(c, MOE_E_CUDA, "cuTensorMapEncodeTiled failed (rows %llu, cols %llu)",
                     static_cast<unsigned long long>(r), static_cast<unsigned long long>(cl));
     *base = p; *rows = r; *cols = cl;

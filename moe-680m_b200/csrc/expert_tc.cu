@@ -11,14 +11,13 @@
 // One persistent CTA per SM (480 threads, warp-specialised), looping over work items
 // (token tile of one bucket x 128-row feature tile):
 //   warp 10     TMA: raw IQ4_XS bytes of the item's 128 weight rows, 512 K (two 136-byte
-//               blocks per row) per load, into a 2- or 3-deep shared-memory ring;
+//               blocks per row) per load, into a 4-deep shared-memory ring;
 //   producer warps (8 or 16) dequantise from that ring (kvalues_iq4nl lookup by byte
 //               permutes, fp16 scale per 32-weight sub-block) and store the fp16 A operand, 64 K
 //               per stage, into TMEM (tcgen05.st) or 128-byte-swizzled shared memory; the warps
 //               of one 32-row quarter take turns by stage;
 //   warp 9      TMA: B operand (fp16 activations of the tile's slots, pre-scaled per slot by a
-//               power of two, K permuted as below), 16-row boxes, 8-deep (A in TMEM) or
-//               4-deep (A in shared memory) ring;
+//               power of two, K permuted as below), one 16/32/64/128-row box per stage;
 //   warp 8      allocates TMEM; one elected lane issues tcgen05.mma (M=128, N=16..kNMax, K=16) and
 //               tcgen05.commit;
 //   warps 11-14 epilogue: TMEM -> registers, undo the activation scale, store f32
@@ -73,11 +72,21 @@ struct Roles {
     static constexpr int kParts = PW / 4;          // producer warps per 32-row quarter
 };
 constexpr int kTmemCols = 512;
-constexpr int kBoxRows = 16;        // B TMA box: 16 rows x 64 fp16
 constexpr int kNMax = 128;          // tokens per tile
 constexpr int kAccStride = 128;     // TMEM columns per accumulator buffer
 constexpr int kACol0 = 256;         // TMEM column of A stage 0 (32 columns per stage)
 constexpr int kRawRowBytes = 2 * kBlockBytes;      // 512 K of one weight row
+#ifndef MOE_TC_RAW_TMAP
+#define MOE_TC_RAW_TMAP 1   // 0: raw chunks with per-row bulk copies instead of tensor-map boxes
+#endif
+#ifndef MOE_TC_RAW_BOX
+#define MOE_TC_RAW_BOX 128
+#endif
+constexpr int kRawBoxRows = MOE_TC_RAW_BOX;        // rows per raw tensor-map box
+#ifndef MOE_TC_RAW_ELEM
+#define MOE_TC_RAW_ELEM 8
+#endif
+constexpr int kRawElem = MOE_TC_RAW_ELEM;          // bytes per element of the raw tensor map
 constexpr int kRawBytes = 128 * kRawRowBytes;      // one raw A chunk (34,816 bytes)
 constexpr int kStagesPerChunk = 8;                 // 512 K / 64 K
 constexpr int kBStageBytes = kNMax * 128;
@@ -104,6 +113,8 @@ struct Layout {
 };
 
 struct TcArgs {
+    ExpertTables tabs;         // per-expert weight pointers (W1, W3, W2)
+    int row_bytes;             // IQ4_XS bytes per row of the item's matrix
     const CUtensorMap* wmaps;  // [3][E+1] raw IQ4_XS maps: W1, W3, W2
     int n_buckets;             // E + 1
     int mat0;                  // matrix of feature tile 0 (0 = W1, 2 = W2)
@@ -161,12 +172,16 @@ __device__ __forceinline__ Item get_item(const TcArgs& a, int item) {
 
 template <bool A_TMEM, int PW>
 __global__ void __launch_bounds__(Roles<PW>::kThreads, 1)
-expert_tc_kernel(const __grid_constant__ CUtensorMap bmap, const TcArgs a) {
+expert_tc_kernel(const __grid_constant__ BMaps bmap, const TcArgs a) {
     using R = Roles<PW>;
     constexpr int kProdWarps = R::kProd, kMmaWarp = R::kMma, kTmaBWarp = R::kTmaB, kTmaAWarp = R::kTmaA;
     using Lay = Layout<A_TMEM>;
     constexpr int kRaw = Lay::kRaw;
     constexpr int kStages = Lay::kStages;
+    // A producer warp waits on the slot of its own previous stage; with fewer slots than warps
+    // per row quarter it would wait on a slot another warp has not filled yet and the barrier
+    // parity would alias.
+    static_assert(kStages >= R::kParts, "MMA ring must have at least one slot per producer warp of a quarter");
     extern __shared__ uint8_t smem_raw[];
     // 128-byte-swizzled operand tiles need 1024-byte aligned shared-memory addresses
     uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
@@ -205,7 +220,7 @@ expert_tc_kernel(const __grid_constant__ CUtensorMap bmap, const TcArgs a) {
         fence_mbar_init();
     }
     if (warp == kMmaWarp) tmem_alloc(tmem_base_p, kTmemCols);
-    if (warp == kTmaBWarp && lane == 0) tma_prefetch_desc(&bmap);
+    if (warp == kTmaBWarp && lane < 4) tma_prefetch_desc(&bmap.m[lane]);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -226,6 +241,7 @@ expert_tc_kernel(const __grid_constant__ CUtensorMap bmap, const TcArgs a) {
             for (int kc = 0; kc < nchunk && ok; ++kc, ++rc) {
                 const int rs = rc % kRaw;
                 if (!mbar_wait(&rfull[rs], (rc / kRaw) & 1, abort)) { ok = false; break; }
+                if (warp == 0 && lane == 0) TC_TRACE(5, 512 + rc);
                 const uint8_t* raw = rst + rs * kRawBytes + row * kRawRowBytes;
                 for (int sc = 0; sc < kStagesPerChunk; ++sc, ++g) {
                     if (g % kParts != part) continue;
@@ -250,6 +266,7 @@ expert_tc_kernel(const __grid_constant__ CUtensorMap bmap, const TcArgs a) {
 #pragma unroll
                     for (int i = 0; i < 8; ++i) word_f16(qw[i], i < 4 ? s0 : s1, v + 4 * i);
 #endif
+                    if (warp == 0 && lane == 0) TC_TRACE(7, g);
                     if (!mbar_wait(&empty[slot], ((g / kStages) & 1) ^ 1, abort)) { ok = false; break; }
                     if (warp == 0 && lane == 0) TC_TRACE(1, g);
 #if defined(MOE_TC_DIAG) && MOE_TC_DIAG == 1
@@ -319,16 +336,17 @@ expert_tc_kernel(const __grid_constant__ CUtensorMap bmap, const TcArgs a) {
             int g = 0;
             for (int item = blockIdx.x; item < n_items && !*abort; item += gridDim.x) {
                 const Item x = get_item(a, item);
-                const int nbox = (x.n + kBoxRows - 1) / kBoxRows;
+                // one box per stage: 16, 32, 64 or 128 rows, the smallest covering the tile
+                const int bsel = x.n <= 16 ? 0 : x.n <= 32 ? 1 : x.n <= 64 ? 2 : 3;
+                const CUtensorMap* bm = &bmap.m[bsel];
+                const uint32_t bbytes = (16u << bsel) * 128u;
                 bool ok = true;
                 for (int s = 0; s < nst; ++s, ++g) {
                     const int slot = g % kStages;
                     if (!mbar_wait(&empty[slot], ((g / kStages) & 1) ^ 1, abort)) { ok = false; break; }
                     TC_TRACE(2, g);
-                    mbar_arrive_expect_tx(&full[slot], nbox * kBoxRows * 128);
-                    for (int i = 0; i < nbox; ++i)
-                        tma_load_2d(bst + slot * kBStageBytes + i * kBoxRows * 128, &bmap, s * 64,
-                                    x.p0 + i * kBoxRows, &full[slot]);
+                    mbar_arrive_expect_tx(&full[slot], bbytes);
+                    tma_load_2d(bst + slot * kBStageBytes, bm, s * 64, x.p0, &full[slot]);
                 }
                 if (!ok) break;
             }
@@ -336,6 +354,7 @@ expert_tc_kernel(const __grid_constant__ CUtensorMap bmap, const TcArgs a) {
         __syncwarp();
     } else if (warp == kTmaAWarp) {
         // ---------------- raw A loads ----------------
+#if MOE_TC_RAW_TMAP
         if (lane == 0) {
             int rc = 0;
             for (int item = blockIdx.x; item < n_items && !*abort; item += gridDim.x) {
@@ -349,11 +368,42 @@ expert_tc_kernel(const __grid_constant__ CUtensorMap bmap, const TcArgs a) {
                     if (!mbar_wait(&rempty[rs], ((rc / kRaw) & 1) ^ 1, abort)) { ok = false; break; }
                     TC_TRACE(3, rc);
                     mbar_arrive_expect_tx(&rfull[rs], kRawBytes);
-                    tma_load_2d(rst + rs * kRawBytes, wm, kc * (kRawRowBytes / 2), row0, &rfull[rs]);
+                    for (int r = 0; r < 128; r += kRawBoxRows)
+                        tma_load_2d(rst + rs * kRawBytes + r * kRawRowBytes, wm, kc * (kRawRowBytes / kRawElem),
+                                    row0 + r, &rfull[rs]);
                 }
                 if (!ok) break;
             }
         }
+#else
+        // One 272-byte bulk copy per weight row (rows are contiguous and 16-byte aligned); the
+        // 32 lanes issue the chunk's 128 copies, which the copy engine serves in parallel.
+        int rc = 0;
+        for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
+            const Item x = get_item(a, item);
+            const int mat = a.mat0 + x.rt / a.rt_per_mat;
+            const int row0 = (x.rt % a.rt_per_mat) * 128;
+            const uint8_t* w = (mat == 0 ? a.tabs.w1 : mat == 1 ? a.tabs.w3 : a.tabs.w2)[x.bucket] +
+                               static_cast<size_t>(row0) * a.row_bytes;
+            bool ok = true;
+            for (int kc = 0; kc < nchunk; ++kc, ++rc) {
+                const int rs = rc % kRaw;
+                if (!mbar_wait_warp(&rempty[rs], ((rc / kRaw) & 1) ^ 1, abort)) { ok = false; break; }
+                if (lane == 0) {
+                    TC_TRACE(3, rc);
+                    mbar_arrive_expect_tx(&rfull[rs], kRawBytes);
+                }
+                __syncwarp();
+                uint8_t* dst = rst + rs * kRawBytes;
+                const uint8_t* src = w + kc * kRawRowBytes;
+#pragma unroll
+                for (int r = lane; r < 128; r += 32)
+                    bulk_load(dst + r * kRawRowBytes, src + static_cast<size_t>(r) * a.row_bytes,
+                              kRawRowBytes, &rfull[rs]);
+            }
+            if (!ok) break;
+        }
+#endif
         __syncwarp();
     } else {
         // ---------------- epilogue ----------------
@@ -495,7 +545,7 @@ convert_h_kernel(const float* __restrict__ gu, int n_rows, int I, __half* __rest
 }
 
 template <bool A_TMEM, int PW>
-void launch_tc_pw(const CUtensorMap& bmap, const TcArgs& args, int n_cta, cudaStream_t s) {
+void launch_tc_pw(const BMaps& bmap, const TcArgs& args, int n_cta, cudaStream_t s) {
     const size_t smem = Layout<A_TMEM>::kTotal;
     cudaFuncSetAttribute(expert_tc_kernel<A_TMEM, PW>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          static_cast<int>(smem));
@@ -511,7 +561,7 @@ int producer_warps() {
 }
 
 template <bool A_TMEM>
-void launch_tc(const CUtensorMap& bmap, const TcArgs& args, int n_cta, cudaStream_t s) {
+void launch_tc(const BMaps& bmap, const TcArgs& args, int n_cta, cudaStream_t s) {
     if (producer_warps() == 8) launch_tc_pw<A_TMEM, 8>(bmap, args, n_cta, s);
     else launch_tc_pw<A_TMEM, 16>(bmap, args, n_cta, s);
 }
@@ -537,10 +587,11 @@ void launch_convert_h(const float* gu, int n_rows, int inter, __half* dst, int* 
     convert_h_kernel<<<(n_rows * 32 + 255) / 256, 256, 0, s>>>(gu, n_rows, inter, dst, sexp);
 }
 
-void launch_tc13(const Layer& L, const CUtensorMap& xmap, const Workspace& ws, int max_items,
+void launch_tc13(const Layer& L, const BMaps& xmap, const Workspace& ws, int max_items,
                  int sm_count, bool a_tmem, cudaStream_t s) {
     const int I = static_cast<int>(L.spec.inter);
-    TcArgs a{L.wmaps, static_cast<int>(L.spec.n_experts) + 1, 0, I / 128, 2 * I / 128,
+    TcArgs a{L.tables(), static_cast<int>(L.spec.hidden / kQK) * kBlockBytes, L.wmaps,
+             static_cast<int>(L.spec.n_experts) + 1, 0, I / 128, 2 * I / 128,
              ws.tiles13, ws.counters, 1, static_cast<int>(L.spec.hidden), ws.xexp, ws.h, 2 * I,
              ws.status};
     const int grid = max_items < sm_count ? (max_items > 0 ? max_items : 1) : sm_count;
@@ -548,10 +599,11 @@ void launch_tc13(const Layer& L, const CUtensorMap& xmap, const Workspace& ws, i
     else launch_tc<false>(xmap, a, grid, s);
 }
 
-void launch_tc2(const Layer& L, const CUtensorMap& hmap, const Workspace& ws, int max_items,
+void launch_tc2(const Layer& L, const BMaps& hmap, const Workspace& ws, int max_items,
                 int sm_count, bool a_tmem, cudaStream_t s) {
     const int H = static_cast<int>(L.spec.hidden);
-    TcArgs a{L.wmaps, static_cast<int>(L.spec.n_experts) + 1, 2, H / 128, H / 128, ws.tiles2,
+    TcArgs a{L.tables(), static_cast<int>(L.spec.inter / kQK) * kBlockBytes, L.wmaps,
+             static_cast<int>(L.spec.n_experts) + 1, 2, H / 128, H / 128, ws.tiles2,
              ws.counters, 2, static_cast<int>(L.spec.inter), ws.hexp, ws.ypart, H, ws.status};
     const int grid = max_items < sm_count ? (max_items > 0 ? max_items : 1) : sm_count;
     if (a_tmem) launch_tc<true>(hmap, a, grid, s);
@@ -570,17 +622,22 @@ static PFN_cuTensorMapEncodeTiled_v12000 tmap_encoder() {
     return encode;
 }
 
-// 2D tensor map over an fp16 [rows][cols] row-major matrix, box 16 rows x 64 cols, 128B swizzle.
-bool make_fp16_tmap(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols) {
+// 2D tensor maps over an fp16 [rows][cols] row-major matrix, boxes of 16/32/64/128 rows x 64
+// cols, 128B swizzle.
+bool make_fp16_tmaps(BMaps* m, const void* base, uint64_t rows, uint64_t cols) {
     auto encode = tmap_encoder();
     if (!encode) return false;
-    const cuuint64_t dims[2] = {cols, rows};
-    const cuuint64_t strides[1] = {cols * 2};
-    const cuuint32_t box[2] = {64, kBoxRows};
-    const cuuint32_t estr[2] = {1, 1};
-    return encode(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box,
-                  estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                  CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+    for (int i = 0; i < 4; ++i) {
+        const cuuint64_t dims[2] = {cols, rows};
+        const cuuint64_t strides[1] = {cols * 2};
+        const cuuint32_t box[2] = {64, 16u << i};
+        const cuuint32_t estr[2] = {1, 1};
+        if (encode(&m->m[i], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides,
+                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return false;
+    }
+    return true;
 }
 
 // 2D tensor map over an f32 [rows][cols] row-major matrix, box box_rows x 32 cols, 128B swizzle.
@@ -596,16 +653,20 @@ bool make_f32_tmap(CUtensorMap* m, const void* base, uint64_t rows, uint64_t col
                   CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-// 2D tensor map over the raw bytes of an IQ4_XS matrix [rows][row_bytes], viewed as 16-bit
-// elements, box 128 rows x 272 bytes (two blocks = 512 weights of K), no swizzle.
+// 2D tensor map over the raw bytes of an IQ4_XS matrix [rows][row_bytes], viewed as 8-byte
+// elements (the 16-bit view measured several times slower per box), box 128 rows x 272 bytes
+// (two blocks = 512 weights of K), no swizzle.
 bool make_iq4_tmap(CUtensorMap* m, const void* base, uint64_t rows, uint64_t row_bytes) {
     auto encode = tmap_encoder();
     if (!encode || row_bytes % 16 != 0) return false;
-    const cuuint64_t dims[2] = {row_bytes / 2, rows};
+    const cuuint64_t dims[2] = {row_bytes / kRawElem, rows};
     const cuuint64_t strides[1] = {row_bytes};
-    const cuuint32_t box[2] = {kRawRowBytes / 2, 128};
+    const cuuint32_t box[2] = {kRawRowBytes / kRawElem, kRawBoxRows};
     const cuuint32_t estr[2] = {1, 1};
-    return encode(m, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void*>(base), dims, strides, box,
+    const CUtensorMapDataType dt = kRawElem == 8 ? CU_TENSOR_MAP_DATA_TYPE_UINT64
+                                 : kRawElem == 4 ? CU_TENSOR_MAP_DATA_TYPE_UINT32
+                                                 : CU_TENSOR_MAP_DATA_TYPE_UINT16;
+    return encode(m, dt, 2, const_cast<void*>(base), dims, strides, box,
                   estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }

@@ -58,6 +58,13 @@ struct IoArgs {
     float* out;          // [M][H]
 };
 
+// fp16 activation tensor maps with 16-, 32-, 64- and 128-row boxes (64 columns, 128B swizzle):
+// the tensor-core kernels load a token tile's B stage with one box of the smallest height that
+// covers it (one large box streams ~2.4x faster per SM than the same bytes in 16-row boxes).
+struct BMaps {
+    CUtensorMap m[4];
+};
+
 // Token tile of one bucket for the tensor-core kernels: slots [p0, p0+n) of the sorted order.
 struct TcTile {
     int bucket;
@@ -104,7 +111,7 @@ struct Workspace {
     uint64_t xh_rows = 0, xh_cols = 0;
     int* hexp = nullptr;          // [S]
     // tensor maps (re-encoded when the buffers or the slot count change)
-    CUtensorMap xmap, hmap;
+    BMaps xmap, hmap;
     const void* xmap_base = nullptr;
     const void* hmap_base = nullptr;
     uint64_t xmap_rows = 0, hmap_rows = 0, xmap_cols = 0, hmap_cols = 0;
@@ -183,11 +190,11 @@ void launch_split_x(const IoArgs* io, size_t n, float* hi, float* lo, cudaStream
 int router_tc_split(int M, int E, int H);
 void launch_router_tc(const Layer& L, const CUtensorMap& xh, const CUtensorMap& xl, int M,
                       float* partial, int* status, cudaStream_t s);
-void launch_tc13(const Layer& L, const CUtensorMap& xmap, const Workspace& ws, int max_items,
+void launch_tc13(const Layer& L, const BMaps& xmap, const Workspace& ws, int max_items,
                  int sm_count, bool a_tmem, cudaStream_t s);
-void launch_tc2(const Layer& L, const CUtensorMap& hmap, const Workspace& ws, int max_items,
+void launch_tc2(const Layer& L, const BMaps& hmap, const Workspace& ws, int max_items,
                 int sm_count, bool a_tmem, cudaStream_t s);
-bool make_fp16_tmap(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols);
+bool make_fp16_tmaps(BMaps* m, const void* base, uint64_t rows, uint64_t cols);
 void launch_combine(const Layer& L, const Workspace& ws, const IoArgs* io, int M,
                     cudaStream_t s);
 void launch_rms_norm(const float* x, float* y, int M, int H, float eps, cudaStream_t s);

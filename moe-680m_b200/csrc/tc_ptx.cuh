@@ -107,6 +107,15 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* m, int
         : "memory");
 }
 
+// 1D bulk copy global -> shared (16-byte aligned, size a multiple of 16), completion counted on
+// `bar` (complete_tx bytes).
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+        ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
 __device__ __forceinline__ void fence_proxy_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
