@@ -125,6 +125,21 @@ int moe_bucket(moe_ctx* ctx, uint32_t n_experts, uint32_t top_k, int has_shared,
                uint64_t topk_off, uint32_t M, uint64_t ranges_off, uint64_t tokens_off,
                uint64_t weights_off, uint64_t slot_pos_off);
 
+/* Allocation-free variant of moe_bucket, with no counterpart in the reference: for callers that
+ * cannot allocate device memory (an engine that sized one arena up front, or code where
+ * cudaMalloc is not allowed), since moe_bucket's context grows its workspace with cudaMalloc.
+ * Same inputs and outputs as moe_bucket, given as device pointers on the current device, and
+ * launched on `stream` (a cudaStream_t, NULL = legacy default stream).  Its scratch is a fixed
+ * file-scope device array of about 190 KB that every GPU loading the library keeps until exit;
+ * M is limited to 8192 tokens (larger M returns MOE_E_UNSUPPORTED), E to 256, top_k to 8.
+ * The first call on a device looks up the array's device address; make that first call before
+ * any stream capture.  All calls on a device share the array: calls that may run concurrently on
+ * the GPU race and must be ordered by the caller.  Asynchronous; failures are reported only by
+ * the return code. */
+int moe_bucket_static(uint32_t n_experts, uint32_t top_k, int has_shared, const void* topk,
+                      uint32_t M, int32_t* ranges, int32_t* tokens, float* weights,
+                      int32_t* slot_pos, void* stream);
+
 /* ---- the MoE layer (record_and_submit_moe, src/inference.rs:663-766) --------------------- */
 
 /* out = resid + scale * (sum_j w_j * E_j(x) + gate * S(x)), E_j(x) = W2 (silu(W1 x) * W3 x),

@@ -30,6 +30,7 @@ EXPORTS = (
     "moe_last_error", "moe_layer_create", "moe_reserve", "moe_route", "moe_do_route",
     "moe_bucket", "moe_forward", "moe_forward_routed", "moe_rms_norm", "moe_dequant_iq4xs",
     "moe_synth_iq4xs", "moe_profile", "moe_profile_read", "moe_launch_count", "moe_set_path",
+    "moe_bucket_static",
 )
 
 PATH_AUTO, PATH_GEMV, PATH_TC_SMEM_A, PATH_TC_TMEM_A = 0, 1, 2, 3
@@ -98,6 +99,7 @@ def lib():
         "moe_profile_read": (i32, [vp, P(StageStatC), i32, P(i32)]),
         "moe_launch_count": (i32, [vp, P(u64)]),
         "moe_set_path": (i32, [vp, i32]),
+        "moe_bucket_static": (i32, [u32, u32, i32, vp, u32, vp, vp, vp, vp, vp]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
