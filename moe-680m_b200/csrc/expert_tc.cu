@@ -76,8 +76,14 @@ constexpr int kNMax = 128;          // tokens per tile
 constexpr int kAccStride = 128;     // TMEM columns per accumulator buffer
 constexpr int kACol0 = 256;         // TMEM column of A stage 0 (32 columns per stage)
 constexpr int kRawRowBytes = 2 * kBlockBytes;      // 512 K of one weight row
+#ifndef MOE_TC_RAW_LDG
+#define MOE_TC_RAW_LDG 0    // 1: raw weights by the producers' own global loads
+#endif
 #ifndef MOE_TC_RAW_TMAP
 #define MOE_TC_RAW_TMAP 1   // 0: raw chunks with per-row bulk copies instead of tensor-map boxes
+#endif
+#ifndef MOE_TC_L2_AHEAD
+#define MOE_TC_L2_AHEAD 6   // raw chunks prefetched into L2 ahead of their tensor-map load
 #endif
 #ifndef MOE_TC_RAW_BOX
 #define MOE_TC_RAW_BOX 128
@@ -235,6 +241,89 @@ expert_tc_kernel(const __grid_constant__ BMaps bmap, const TcArgs a) {
         const int q = warp & 3;
         const int part = warp >> 2;
         const int row = q * 32 + lane;
+        // dequantise one 64-K stage (header + 32 qs bytes of this thread's row), wait for the
+        // slot, store the fp16 A operand, signal the MMA warp
+        auto produce = [&](int g, uint2 hdr, const uint32_t (&qw)[8], int ib0) -> bool {
+            const int slot = g % kStages;
+            uint32_t v[32];
+            const __half2 s0 = subscale_h2(hdr.x, hdr.y, ib0);
+            const __half2 s1 = subscale_h2(hdr.x, hdr.y, ib0 + 1);
+#if defined(MOE_TC_DIAG) && MOE_TC_DIAG == 2
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] = qw[i & 7] ^ hdr.x;  // diagnostic: no dequant
+#else
+#pragma unroll
+            for (int i = 0; i < 8; ++i) word_f16(qw[i], i < 4 ? s0 : s1, v + 4 * i);
+#endif
+            if (warp == 0 && lane == 0) TC_TRACE(7, g);
+            if (!mbar_wait(&empty[slot], ((g / kStages) & 1) ^ 1, abort)) return false;
+            if (warp == 0 && lane == 0) TC_TRACE(1, g);
+#if defined(MOE_TC_DIAG) && MOE_TC_DIAG == 1
+            if (v[0] == 0x12345678u && v[31] == 0x9abcdef0u) g_tc_trace[1][7][0] = v[5];  // keep work
+            if constexpr (false) {
+#else
+            if constexpr (A_TMEM) {
+#endif
+                tmem_st32(tmem + (static_cast<uint32_t>(q * 32) << 16) + kACol0 + slot * 32, v);
+                tmem_wait_st();
+                tc_fence_before();
+            } else if constexpr (!A_TMEM) {
+                uint8_t* rowp = ast + slot * kAStageBytes + row * 128;
+#pragma unroll
+                for (int c = 0; c < 8; ++c)
+                    *reinterpret_cast<uint4*>(rowp + ((c ^ (row & 7)) << 4)) =
+                        make_uint4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
+                fence_proxy_async_smem();
+            }
+            mbar_arrive(&full[slot]);
+            return true;
+        };
+#if MOE_TC_RAW_LDG
+        // Raw weights straight from global memory into registers (streaming 8-byte loads),
+        // kPre own stages ahead: the load/store path keeps far more bytes in flight per SM than
+        // the tensor-memory-access engine did for these short row segments.
+        struct RawRegs { uint2 hdr; uint32_t qw[8]; };
+        const int my_items = (n_items - static_cast<int>(blockIdx.x) + static_cast<int>(gridDim.x) - 1) /
+                             static_cast<int>(gridDim.x);
+        const int total_st = my_items > 0 ? my_items * nst : 0;
+        int cached_it = -1;
+        const uint8_t* cached_row = nullptr;  // this thread's weight row of item cached_it
+        auto load = [&](int g, RawRegs& r) {
+            if (g >= total_st) return;
+            const int it = g / nst, st = g - it * nst;
+            if (it != cached_it) {  // loads run in increasing g: one cached item suffices
+                const Item x = get_item(a, static_cast<int>(blockIdx.x) + it * static_cast<int>(gridDim.x));
+                const int mat = a.mat0 + x.rt / a.rt_per_mat;
+                const uint8_t* w = (mat == 0 ? a.tabs.w1 : mat == 1 ? a.tabs.w3 : a.tabs.w2)[x.bucket];
+                cached_row = w + static_cast<size_t>((x.rt % a.rt_per_mat) * 128 + row) * a.row_bytes;
+                cached_it = it;
+            }
+            const uint8_t* blk = cached_row + (st >> 2) * kBlockBytes;
+            r.hdr = ldg_stream_u2(blk);
+            const uint8_t* qp = blk + 8 + (st & 3) * 32;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const uint2 v = ldg_stream_u2(qp + 8 * i);
+                r.qw[2 * i] = v.x;
+                r.qw[2 * i + 1] = v.y;
+            }
+        };
+        // a register ring of kPre+1 stages, rotated by value (no dynamic register indexing)
+        RawRegs r0, r1, r2, r3, r4;
+        load(part, r0);
+        load(part + kParts, r1);
+        load(part + 2 * kParts, r2);
+        load(part + 3 * kParts, r3);
+        for (int g = part; g < total_st; g += kParts) {
+            load(g + 4 * kParts, r4);
+            const int st = g % nst;
+            if (!produce(g, r0.hdr, r0.qw, (st & 3) * 2)) break;
+            r0 = r1;
+            r1 = r2;
+            r2 = r3;
+            r3 = r4;
+        }
+#else
         int g = 0, rc = 0;
         for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
             bool ok = true;
@@ -245,7 +334,6 @@ expert_tc_kernel(const __grid_constant__ BMaps bmap, const TcArgs a) {
                 const uint8_t* raw = rst + rs * kRawBytes + row * kRawRowBytes;
                 for (int sc = 0; sc < kStagesPerChunk; ++sc, ++g) {
                     if (g % kParts != part) continue;
-                    const int slot = g % kStages;
                     const uint8_t* blk = raw + (sc >> 2) * kBlockBytes;
                     const int ib0 = (sc & 3) * 2;
                     const uint2 hdr = lds64(blk);
@@ -256,42 +344,13 @@ expert_tc_kernel(const __grid_constant__ BMaps bmap, const TcArgs a) {
                         qw[i] = qq.x;
                         qw[i + 1] = qq.y;
                     }
-                    uint32_t v[32];
-                    const __half2 s0 = subscale_h2(hdr.x, hdr.y, ib0);
-                    const __half2 s1 = subscale_h2(hdr.x, hdr.y, ib0 + 1);
-#if defined(MOE_TC_DIAG) && MOE_TC_DIAG == 2
-#pragma unroll
-                    for (int i = 0; i < 32; ++i) v[i] = qw[i & 7] ^ hdr.x;  // diagnostic: no dequant
-#else
-#pragma unroll
-                    for (int i = 0; i < 8; ++i) word_f16(qw[i], i < 4 ? s0 : s1, v + 4 * i);
-#endif
-                    if (warp == 0 && lane == 0) TC_TRACE(7, g);
-                    if (!mbar_wait(&empty[slot], ((g / kStages) & 1) ^ 1, abort)) { ok = false; break; }
-                    if (warp == 0 && lane == 0) TC_TRACE(1, g);
-#if defined(MOE_TC_DIAG) && MOE_TC_DIAG == 1
-                    if (v[0] == 0x12345678u && v[31] == 0x9abcdef0u) g_tc_trace[1][7][0] = v[5];  // keep work
-                    if constexpr (false) {
-#else
-                    if constexpr (A_TMEM) {
-#endif
-                        tmem_st32(tmem + (static_cast<uint32_t>(q * 32) << 16) + kACol0 + slot * 32, v);
-                        tmem_wait_st();
-                        tc_fence_before();
-                    } else if constexpr (!A_TMEM) {
-                        uint8_t* rowp = ast + slot * kAStageBytes + row * 128;
-#pragma unroll
-                        for (int c = 0; c < 8; ++c)
-                            *reinterpret_cast<uint4*>(rowp + ((c ^ (row & 7)) << 4)) =
-                                make_uint4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
-                        fence_proxy_async_smem();
-                    }
-                    mbar_arrive(&full[slot]);
+                    if (!produce(g, hdr, qw, ib0)) { ok = false; break; }
                 }
                 if (ok) mbar_arrive(&rempty[rs]);
             }
             if (!ok) break;
         }
+#endif
     } else if (warp == kMmaWarp) {
         // ---------------- MMA issuer (whole warp loops, one elected lane issues) ----------------
         int g = 0, it = 0;
@@ -345,34 +404,59 @@ expert_tc_kernel(const __grid_constant__ BMaps bmap, const TcArgs a) {
                     const int slot = g % kStages;
                     if (!mbar_wait(&empty[slot], ((g / kStages) & 1) ^ 1, abort)) { ok = false; break; }
                     TC_TRACE(2, g);
+#if defined(MOE_TC_DIAG) && MOE_TC_DIAG == 4
+                    (void)bm; (void)bbytes;
+                    mbar_arrive(&full[slot]);  // diagnostic: no B traffic (results wrong)
+#else
                     mbar_arrive_expect_tx(&full[slot], bbytes);
                     tma_load_2d(bst + slot * kBStageBytes, bm, s * 64, x.p0, &full[slot]);
+#endif
                 }
                 if (!ok) break;
             }
         }
         __syncwarp();
     } else if (warp == kTmaAWarp) {
-        // ---------------- raw A loads ----------------
-#if MOE_TC_RAW_TMAP
+        // ---------------- raw A loads (tensor-map variant only) ----------------
+#if MOE_TC_RAW_LDG
+#elif MOE_TC_RAW_TMAP
+        // The tensor-memory-access engine keeps only ~35 KB in flight per SM, which covers L2
+        // latency but not HBM latency; tiles are therefore prefetched into L2 MOE_TC_L2_AHEAD
+        // chunks before their load.
         if (lane == 0) {
-            int rc = 0;
-            for (int item = blockIdx.x; item < n_items && !*abort; item += gridDim.x) {
-                const Item x = get_item(a, item);
+            const int my_items = (n_items - static_cast<int>(blockIdx.x) + static_cast<int>(gridDim.x) - 1) /
+                                 static_cast<int>(gridDim.x);
+            const int total_rc = my_items > 0 ? my_items * nchunk : 0;
+            auto chunk_src = [&](int c, const CUtensorMap*& wm, int& row0, int& kc) {
+                const int it = c / nchunk;
+                kc = c - it * nchunk;
+                const Item x = get_item(a, static_cast<int>(blockIdx.x) + it * static_cast<int>(gridDim.x));
                 const int mat = a.mat0 + x.rt / a.rt_per_mat;
-                const int row0 = (x.rt % a.rt_per_mat) * 128;
-                const CUtensorMap* wm = a.wmaps + mat * a.n_buckets + x.bucket;
-                bool ok = true;
-                for (int kc = 0; kc < nchunk; ++kc, ++rc) {
-                    const int rs = rc % kRaw;
-                    if (!mbar_wait(&rempty[rs], ((rc / kRaw) & 1) ^ 1, abort)) { ok = false; break; }
-                    TC_TRACE(3, rc);
-                    mbar_arrive_expect_tx(&rfull[rs], kRawBytes);
+                row0 = (x.rt % a.rt_per_mat) * 128;
+                wm = a.wmaps + mat * a.n_buckets + x.bucket;
+            };
+            for (int c = 0; c < MOE_TC_L2_AHEAD && c < total_rc; ++c) {
+                const CUtensorMap* wm; int row0, kc;
+                chunk_src(c, wm, row0, kc);
+                for (int r = 0; r < 128; r += kRawBoxRows)
+                    tma_prefetch_l2_2d(wm, kc * (kRawRowBytes / kRawElem), row0 + r);
+            }
+            for (int rc = 0; rc < total_rc && !*abort; ++rc) {
+                const int rs = rc % kRaw;
+                if (!mbar_wait(&rempty[rs], ((rc / kRaw) & 1) ^ 1, abort)) break;
+                TC_TRACE(3, rc);
+                if (rc + MOE_TC_L2_AHEAD < total_rc) {
+                    const CUtensorMap* wp; int prow, pkc;
+                    chunk_src(rc + MOE_TC_L2_AHEAD, wp, prow, pkc);
                     for (int r = 0; r < 128; r += kRawBoxRows)
-                        tma_load_2d(rst + rs * kRawBytes + r * kRawRowBytes, wm, kc * (kRawRowBytes / kRawElem),
-                                    row0 + r, &rfull[rs]);
+                        tma_prefetch_l2_2d(wp, pkc * (kRawRowBytes / kRawElem), prow + r);
                 }
-                if (!ok) break;
+                const CUtensorMap* wm; int row0, kc;
+                chunk_src(rc, wm, row0, kc);
+                mbar_arrive_expect_tx(&rfull[rs], kRawBytes);
+                for (int r = 0; r < 128; r += kRawBoxRows)
+                    tma_load_2d(rst + rs * kRawBytes + r * kRawRowBytes, wm, kc * (kRawRowBytes / kRawElem),
+                                row0 + r, &rfull[rs]);
             }
         }
 #else

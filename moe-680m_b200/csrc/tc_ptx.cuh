@@ -107,6 +107,12 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* m, int
         : "memory");
 }
 
+// Prefetch a 2D tile into L2 (no shared-memory destination, no completion tracking).
+__device__ __forceinline__ void tma_prefetch_l2_2d(const CUtensorMap* m, int c0, int c1) {
+    asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global [%0, {%1, %2}];"
+                 ::"l"(reinterpret_cast<uint64_t>(m)), "r"(c0), "r"(c1) : "memory");
+}
+
 // 1D bulk copy global -> shared (16-byte aligned, size a multiple of 16), completion counted on
 // `bar` (complete_tx bytes).
 __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
