@@ -325,6 +325,13 @@ void destroy_graph(moe::GraphEntry& g) {
 
 int record_forward(Ctx* c, const Layer& L, uint32_t M, const float* x, const float* resid, float* out) {
     run_set_io(c, x, resid, out);
+    if (M == 1 && (c->path == moe::kPathAuto || c->path == moe::kPathGemv) && moe::decode_supported(L)) {
+        // single token: the whole layer in one fused launch; its self-resetting grid-sync words
+        // live after the status word (zeroed at context creation)
+        moe::launch_decode(L, c->ws, c->ws.status + 16, c->sm_count, c->stream);
+        stage(c, "decode", 1);
+        return check_launch(c, "decode");
+    }
     int rc = run_route(c, L, M);
     if (rc) return rc;
     return run_experts(c, L, M);

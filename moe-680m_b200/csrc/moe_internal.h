@@ -195,6 +195,8 @@ void launch_tc13(const Layer& L, const BMaps& xmap, const Workspace& ws, int max
 void launch_tc2(const Layer& L, const BMaps& hmap, const Workspace& ws, int max_items,
                 int sm_count, bool a_tmem, cudaStream_t s);
 bool make_fp16_tmaps(BMaps* m, const void* base, uint64_t rows, uint64_t cols);
+bool decode_supported(const Layer& L);
+void launch_decode(const Layer& L, const Workspace& ws, int* sync, int sm_count, cudaStream_t s);
 void launch_combine(const Layer& L, const Workspace& ws, const IoArgs* io, int M,
                     cudaStream_t s);
 void launch_rms_norm(const float* x, float* y, int M, int H, float eps, cudaStream_t s);

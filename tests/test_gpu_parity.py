@@ -246,3 +246,21 @@ def test_graph_replay_new_pointers(ctx):
     for x, out in zip(xs, outs):
         ref = coracle.moe_forward(hl, x, x, acc64=True)
         check_close(out, ref["out64"], "graph replay")
+
+
+@pytest.mark.parametrize("name", ["a", "b", "compat"])
+def test_decode_single_token_small(ctx, name):
+    """M = 1 runs the fused single-launch decode kernel; small shapes, with and without gate."""
+    from pathlib import Path
+    z = np.load(Path(__file__).resolve().parent / "golden" / f"moe_small_{name}.npz")
+    H, I, E, k = (int(z[n]) for n in ("H", "I", "E", "k"))
+    zipf = None if np.isnan(z["zipf"]) else float(z["zipf"])
+    gate = bool(z["gate"])
+    flags = host.MOE_F_SHARED | (host.MOE_F_SHARED_GATE if gate else 0)
+    sh = synth.LayerShapes(H, I, E, k, I)
+    lid, hl = model(ctx, int(z["seed"]), sh, zipf, flags, float(z["scale"]))
+    for t in range(2):  # two calls in a row exercise the self-resetting grid synchronisation
+        x = np.ascontiguousarray(z["x"][t:t + 1])
+        out, _ = run_forward(ctx, lid, x, x)
+        ref = coracle.moe_forward(hl, x, x, acc64=True)
+        check_close(out, ref["out64"], f"decode {name} t={t}")
