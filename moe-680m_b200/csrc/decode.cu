@@ -3,7 +3,7 @@
 // moe-680m's router.comp + router_topk.comp + do_route + the 18 w1_w3_fused / w2_scatter
 // dispatches of record_and_submit_moe's decode branch (src/inference.rs:734-762).
 //
-// One CTA per SM, 8 warps.  Phases:
+// One CTA per SM, 16 warps.  Phases:
 //   1. every warp computes router rows (x . Wr[e], f32; row E = the shared-expert gate g . x);
 //      the last CTA to finish (ticket counter) does softmax + top-k and publishes the routing
 //      by bumping a generation word;
@@ -21,9 +21,20 @@
 #include "tc_ptx.cuh"
 
 namespace moe {
+
+#ifdef MOE_TC_TRACE
+__device__ unsigned long long g_dec_trace[4][8];  // CTAs 0..3: phase timestamps (debug builds)
+#define DEC_TRACE(i) do { if (blockIdx.x < 4 && threadIdx.x == 0) g_dec_trace[blockIdx.x][i] = tc::globaltimer_ns(); } while (0)
+extern "C" int moe_debug_dec_trace(unsigned long long* out) {
+    return cudaMemcpyFromSymbol(out, g_dec_trace, sizeof(g_dec_trace)) == cudaSuccess ? 0 : -2;
+}
+#else
+#define DEC_TRACE(i) do {} while (0)
+#endif
+
 namespace {
 
-constexpr int kDWarps = 8;
+constexpr int kDWarps = 16;
 constexpr uint64_t kSpinLimitNs = 100000000ull;  // 100 ms
 
 struct DecodeArgs {
@@ -87,32 +98,41 @@ __global__ void __launch_bounds__(32 * kDWarps, 1) decode_kernel(const DecodeArg
     float* xs = sm;                          // padded x [H]
     float* hs = sm + padded_len(a.H);        // padded h [k+1][I] (phase 3)
     __shared__ int route_seen;
+    __shared__ int eid[kMaxTopK + 1];
+    __shared__ float wgt[kMaxTopK + 1];
+    __shared__ const uint8_t* p1[kMaxTopK + 1];
+    __shared__ const uint8_t* p3[kMaxTopK + 1];
+    __shared__ const uint8_t* p2[kMaxTopK + 1];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int gwarp = blockIdx.x * kDWarps + warp, nwarps = gridDim.x * kDWarps;
     const float* x = a.io->x;
     const int H = a.H, I = a.I, E = a.E, k = a.k;
     const int ns = k + (a.has_shared ? 1 : 0);
 
+    DEC_TRACE(0);
     if (threadIdx.x == 0) route_seen = ld_volatile(&a.sync[1]);
     for (int i = threadIdx.x * 4; i < H; i += blockDim.x * 4)
         *reinterpret_cast<float4*>(xs + padded_idx(i)) = *reinterpret_cast<const float4*>(x + i);
     __syncthreads();
 
-    // ---- phase 1: router rows -------------------------------------------------------------
+    // ---- phase 1: router rows, each split in 4 column quarters ------------------------------
     const int n_rows = E + (a.gate_w ? 1 : 0);
-    for (int r = gwarp; r < n_rows; r += nwarps) {
-        const float* w = r < E ? a.wr + static_cast<size_t>(r) * H : a.gate_w;
+    const int qlen = H / 4;
+    for (int w = gwarp; w < n_rows * 4; w += nwarps) {
+        const int r = w >> 2, part = w & 3;
+        const float* wrow = (r < E ? a.wr + static_cast<size_t>(r) * H : a.gate_w) + part * qlen;
         float acc = 0.f;
-        for (int i = lane * 4; i < H; i += 128) {
-            const float4 wv = __ldg(reinterpret_cast<const float4*>(w + i));
-            const float4 xv = *reinterpret_cast<const float4*>(xs + padded_idx(i));
+        for (int i = lane * 4; i < qlen; i += 128) {
+            const float4 wv = __ldg(reinterpret_cast<const float4*>(wrow + i));
+            const float4 xv = *reinterpret_cast<const float4*>(xs + padded_idx(part * qlen + i));
             acc = fmaf(wv.x, xv.x, acc); acc = fmaf(wv.y, xv.y, acc);
             acc = fmaf(wv.z, xv.z, acc); acc = fmaf(wv.w, xv.w, acc);
         }
         acc = warp_sum(acc);
-        if (lane == 0) a.logits[r] = acc;
+        if (lane == 0) a.logits[part * (E + 1) + r] = acc;
     }
     __syncthreads();
+    DEC_TRACE(1);
     if (threadIdx.x == 0) {
         __threadfence();
         const bool last = atomicAdd(&a.sync[0], 1) == static_cast<int>(gridDim.x) - 1;
@@ -120,7 +140,8 @@ __global__ void __launch_bounds__(32 * kDWarps, 1) decode_kernel(const DecodeArg
     }
     __syncthreads();
     if (route_seen < 0 && warp == 0) {
-        // softmax + top-k over the E logits (router_topk.comp:36-92), ties to the lower index
+        // softmax + top-k over the E logits (router_topk.comp:36-92), ties to the lower index;
+        // the four quarter sums of a logit are added in a fixed order
         __threadfence();
         float p[8];
         float mx = -INFINITY;
@@ -128,7 +149,11 @@ __global__ void __launch_bounds__(32 * kDWarps, 1) decode_kernel(const DecodeArg
         for (int i = 0; i < 8; ++i) {
             const int e = lane + 32 * i;
             float l = -INFINITY;
-            if (e < E) { l = __ldcg(a.logits + e); if (a.bias) l += a.bias[e]; }
+            if (e < E) {
+                l = ((__ldcg(a.logits + e) + __ldcg(a.logits + (E + 1) + e)) + __ldcg(a.logits + 2 * (E + 1) + e)) +
+                    __ldcg(a.logits + 3 * (E + 1) + e);
+                if (a.bias) l += a.bias[e];
+            }
             p[i] = l;
             mx = fmaxf(mx, l);
         }
@@ -159,7 +184,12 @@ __global__ void __launch_bounds__(32 * kDWarps, 1) decode_kernel(const DecodeArg
         }
         if (lane == 0) {
             float g = 1.0f;
-            if (a.gate_w) g = 1.0f / (1.0f + expf(-__ldcg(a.logits + E)));
+            if (a.gate_w) {
+                const int e = E;
+                const float z = ((__ldcg(a.logits + e) + __ldcg(a.logits + (E + 1) + e)) +
+                                 __ldcg(a.logits + 2 * (E + 1) + e)) + __ldcg(a.logits + 3 * (E + 1) + e);
+                g = 1.0f / (1.0f + expf(-z));
+            }
             a.topk[0] = make_uint2(static_cast<uint32_t>(E), __float_as_uint(g));
             a.sync[0] = 0;
             __threadfence();
@@ -168,43 +198,75 @@ __global__ void __launch_bounds__(32 * kDWarps, 1) decode_kernel(const DecodeArg
     }
     const int seen = route_seen < 0 ? -1 - route_seen : route_seen;
 
-    // ---- phase 2: gate/up units; shared expert first ----------------------------------------
-    const int nsb_h = H / 32;
+    // ---- phase 2: gate/up units ------------------------------------------------------------
+    // Per-slot weight pointers and combine weights are cached in shared memory; each warp
+    // issues the loads of its next unit before computing the current one.
     const size_t rb13 = static_cast<size_t>(H / kQK) * kBlockBytes;
-    const int n_units = ns * I;
-    const int shared_units = a.has_shared ? I : 0;
-    bool routed_known = false;
-    for (int u = gwarp; u < n_units; u += nwarps) {
-        int slot, j, e;
-        if (u < shared_units) {
-            slot = k; j = u; e = E;
-        } else {
-            const int v = u - shared_units;
-            slot = v / I; j = v - slot * I;
-            if (!routed_known) { wait_gen(&a.sync[1], seen, a.status); routed_known = true; __threadfence(); }
-            e = static_cast<int>(__ldcg(reinterpret_cast<const unsigned int*>(a.topk + 1 + slot)));
-            if (e < 0 || e >= E) { set_dev_error(a.status, kDevBadExpert); e = 0; }
-        }
-        const float g = row_dot(a.tabs.w1[e] + j * rb13, xs, nsb_h, lane);
-        const float up = row_dot(a.tabs.w3[e] + j * rb13, xs, nsb_h, lane);
-        if (lane == 0) a.h[static_cast<size_t>(slot) * I + j] = silu_f(g) * up;
+    const int nsb_h = H / 32;  // <= 64: two sub-blocks per lane at most
+    if (threadIdx.x == 0 && a.has_shared) {
+        p1[k] = a.tabs.w1[E]; p3[k] = a.tabs.w3[E]; p2[k] = a.tabs.w2[E];
     }
-    if (!routed_known) wait_gen(&a.sync[1], seen, a.status);
+    __syncthreads();
+    auto load_unit = [&](const uint8_t* r1, const uint8_t* r3, SubBlk (&b1)[2], SubBlk (&b3)[2]) {
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+            const int sb = lane + 32 * i;
+            if (sb < nsb_h) { b1[i] = load_subblk(r1, sb); b3[i] = load_subblk(r3, sb); }
+        }
+    };
+    auto finish_unit = [&](int slot, int j, const SubBlk (&b1)[2], const SubBlk (&b3)[2]) {
+        float g = 0.f, up = 0.f;
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+            const int sb = lane + 32 * i;
+            if (sb < nsb_h) {
+                g = fmaf(iq4_subscale(b1[i].hdr.x, b1[i].hdr.y, sb & 7), dot_subblk(b1[i], xs + sb * 36), g);
+                up = fmaf(iq4_subscale(b3[i].hdr.x, b3[i].hdr.y, sb & 7), dot_subblk(b3[i], xs + sb * 36), up);
+            }
+        }
+        g = warp_sum(g);
+        up = warp_sum(up);
+        if (lane == 0) a.h[static_cast<size_t>(slot) * I + j] = silu_f(g) * up;
+    };
+    // runs units u = first, first+nwarps, ... < n of slot(u) = slot0 + u / I, row u % I
+    auto run_units = [&](int n, int slot0) {
+        SubBlk c1[2], c3[2], n1[2], n3[2];
+        int u = gwarp;
+        if (u < n) { const int sl = slot0 + u / I, j = u % I; load_unit(p1[sl] + j * rb13, p3[sl] + j * rb13, c1, c3); }
+        for (; u < n; u += nwarps) {
+            const int un = u + nwarps;
+            if (un < n) { const int sl = slot0 + un / I, j = un % I; load_unit(p1[sl] + j * rb13, p3[sl] + j * rb13, n1, n3); }
+            finish_unit(slot0 + u / I, u % I, c1, c3);
+#pragma unroll
+            for (int i = 0; i < 2; ++i) { c1[i] = n1[i]; c3[i] = n3[i]; }
+        }
+    };
+    if (a.has_shared) run_units(I, k);  // the shared expert needs no routing
+    if (threadIdx.x == 0) {
+        wait_gen(&a.sync[1], seen, a.status);
+        __threadfence();
+    }
+    __syncthreads();
+    if (threadIdx.x < ns) {
+        const int s2 = threadIdx.x;  // slots 0..k-1 routed, k shared (record 0)
+        const uint2 r = __ldcg(reinterpret_cast<const uint2*>(a.topk) + (s2 < k ? 1 + s2 : 0));
+        int e = s2 < k ? static_cast<int>(r.x) : E;
+        if (e < 0 || e > E) { set_dev_error(a.status, kDevBadExpert); e = 0; }
+        eid[s2] = e;
+        wgt[s2] = __uint_as_float(r.y);
+        if (s2 < k) { p1[s2] = a.tabs.w1[e]; p3[s2] = a.tabs.w3[e]; p2[s2] = a.tabs.w2[e]; }
+    }
+    __syncthreads();
+    run_units(k * I, 0);
+    DEC_TRACE(2);
     grid_barrier(&a.sync[2], &a.sync[3], a.status);
+    DEC_TRACE(3);
 
     // ---- phase 3: down projection + weighted combine + residual ----------------------------
     for (int i = threadIdx.x * 4; i < ns * I; i += blockDim.x * 4) {
         const int s = i / I, c = i - s * I;
         *reinterpret_cast<float4*>(hs + s * padded_len(I) + padded_idx(c)) =
             __ldcg(reinterpret_cast<const float4*>(a.h + static_cast<size_t>(s) * I + c));
-    }
-    __shared__ int eid[kMaxTopK + 1];
-    __shared__ float wgt[kMaxTopK + 1];
-    if (threadIdx.x < ns) {
-        const int s = threadIdx.x;  // slots 0..k-1 routed, k shared (record 0)
-        const uint2 r = __ldcg(reinterpret_cast<const uint2*>(a.topk) + (s < k ? 1 + s : 0));
-        eid[s] = s < k ? static_cast<int>(r.x) : E;
-        wgt[s] = __uint_as_float(r.y);
     }
     __syncthreads();
     const int spr = I / 32, rpi = 32 / spr;  // sub-blocks per W2 row; rows per warp pass
@@ -214,23 +276,32 @@ __global__ void __launch_bounds__(32 * kDWarps, 1) decode_kernel(const DecodeArg
     float* out = a.io->out;
     for (int n0 = gwarp * rpi; n0 < H; n0 += nwarps * rpi) {
         const int n = n0 + r_in;
+        // the 9 experts' sub-blocks of row n are loaded together, then reduced in slot order
+        SubBlk b[kMaxTopK + 1];
+#pragma unroll
+        for (int s = 0; s < kMaxTopK + 1; ++s)
+            if (s < ns) b[s] = load_subblk(p2[s] + n * rb2, sb);
         float y = 0.f;
-        for (int s = 0; s < ns; ++s) {
-            const int e = eid[s];
-            const SubBlk b = load_subblk(a.tabs.w2[e] + n * rb2, sb);
-            const float d = iq4_subscale(b.hdr.x, b.hdr.y, sb & 7) *
-                            dot_subblk(b, hs + s * padded_len(I) + sb * 36);
-            y = fmaf(wgt[s], d, y);
+#pragma unroll
+        for (int s = 0; s < kMaxTopK + 1; ++s) {
+            if (s < ns) {
+                const float d = iq4_subscale(b[s].hdr.x, b[s].hdr.y, sb & 7) *
+                                dot_subblk(b[s], hs + s * padded_len(I) + sb * 36);
+                y = fmaf(wgt[s], d, y);
+            }
         }
         for (int o = spr >> 1; o > 0; o >>= 1) y += __shfl_xor_sync(0xffffffffu, y, o);
         if (sb == 0 && n < H) out[n] = (resid ? resid[n] : 0.f) + a.scale * y;
     }
+    __syncthreads();
+    DEC_TRACE(4);
 }
 
 }  // namespace
 
 bool decode_supported(const Layer& L) {
-    return L.spec.inter >= 256 && L.spec.inter <= 1024 && L.spec.n_experts <= kMaxExperts;
+    return L.spec.hidden <= 2048 && L.spec.inter >= 256 && L.spec.inter <= 1024 &&
+           L.spec.n_experts <= kMaxExperts;
 }
 
 void launch_decode(const Layer& L, const Workspace& ws, int* sync, int sm_count, cudaStream_t s) {
