@@ -546,6 +546,7 @@ int moe_sync(moe_ctx* c) {
     MOE_CUDA(c, cudaMemcpy(&st, c->ws.status, sizeof(int), cudaMemcpyDeviceToHost));
     if (st != 0) {
         cudaMemset(c->ws.status, 0, sizeof(int));
+        cudaMemset(c->ws.status + 16, 0, 64);  // the decode kernel's grid counter
         const char* what = st == moe::kDevBadExpert ? "expert id out of range"
                          : st == moe::kDevBadToken ? "token index out of range"
                          : st == moe::kDevOverflow ? "chunk list overflow" : "device error";
@@ -600,6 +601,9 @@ int moe_layer_create(moe_ctx* c, const moe_layer_spec* spec, const uint64_t* w1,
     Layer L;
     L.spec = s;
     L.tab = static_cast<const uint8_t**>(d);
+    L.tab_aligned16 = true;
+    for (const uint8_t* q : tab)
+        if (q && reinterpret_cast<uintptr_t>(q) % 16 != 0) L.tab_aligned16 = false;
     if (H % 32 == 0) {
         // router weight split for the tensor-core router: [Wh | Wl], each [E][H] f32
         void* wsd = nullptr;

@@ -25,6 +25,7 @@ struct ExpertTables {
 struct Layer {
     moe_layer_spec spec;
     const uint8_t** tab = nullptr;  // device [3][E+1]
+    bool tab_aligned16 = false;     // every expert weight pointer is 16-byte aligned
     const uint8_t* router_w_ptr = nullptr;
     const uint8_t* bias_ptr = nullptr;  // may be null
     const uint8_t* gate_ptr = nullptr;  // may be null
