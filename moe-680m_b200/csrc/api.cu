@@ -272,11 +272,13 @@ int ensure_tmap(Ctx* c, moe::BMaps* m, const void** base, uint64_t* rows, uint64
     return MOE_OK;
 }
 
-int run_experts(Ctx* c, const Layer& L, uint32_t M) {
+// routed: use the routed entries of the records; shared: add the shared expert's slot; scale:
+// the combine scale (the layer's, or 1 for expert-parallel partial rows).
+int run_experts(Ctx* c, const Layer& L, uint32_t M, bool routed, bool shared, float scale) {
     Workspace& ws = c->ws;
-    const int slots = L.slots();
+    const int slots = static_cast<int>(L.spec.top_k) + (shared ? 1 : 0);
     const int E = static_cast<int>(L.spec.n_experts);
-    moe::launch_bucket(E, static_cast<int>(L.spec.top_k), L.has_shared(), ws.topk,
+    moe::launch_bucket(E, static_cast<int>(L.spec.top_k), routed, shared, ws.topk,
                        static_cast<int>(M), ws, ws.ranges, ws.sorted_tok, ws.sorted_w,
                        ws.slot_pos, ws.status, c->stream);
     stage(c, "bucket", 3);
@@ -308,7 +310,7 @@ int run_experts(Ctx* c, const Layer& L, uint32_t M) {
         moe::launch_tc2(L, ws.hmap, ws, items2, c->sm_count, a_tmem, c->stream);
         stage(c, "tc2", 1);
     }
-    moe::launch_combine(L, ws, ws.io, static_cast<int>(M), c->stream);
+    moe::launch_combine(L, ws, ws.io, static_cast<int>(M), slots, scale, c->stream);
     stage(c, "combine", 1);
     return check_launch(c, "experts");
 }
@@ -334,7 +336,7 @@ int record_forward(Ctx* c, const Layer& L, uint32_t M, const float* x, const flo
     }
     int rc = run_route(c, L, M);
     if (rc) return rc;
-    return run_experts(c, L, M);
+    return run_experts(c, L, M, true, L.has_shared(), L.spec.scale);
 }
 
 // Replay (capturing on first use) the forward of (layer, M, path) with new activation pointers:
@@ -578,7 +580,9 @@ int moe_layer_create(moe_ctx* c, const moe_layer_spec* spec, const uint64_t* w1,
     }
     const uint64_t b13 = I * (H / 256) * 136, b2 = H * (I / 256) * 136;
     std::vector<const uint8_t*> tab(3 * (E + 1), nullptr);
+    const bool subset = (s.flags & MOE_F_EXPERT_SUBSET) != 0;
     for (uint64_t e = 0; e < E; ++e) {
+        if (subset && w1[e] == 0 && w3[e] == 0 && w2[e] == 0) continue;  // held by another rank
         if (!off_ok(c, w1[e], b13, 256) || !off_ok(c, w3[e], b13, 256) || !off_ok(c, w2[e], b2, 256))
             return fail(c, MOE_E_INVALID, "expert %llu: weight offset missing, misaligned or outside arena",
                         static_cast<unsigned long long>(e));
@@ -622,14 +626,21 @@ int moe_layer_create(moe_ctx* c, const moe_layer_spec* spec, const uint64_t* w1,
         std::vector<CUtensorMap> maps(3 * (E + 1));
         bool ok = true;
         const uint64_t nb = E + 1;
+        // absent entries (no shared expert, experts held by other ranks) repeat the maps of a
+        // present expert; they are never used
+        uint64_t first = E + 1;
+        for (uint64_t e = 0; e <= E && first > E; ++e)
+            if (tab[e]) first = e;
+        ok = first <= E;
         for (uint64_t e = 0; e <= E && ok; ++e) {
-            if (e == E && !(s.flags & MOE_F_SHARED)) {
-                maps[e] = maps[0]; maps[nb + e] = maps[nb]; maps[2 * nb + e] = maps[2 * nb];
-                continue;
-            }
+            if (!tab[e]) continue;
             ok = moe::make_iq4_tmap(&maps[e], tab[e], I, b13 / I) &&
                  moe::make_iq4_tmap(&maps[nb + e], tab[nb + e], I, b13 / I) &&
                  moe::make_iq4_tmap(&maps[2 * nb + e], tab[2 * nb + e], H, b2 / H);
+        }
+        for (uint64_t e = 0; e <= E && ok; ++e) {
+            if (tab[e]) continue;
+            maps[e] = maps[first]; maps[nb + e] = maps[nb + first]; maps[2 * nb + e] = maps[2 * nb + first];
         }
         if (ok) {
             void* dm = nullptr;
@@ -719,7 +730,7 @@ int moe_bucket(moe_ctx* c, uint32_t n_experts, uint32_t top_k, int has_shared, u
     DeviceGuard g(c->device);
     int rc = ensure_ws(c, M, n_experts, top_k, static_cast<uint32_t>(slots), 0, 0);
     if (rc) return rc;
-    moe::launch_bucket(static_cast<int>(n_experts), static_cast<int>(top_k), has_shared != 0,
+    moe::launch_bucket(static_cast<int>(n_experts), static_cast<int>(top_k), true, has_shared != 0,
                        at<uint2>(c, topk_off), static_cast<int>(M), c->ws, at<int>(c, ranges_off),
                        at<int>(c, tokens_off), at<float>(c, weights_off), at<int>(c, slot_pos_off),
                        c->ws.status, c->stream);
@@ -733,6 +744,8 @@ int moe_forward(moe_ctx* c, uint32_t layer_id, uint64_t x_off, uint64_t resid_of
     Layer* L;
     int rc = get_layer(c, layer_id, &L);
     if (rc) return rc;
+    if (L->subset())
+        return fail(c, MOE_E_UNSUPPORTED, "expert-subset layer: route with moe_route and run moe_forward_topk");
     if (M == 0) return MOE_OK;
     if ((rc = check_tokens(c, *L, x_off, M, "x"))) return rc;
     if (resid_off && (rc = check_tokens(c, *L, resid_off, M, "resid"))) return rc;
@@ -757,6 +770,8 @@ int moe_forward_routed(moe_ctx* c, uint32_t layer_id, uint64_t x_off, uint64_t r
     Layer* L;
     int rc = get_layer(c, layer_id, &L);
     if (rc) return rc;
+    if (L->subset())
+        return fail(c, MOE_E_UNSUPPORTED, "expert-subset layer: route with moe_route and run moe_forward_topk");
     if (M == 0) return MOE_OK;
     if ((rc = check_tokens(c, *L, x_off, M, "x"))) return rc;
     if (resid_off && (rc = check_tokens(c, *L, resid_off, M, "resid"))) return rc;
@@ -788,9 +803,110 @@ int moe_forward_routed(moe_ctx* c, uint32_t layer_id, uint64_t x_off, uint64_t r
                                 cudaMemcpyHostToDevice, c->stream));
     prof_begin(c);
     run_set_io(c, at<float>(c, x_off), resid_off ? at<float>(c, resid_off) : nullptr, at<float>(c, out_off));
-    rc = run_experts(c, *L, M);
+    rc = run_experts(c, *L, M, true, L->has_shared(), L->spec.scale);
     prof_end(c);
     return rc;
+}
+
+int moe_forward_topk(moe_ctx* c, uint32_t layer_id, uint64_t x_off, uint64_t resid_off,
+                     uint64_t out_off, uint32_t M, uint64_t topk_off, uint32_t flags) {
+    if (!c) return fail(c, MOE_E_INVALID, "NULL context");
+    Layer* L;
+    int rc = get_layer(c, layer_id, &L);
+    if (rc) return rc;
+    if (flags & ~(MOE_FT_NO_SHARED | MOE_FT_SHARED_ONLY | MOE_FT_UNSCALED))
+        return fail(c, MOE_E_INVALID, "unknown flags 0x%x", flags);
+    if ((flags & MOE_FT_NO_SHARED) && (flags & MOE_FT_SHARED_ONLY))
+        return fail(c, MOE_E_INVALID, "MOE_FT_NO_SHARED and MOE_FT_SHARED_ONLY exclude each other");
+    if ((flags & MOE_FT_SHARED_ONLY) && !L->has_shared())
+        return fail(c, MOE_E_INVALID, "MOE_FT_SHARED_ONLY on a layer without a shared expert");
+    if (M == 0) return MOE_OK;
+    if ((rc = check_tokens(c, *L, x_off, M, "x"))) return rc;
+    if (resid_off && (rc = check_tokens(c, *L, resid_off, M, "resid"))) return rc;
+    if ((rc = check_tokens(c, *L, out_off, M, "out"))) return rc;
+    const uint64_t rec = static_cast<uint64_t>(M) * (L->spec.top_k + 1) * 8;
+    if (!off_ok(c, topk_off, rec, 8)) return fail(c, MOE_E_INVALID, "topk offset invalid");
+    DeviceGuard g(c->device);
+    if ((rc = ensure_layer_ws(c, *L, M))) return rc;
+    MOE_CUDA(c, cudaMemcpyAsync(c->ws.topk, c->base + topk_off, rec, cudaMemcpyDeviceToDevice, c->stream));
+    prof_begin(c);
+    run_set_io(c, at<float>(c, x_off), resid_off ? at<float>(c, resid_off) : nullptr, at<float>(c, out_off));
+    rc = run_experts(c, *L, M, !(flags & MOE_FT_SHARED_ONLY), L->has_shared() && !(flags & MOE_FT_NO_SHARED),
+                     (flags & MOE_FT_UNSCALED) ? 1.0f : L->spec.scale);
+    prof_end(c);
+    return rc;
+}
+
+uint64_t moe_ep_plan_bytes(uint32_t M, uint32_t n_ranks) {
+    const uint64_t a = (4ull * M + 255) / 256 * 256;
+    const uint64_t b = (4ull * M * n_ranks + 255) / 256 * 256;
+    return a + b + 4ull * (n_ranks + 1);
+}
+
+static moe::EpPlan ep_plan_at(Ctx* c, uint64_t plan_off, uint32_t M, uint32_t n_ranks) {
+    const uint64_t a = (4ull * M + 255) / 256 * 256;
+    const uint64_t b = (4ull * M * n_ranks + 255) / 256 * 256;
+    return moe::EpPlan{at<uint32_t>(c, plan_off), at<int>(c, plan_off + a), at<int>(c, plan_off + a + b)};
+}
+
+int moe_ep_dispatch(moe_ctx* c, uint32_t n_experts, uint32_t top_k, uint32_t n_ranks,
+                    uint64_t topk_off, uint64_t x_off, uint32_t M, uint32_t H, uint64_t plan_off,
+                    uint64_t send_x_off, uint64_t send_topk_off, int32_t* counts) {
+    if (!c || !counts) return fail(c, MOE_E_INVALID, "NULL argument");
+    if (n_ranks == 0 || n_ranks > static_cast<uint32_t>(moe::kMaxEpRanks) || n_experts == 0 ||
+        n_experts > moe::kMaxExperts || n_experts % n_ranks != 0 || top_k == 0 || top_k > moe::kMaxTopK)
+        return fail(c, MOE_E_UNSUPPORTED, "n_ranks %u (1..%d, dividing n_experts %u), top_k %u", n_ranks,
+                    moe::kMaxEpRanks, n_experts, top_k);
+    if (H == 0 || H % 4 != 0) return fail(c, MOE_E_INVALID, "H must be a positive multiple of 4");
+    if (M == 0) {
+        for (uint32_t d = 0; d < n_ranks; ++d) counts[d] = 0;
+        return MOE_OK;
+    }
+    const uint64_t max_pairs = static_cast<uint64_t>(M) * std::min(top_k, n_ranks);
+    if (!off_ok(c, topk_off, static_cast<uint64_t>(M) * (top_k + 1) * 8, 8) ||
+        !off_ok(c, x_off, static_cast<uint64_t>(M) * H * 4, 16) ||
+        !off_ok(c, plan_off, moe_ep_plan_bytes(M, n_ranks), 256) ||
+        !off_ok(c, send_x_off, max_pairs * H * 4, 16) ||
+        !off_ok(c, send_topk_off, max_pairs * (top_k + 1) * 8, 8))
+        return fail(c, MOE_E_INVALID, "ep dispatch buffer offsets invalid (send buffers hold M*min(k, n_ranks) rows)");
+    DeviceGuard g(c->device);
+    const moe::EpPlan plan = ep_plan_at(c, plan_off, M, n_ranks);
+    const int epr = static_cast<int>(n_experts / n_ranks);
+    moe::launch_ep_plan(at<uint2>(c, topk_off), static_cast<int>(M), static_cast<int>(top_k), epr,
+                        static_cast<int>(n_ranks), plan, c->ws.status, c->stream);
+    moe::launch_ep_gather(at<float>(c, x_off), at<uint2>(c, topk_off), plan, static_cast<int>(M),
+                          static_cast<int>(H), static_cast<int>(top_k), epr, static_cast<int>(n_ranks),
+                          at<float>(c, send_x_off), at<uint2>(c, send_topk_off), c->stream);
+    stage(c, "ep_dispatch", 3);
+    int off[moe::kMaxEpRanks + 1];
+    MOE_CUDA(c, cudaMemcpyAsync(off, plan.offsets, sizeof(int) * (n_ranks + 1), cudaMemcpyDeviceToHost, c->stream));
+    int rc = moe_sync(c);
+    if (rc) return rc;
+    for (uint32_t d = 0; d < n_ranks; ++d) counts[d] = off[d + 1] - off[d];
+    return MOE_OK;
+}
+
+int moe_ep_combine(moe_ctx* c, uint32_t n_ranks, uint32_t H, uint32_t M, uint64_t plan_off,
+                   uint64_t y_back_off, uint64_t shared_off, uint64_t resid_off, uint64_t out_off,
+                   float scale) {
+    if (!c) return fail(c, MOE_E_INVALID, "NULL context");
+    if (n_ranks == 0 || n_ranks > static_cast<uint32_t>(moe::kMaxEpRanks))
+        return fail(c, MOE_E_UNSUPPORTED, "n_ranks %u outside 1..%d", n_ranks, moe::kMaxEpRanks);
+    if (H == 0 || H % 4 != 0) return fail(c, MOE_E_INVALID, "H must be a positive multiple of 4");
+    if (M == 0) return MOE_OK;
+    const uint64_t row = static_cast<uint64_t>(H) * 4, rows = static_cast<uint64_t>(M) * row;
+    if (!off_ok(c, plan_off, moe_ep_plan_bytes(M, n_ranks), 256) ||
+        (y_back_off && !off_ok(c, y_back_off, row, 16)) ||
+        (shared_off && !off_ok(c, shared_off, rows, 16)) || (resid_off && !off_ok(c, resid_off, rows, 16)) ||
+        !off_ok(c, out_off, rows, 16))
+        return fail(c, MOE_E_INVALID, "ep combine buffer offsets invalid");
+    DeviceGuard g(c->device);
+    moe::launch_ep_combine(ep_plan_at(c, plan_off, M, n_ranks), static_cast<int>(M), static_cast<int>(n_ranks),
+                           static_cast<int>(H), y_back_off ? at<float>(c, y_back_off) : nullptr,
+                           shared_off ? at<float>(c, shared_off) : nullptr,
+                           resid_off ? at<float>(c, resid_off) : nullptr, scale, at<float>(c, out_off), c->stream);
+    stage(c, "ep_combine", 1);
+    return check_launch(c, "ep_combine");
 }
 
 int moe_set_path(moe_ctx* c, int path) {

@@ -9,6 +9,8 @@
 //  3. scatter: recomputes the masks; a slot's position is its tile offset plus the popcount of
 //              the lower warps' masks and of the lower lanes of its own warp.  Positions are
 //              therefore in token order inside each bucket (the reference's stable fill).
+// A routed record whose expert id is kNoExpert (0xFFFFFFFF) is an empty slot: it gets no
+// position (slot_pos -1).  Expert-parallel ranks use it for the experts another rank owns.
 // Bucket E holds the shared expert: every token, in order (the reference instead counts the
 // shared slot into bucket shared_id = 0, which it also uses for routed expert 0).
 #include <cuda_runtime.h>
@@ -24,14 +26,15 @@ constexpr int kTile = 256;  // tokens per tile (8 warps x 32)
 constexpr int kScanThreads = 288;  // >= kMaxExperts + 1, whole warps
 
 __device__ __forceinline__ void build_masks(uint32_t* masks, int nb, const uint2* topk, int M,
-                                            int E, int k, int* status) {
+                                            int E, int k, int routed, int* status) {
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     for (int i = tid; i < 8 * nb; i += blockDim.x) masks[i] = 0u;
     __syncthreads();
     const int t = blockIdx.x * kTile + tid;
     if (t < M) {
         const uint2* rec = topk + static_cast<size_t>(t) * (k + 1);
-        for (int s = 0; s < k; ++s) {
+        for (int s = 0; s < (routed ? k : 0); ++s) {
+            if (rec[1 + s].x == kNoExpert) continue;  // empty slot
             const int e = static_cast<int>(rec[1 + s].x);
             if (e < 0 || e >= E) { set_dev_error(status, kDevBadExpert); continue; }
             atomicOr(&masks[warp * nb + e], 1u << lane);
@@ -41,11 +44,11 @@ __device__ __forceinline__ void build_masks(uint32_t* masks, int nb, const uint2
 }
 
 __global__ void __launch_bounds__(kTile)
-bucket_count_kernel(const uint2* __restrict__ topk, int M, int E, int k, int has_shared,
+bucket_count_kernel(const uint2* __restrict__ topk, int M, int E, int k, int routed, int has_shared,
                     int* __restrict__ tilecnt, int* status) {
     extern __shared__ uint32_t masks[];  // [8][E+1]
     const int nb = E + 1;
-    build_masks(masks, nb, topk, M, E, k, status);
+    build_masks(masks, nb, topk, M, E, k, routed, status);
     const int tile_tokens = min(kTile, M - static_cast<int>(blockIdx.x) * kTile);
     for (int e = threadIdx.x; e < nb; e += blockDim.x) {
         int c = 0;
@@ -145,12 +148,12 @@ bucket_scan_kernel(int* __restrict__ tilecnt, int n_tiles, int E, int* __restric
 }
 
 __global__ void __launch_bounds__(kTile)
-bucket_scatter_kernel(const uint2* __restrict__ topk, int M, int E, int k, int has_shared,
+bucket_scatter_kernel(const uint2* __restrict__ topk, int M, int E, int k, int routed, int has_shared,
                       const int* __restrict__ tileoff, int* __restrict__ sorted_tok,
                       float* __restrict__ sorted_w, int* __restrict__ slot_pos, int* status) {
     extern __shared__ uint32_t masks[];
     const int nb = E + 1;
-    build_masks(masks, nb, topk, M, E, k, status);
+    build_masks(masks, nb, topk, M, E, k, routed, status);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int t = blockIdx.x * kTile + tid;
     if (t >= M) return;
@@ -161,7 +164,7 @@ bucket_scatter_kernel(const uint2* __restrict__ topk, int M, int E, int k, int h
     int* sp = slot_pos + static_cast<size_t>(t) * ns;
     for (int s = 0; s < k; ++s) {
         const int e = static_cast<int>(rec[1 + s].x);
-        if (e < 0 || e >= E) { sp[s] = -1; continue; }
+        if (!routed || e < 0 || e >= E) { sp[s] = -1; continue; }
         int pos = off[e] + __popc(masks[warp * nb + e] & lt);
         for (int w = 0; w < warp; ++w) pos += __popc(masks[w * nb + e]);
         sorted_tok[pos] = t;
@@ -178,18 +181,18 @@ bucket_scatter_kernel(const uint2* __restrict__ topk, int M, int E, int k, int h
 
 }  // namespace
 
-void launch_bucket(int E, int k, bool has_shared, const uint2* topk, int M, Workspace& ws,
+void launch_bucket(int E, int k, bool routed, bool has_shared, const uint2* topk, int M, Workspace& ws,
                    int* ranges, int* sorted_tok, float* sorted_w, int* slot_pos, int* status,
                    cudaStream_t s) {
     const int n_tiles = (M + kTile - 1) / kTile;
     const size_t smem = 8 * (E + 1) * sizeof(uint32_t);
-    bucket_count_kernel<<<n_tiles, kTile, smem, s>>>(topk, M, E, k, has_shared ? 1 : 0,
+    bucket_count_kernel<<<n_tiles, kTile, smem, s>>>(topk, M, E, k, routed ? 1 : 0, has_shared ? 1 : 0,
                                                      ws.tilecnt, status);
     TileLists tl{ws.tiles13, static_cast<int>(ws.max_tiles13), ws.tiles2,
                  static_cast<int>(ws.max_tiles2), tc_max_n(13), tc_max_n(2)};
     bucket_scan_kernel<<<1, kScanThreads, 0, s>>>(ws.tilecnt, n_tiles, E, ranges, ws.chunks,
                                           static_cast<int>(ws.max_chunks), tl, ws.counters, status);
-    bucket_scatter_kernel<<<n_tiles, kTile, smem, s>>>(topk, M, E, k, has_shared ? 1 : 0,
+    bucket_scatter_kernel<<<n_tiles, kTile, smem, s>>>(topk, M, E, k, routed ? 1 : 0, has_shared ? 1 : 0,
                                                        ws.tilecnt, sorted_tok, sorted_w, slot_pos,
                                                        status);
 }

@@ -84,7 +84,7 @@ int moe_bucket_static(uint32_t n_experts, uint32_t top_k, int has_shared, const 
     ws.counters = reinterpret_cast<int*>(base + kCounterOff);
     ws.tiles13 = nullptr;  // no tensor-core tile lists
     ws.tiles2 = nullptr;
-    launch_bucket(static_cast<int>(n_experts), static_cast<int>(top_k), has_shared != 0,
+    launch_bucket(static_cast<int>(n_experts), static_cast<int>(top_k), true, has_shared != 0,
                   static_cast<const uint2*>(topk), static_cast<int>(M), ws, ranges, tokens, weights,
                   slot_pos, reinterpret_cast<int*>(base + kStatusOff), s);
     const cudaError_t e = cudaGetLastError();

@@ -1,0 +1,187 @@
+// Expert-parallel prefill: the device side of the dispatch and combine around an all-to-all.
+//
+// Rank d of N owns experts [d*epr, (d+1)*epr), epr = E/N.  For the M local tokens of this rank:
+//   plan:    mask[t]  = bit d set when one of token t's k routed experts lives on rank d;
+//            pos[t][d] = rank of t among the tokens with bit d (token order), offsets[d] =
+//            exclusive prefix over d of the per-rank pair counts -> the send buffer is
+//            rank-major, token order inside a rank (deterministic);
+//   gather:  send_x[off[d] + pos[t][d]] = x[t] (f32 row, exact), and the token's (k+1)-entry
+//            routing record keeping the experts of rank d (global ids) and emptying every other
+//            routed entry (kNoExpert); entry 0 (shared gate) is copied;
+//   combine: out[t] = resid[t] + scale * (sum over d in mask, ascending, of y_back[off[d] +
+//            pos[t][d]] + shared[t]), where y_back are the partial rows returned by the ranks
+//            (sum_j w_j E_j(x) over the rank's experts, unscaled) and shared[t] = gate * S(x_t)
+//            computed locally.
+// The reference runs on one device and has no counterpart; this follows the exchange steps of
+// the expert-parallel layout (router -> per-rank histogram -> count exchange -> dispatch ->
+// local grouped experts -> return of one partial row per (token, rank) -> ordered sum).
+#include <cuda_runtime.h>
+
+#include "moe_common.cuh"
+#include "moe_internal.h"
+
+namespace moe {
+
+namespace {
+
+constexpr int kScanT = 1024;
+
+__global__ void ep_mask_kernel(const uint2* __restrict__ topk, int M, int k, int epr, int n_ranks,
+                               uint32_t* __restrict__ mask, int* status) {
+    const int t = blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= M) return;
+    const uint2* rec = topk + static_cast<size_t>(t) * (k + 1);
+    uint32_t m = 0;
+    for (int s = 0; s < k; ++s) {
+        const uint32_t e = rec[1 + s].x;
+        if (e == kNoExpert) continue;
+        const uint32_t d = e / static_cast<uint32_t>(epr);
+        if (d >= static_cast<uint32_t>(n_ranks)) { set_dev_error(status, kDevBadExpert); continue; }
+        m |= 1u << d;
+    }
+    mask[t] = m;
+}
+
+// One CTA: per rank d, exclusive scan of mask bit d over the tokens (each thread a contiguous
+// run of tokens), pair counts and rank offsets.
+__global__ void __launch_bounds__(kScanT) ep_scan_kernel(const uint32_t* __restrict__ mask, int M,
+                                                         int n_ranks, int* __restrict__ pos,
+                                                         int* __restrict__ offsets) {
+    __shared__ int wsum[kScanT / 32][kMaxEpRanks];
+    __shared__ int tot[kMaxEpRanks];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int per = (M + kScanT - 1) / kScanT;
+    const int t0 = min(M, tid * per), t1 = min(M, t0 + per);
+    int cnt[kMaxEpRanks];
+#pragma unroll
+    for (int d = 0; d < kMaxEpRanks; ++d) cnt[d] = 0;
+    for (int t = t0; t < t1; ++t) {
+        const uint32_t m = mask[t];
+#pragma unroll
+        for (int d = 0; d < kMaxEpRanks; ++d) cnt[d] += (m >> d) & 1u;
+    }
+    // inclusive warp scan, then over warps
+    int inc[kMaxEpRanks];
+#pragma unroll
+    for (int d = 0; d < kMaxEpRanks; ++d) {
+        int v = cnt[d];
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int u = __shfl_up_sync(0xffffffffu, v, o);
+            if (lane >= o) v += u;
+        }
+        inc[d] = v;
+        if (lane == 31) wsum[warp][d] = v;
+    }
+    __syncthreads();
+    if (tid < kMaxEpRanks) {
+        int run = 0;
+        for (int w = 0; w < kScanT / 32; ++w) {
+            const int v = wsum[w][tid];
+            wsum[w][tid] = run;
+            run += v;
+        }
+        tot[tid] = run;
+    }
+    __syncthreads();
+    int base[kMaxEpRanks];
+#pragma unroll
+    for (int d = 0; d < kMaxEpRanks; ++d) base[d] = wsum[warp][d] + inc[d] - cnt[d];
+    for (int t = t0; t < t1; ++t) {
+        const uint32_t m = mask[t];
+#pragma unroll
+        for (int d = 0; d < kMaxEpRanks; ++d) {
+            if (d < n_ranks) {
+                pos[static_cast<size_t>(t) * n_ranks + d] = ((m >> d) & 1u) ? base[d] : -1;
+                base[d] += (m >> d) & 1u;
+            }
+        }
+    }
+    if (tid == 0) {
+        int run = 0;
+        for (int d = 0; d < n_ranks; ++d) {
+            offsets[d] = run;
+            run += tot[d];
+        }
+        offsets[n_ranks] = run;
+    }
+}
+
+// Warp per token: its row and record to every rank it visits.
+__global__ void ep_gather_kernel(const float* __restrict__ x, const uint2* __restrict__ topk,
+                                 const uint32_t* __restrict__ mask, const int* __restrict__ pos,
+                                 const int* __restrict__ offsets, int M, int H, int k, int epr,
+                                 int n_ranks, float* __restrict__ send_x, uint2* __restrict__ send_rec) {
+    const int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    if (t >= M) return;
+    const uint32_t m = mask[t];
+    if (!m) return;
+    const float4* src = reinterpret_cast<const float4*>(x + static_cast<size_t>(t) * H);
+    const uint2* rec = topk + static_cast<size_t>(t) * (k + 1);
+    const uint2 r = lane <= k ? rec[lane] : make_uint2(0, 0);
+    for (int d = 0; d < n_ranks; ++d) {
+        if (!((m >> d) & 1u)) continue;
+        const size_t p = static_cast<size_t>(offsets[d] + pos[static_cast<size_t>(t) * n_ranks + d]);
+        float4* dst = reinterpret_cast<float4*>(send_x + p * H);
+        for (int i = lane; i < H / 4; i += 32) dst[i] = src[i];
+        if (lane <= k) {
+            uint2 o = r;
+            if (lane > 0) {
+                const uint32_t e = r.x;
+                o.x = (e != kNoExpert && e / static_cast<uint32_t>(epr) == static_cast<uint32_t>(d))
+                          ? e : kNoExpert;
+            }
+            send_rec[p * (k + 1) + lane] = o;
+        }
+    }
+}
+
+__global__ void ep_combine_kernel(const uint32_t* __restrict__ mask, const int* __restrict__ pos,
+                                  const int* __restrict__ offsets, int n_ranks, int H,
+                                  const float* __restrict__ y_back, const float* __restrict__ shared,
+                                  const float* __restrict__ resid, float scale, float* __restrict__ out) {
+    const int t = blockIdx.x;
+    const int c = (blockIdx.y * blockDim.x + threadIdx.x) * 4;
+    if (c >= H) return;
+    const uint32_t m = mask[t];
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int d = 0; d < n_ranks; ++d) {
+        if (!((m >> d) & 1u)) continue;
+        const size_t p = static_cast<size_t>(offsets[d] + pos[static_cast<size_t>(t) * n_ranks + d]);
+        const float4 y = *reinterpret_cast<const float4*>(y_back + p * H + c);
+        acc.x += y.x; acc.y += y.y; acc.z += y.z; acc.w += y.w;
+    }
+    const size_t row = static_cast<size_t>(t) * H + c;
+    if (shared) {
+        const float4 y = *reinterpret_cast<const float4*>(shared + row);
+        acc.x += y.x; acc.y += y.y; acc.z += y.z; acc.w += y.w;
+    }
+    float4 r = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (resid) r = *reinterpret_cast<const float4*>(resid + row);
+    r.x = fmaf(scale, acc.x, r.x); r.y = fmaf(scale, acc.y, r.y);
+    r.z = fmaf(scale, acc.z, r.z); r.w = fmaf(scale, acc.w, r.w);
+    *reinterpret_cast<float4*>(out + row) = r;
+}
+
+}  // namespace
+
+void launch_ep_plan(const uint2* topk, int M, int k, int epr, int n_ranks, EpPlan plan, int* status,
+                    cudaStream_t s) {
+    ep_mask_kernel<<<(M + 255) / 256, 256, 0, s>>>(topk, M, k, epr, n_ranks, plan.mask, status);
+    ep_scan_kernel<<<1, kScanT, 0, s>>>(plan.mask, M, n_ranks, plan.pos, plan.offsets);
+}
+
+void launch_ep_gather(const float* x, const uint2* topk, EpPlan plan, int M, int H, int k, int epr,
+                      int n_ranks, float* send_x, uint2* send_rec, cudaStream_t s) {
+    ep_gather_kernel<<<(M * 32 + 255) / 256, 256, 0, s>>>(x, topk, plan.mask, plan.pos, plan.offsets, M,
+                                                         H, k, epr, n_ranks, send_x, send_rec);
+}
+
+void launch_ep_combine(EpPlan plan, int M, int n_ranks, int H, const float* y_back, const float* shared,
+                       const float* resid, float scale, float* out, cudaStream_t s) {
+    dim3 grid(M, (H / 4 + 255) / 256);
+    ep_combine_kernel<<<grid, 256, 0, s>>>(plan.mask, plan.pos, plan.offsets, n_ranks, H, y_back,
+                                           shared, resid, scale, out);
+}
+
+}  // namespace moe

@@ -275,11 +275,11 @@ void launch_gemv2(const Layer& L, const Workspace& ws, int M, int max_chunks, in
     }
 }
 
-void launch_combine(const Layer& L, const Workspace& ws, const IoArgs* io, int M, cudaStream_t s) {
+void launch_combine(const Layer& L, const Workspace& ws, const IoArgs* io, int M, int ns, float scale,
+                    cudaStream_t s) {
     const int H = L.spec.hidden;
     dim3 grid(M, (H / 4 + 255) / 256);
-    combine_kernel<<<grid, 256, 0, s>>>(ws.ypart, ws.slot_pos, ws.sorted_w,
-                                        L.slots(), H, L.spec.scale, io);
+    combine_kernel<<<grid, 256, 0, s>>>(ws.ypart, ws.slot_pos, ws.sorted_w, ns, H, scale, io);
 }
 
 }  // namespace moe

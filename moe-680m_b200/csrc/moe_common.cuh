@@ -20,6 +20,7 @@ constexpr int kBlockBytes = 136;  // bytes per block
 constexpr int kSubPerBlock = 8;   // 32-weight sub-blocks per block
 constexpr int kMaxTopK = 8;
 constexpr int kMaxExperts = 256;
+constexpr uint32_t kNoExpert = 0xFFFFFFFFu;  // expert id of an empty routed slot
 
 // kvalues_iq4nl + 128 as unsigned bytes, packed 4 per word (entries 0-3, 4-7, 8-11, 12-15):
 // {-127,-104,-83,-65, -49,-35,-22,-10, 1,13,25,38, 53,69,89,113} + 128

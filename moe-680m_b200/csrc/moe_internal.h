@@ -38,6 +38,7 @@ struct Layer {
         return ExpertTables{tab, tab + n, tab + 2 * n};
     }
     bool has_shared() const { return (spec.flags & MOE_F_SHARED) != 0; }
+    bool subset() const { return (spec.flags & MOE_F_EXPERT_SUBSET) != 0; }
     int slots() const { return static_cast<int>(spec.top_k) + (has_shared() ? 1 : 0); }
 };
 
@@ -171,7 +172,7 @@ const void* set_io_func();
 void launch_router_logits(const Layer& L, const IoArgs* io, int M, float* logits, cudaStream_t s);
 void launch_topk(const Layer& L, const float* logits, int n_split, bool gate_in_logits,
                  const IoArgs* io, int M, uint2* topk, int* status, cudaStream_t s);
-void launch_bucket(int E, int k, bool has_shared, const uint2* topk, int M, Workspace& ws,
+void launch_bucket(int E, int k, bool routed, bool has_shared, const uint2* topk, int M, Workspace& ws,
                    int* ranges, int* sorted_tok, float* sorted_w, int* slot_pos, int* status,
                    cudaStream_t s);
 void launch_gemv13(const Layer& L, const IoArgs* io, const Workspace& ws, int M, int max_chunks,
@@ -198,8 +199,22 @@ void launch_tc2(const Layer& L, const BMaps& hmap, const Workspace& ws, int max_
 bool make_fp16_tmaps(BMaps* m, const void* base, uint64_t rows, uint64_t cols);
 bool decode_supported(const Layer& L);
 void launch_decode(const Layer& L, const Workspace& ws, int* sync, int sm_count, cudaStream_t s);
-void launch_combine(const Layer& L, const Workspace& ws, const IoArgs* io, int M,
+void launch_combine(const Layer& L, const Workspace& ws, const IoArgs* io, int M, int ns,
+                    float scale, cudaStream_t s);
+// Expert-parallel dispatch plan (arena or workspace memory): mask[M], pos[M][n_ranks],
+// offsets[n_ranks + 1].
+constexpr int kMaxEpRanks = 8;
+struct EpPlan {
+    uint32_t* mask;
+    int* pos;
+    int* offsets;
+};
+void launch_ep_plan(const uint2* topk, int M, int k, int epr, int n_ranks, EpPlan plan, int* status,
                     cudaStream_t s);
+void launch_ep_gather(const float* x, const uint2* topk, EpPlan plan, int M, int H, int k, int epr,
+                      int n_ranks, float* send_x, uint2* send_rec, cudaStream_t s);
+void launch_ep_combine(EpPlan plan, int M, int n_ranks, int H, const float* y_back, const float* shared,
+                       const float* resid, float scale, float* out, cudaStream_t s);
 void launch_rms_norm(const float* x, float* y, int M, int H, float eps, cudaStream_t s);
 void launch_dequant(const uint8_t* src, uint64_t n_blocks, float* dst, cudaStream_t s);
 void launch_synth(uint8_t* dst, uint64_t key, uint64_t block_start, uint64_t n_blocks,

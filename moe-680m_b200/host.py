@@ -22,6 +22,9 @@ LIB_PATH = PKG / "lib" / "libmoe_b200.so"
 MOE_OK = 0
 MOE_F_SHARED = 1
 MOE_F_SHARED_GATE = 2
+MOE_F_EXPERT_SUBSET = 4
+MOE_NO_EXPERT = 0xFFFFFFFF
+MOE_FT_NO_SHARED, MOE_FT_SHARED_ONLY, MOE_FT_UNSCALED = 1, 2, 4
 
 # Every symbol include/moe_b200.h declares.
 EXPORTS = (
@@ -30,7 +33,8 @@ EXPORTS = (
     "moe_last_error", "moe_layer_create", "moe_reserve", "moe_route", "moe_do_route",
     "moe_bucket", "moe_forward", "moe_forward_routed", "moe_rms_norm", "moe_dequant_iq4xs",
     "moe_synth_iq4xs", "moe_profile", "moe_profile_read", "moe_launch_count", "moe_set_path",
-    "moe_bucket_static",
+    "moe_bucket_static", "moe_forward_topk", "moe_ep_plan_bytes", "moe_ep_dispatch",
+    "moe_ep_combine",
 )
 
 PATH_AUTO, PATH_GEMV, PATH_TC_SMEM_A, PATH_TC_TMEM_A = 0, 1, 2, 3
@@ -100,6 +104,10 @@ def lib():
         "moe_launch_count": (i32, [vp, P(u64)]),
         "moe_set_path": (i32, [vp, i32]),
         "moe_bucket_static": (i32, [u32, u32, i32, vp, u32, vp, vp, vp, vp, vp]),
+        "moe_forward_topk": (i32, [vp, u32, u64, u64, u64, u32, u64, u32]),
+        "moe_ep_plan_bytes": (u64, [u32, u32]),
+        "moe_ep_dispatch": (i32, [vp, u32, u32, u32, u64, u64, u32, u32, u64, u64, u64, P(C.c_int32)]),
+        "moe_ep_combine": (i32, [vp, u32, u32, u32, u64, u64, u64, u64, u64, f32]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -243,6 +251,20 @@ class Context:
         self._check(lib().moe_forward_routed(self.h, layer, x_off, resid_off, out_off, m,
                                              _ptr(r, C.c_uint16), _ptr(w, C.c_float), gp))
 
+    def forward_topk(self, layer, x_off, resid_off, out_off, m, topk_off, flags=0):
+        self._check(lib().moe_forward_topk(self.h, layer, x_off, resid_off, out_off, m, topk_off, flags))
+
+    def ep_dispatch(self, n_experts, top_k, n_ranks, topk_off, x_off, m, hidden, plan_off,
+                    send_x_off, send_topk_off) -> list[int]:
+        counts = np.zeros(n_ranks, np.int32)
+        self._check(lib().moe_ep_dispatch(self.h, n_experts, top_k, n_ranks, topk_off, x_off, m, hidden,
+                                          plan_off, send_x_off, send_topk_off, _ptr(counts, C.c_int32)))
+        return [int(v) for v in counts]
+
+    def ep_combine(self, n_ranks, hidden, m, plan_off, y_back_off, shared_off, resid_off, out_off, scale):
+        self._check(lib().moe_ep_combine(self.h, n_ranks, hidden, m, plan_off, y_back_off, shared_off,
+                                         resid_off, out_off, scale))
+
     def rms_norm(self, x_off, y_off, m, hidden, eps=1e-6):
         self._check(lib().moe_rms_norm(self.h, x_off, y_off, m, hidden, eps))
 
@@ -353,9 +375,13 @@ class LayerWeights:
 
 def build_synthetic_model(ctx: Context, seed: int, n_layers: int = 1,
                           shapes: synth.LayerShapes | None = None, zipf_s: float | None = None,
-                          flags: int = MOE_F_SHARED | MOE_F_SHARED_GATE, scale: float = 1.0):
+                          flags: int = MOE_F_SHARED | MOE_F_SHARED_GATE, scale: float = 1.0,
+                          experts: range | None = None):
     """Place a seeded synthetic model in the arena (weights generated on the device), register
     every tensor by its GGUF-style name and create one library layer per model layer.
+
+    ``experts``: the routed experts this context holds (an expert-parallel rank); the others
+    get no weights and the layers are created with MOE_F_EXPERT_SUBSET.
 
     Returns (registry, LayerWeights, [layer ids])."""
     sh = shapes or synth.LayerShapes()
@@ -381,11 +407,13 @@ def build_synthetic_model(ctx: Context, seed: int, n_layers: int = 1,
             synth_matrix(f"blk.{l}.shared_expert.w1.weight", l, E, synth.W1, I, H)
             synth_matrix(f"blk.{l}.shared_expert.w3.weight", l, E, synth.W3, I, H)
             synth_matrix(f"blk.{l}.shared_expert.w2.weight", l, E, synth.W2, H, I)
-        for e in range(E):
+        for e in (range(E) if experts is None else experts):
             synth_matrix(f"blk.{l}.experts.{e}.w1.weight", l, e, synth.W1, I, H)
             synth_matrix(f"blk.{l}.experts.{e}.w3.weight", l, e, synth.W3, I, H)
             synth_matrix(f"blk.{l}.experts.{e}.w2.weight", l, e, synth.W2, H, I)
     lw = LayerWeights.from_registry(reg, n_layers, E)
+    if experts is not None:
+        flags |= MOE_F_EXPERT_SUBSET
     ids = []
     for l in range(n_layers):
         spec = LayerSpec(H, I, E, sh.top_k, flags, scale, lw.ffn_gate[l], lw.router_bias[l],

@@ -1,0 +1,226 @@
+"""GPU tests of the expert-parallel building blocks (all through the C ABI) and of the
+expert-parallel layer over NCCL.
+
+* moe_forward_topk: flags 0 equals moe_forward bit for bit on the same routing; the partial
+  (routed only, unscaled) plus the shared-only part, scaled, plus the residual equals it to f32
+  rounding; empty routed entries (MOE_NO_EXPERT) are skipped (checked against the oracle).
+* moe_ep_dispatch: plan, send rows and records equal a NumPy restatement exactly.
+* one-rank expert-parallel layer (an NCCL group of 1): equals moe_forward to f32 rounding and
+  the f64 oracle to the layer tolerance.
+* two ranks on two GPUs (skipped with fewer GPUs): each rank's output equals the single-GPU
+  layer on the same tokens to f32 rounding.
+"""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+
+import coracle
+import conftest  # noqa: F401  (registers the package for spawned ranks too)
+import moe_oracle as O
+from moe680m_b200 import ep, host, synth
+
+pytestmark = pytest.mark.gpu
+
+FULL = synth.LayerShapes(2048, 512, 256, 8, 512)
+SEED = 777
+
+
+@pytest.fixture(scope="module")
+def full():
+    ctx = host.Context(0, 2 << 30)
+    _, _, ids = host.build_synthetic_model(ctx, SEED, 1, FULL, 1.1)
+    yield ctx, ids[0]
+    ctx.close()
+
+
+def _route(ctx, lid, x):
+    m = x.shape[0]
+    xo = ctx.put(x)
+    topk = ctx.alloc(m * 9 * 8)
+    ctx.route(lid, xo, m, topk)
+    return xo, topk
+
+
+@pytest.mark.parametrize("m", [37, 300])
+def test_forward_topk_matches_forward(full, m):
+    ctx, lid = full
+    x = synth.tokens(SEED, m, m, FULL.hidden)
+    xo, topk = _route(ctx, lid, x)
+    ref_o, a_o, p_o, s_o = (ctx.alloc(x.nbytes) for _ in range(4))
+    ctx.forward(lid, xo, xo, ref_o, m)
+    ctx.forward_topk(lid, xo, xo, a_o, m, topk, 0)
+    ctx.forward_topk(lid, xo, 0, p_o, m, topk, host.MOE_FT_NO_SHARED | host.MOE_FT_UNSCALED)
+    ctx.forward_topk(lid, xo, 0, s_o, m, topk, host.MOE_FT_SHARED_ONLY | host.MOE_FT_UNSCALED)
+    ctx.sync()
+    ref = ctx.download(ref_o, (m, FULL.hidden))
+    assert np.array_equal(ctx.download(a_o, (m, FULL.hidden)).view(np.uint32), ref.view(np.uint32))
+    parts = ctx.download(p_o, (m, FULL.hidden)).astype(np.float64) + ctx.download(s_o, (m, FULL.hidden))
+    assert O.rel_l2(x.astype(np.float64) + parts, ref) < 1e-6
+
+
+def test_forward_topk_empty_slots(full):
+    ctx, lid = full
+    m = 50
+    x = synth.tokens(SEED, 5, m, FULL.hidden)
+    xo, topk = _route(ctx, lid, x)
+    rec = ctx.download(topk, (m, 9, 2), np.uint32)
+    rng = np.random.default_rng(1)
+    drop = rng.random((m, 8)) < 0.5
+    rec[:, 1:, 0] = np.where(drop, host.MOE_NO_EXPERT, rec[:, 1:, 0])
+    ctx.upload(topk, rec)
+    out = ctx.alloc(x.nbytes)
+    ctx.forward_topk(lid, xo, 0, out, m, topk, host.MOE_FT_NO_SHARED)
+    ctx.sync()
+    got = ctx.download(out, (m, FULL.hidden))
+    hl = coracle.synthetic_layer(SEED, 0, FULL, 1.1)
+    ref = np.zeros((m, FULL.hidden))
+    x64 = x.astype(np.float64)
+    for t in range(m):
+        for s in range(8):
+            e = int(rec[t, 1 + s, 0])
+            if e == host.MOE_NO_EXPERT:
+                continue
+            w = float(rec[t, 1 + s, 1:2].view(np.float32)[0])
+            ws = [O.dequant_matrix(raw, r, c) for raw, r, c in
+                  zip(hl.experts[e], (512, 512, 2048), (2048, 2048, 512))]
+            ref[t] += w * O.expert_ffn(x64[t:t + 1], *ws)[0]
+    assert O.rel_l2(got, ref) <= 1e-3
+
+
+def _plan_ref(rec, n_ranks, epr):
+    m = rec.shape[0]
+    pairs = [[t for t in range(m) if np.any(rec[t, 1:, 0] // epr == d)] for d in range(n_ranks)]
+    return pairs
+
+
+@pytest.mark.parametrize("n_ranks", [1, 2, 4, 8])
+def test_ep_dispatch_exact(full, n_ranks):
+    ctx, lid = full
+    m, H, k, E = 300, FULL.hidden, 8, 256
+    x = synth.tokens(SEED, 9, m, H)
+    xo, topk = _route(ctx, lid, x)
+    rec = ctx.download(topk, (m, k + 1, 2), np.uint32)
+    plan = ctx.alloc(int(host.lib().moe_ep_plan_bytes(m, n_ranks)))
+    mp_ = m * min(k, n_ranks)
+    sx, sr = ctx.alloc(mp_ * H * 4), ctx.alloc(mp_ * (k + 1) * 8)
+    counts = ctx.ep_dispatch(E, k, n_ranks, topk, xo, m, H, plan, sx, sr)
+    epr = E // n_ranks
+    pairs = _plan_ref(rec, n_ranks, epr)
+    assert counts == [len(p) for p in pairs]
+    n = sum(counts)
+    got_x = ctx.download(sx, (n, H))
+    got_r = ctx.download(sr, (n, k + 1, 2), np.uint32)
+    p = 0
+    for d in range(n_ranks):
+        for t in pairs[d]:
+            assert np.array_equal(got_x[p], x[t])
+            r = rec[t].copy()
+            r[1:, 0] = np.where(r[1:, 0] // epr == d, r[1:, 0], host.MOE_NO_EXPERT)
+            assert np.array_equal(got_r[p], r)
+            p += 1
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _ep_rank_forward(rank, world, tokens_per_rank, seed):
+    """Builds this rank's expert subset and runs one expert-parallel forward of its tokens."""
+    import torch.distributed as dist
+    dev = torch.device("cuda", rank)
+    torch.cuda.set_device(dev)
+    E, H = FULL.n_experts, FULL.hidden
+    epr = E // world
+    m_max = max(tokens_per_rank)
+    arena_bytes = 1 << 30
+    arena = torch.empty(arena_bytes, dtype=torch.uint8, device=dev)
+    ctx = host.Context(rank, arena_bytes, external_ptr=arena.data_ptr())
+    _, _, ids = host.build_synthetic_model(ctx, seed, 1, FULL, 1.1, experts=range(rank * epr, (rank + 1) * epr))
+    m = tokens_per_rank[rank]
+    x_all = synth.tokens(seed, 1, sum(tokens_per_rank), H)
+    start = sum(tokens_per_rank[:rank])
+    x = x_all[start:start + m]
+    xo = ctx.put(x if m else np.zeros((1, H), np.float32))
+    out = ctx.alloc(max(m, 1) * H * 4)
+    ops = ep.LibraryEpOps(ctx, arena, ids[0], ep.EpShape(H, E, FULL.top_k, world, m_max), xo, xo, out)
+    ep.exchange_forward(ops, None, m, 1.0)
+    torch.cuda.synchronize(dev)
+    ctx.sync()
+    got = ctx.download(out, (m, H)) if m else np.zeros((0, H), np.float32)
+    ctx.close()
+    del arena
+    dist.barrier()
+    return x, got
+
+
+def _ep_worker(rank, world, port, tokens_per_rank, q):
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank))
+    try:
+        x, got = _ep_rank_forward(rank, world, tokens_per_rank, SEED)
+        q.put((rank, x, got))
+    except Exception as e:  # reported to the parent
+        q.put((rank, None, repr(e)))
+    finally:
+        dist.destroy_process_group()
+
+
+def _run_ranks(world, tokens_per_rank):
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_ep_worker, args=(r, world, port, tokens_per_rank, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = {}
+    try:
+        for _ in range(world):
+            r, x, got = q.get(timeout=300)
+            assert x is not None, f"rank {r}: {got}"
+            res[r] = (x, got)
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.kill()
+    return res
+
+
+def _single_gpu_reference(x):
+    ctx = host.Context(0, 2 << 30)
+    try:
+        _, _, ids = host.build_synthetic_model(ctx, SEED, 1, FULL, 1.1)
+        xo = ctx.put(x)
+        out = ctx.alloc(x.nbytes)
+        ctx.forward(ids[0], xo, xo, out, x.shape[0])
+        ctx.sync()
+        return ctx.download(out, x.shape)
+    finally:
+        ctx.close()
+
+
+def test_ep_one_rank_matches_forward():
+    res = _run_ranks(1, [260])
+    x, got = res[0]
+    ref = _single_gpu_reference(x)
+    assert O.rel_l2(got, ref) < 1e-6
+    hl = coracle.synthetic_layer(SEED, 0, FULL, 1.1)
+    oref = coracle.moe_forward(hl, x, x)["out64"]
+    assert O.rel_l2(got, oref) <= 1e-3
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_ep_two_ranks_match_single_gpu():
+    res = _run_ranks(2, [300, 212])
+    x = np.concatenate([res[0][0], res[1][0]])
+    got = np.concatenate([res[0][1], res[1][1]])
+    ref = _single_gpu_reference(x)
+    assert O.rel_l2(got, ref) < 1e-6
