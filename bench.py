@@ -10,7 +10,10 @@ line carries the decode (M=1, config 0) figures under "decode".
 
 --impl reference times the reference's algorithm on the host cores (the C restatement in
 oracle/, f32 accumulation, all threads), on a bounded sample of the same workload.
-With N > 1 (torchrun), every rank runs an independent replica of the workload (weak scaling).
+With N > 1 (torchrun), the prefill is expert parallel: rank r holds experts [r*256/N, (r+1)*256/N)
+and 512 tokens of its own; tokens travel to the ranks owning their experts and partial rows come
+back through NCCL all-to-all (weak scaling, 512 tokens per GPU).  "config3" times 8192 tokens in
+total over the N GPUs (strong scaling).  Decode runs on every GPU independently.
 """
 from __future__ import annotations
 
@@ -34,6 +37,7 @@ SEED = 20240601
 PREFILL_M = 512
 ZIPF = 1.1
 CPU_SAMPLE_TOKENS = 512
+CONFIG3_M = 8192
 
 
 def load_pkg():
@@ -157,6 +161,22 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def _max_over_ranks(v: float, world: int) -> float:
+    if world == 1:
+        return v
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([v], device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def _barrier(world: int):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -165,7 +185,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--only", default="all", choices=["all", "prefill"],
-                    help="prefill: skip the decode, end-to-end and CPU legs (profiling runs)")
+                    help="prefill: skip the decode, config-3, end-to-end and CPU legs (profiling runs)")
     ap.add_argument("--path", type=int, default=0,
                     help="expert kernels: 0 auto, 1 CUDA-core GEMV, 2 tcgen05 (A in smem), 3 tcgen05 (A in TMEM)")
     args = ap.parse_args()
@@ -180,33 +200,54 @@ def main():
     torch.cuda.set_device(local)
     if world > 1:
         dist.init_process_group("nccl", device_id=torch.device("cuda", local))
-    pkg = load_pkg()
-    from moe680m_b200 import host, synth
+    load_pkg()
+    from moe680m_b200 import ep, host, synth
 
     sh = synth.LayerShapes()
+    E, H = sh.n_experts, sh.hidden
+    ep_mode = world > 1
+    epr = E // world
+    my_experts = range(rank * epr, (rank + 1) * epr) if ep_mode else None
     only_prefill = args.only == "prefill"
     n_dec_layers = 0 if only_prefill else 16  # decode cycles through 16 layers (6.9 GB): no L2 hits
-    arena = (n_dec_layers + 1) * sh.expert_bytes * (sh.n_experts + 1) + (256 << 20)
-    ctx = host.Context(local, arena)
-    stream = torch.cuda.Stream()  # a real stream: torch events and the library share it
+    c3_tokens = CONFIG3_M // world
+    arena_bytes = ((n_dec_layers + 1) * sh.expert_bytes * (E + 1)
+                   + (0 if only_prefill else 2 * sh.expert_bytes * (E + 1))
+                   + (3 << 30))
+    arena = torch.empty(arena_bytes, dtype=torch.uint8, device=torch.device("cuda", local))
+    ctx = host.Context(local, arena_bytes, external_ptr=arena.data_ptr())
+    stream = torch.cuda.Stream()  # a real stream: torch events, NCCL and the library share it
     torch.cuda.set_stream(stream)
     ctx.set_stream(stream.cuda_stream)
     ctx.set_path(args.path)
-    _, _, pre_ids = host.build_synthetic_model(ctx, SEED, 1, sh, ZIPF)
-    pre = pre_ids[0]
+    pre = host.build_synthetic_model(ctx, SEED, 1, sh, ZIPF, experts=my_experts)[2][0]
     dec_ids = host.build_synthetic_model(ctx, SEED + 1, n_dec_layers, sh, None)[2] if n_dec_layers else []
     K, W = args.steps, args.warmup
     n_x = K + W
-    H = sh.hidden
     xs = [synth.tokens(SEED, rank * 1000 + i, PREFILL_M, H) for i in range(n_x)]
     x_offs = [ctx.put(x) for x in xs]
     out_off = ctx.alloc(PREFILL_M * H * 4)
-    ctx.reserve(pre, PREFILL_M)
+
+    def make_step(lid, m, out):
+        if ep_mode:
+            ops = ep.LibraryEpOps(ctx, arena, lid, ep.EpShape(H, E, sh.top_k, world, m), rank, 0, 0, out)
+
+            def step(x_off):
+                ops.x_off = ops.resid_off = x_off
+                ep.exchange_forward(ops, None, m, 1.0)
+        else:
+            ctx.reserve(lid, m)
+
+            def step(x_off):
+                ctx.forward(lid, x_off, x_off, out, m)
+        return step
+
+    step = make_step(pre, PREFILL_M, out_off)
     torch.cuda.synchronize()
 
     # ---- prefill: inputs resident in HBM ----------------------------------------------------
     for i in range(W):
-        ctx.forward(pre, x_offs[i], x_offs[i], out_off, PREFILL_M)
+        step(x_offs[i])
     ctx.sync()
     dev_uuid = None
     try:
@@ -216,38 +257,41 @@ def main():
         pass
     l0 = ctx.launch_count()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    if world > 1:
-        dist.barrier()
+    _barrier(world)
     torch.cuda.synchronize()
     with ClockSampler(dev_uuid) as clk:
         ev0.record(stream)
         for i in range(K):
-            ctx.forward(pre, x_offs[W + i], x_offs[W + i], out_off, PREFILL_M)
+            step(x_offs[W + i])
         ev1.record(stream)
         torch.cuda.synchronize()
     launches = ctx.launch_count() - l0
-    ms = ev0.elapsed_time(ev1) / K
-    if world > 1:
-        t = torch.tensor([ms], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
-        dist.barrier()
+    ms = _max_over_ranks(ev0.elapsed_time(ev1) / K, world)
+    _barrier(world)
     value = world * PREFILL_M / (ms / 1e3)
 
     # ---- per-stage device times (profiling pass, not the timed run) -------------------------
     ctx.profile(True)
     for i in range(K):
-        ctx.forward(pre, x_offs[W + i], x_offs[W + i], out_off, PREFILL_M)
+        step(x_offs[W + i])
     stages = ctx.profile_read()
     ctx.profile(False)
-    distinct = [distinct_experts(ctx.do_route(pre, x_offs[W + i], PREFILL_M, sh.top_k)[0])
+    # distinct experts whose weights this GPU streams (all ranks' tokens reach a rank's experts)
+    routed = np.concatenate([ctx.do_route(pre, x_offs[W + i], PREFILL_M, sh.top_k)[0][None]
+                             for i in range(K)])  # [K, M, k]
+    if ep_mode:
+        t = torch.from_numpy(routed.astype(np.int64)).cuda()
+        allr = [torch.empty_like(t) for _ in range(world)]
+        dist.all_gather(allr, t)
+        routed = np.concatenate([a.cpu().numpy() for a in allr], axis=1)
+    distinct = [len([e for e in np.unique(routed[i]) if my_experts is None or e in my_experts])
                 for i in range(K)]
     n_mats = statistics.mean(distinct) + 1  # + shared expert
     hbm, tfl, peak_kind = peaks()
     stage_ms = {k: v[1] / max(v[0], 1) for k, v in stages.items()}
     alg_bytes = {"gemv13": n_mats * 2 * sh.w13_bytes, "gemv2": n_mats * sh.w2_bytes,
                  "tc13": n_mats * 2 * sh.w13_bytes, "tc2": n_mats * sh.w2_bytes,
-                 "router": sh.n_experts * H * 4 + H * 4 + PREFILL_M * H * 4}
+                 "router": E * H * 4 + H * 4 + PREFILL_M * H * 4}
     dom = max(stage_ms, key=stage_ms.get)
     layer_bytes = n_mats * sh.expert_bytes
     ach = alg_bytes.get(dom, 0.0) / (stage_ms[dom] / 1e3) / 1e9 if dom in alg_bytes else None
@@ -258,30 +302,53 @@ def main():
                 "layer_frac": layer_bytes / (ms / 1e3) / 1e9 / hbm,
                 "stage_ms": {k: round(v, 4) for k, v in stage_ms.items()}}
 
-    e2e, decode, cpu = None, None, None
+    e2e, decode, cpu, config3 = None, None, None, None
     if not only_prefill:
         # ---- end to end through the public API: pinned host buffers, copies inside --------------
         hx = [torch.from_numpy(x).pin_memory() for x in xs[:4]]
         hout = torch.empty((PREFILL_M, H), dtype=torch.float32).pin_memory()
         xin = ctx.alloc(PREFILL_M * H * 4)
         nbytes = PREFILL_M * H * 4
-        for i in range(2):
-            ctx.upload_ptr(xin, hx[i].data_ptr(), nbytes)
-            ctx.forward(pre, xin, xin, out_off, PREFILL_M)
+
+        def e2e_step(i):
+            ctx.upload_ptr(xin, hx[i % 4].data_ptr(), nbytes)
+            step(xin)
             ctx.download_ptr(out_off, hout.data_ptr(), nbytes)
+        for i in range(2):
+            e2e_step(i)
         torch.cuda.synchronize()
+        _barrier(world)
         t0 = time.perf_counter()
         for i in range(K):
-            ctx.upload_ptr(xin, hx[i % 4].data_ptr(), nbytes)
-            ctx.forward(pre, xin, xin, out_off, PREFILL_M)
-            ctx.download_ptr(out_off, hout.data_ptr(), nbytes)
-        e2e_s = (time.perf_counter() - t0) / K
-        if world > 1:
-            t = torch.tensor([e2e_s], device="cuda")
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            e2e_s = float(t.item())
+            e2e_step(i)
+        e2e_s = _max_over_ranks((time.perf_counter() - t0) / K, world)
         e2e = {"value": world * PREFILL_M / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": nbytes,
                "d2h_bytes_per_step": nbytes}
+
+        # ---- config 3: 8192 tokens in total over the N GPUs (strong scaling), uniform router
+        # logits and the config-1 Zipf skew ------------------------------------------------------
+        config3 = {"tokens_total": CONFIG3_M, "tokens_per_gpu": c3_tokens,
+                   "parallelism": f"ep{world}" if ep_mode else "single GPU"}
+        for name, zipf in (("uniform", None), ("zipf1.1", ZIPF)):
+            lid = host.build_synthetic_model(ctx, SEED + 3, 1, sh, zipf, experts=my_experts)[2][0]
+            xc = [ctx.put(synth.tokens(SEED + 3, rank * 1000 + i, c3_tokens, H)) for i in range(4)]
+            oc = ctx.alloc(c3_tokens * H * 4)
+            step3 = make_step(lid, c3_tokens, oc)
+            for i in range(3):
+                step3(xc[i % 4])
+            torch.cuda.synchronize()
+            _barrier(world)
+            k3 = max(5, K // 2)
+            ev0.record(stream)
+            for i in range(k3):
+                step3(xc[i % 4])
+            ev1.record(stream)
+            torch.cuda.synchronize()
+            ms3 = _max_over_ranks(ev0.elapsed_time(ev1) / k3, world)
+            flops = CONFIG3_M * (sh.top_k + 1) * 6 * sh.inter * H
+            config3[name] = {"ms_per_step": ms3, "tok_s": CONFIG3_M / (ms3 / 1e3),
+                             "tensor_tflops_per_gpu": flops / (ms3 / 1e3) / 1e12 / world,
+                             "tensor_frac": flops / (ms3 / 1e3) / 1e12 / world / tfl}
 
         # ---- decode (config 0): M=1, cycling through 16 layers ----------------------------------
         kd = max(K, 64)
@@ -306,7 +373,8 @@ def main():
                   "layer_achieved_gbs": dec_bytes / (dms / 1e3) / 1e9,
                   "layer_frac": dec_bytes / (dms / 1e3) / 1e9 / hbm,
                   "alg_bytes_per_token": dec_bytes, "stage_us": {k: round(v * 1e3, 2) for k, v in dstages.items()},
-                  "l2": "16 layers (6.9 GB) cycled, a fresh token per step"}
+                  "l2": "16 layers (6.9 GB) cycled, a fresh token per step",
+                  "parallelism": "one GPU per replica" if world > 1 else "single GPU"}
 
         # ---- CPU baseline (rank 0, N=1 only) ------------------------------------------------------
         if rank == 0 and world == 1 and not args.no_cpu:
@@ -320,17 +388,20 @@ def main():
                 "warmup": W, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
                 "vs_baseline": None, "dtype": "f32" if args.path == 1 else "f16 (f32 accumulate)",
                 "data": "synthetic (seeded IQ4_XS weights generated on device, N(0,1) tokens)",
-                "config": {"workload": "config1: prefill 512 tok, Zipf(1.1) router bias, 1 MoE layer "
+                "config": {"workload": "config1: prefill 512 tok per GPU, Zipf(1.1) router bias, 1 MoE layer "
                                        "(H=2048, I=512, E=256, top-8 + gated shared, IQ4_XS)",
-                           "tokens_per_step": PREFILL_M, "parallelism": f"replicas x{world}",
+                           "tokens_per_step": PREFILL_M * world,
+                           "parallelism": (f"ep{world}: {epr} experts per GPU, NCCL all-to-all dispatch "
+                                           "and combine") if ep_mode else "single GPU",
                            "expert_kernels": {0: "auto (tcgen05, A in TMEM)", 1: "CUDA-core GEMV",
                                               2: "tcgen05, A in smem", 3: "tcgen05, A in TMEM"}[args.path],
-                           "distinct_experts": round(statistics.mean(distinct), 1),
+                           "distinct_experts_per_gpu": round(statistics.mean(distinct), 1),
                            "l2": "weights 430 MB per layer exceed the 126 MB L2; fresh tokens per step"},
                 "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches,
-                "clocks": clk.summary(), "decode": decode}
+                "clocks": clk.summary(), "decode": decode, "config3": config3}
         print(json.dumps(line), flush=True)
     ctx.close()
+    del arena
     if world > 1:
         dist.destroy_process_group()
 

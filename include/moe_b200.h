@@ -163,9 +163,9 @@ int moe_forward_routed(moe_ctx* ctx, uint32_t layer_id, uint64_t x_off, uint64_t
 
 /* Experts and combine from device routing records (format of moe_route, M records of k+1
  * entries at topk_off; routed entries equal to MOE_NO_EXPERT are skipped).  The expert-parallel
- * building block: a rank runs its own experts on the rows other ranks dispatched to it
- * (MOE_FT_NO_SHARED | MOE_FT_UNSCALED, resid 0 -> one partial row per received row), and the
- * shared expert on its own tokens (MOE_FT_SHARED_ONLY | MOE_FT_UNSCALED). */
+ * building block: a rank runs its own experts on the rows dispatched to it (MOE_FT_UNSCALED,
+ * resid 0 -> one partial row per received row).  An entry 0 with id MOE_NO_EXPERT drops that
+ * row's shared expert. */
 #define MOE_FT_NO_SHARED 1u   /* leave out the shared expert */
 #define MOE_FT_SHARED_ONLY 2u /* only the shared expert (routed entries ignored) */
 #define MOE_FT_UNSCALED 4u    /* combine scale 1 instead of the layer's scale */
@@ -173,29 +173,31 @@ int moe_forward_topk(moe_ctx* ctx, uint32_t layer_id, uint64_t x_off, uint64_t r
                      uint64_t out_off, uint32_t M, uint64_t topk_off, uint32_t flags);
 
 /* ---- expert-parallel prefill (no counterpart in the single-device reference) -------------
- * Rank d of n_ranks (1..8) owns experts [d*E/n, (d+1)*E/n).  Per layer and batch:
- *   moe_route -> moe_ep_dispatch -> all-to-all of counts and of the send rows/records (NCCL,
- *   by the caller) -> moe_forward_topk(received, NO_SHARED|UNSCALED) -> all-to-all back ->
- *   moe_forward_topk(own tokens, SHARED_ONLY|UNSCALED) -> moe_ep_combine. */
+ * Rank r of n_ranks (1..8) owns experts [r*E/n, (r+1)*E/n).  Every rank sends each peer a block
+ * of `capacity` rows (capacity >= the largest per-rank token count), so the all-to-alls have
+ * fixed, equal splits and need no host synchronisation.  Per layer and batch:
+ *   moe_route -> moe_ep_dispatch -> all-to-all of the send rows and records (NCCL, by the
+ *   caller) -> moe_forward_topk(received n_ranks*capacity rows, MOE_FT_UNSCALED, resid 0) ->
+ *   all-to-all of the partial rows back -> moe_ep_combine.
+ * A token's shared expert runs on its own rank (its record to itself keeps entry 0). */
 
 /* Bytes of the dispatch plan of M tokens over n_ranks ranks (arena offset 256-aligned). */
 uint64_t moe_ep_plan_bytes(uint32_t M, uint32_t n_ranks);
 
-/* Builds the plan and the rank-major send buffers from M routing records and rows x (f32
- * [M][H]): one f32 row and one record per (token, destination rank) pair, tokens in order
- * inside each destination, records keeping only the destination's experts.  send_x and
- * send_topk hold up to M*min(top_k, n_ranks) rows.  Writes the per-destination row counts to
- * counts[n_ranks] (host) and therefore synchronises the context's stream. */
-int moe_ep_dispatch(moe_ctx* ctx, uint32_t n_experts, uint32_t top_k, uint32_t n_ranks,
-                    uint64_t topk_off, uint64_t x_off, uint32_t M, uint32_t H, uint64_t plan_off,
-                    uint64_t send_x_off, uint64_t send_topk_off, int32_t* counts);
+/* Builds the plan and the send buffers (n_ranks blocks of `capacity` rows: f32 rows of x and
+ * (top_k+1)-entry records) from M routing records and rows x (f32 [M][H]).  Block d holds, in
+ * token order, the tokens routed to at least one of rank d's experts (and every token in block
+ * my_rank), each record keeping only rank d's experts; unused rows carry empty records.
+ * Asynchronous on the context's stream. */
+int moe_ep_dispatch(moe_ctx* ctx, uint32_t n_experts, uint32_t top_k, uint32_t n_ranks, uint32_t my_rank,
+                    uint32_t capacity, uint64_t topk_off, uint64_t x_off, uint32_t M, uint32_t H,
+                    uint64_t plan_off, uint64_t send_x_off, uint64_t send_topk_off);
 
 /* out[t] = resid[t] + scale * (sum over the ranks t was sent to, ascending, of its returned
- * partial row + shared[t]).  y_back holds the returned rows in send order (as many rows as
- * moe_ep_dispatch sent); shared_off and resid_off may be 0. */
-int moe_ep_combine(moe_ctx* ctx, uint32_t n_ranks, uint32_t H, uint32_t M, uint64_t plan_off,
-                   uint64_t y_back_off, uint64_t shared_off, uint64_t resid_off, uint64_t out_off,
-                   float scale);
+ * partial row).  y_back holds the returned blocks in send layout (n_ranks*capacity rows);
+ * resid_off may be 0. */
+int moe_ep_combine(moe_ctx* ctx, uint32_t n_ranks, uint32_t capacity, uint32_t H, uint32_t M,
+                   uint64_t plan_off, uint64_t y_back_off, uint64_t resid_off, uint64_t out_off, float scale);
 
 /* Expert-product kernels used by moe_forward / moe_forward_routed (a tuning and diagnostic
  * knob; the default picks by batch size: CUDA-core grouped GEMV for M <= 8, tcgen05 grouped

@@ -840,7 +840,7 @@ int moe_forward_topk(moe_ctx* c, uint32_t layer_id, uint64_t x_off, uint64_t res
 uint64_t moe_ep_plan_bytes(uint32_t M, uint32_t n_ranks) {
     const uint64_t a = (4ull * M + 255) / 256 * 256;
     const uint64_t b = (4ull * M * n_ranks + 255) / 256 * 256;
-    return a + b + 4ull * (n_ranks + 1);
+    return a + b + 8ull * n_ranks;
 }
 
 static moe::EpPlan ep_plan_at(Ctx* c, uint64_t plan_off, uint32_t M, uint32_t n_ranks) {
@@ -849,61 +849,63 @@ static moe::EpPlan ep_plan_at(Ctx* c, uint64_t plan_off, uint32_t M, uint32_t n_
     return moe::EpPlan{at<uint32_t>(c, plan_off), at<int>(c, plan_off + a), at<int>(c, plan_off + a + b)};
 }
 
-int moe_ep_dispatch(moe_ctx* c, uint32_t n_experts, uint32_t top_k, uint32_t n_ranks,
-                    uint64_t topk_off, uint64_t x_off, uint32_t M, uint32_t H, uint64_t plan_off,
-                    uint64_t send_x_off, uint64_t send_topk_off, int32_t* counts) {
-    if (!c || !counts) return fail(c, MOE_E_INVALID, "NULL argument");
-    if (n_ranks == 0 || n_ranks > static_cast<uint32_t>(moe::kMaxEpRanks) || n_experts == 0 ||
-        n_experts > moe::kMaxExperts || n_experts % n_ranks != 0 || top_k == 0 || top_k > moe::kMaxTopK)
-        return fail(c, MOE_E_UNSUPPORTED, "n_ranks %u (1..%d, dividing n_experts %u), top_k %u", n_ranks,
-                    moe::kMaxEpRanks, n_experts, top_k);
-    if (H == 0 || H % 4 != 0) return fail(c, MOE_E_INVALID, "H must be a positive multiple of 4");
-    if (M == 0) {
-        for (uint32_t d = 0; d < n_ranks; ++d) counts[d] = 0;
-        return MOE_OK;
-    }
-    const uint64_t max_pairs = static_cast<uint64_t>(M) * std::min(top_k, n_ranks);
-    if (!off_ok(c, topk_off, static_cast<uint64_t>(M) * (top_k + 1) * 8, 8) ||
-        !off_ok(c, x_off, static_cast<uint64_t>(M) * H * 4, 16) ||
-        !off_ok(c, plan_off, moe_ep_plan_bytes(M, n_ranks), 256) ||
-        !off_ok(c, send_x_off, max_pairs * H * 4, 16) ||
-        !off_ok(c, send_topk_off, max_pairs * (top_k + 1) * 8, 8))
-        return fail(c, MOE_E_INVALID, "ep dispatch buffer offsets invalid (send buffers hold M*min(k, n_ranks) rows)");
-    DeviceGuard g(c->device);
-    const moe::EpPlan plan = ep_plan_at(c, plan_off, M, n_ranks);
-    const int epr = static_cast<int>(n_experts / n_ranks);
-    moe::launch_ep_plan(at<uint2>(c, topk_off), static_cast<int>(M), static_cast<int>(top_k), epr,
-                        static_cast<int>(n_ranks), plan, c->ws.status, c->stream);
-    moe::launch_ep_gather(at<float>(c, x_off), at<uint2>(c, topk_off), plan, static_cast<int>(M),
-                          static_cast<int>(H), static_cast<int>(top_k), epr, static_cast<int>(n_ranks),
-                          at<float>(c, send_x_off), at<uint2>(c, send_topk_off), c->stream);
-    stage(c, "ep_dispatch", 3);
-    int off[moe::kMaxEpRanks + 1];
-    MOE_CUDA(c, cudaMemcpyAsync(off, plan.offsets, sizeof(int) * (n_ranks + 1), cudaMemcpyDeviceToHost, c->stream));
-    int rc = moe_sync(c);
-    if (rc) return rc;
-    for (uint32_t d = 0; d < n_ranks; ++d) counts[d] = off[d + 1] - off[d];
+static int ep_check_ranks(Ctx* c, uint32_t n_ranks, uint32_t my_rank, uint32_t capacity, uint32_t M) {
+    if (n_ranks == 0 || n_ranks > static_cast<uint32_t>(moe::kMaxEpRanks) || my_rank >= n_ranks)
+        return fail(c, MOE_E_UNSUPPORTED, "n_ranks %u (1..%d) / rank %u", n_ranks, moe::kMaxEpRanks, my_rank);
+    if (capacity < M) return fail(c, MOE_E_INVALID, "capacity %u below the %u local tokens", capacity, M);
     return MOE_OK;
 }
 
-int moe_ep_combine(moe_ctx* c, uint32_t n_ranks, uint32_t H, uint32_t M, uint64_t plan_off,
-                   uint64_t y_back_off, uint64_t shared_off, uint64_t resid_off, uint64_t out_off,
-                   float scale) {
+int moe_ep_dispatch(moe_ctx* c, uint32_t n_experts, uint32_t top_k, uint32_t n_ranks, uint32_t my_rank,
+                    uint32_t capacity, uint64_t topk_off, uint64_t x_off, uint32_t M, uint32_t H,
+                    uint64_t plan_off, uint64_t send_x_off, uint64_t send_topk_off) {
     if (!c) return fail(c, MOE_E_INVALID, "NULL context");
-    if (n_ranks == 0 || n_ranks > static_cast<uint32_t>(moe::kMaxEpRanks))
-        return fail(c, MOE_E_UNSUPPORTED, "n_ranks %u outside 1..%d", n_ranks, moe::kMaxEpRanks);
+    int rc = ep_check_ranks(c, n_ranks, my_rank, capacity, M);
+    if (rc) return rc;
+    if (n_experts == 0 || n_experts > moe::kMaxExperts || n_experts % n_ranks != 0 || top_k == 0 ||
+        top_k > moe::kMaxTopK)
+        return fail(c, MOE_E_UNSUPPORTED, "n_experts %u (a multiple of n_ranks %u), top_k %u", n_experts,
+                    n_ranks, top_k);
+    if (H == 0 || H % 4 != 0) return fail(c, MOE_E_INVALID, "H must be a positive multiple of 4");
+    const uint64_t rows = static_cast<uint64_t>(n_ranks) * capacity;
+    const uint64_t rec_bytes = rows * (top_k + 1) * 8;
+    if (!off_ok(c, send_x_off, rows * H * 4, 16) || !off_ok(c, send_topk_off, rec_bytes, 8) ||
+        !off_ok(c, plan_off, moe_ep_plan_bytes(std::max(M, 1u), n_ranks), 256) ||
+        (M && (!off_ok(c, topk_off, static_cast<uint64_t>(M) * (top_k + 1) * 8, 8) ||
+               !off_ok(c, x_off, static_cast<uint64_t>(M) * H * 4, 16))))
+        return fail(c, MOE_E_INVALID, "ep dispatch buffer offsets invalid (send buffers hold n_ranks*capacity rows)");
+    DeviceGuard g(c->device);
+    // every record starts empty (id 0xFFFFFFFF): rows no token uses are skipped by the experts
+    MOE_CUDA(c, cudaMemsetAsync(c->base + send_topk_off, 0xFF, rec_bytes, c->stream));
+    if (M == 0) return MOE_OK;
+    const moe::EpPlan plan = ep_plan_at(c, plan_off, M, n_ranks);
+    const int epr = static_cast<int>(n_experts / n_ranks);
+    moe::launch_ep_plan(at<uint2>(c, topk_off), static_cast<int>(M), static_cast<int>(top_k), epr,
+                        static_cast<int>(n_ranks), static_cast<int>(my_rank), static_cast<int>(capacity),
+                        plan, c->ws.status, c->stream);
+    moe::launch_ep_gather(at<float>(c, x_off), at<uint2>(c, topk_off), plan, static_cast<int>(M),
+                          static_cast<int>(H), static_cast<int>(top_k), epr, static_cast<int>(n_ranks),
+                          static_cast<int>(my_rank), at<float>(c, send_x_off), at<uint2>(c, send_topk_off),
+                          c->stream);
+    stage(c, "ep_dispatch", 3);
+    return check_launch(c, "ep_dispatch");
+}
+
+int moe_ep_combine(moe_ctx* c, uint32_t n_ranks, uint32_t capacity, uint32_t H, uint32_t M,
+                   uint64_t plan_off, uint64_t y_back_off, uint64_t resid_off, uint64_t out_off, float scale) {
+    if (!c) return fail(c, MOE_E_INVALID, "NULL context");
+    int rc = ep_check_ranks(c, n_ranks, 0, capacity, M);
+    if (rc) return rc;
     if (H == 0 || H % 4 != 0) return fail(c, MOE_E_INVALID, "H must be a positive multiple of 4");
     if (M == 0) return MOE_OK;
     const uint64_t row = static_cast<uint64_t>(H) * 4, rows = static_cast<uint64_t>(M) * row;
     if (!off_ok(c, plan_off, moe_ep_plan_bytes(M, n_ranks), 256) ||
-        (y_back_off && !off_ok(c, y_back_off, row, 16)) ||
-        (shared_off && !off_ok(c, shared_off, rows, 16)) || (resid_off && !off_ok(c, resid_off, rows, 16)) ||
-        !off_ok(c, out_off, rows, 16))
+        !off_ok(c, y_back_off, static_cast<uint64_t>(n_ranks) * capacity * row, 16) ||
+        (resid_off && !off_ok(c, resid_off, rows, 16)) || !off_ok(c, out_off, rows, 16))
         return fail(c, MOE_E_INVALID, "ep combine buffer offsets invalid");
     DeviceGuard g(c->device);
     moe::launch_ep_combine(ep_plan_at(c, plan_off, M, n_ranks), static_cast<int>(M), static_cast<int>(n_ranks),
-                           static_cast<int>(H), y_back_off ? at<float>(c, y_back_off) : nullptr,
-                           shared_off ? at<float>(c, shared_off) : nullptr,
+                           static_cast<int>(H), at<float>(c, y_back_off),
                            resid_off ? at<float>(c, resid_off) : nullptr, scale, at<float>(c, out_off), c->stream);
     stage(c, "ep_combine", 1);
     return check_launch(c, "ep_combine");

@@ -10,7 +10,8 @@
 //              the lower warps' masks and of the lower lanes of its own warp.  Positions are
 //              therefore in token order inside each bucket (the reference's stable fill).
 // A routed record whose expert id is kNoExpert (0xFFFFFFFF) is an empty slot: it gets no
-// position (slot_pos -1).  Expert-parallel ranks use it for the experts another rank owns.
+// position (slot_pos -1); so does the shared slot of a token whose entry 0 has id kNoExpert.
+// Expert-parallel ranks use them for experts another rank owns and for padding rows.
 // Bucket E holds the shared expert: every token, in order (the reference instead counts the
 // shared slot into bucket shared_id = 0, which it also uses for routed expert 0).
 #include <cuda_runtime.h>
@@ -26,7 +27,7 @@ constexpr int kTile = 256;  // tokens per tile (8 warps x 32)
 constexpr int kScanThreads = 288;  // >= kMaxExperts + 1, whole warps
 
 __device__ __forceinline__ void build_masks(uint32_t* masks, int nb, const uint2* topk, int M,
-                                            int E, int k, int routed, int* status) {
+                                            int E, int k, int routed, int has_shared, int* status) {
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     for (int i = tid; i < 8 * nb; i += blockDim.x) masks[i] = 0u;
     __syncthreads();
@@ -39,6 +40,7 @@ __device__ __forceinline__ void build_masks(uint32_t* masks, int nb, const uint2
             if (e < 0 || e >= E) { set_dev_error(status, kDevBadExpert); continue; }
             atomicOr(&masks[warp * nb + e], 1u << lane);
         }
+        if (has_shared && rec[0].x != kNoExpert) atomicOr(&masks[warp * nb + E], 1u << lane);
     }
     __syncthreads();
 }
@@ -48,13 +50,11 @@ bucket_count_kernel(const uint2* __restrict__ topk, int M, int E, int k, int rou
                     int* __restrict__ tilecnt, int* status) {
     extern __shared__ uint32_t masks[];  // [8][E+1]
     const int nb = E + 1;
-    build_masks(masks, nb, topk, M, E, k, routed, status);
-    const int tile_tokens = min(kTile, M - static_cast<int>(blockIdx.x) * kTile);
+    build_masks(masks, nb, topk, M, E, k, routed, has_shared, status);
     for (int e = threadIdx.x; e < nb; e += blockDim.x) {
         int c = 0;
 #pragma unroll
         for (int w = 0; w < 8; ++w) c += __popc(masks[w * nb + e]);
-        if (e == E && has_shared) c = tile_tokens;
         tilecnt[static_cast<size_t>(blockIdx.x) * nb + e] = c;
     }
 }
@@ -153,7 +153,7 @@ bucket_scatter_kernel(const uint2* __restrict__ topk, int M, int E, int k, int r
                       float* __restrict__ sorted_w, int* __restrict__ slot_pos, int* status) {
     extern __shared__ uint32_t masks[];
     const int nb = E + 1;
-    build_masks(masks, nb, topk, M, E, k, routed, status);
+    build_masks(masks, nb, topk, M, E, k, routed, has_shared, status);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int t = blockIdx.x * kTile + tid;
     if (t >= M) return;
@@ -162,20 +162,17 @@ bucket_scatter_kernel(const uint2* __restrict__ topk, int M, int E, int k, int r
     const uint2* rec = topk + static_cast<size_t>(t) * (k + 1);
     const int ns = k + (has_shared ? 1 : 0);
     int* sp = slot_pos + static_cast<size_t>(t) * ns;
-    for (int s = 0; s < k; ++s) {
-        const int e = static_cast<int>(rec[1 + s].x);
-        if (!routed || e < 0 || e >= E) { sp[s] = -1; continue; }
+    for (int s = 0; s < ns; ++s) {
+        const uint2 r = rec[s == k ? 0 : 1 + s];  // slot k: the shared expert, record entry 0
+        int e;
+        if (s == k) e = r.x == kNoExpert ? -1 : E;
+        else e = (!routed || r.x >= static_cast<uint32_t>(E)) ? -1 : static_cast<int>(r.x);
+        if (e < 0) { sp[s] = -1; continue; }
         int pos = off[e] + __popc(masks[warp * nb + e] & lt);
         for (int w = 0; w < warp; ++w) pos += __popc(masks[w * nb + e]);
         sorted_tok[pos] = t;
-        sorted_w[pos] = __uint_as_float(rec[1 + s].y);
+        sorted_w[pos] = __uint_as_float(r.y);
         sp[s] = pos;
-    }
-    if (has_shared) {
-        const int pos = off[E] + tid;
-        sorted_tok[pos] = t;
-        sorted_w[pos] = __uint_as_float(rec[0].y);
-        sp[k] = pos;
     }
 }
 

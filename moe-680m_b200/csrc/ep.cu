@@ -1,20 +1,21 @@
 // Expert-parallel prefill: the device side of the dispatch and combine around an all-to-all.
 //
-// Rank d of N owns experts [d*epr, (d+1)*epr), epr = E/N.  For the M local tokens of this rank:
-//   plan:    mask[t]  = bit d set when one of token t's k routed experts lives on rank d;
-//            pos[t][d] = rank of t among the tokens with bit d (token order), offsets[d] =
-//            exclusive prefix over d of the per-rank pair counts -> the send buffer is
-//            rank-major, token order inside a rank (deterministic);
-//   gather:  send_x[off[d] + pos[t][d]] = x[t] (f32 row, exact), and the token's (k+1)-entry
-//            routing record keeping the experts of rank d (global ids) and emptying every other
-//            routed entry (kNoExpert); entry 0 (shared gate) is copied;
-//   combine: out[t] = resid[t] + scale * (sum over d in mask, ascending, of y_back[off[d] +
-//            pos[t][d]] + shared[t]), where y_back are the partial rows returned by the ranks
-//            (sum_j w_j E_j(x) over the rank's experts, unscaled) and shared[t] = gate * S(x_t)
-//            computed locally.
-// The reference runs on one device and has no counterpart; this follows the exchange steps of
-// the expert-parallel layout (router -> per-rank histogram -> count exchange -> dispatch ->
-// local grouped experts -> return of one partial row per (token, rank) -> ordered sum).
+// Rank d of N owns experts [d*epr, (d+1)*epr), epr = E/N.  Every rank sends every peer a block
+// of `capacity` rows (capacity >= the tokens of any rank), so the all-to-alls have fixed,
+// equal splits: no count exchange and no host synchronisation, and a whole layer can be
+// replayed from a CUDA graph.  For the M local tokens of rank r:
+//   plan:    mask[t] = bit d set when one of token t's k routed experts lives on rank d, and
+//            bit r always (the shared expert of r's own tokens runs on r); pos[t][d] = rank of
+//            t among the tokens with bit d (token order);
+//   gather:  send_x[d*capacity + pos[t][d]] = x[t] (f32 row, exact) and the token's routing
+//            record keeping only rank d's experts (others kNoExpert), with the shared entry 0
+//            kept for d == r and emptied otherwise; rows no token uses carry empty records;
+//   combine: out[t] = resid[t] + scale * sum over d in mask, ascending, of the partial row
+//            y_back[d*capacity + pos[t][d]] returned by rank d (sum_j w_j E_j(x) over d's
+//            experts, plus gate * S(x) from rank r itself).
+// The single-device reference has no counterpart; this follows the exchange steps of the
+// expert-parallel layout (router -> per-rank histogram -> dispatch -> local grouped experts ->
+// return of one partial row per (token, rank) -> ordered sum).
 #include <cuda_runtime.h>
 
 #include "moe_common.cuh"
@@ -27,11 +28,11 @@ namespace {
 constexpr int kScanT = 1024;
 
 __global__ void ep_mask_kernel(const uint2* __restrict__ topk, int M, int k, int epr, int n_ranks,
-                               uint32_t* __restrict__ mask, int* status) {
+                               int my_rank, uint32_t* __restrict__ mask, int* status) {
     const int t = blockIdx.x * blockDim.x + threadIdx.x;
     if (t >= M) return;
     const uint2* rec = topk + static_cast<size_t>(t) * (k + 1);
-    uint32_t m = 0;
+    uint32_t m = 1u << my_rank;
     for (int s = 0; s < k; ++s) {
         const uint32_t e = rec[1 + s].x;
         if (e == kNoExpert) continue;
@@ -45,7 +46,7 @@ __global__ void ep_mask_kernel(const uint2* __restrict__ topk, int M, int k, int
 // One CTA: per rank d, exclusive scan of mask bit d over the tokens (each thread a contiguous
 // run of tokens), pair counts and rank offsets.
 __global__ void __launch_bounds__(kScanT) ep_scan_kernel(const uint32_t* __restrict__ mask, int M,
-                                                         int n_ranks, int* __restrict__ pos,
+                                                         int n_ranks, int capacity, int* __restrict__ pos,
                                                          int* __restrict__ offsets) {
     __shared__ int wsum[kScanT / 32][kMaxEpRanks];
     __shared__ int tot[kMaxEpRanks];
@@ -97,13 +98,11 @@ __global__ void __launch_bounds__(kScanT) ep_scan_kernel(const uint32_t* __restr
             }
         }
     }
-    if (tid == 0) {
-        int run = 0;
+    if (tid == 0) {  // block d starts at d * capacity; offsets[n_ranks + d] = rows used in it
         for (int d = 0; d < n_ranks; ++d) {
-            offsets[d] = run;
-            run += tot[d];
+            offsets[d] = d * capacity;
+            offsets[n_ranks + d] = tot[d];
         }
-        offsets[n_ranks] = run;
     }
 }
 
@@ -111,7 +110,8 @@ __global__ void __launch_bounds__(kScanT) ep_scan_kernel(const uint32_t* __restr
 __global__ void ep_gather_kernel(const float* __restrict__ x, const uint2* __restrict__ topk,
                                  const uint32_t* __restrict__ mask, const int* __restrict__ pos,
                                  const int* __restrict__ offsets, int M, int H, int k, int epr,
-                                 int n_ranks, float* __restrict__ send_x, uint2* __restrict__ send_rec) {
+                                 int n_ranks, int my_rank, float* __restrict__ send_x,
+                                 uint2* __restrict__ send_rec) {
     const int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
     if (t >= M) return;
     const uint32_t m = mask[t];
@@ -130,6 +130,8 @@ __global__ void ep_gather_kernel(const float* __restrict__ x, const uint2* __res
                 const uint32_t e = r.x;
                 o.x = (e != kNoExpert && e / static_cast<uint32_t>(epr) == static_cast<uint32_t>(d))
                           ? e : kNoExpert;
+            } else if (d != my_rank) {
+                o.x = kNoExpert;  // the shared expert runs on the token's own rank
             }
             send_rec[p * (k + 1) + lane] = o;
         }
@@ -138,8 +140,8 @@ __global__ void ep_gather_kernel(const float* __restrict__ x, const uint2* __res
 
 __global__ void ep_combine_kernel(const uint32_t* __restrict__ mask, const int* __restrict__ pos,
                                   const int* __restrict__ offsets, int n_ranks, int H,
-                                  const float* __restrict__ y_back, const float* __restrict__ shared,
-                                  const float* __restrict__ resid, float scale, float* __restrict__ out) {
+                                  const float* __restrict__ y_back, const float* __restrict__ resid,
+                                  float scale, float* __restrict__ out) {
     const int t = blockIdx.x;
     const int c = (blockIdx.y * blockDim.x + threadIdx.x) * 4;
     if (c >= H) return;
@@ -152,10 +154,6 @@ __global__ void ep_combine_kernel(const uint32_t* __restrict__ mask, const int* 
         acc.x += y.x; acc.y += y.y; acc.z += y.z; acc.w += y.w;
     }
     const size_t row = static_cast<size_t>(t) * H + c;
-    if (shared) {
-        const float4 y = *reinterpret_cast<const float4*>(shared + row);
-        acc.x += y.x; acc.y += y.y; acc.z += y.z; acc.w += y.w;
-    }
     float4 r = make_float4(0.f, 0.f, 0.f, 0.f);
     if (resid) r = *reinterpret_cast<const float4*>(resid + row);
     r.x = fmaf(scale, acc.x, r.x); r.y = fmaf(scale, acc.y, r.y);
@@ -165,23 +163,23 @@ __global__ void ep_combine_kernel(const uint32_t* __restrict__ mask, const int* 
 
 }  // namespace
 
-void launch_ep_plan(const uint2* topk, int M, int k, int epr, int n_ranks, EpPlan plan, int* status,
-                    cudaStream_t s) {
-    ep_mask_kernel<<<(M + 255) / 256, 256, 0, s>>>(topk, M, k, epr, n_ranks, plan.mask, status);
-    ep_scan_kernel<<<1, kScanT, 0, s>>>(plan.mask, M, n_ranks, plan.pos, plan.offsets);
+void launch_ep_plan(const uint2* topk, int M, int k, int epr, int n_ranks, int my_rank, int capacity,
+                    EpPlan plan, int* status, cudaStream_t s) {
+    ep_mask_kernel<<<(M + 255) / 256, 256, 0, s>>>(topk, M, k, epr, n_ranks, my_rank, plan.mask, status);
+    ep_scan_kernel<<<1, kScanT, 0, s>>>(plan.mask, M, n_ranks, capacity, plan.pos, plan.offsets);
 }
 
 void launch_ep_gather(const float* x, const uint2* topk, EpPlan plan, int M, int H, int k, int epr,
-                      int n_ranks, float* send_x, uint2* send_rec, cudaStream_t s) {
+                      int n_ranks, int my_rank, float* send_x, uint2* send_rec, cudaStream_t s) {
     ep_gather_kernel<<<(M * 32 + 255) / 256, 256, 0, s>>>(x, topk, plan.mask, plan.pos, plan.offsets, M,
-                                                         H, k, epr, n_ranks, send_x, send_rec);
+                                                         H, k, epr, n_ranks, my_rank, send_x, send_rec);
 }
 
-void launch_ep_combine(EpPlan plan, int M, int n_ranks, int H, const float* y_back, const float* shared,
-                       const float* resid, float scale, float* out, cudaStream_t s) {
+void launch_ep_combine(EpPlan plan, int M, int n_ranks, int H, const float* y_back, const float* resid,
+                       float scale, float* out, cudaStream_t s) {
     dim3 grid(M, (H / 4 + 255) / 256);
-    ep_combine_kernel<<<grid, 256, 0, s>>>(plan.mask, plan.pos, plan.offsets, n_ranks, H, y_back,
-                                           shared, resid, scale, out);
+    ep_combine_kernel<<<grid, 256, 0, s>>>(plan.mask, plan.pos, plan.offsets, n_ranks, H, y_back, resid,
+                                           scale, out);
 }
 
 }  // namespace moe

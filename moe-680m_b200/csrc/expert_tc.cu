@@ -571,6 +571,14 @@ convert_x_kernel(const IoArgs* __restrict__ io, const int* __restrict__ slot_pos
     const int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
     if (t >= M) return;
     const float* s = io->x + static_cast<size_t>(t) * len;
+    int pos[kMaxTopK + 1];
+    bool any = false;
+#pragma unroll
+    for (int j = 0; j < kMaxTopK + 1; ++j) {
+        pos[j] = j < ns ? slot_pos[static_cast<size_t>(t) * ns + j] : -1;
+        any |= pos[j] >= 0;
+    }
+    if (!any) return;  // a token without slots (expert-parallel padding rows): row not read
     float mx = 0.f;
     for (int i = lane * 4; i < len; i += 128) {
         const float4 v = *reinterpret_cast<const float4*>(s + i);
@@ -578,9 +586,6 @@ convert_x_kernel(const IoArgs* __restrict__ io, const int* __restrict__ slot_pos
     }
     const int e = row_exp(warp_max(mx));
     const float sc = pow2f(-e);
-    int pos[kMaxTopK + 1];
-#pragma unroll
-    for (int j = 0; j < kMaxTopK + 1; ++j) pos[j] = j < ns ? slot_pos[static_cast<size_t>(t) * ns + j] : -1;
     if (lane < ns && pos[lane] >= 0) sexp[pos[lane]] = e;
     for (int c = lane; c < len / 8; c += 32) {
         const int kb = chunk_k(c);

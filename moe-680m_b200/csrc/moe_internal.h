@@ -202,19 +202,19 @@ void launch_decode(const Layer& L, const Workspace& ws, int* sync, int sm_count,
 void launch_combine(const Layer& L, const Workspace& ws, const IoArgs* io, int M, int ns,
                     float scale, cudaStream_t s);
 // Expert-parallel dispatch plan (arena or workspace memory): mask[M], pos[M][n_ranks],
-// offsets[n_ranks + 1].
+// offsets[2 * n_ranks] (block starts, rows used per block).
 constexpr int kMaxEpRanks = 8;
 struct EpPlan {
     uint32_t* mask;
     int* pos;
     int* offsets;
 };
-void launch_ep_plan(const uint2* topk, int M, int k, int epr, int n_ranks, EpPlan plan, int* status,
-                    cudaStream_t s);
+void launch_ep_plan(const uint2* topk, int M, int k, int epr, int n_ranks, int my_rank, int capacity,
+                    EpPlan plan, int* status, cudaStream_t s);
 void launch_ep_gather(const float* x, const uint2* topk, EpPlan plan, int M, int H, int k, int epr,
-                      int n_ranks, float* send_x, uint2* send_rec, cudaStream_t s);
-void launch_ep_combine(EpPlan plan, int M, int n_ranks, int H, const float* y_back, const float* shared,
-                       const float* resid, float scale, float* out, cudaStream_t s);
+                      int n_ranks, int my_rank, float* send_x, uint2* send_rec, cudaStream_t s);
+void launch_ep_combine(EpPlan plan, int M, int n_ranks, int H, const float* y_back, const float* resid,
+                       float scale, float* out, cudaStream_t s);
 void launch_rms_norm(const float* x, float* y, int M, int H, float eps, cudaStream_t s);
 void launch_dequant(const uint8_t* src, uint64_t n_blocks, float* dst, cudaStream_t s);
 void launch_synth(uint8_t* dst, uint64_t key, uint64_t block_start, uint64_t n_blocks,

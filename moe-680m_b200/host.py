@@ -106,8 +106,8 @@ def lib():
         "moe_bucket_static": (i32, [u32, u32, i32, vp, u32, vp, vp, vp, vp, vp]),
         "moe_forward_topk": (i32, [vp, u32, u64, u64, u64, u32, u64, u32]),
         "moe_ep_plan_bytes": (u64, [u32, u32]),
-        "moe_ep_dispatch": (i32, [vp, u32, u32, u32, u64, u64, u32, u32, u64, u64, u64, P(C.c_int32)]),
-        "moe_ep_combine": (i32, [vp, u32, u32, u32, u64, u64, u64, u64, u64, f32]),
+        "moe_ep_dispatch": (i32, [vp, u32, u32, u32, u32, u32, u64, u64, u32, u32, u64, u64, u64]),
+        "moe_ep_combine": (i32, [vp, u32, u32, u32, u32, u64, u64, u64, u64, f32]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -254,15 +254,13 @@ class Context:
     def forward_topk(self, layer, x_off, resid_off, out_off, m, topk_off, flags=0):
         self._check(lib().moe_forward_topk(self.h, layer, x_off, resid_off, out_off, m, topk_off, flags))
 
-    def ep_dispatch(self, n_experts, top_k, n_ranks, topk_off, x_off, m, hidden, plan_off,
-                    send_x_off, send_topk_off) -> list[int]:
-        counts = np.zeros(n_ranks, np.int32)
-        self._check(lib().moe_ep_dispatch(self.h, n_experts, top_k, n_ranks, topk_off, x_off, m, hidden,
-                                          plan_off, send_x_off, send_topk_off, _ptr(counts, C.c_int32)))
-        return [int(v) for v in counts]
+    def ep_dispatch(self, n_experts, top_k, n_ranks, my_rank, capacity, topk_off, x_off, m, hidden,
+                    plan_off, send_x_off, send_topk_off):
+        self._check(lib().moe_ep_dispatch(self.h, n_experts, top_k, n_ranks, my_rank, capacity, topk_off,
+                                          x_off, m, hidden, plan_off, send_x_off, send_topk_off))
 
-    def ep_combine(self, n_ranks, hidden, m, plan_off, y_back_off, shared_off, resid_off, out_off, scale):
-        self._check(lib().moe_ep_combine(self.h, n_ranks, hidden, m, plan_off, y_back_off, shared_off,
+    def ep_combine(self, n_ranks, capacity, hidden, m, plan_off, y_back_off, resid_off, out_off, scale):
+        self._check(lib().moe_ep_combine(self.h, n_ranks, capacity, hidden, m, plan_off, y_back_off,
                                          resid_off, out_off, scale))
 
     def rms_norm(self, x_off, y_off, m, hidden, eps=1e-6):

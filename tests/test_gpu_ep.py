@@ -4,7 +4,8 @@ expert-parallel layer over NCCL.
 * moe_forward_topk: flags 0 equals moe_forward bit for bit on the same routing; the partial
   (routed only, unscaled) plus the shared-only part, scaled, plus the residual equals it to f32
   rounding; empty routed entries (MOE_NO_EXPERT) are skipped (checked against the oracle).
-* moe_ep_dispatch: plan, send rows and records equal a NumPy restatement exactly.
+* moe_ep_dispatch: the rank blocks (rows, reduced records, empty padding) equal a NumPy
+  restatement exactly.
 * one-rank expert-parallel layer (an NCCL group of 1): equals moe_forward to f32 rounding and
   the f64 oracle to the layer tolerance.
 * two ranks on two GPUs (skipped with fewer GPUs): each rank's output equals the single-GPU
@@ -90,37 +91,32 @@ def test_forward_topk_empty_slots(full):
     assert O.rel_l2(got, ref) <= 1e-3
 
 
-def _plan_ref(rec, n_ranks, epr):
-    m = rec.shape[0]
-    pairs = [[t for t in range(m) if np.any(rec[t, 1:, 0] // epr == d)] for d in range(n_ranks)]
-    return pairs
-
-
-@pytest.mark.parametrize("n_ranks", [1, 2, 4, 8])
-def test_ep_dispatch_exact(full, n_ranks):
+@pytest.mark.parametrize("n_ranks,my_rank", [(1, 0), (2, 1), (4, 2), (8, 7)])
+def test_ep_dispatch_exact(full, n_ranks, my_rank):
     ctx, lid = full
     m, H, k, E = 300, FULL.hidden, 8, 256
+    cap = 320
     x = synth.tokens(SEED, 9, m, H)
     xo, topk = _route(ctx, lid, x)
     rec = ctx.download(topk, (m, k + 1, 2), np.uint32)
     plan = ctx.alloc(int(host.lib().moe_ep_plan_bytes(m, n_ranks)))
-    mp_ = m * min(k, n_ranks)
-    sx, sr = ctx.alloc(mp_ * H * 4), ctx.alloc(mp_ * (k + 1) * 8)
-    counts = ctx.ep_dispatch(E, k, n_ranks, topk, xo, m, H, plan, sx, sr)
+    rows = n_ranks * cap
+    sx, sr = ctx.alloc(rows * H * 4), ctx.alloc(rows * (k + 1) * 8)
+    ctx.ep_dispatch(E, k, n_ranks, my_rank, cap, topk, xo, m, H, plan, sx, sr)
+    ctx.sync()
+    got_x = ctx.download(sx, (rows, H))
+    got_r = ctx.download(sr, (rows, k + 1, 2), np.uint32)
     epr = E // n_ranks
-    pairs = _plan_ref(rec, n_ranks, epr)
-    assert counts == [len(p) for p in pairs]
-    n = sum(counts)
-    got_x = ctx.download(sx, (n, H))
-    got_r = ctx.download(sr, (n, k + 1, 2), np.uint32)
-    p = 0
     for d in range(n_ranks):
-        for t in pairs[d]:
-            assert np.array_equal(got_x[p], x[t])
+        toks = [t for t in range(m) if d == my_rank or np.any(rec[t, 1:, 0] // epr == d)]
+        for i, t in enumerate(toks):
+            assert np.array_equal(got_x[d * cap + i], x[t])
             r = rec[t].copy()
             r[1:, 0] = np.where(r[1:, 0] // epr == d, r[1:, 0], host.MOE_NO_EXPERT)
-            assert np.array_equal(got_r[p], r)
-            p += 1
+            if d != my_rank:
+                r[0, 0] = host.MOE_NO_EXPERT
+            assert np.array_equal(got_r[d * cap + i], r)
+        assert (got_r[d * cap + len(toks):(d + 1) * cap, :, 0] == host.MOE_NO_EXPERT).all()
 
 
 def _free_port() -> int:
@@ -147,8 +143,9 @@ def _ep_rank_forward(rank, world, tokens_per_rank, seed):
     x = x_all[start:start + m]
     xo = ctx.put(x if m else np.zeros((1, H), np.float32))
     out = ctx.alloc(max(m, 1) * H * 4)
-    ops = ep.LibraryEpOps(ctx, arena, ids[0], ep.EpShape(H, E, FULL.top_k, world, m_max), xo, xo, out)
-    ep.exchange_forward(ops, None, m, 1.0)
+    ops = ep.LibraryEpOps(ctx, arena, ids[0], ep.EpShape(H, E, FULL.top_k, world, m_max), rank, xo, xo, out)
+    for _ in range(2):  # a second step checks that reused buffers hold nothing stale
+        ep.exchange_forward(ops, None, m, 1.0)
     torch.cuda.synchronize(dev)
     ctx.sync()
     got = ctx.download(out, (m, H)) if m else np.zeros((0, H), np.float32)
