@@ -228,13 +228,45 @@ def main():
     x_offs = [ctx.put(x) for x in xs]
     out_off = ctx.alloc(PREFILL_M * H * 4)
 
+    ep_graphs, ep_caps = [], []
+
     def make_step(lid, m, out):
         if ep_mode:
-            ops = ep.LibraryEpOps(ctx, arena, lid, ep.EpShape(H, E, sh.top_k, world, m), rank, 0, 0, out)
+            xin_ep = ctx.alloc(m * H * 4)  # the captured step's fixed input rows
+            ops = ep.LibraryEpOps(ctx, arena, lid, ep.EpShape(H, E, sh.top_k, world, m), rank,
+                                  xin_ep, xin_ep, out)
+            nb = m * H * 4
+            arena[xin_ep:xin_ep + nb].zero_()
+            ep.exchange_forward(ops, None, m, 1.0)  # eager first step: caches, workspace
+            try:
+                ep_caps.append(ep.CapturedExchange(ops, None, m, 1.0))
+                ok = 1
+            except Exception as e:  # noqa: BLE001 - reported in the JSON line
+                ok, why = 0, type(e).__name__
+            # every rank replays a graph or none does (collectives must match)
+            flag = torch.tensor([ok], device=arena.device)
+            dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+            if int(flag.item()):
+                ci = len(ep_caps) - 1
+                ep_graphs.append("captured")
+            else:
+                if ok:
+                    ep_caps.pop()
+                ci = None
+                ep_graphs.append("eager" + ("" if ok else f" ({why})"))
 
             def step(x_off):
-                ops.x_off = ops.resid_off = x_off
+                if x_off != xin_ep:
+                    arena[xin_ep:xin_ep + nb].copy_(arena[x_off:x_off + nb])
+                if ci is not None:
+                    ep_caps[ci].replay()
+                else:
+                    ep.exchange_forward(ops, None, m, 1.0)
+
+            def eager(x_off):
+                arena[xin_ep:xin_ep + nb].copy_(arena[x_off:x_off + nb])
                 ep.exchange_forward(ops, None, m, 1.0)
+            step.eager = eager
         else:
             ctx.reserve(lid, m)
 
@@ -266,6 +298,11 @@ def main():
         ev1.record(stream)
         torch.cuda.synchronize()
     launches = ctx.launch_count() - l0
+    if ep_caps:  # graph replays do not pass through the library's launch counter
+        l1 = ctx.launch_count()
+        step.eager(x_offs[W])
+        torch.cuda.synchronize()
+        launches = (ctx.launch_count() - l1) * K
     ms = _max_over_ranks(ev0.elapsed_time(ev1) / K, world)
     _barrier(world)
     value = world * PREFILL_M / (ms / 1e3)
@@ -273,7 +310,7 @@ def main():
     # ---- per-stage device times (profiling pass, not the timed run) -------------------------
     ctx.profile(True)
     for i in range(K):
-        step(x_offs[W + i])
+        getattr(step, "eager", step)(x_offs[W + i])
     stages = ctx.profile_read()
     ctx.profile(False)
     # distinct experts whose weights this GPU streams (all ranks' tokens reach a rank's experts)
@@ -396,10 +433,14 @@ def main():
                            "expert_kernels": {0: "auto (tcgen05, A in TMEM)", 1: "CUDA-core GEMV",
                                               2: "tcgen05, A in smem", 3: "tcgen05, A in TMEM"}[args.path],
                            "distinct_experts_per_gpu": round(statistics.mean(distinct), 1),
+                           "ep_step": ep_graphs[0] if ep_graphs else None,
                            "l2": "weights 430 MB per layer exceed the 126 MB L2; fresh tokens per step"},
                 "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches,
                 "clocks": clk.summary(), "decode": decode, "config3": config3}
         print(json.dumps(line), flush=True)
+    torch.cuda.synchronize()
+    ep_caps.clear()  # captured NCCL work must be released before the process group
+    _barrier(world)
     ctx.close()
     del arena
     if world > 1:

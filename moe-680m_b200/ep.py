@@ -137,3 +137,26 @@ class LibraryEpOps:
     def combine(self, m, scale):
         self.ctx.ep_combine(self.sh.n_ranks, self.sh.capacity, self.sh.hidden, m, self.plan, self.yb_off,
                             self.resid_off, self.out_off, scale)
+
+
+class CapturedExchange:
+    """One layer step of ``exchange_forward`` captured in a CUDA graph (library kernels and
+    NCCL collectives), replayed with ``replay()``: no per-step host work beyond one launch.
+    The captured step reads its tokens at ``ops.x_off`` and writes ``ops.out_off``; callers
+    copy new tokens there between replays.  Run one eager step first (the library caches its
+    tensor maps and workspace on first use; nothing may allocate during capture)."""
+
+    def __init__(self, ops: LibraryEpOps, group, m: int, scale: float):
+        self.ops = ops
+        self.graph = torch.cuda.CUDAGraph()
+        torch.cuda.synchronize(ops.device)
+        with torch.cuda.graph(self.graph, stream=ops.stream):
+            _exchange(ops, group, m, scale)
+        torch.cuda.synchronize(ops.device)
+
+    def replay(self):
+        caller = torch.cuda.current_stream(self.ops.device)
+        self.ops.stream.wait_stream(caller)
+        with torch.cuda.stream(self.ops.stream):
+            self.graph.replay()
+        caller.wait_stream(self.ops.stream)
