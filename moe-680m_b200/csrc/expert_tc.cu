@@ -79,6 +79,9 @@ constexpr int kRawRowBytes = 2 * kBlockBytes;      // 512 K of one weight row
 #ifndef MOE_TC_RAW_LDG
 #define MOE_TC_RAW_LDG 0    // 1: raw weights by the producers' own global loads
 #endif
+#ifndef MOE_TC_RAW_CPASYNC
+#define MOE_TC_RAW_CPASYNC 0  // 1: raw chunks by the raw-A warp's coalesced 16-byte cp.async
+#endif
 #ifndef MOE_TC_RAW_TMAP
 #define MOE_TC_RAW_TMAP 1   // 0: raw chunks with per-row bulk copies instead of tensor-map boxes
 #endif
@@ -215,7 +218,7 @@ expert_tc_kernel(const __grid_constant__ BMaps bmap, const TcArgs a) {
             mbar_init(&empty[i], 1);
         }
         for (int i = 0; i < kRaw; ++i) {
-            mbar_init(&rfull[i], 1);
+            mbar_init(&rfull[i], MOE_TC_RAW_CPASYNC == 2 ? kProdWarps * 32 : MOE_TC_RAW_CPASYNC ? 32 : 1);
             mbar_init(&rempty[i], kProdWarps * 32);
         }
         for (int i = 0; i < 2; ++i) {
@@ -225,6 +228,22 @@ expert_tc_kernel(const __grid_constant__ BMaps bmap, const TcArgs a) {
         *abort = 0;
         fence_mbar_init();
     }
+#if MOE_TC_RAW_CPASYNC == 2
+    // weight tile base of each of this CTA's items (row tile start, chunk 0), looked up once
+    // here so that issuing a chunk's copies involves no dependent global loads
+    constexpr int kMaxItemsCached = 128;
+    __shared__ const uint8_t* item_src[kMaxItemsCached];
+    {
+        const int my = (n_items - static_cast<int>(blockIdx.x) + static_cast<int>(gridDim.x) - 1) /
+                       static_cast<int>(gridDim.x);
+        for (int it = threadIdx.x; it < my && it < kMaxItemsCached; it += blockDim.x) {
+            const Item x = get_item(a, static_cast<int>(blockIdx.x) + it * static_cast<int>(gridDim.x));
+            const int mat = a.mat0 + x.rt / a.rt_per_mat;
+            item_src[it] = (mat == 0 ? a.tabs.w1 : mat == 1 ? a.tabs.w3 : a.tabs.w2)[x.bucket] +
+                           static_cast<size_t>((x.rt % a.rt_per_mat) * 128) * a.row_bytes;
+        }
+    }
+#endif
     if (warp == kMmaWarp) tmem_alloc(tmem_base_p, kTmemCols);
     if (warp == kTmaBWarp && lane < 4) tma_prefetch_desc(&bmap.m[lane]);
     tc_fence_before();
@@ -325,10 +344,53 @@ expert_tc_kernel(const __grid_constant__ BMaps bmap, const TcArgs a) {
         }
 #else
         int g = 0, rc = 0;
+#if MOE_TC_RAW_CPASYNC == 2
+        // The producers themselves copy raw chunks ahead with coalesced 16-byte cp.async
+        // (512 threads, ~4 copies each per chunk), so many more bytes are in flight per SM than
+        // one copy engine or one warp keeps.
+        const int my_items = (n_items - static_cast<int>(blockIdx.x) + static_cast<int>(gridDim.x) - 1) /
+                             static_cast<int>(gridDim.x);
+        const int total_rc = my_items > 0 ? my_items * nchunk : 0;
+        const int ptid = warp * 32 + lane;
+        // one cp.async group per chunk (empty past the end), so wait_group(kRaw - 2) before a
+        // chunk's plain rfull arrival means "this thread's copies of that chunk have landed"
+        auto issue_chunk = [&](int c) -> bool {
+            if (c >= total_rc) { asm volatile("cp.async.commit_group;" ::: "memory"); return true; }
+            const int slot = c % kRaw;
+            if (!mbar_wait(&rempty[slot], ((c / kRaw) & 1) ^ 1, abort)) return false;
+            const int it = c / nchunk, kc = c - it * nchunk;
+            const uint8_t* base;
+            if (it < kMaxItemsCached) {
+                base = item_src[it];
+            } else {
+                const Item x = get_item(a, static_cast<int>(blockIdx.x) + it * static_cast<int>(gridDim.x));
+                const int mat = a.mat0 + x.rt / a.rt_per_mat;
+                base = (mat == 0 ? a.tabs.w1 : mat == 1 ? a.tabs.w3 : a.tabs.w2)[x.bucket] +
+                       static_cast<size_t>((x.rt % a.rt_per_mat) * 128) * a.row_bytes;
+            }
+            const uint8_t* src = base + kc * kRawRowBytes;
+            uint8_t* dst = rst + slot * kRawBytes;
+            constexpr int kPieces = kRawRowBytes / 16;
+            for (int pc = ptid; pc < 128 * kPieces; pc += kProdWarps * 32) {
+                const int r = pc / kPieces, o = (pc - r * kPieces) * 16;
+                cp_async16_cg(dst + r * kRawRowBytes + o, src + static_cast<size_t>(r) * a.row_bytes + o);
+            }
+            asm volatile("cp.async.commit_group;" ::: "memory");
+            return true;
+        };
+        // kRaw-2 chunks ahead: the slot of chunk c+kRaw-2 was released by chunk c-2, long done,
+        // so issuing never waits for the slowest producer of the previous chunk
+        for (int c = 0; c < kRaw - 2; ++c) issue_chunk(c);
+#endif
         for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
             bool ok = true;
             for (int kc = 0; kc < nchunk && ok; ++kc, ++rc) {
                 const int rs = rc % kRaw;
+#if MOE_TC_RAW_CPASYNC == 2
+                if (!issue_chunk(rc + kRaw - 2)) { ok = false; break; }
+                asm volatile("cp.async.wait_group %0;" :: "n"(kRaw - 2) : "memory");
+                mbar_arrive(&rfull[rs]);
+#endif
                 if (!mbar_wait(&rfull[rs], (rc / kRaw) & 1, abort)) { ok = false; break; }
                 if (warp == 0 && lane == 0) TC_TRACE(5, 512 + rc);
                 const uint8_t* raw = rst + rs * kRawBytes + row * kRawRowBytes;
@@ -350,6 +412,9 @@ expert_tc_kernel(const __grid_constant__ BMaps bmap, const TcArgs a) {
             }
             if (!ok) break;
         }
+#if MOE_TC_RAW_CPASYNC == 2
+        asm volatile("cp.async.wait_all;" ::: "memory");
+#endif
 #endif
     } else if (warp == kMmaWarp) {
         // ---------------- MMA issuer (whole warp loops, one elected lane issues) ----------------
@@ -418,7 +483,35 @@ expert_tc_kernel(const __grid_constant__ BMaps bmap, const TcArgs a) {
         __syncwarp();
     } else if (warp == kTmaAWarp) {
         // ---------------- raw A loads (tensor-map variant only) ----------------
-#if MOE_TC_RAW_LDG
+#if MOE_TC_RAW_LDG || MOE_TC_RAW_CPASYNC == 2
+#elif MOE_TC_RAW_CPASYNC
+        // Rows of the chunk (272 bytes = 17 x 16 bytes, 16-byte aligned) by 16-byte cp.async
+        // from all 32 lanes: consecutive lanes copy consecutive 16-byte pieces, so one warp
+        // instruction covers 512 contiguous-ish bytes; each lane's copies complete on rfull.
+        int rc = 0;
+        constexpr int kPieces = kRawRowBytes / 16;
+        for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
+            const Item x = get_item(a, item);
+            const int mat = a.mat0 + x.rt / a.rt_per_mat;
+            const int row0 = (x.rt % a.rt_per_mat) * 128;
+            const uint8_t* w = (mat == 0 ? a.tabs.w1 : mat == 1 ? a.tabs.w3 : a.tabs.w2)[x.bucket] +
+                               static_cast<size_t>(row0) * a.row_bytes;
+            bool ok = true;
+            for (int kc = 0; kc < nchunk; ++kc, ++rc) {
+                const int rs = rc % kRaw;
+                if (!mbar_wait_warp(&rempty[rs], ((rc / kRaw) & 1) ^ 1, abort)) { ok = false; break; }
+                if (lane == 0) TC_TRACE(3, rc);
+                uint8_t* dst = rst + rs * kRawBytes;
+                const uint8_t* src = w + kc * kRawRowBytes;
+                for (int c = lane; c < 128 * kPieces; c += 32) {
+                    const int r = c / kPieces, o = (c - r * kPieces) * 16;
+                    cp_async16_cg(dst + r * kRawRowBytes + o, src + static_cast<size_t>(r) * a.row_bytes + o);
+                }
+                cp_async_mbar_arrive(&rfull[rs]);
+            }
+            if (!ok) break;
+        }
+        asm volatile("cp.async.wait_all;" ::: "memory");
 #elif MOE_TC_RAW_TMAP
         // The tensor-memory-access engine keeps only ~35 KB in flight per SM, which covers L2
         // latency but not HBM latency; tiles are therefore prefetched into L2 MOE_TC_L2_AHEAD

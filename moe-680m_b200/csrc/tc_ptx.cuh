@@ -23,7 +23,7 @@ __device__ __forceinline__ void fence_mbar_init() {
 
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
     asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.shared::cta.b64 st, [%0];\n\t}"
-                 ::"r"(smem_u32(bar)) : "memory");
+                 ::"r"(tc::smem_u32(bar)) : "memory");
 }
 
 __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
@@ -176,7 +176,7 @@ __device__ __forceinline__ void mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_
 // Arrive once on `bar` when all previously issued MMAs of this thread have completed.
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
-                 ::"r"(smem_u32(bar)) : "memory");
+                 ::"r"(tc::smem_u32(bar)) : "memory");
 }
 
 // Each thread of the warp stores 32 consecutive 32-bit columns of its own TMEM lane.
@@ -252,4 +252,13 @@ __host__ __device__ constexpr uint32_t idesc_f16(int M, int N) {
 }
 
 }  // namespace tc
+// 16-byte cp.async (L2 only) into shared memory, and an mbarrier arrival (without a pending
+// count increment) once all of this thread's earlier cp.async copies have landed.
+__device__ __forceinline__ void cp_async16_cg(void* smem, const void* gmem) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" :: "r"(tc::smem_u32(smem)), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_mbar_arrive(uint64_t* bar) {
+    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" :: "r"(tc::smem_u32(bar)) : "memory");
+}
+
 }  // namespace moe
