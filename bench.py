@@ -38,6 +38,9 @@ PREFILL_M = 512
 ZIPF = 1.1
 CPU_SAMPLE_TOKENS = 512
 CONFIG3_M = 8192
+CONFIG2_LAYERS = 40
+CONFIG2_STEPS = 256
+CONFIG4_M = 64
 
 
 def load_pkg():
@@ -209,7 +212,9 @@ def main():
     epr = E // world
     my_experts = range(rank * epr, (rank + 1) * epr) if ep_mode else None
     only_prefill = args.only == "prefill"
-    n_dec_layers = 0 if only_prefill else 16  # decode cycles through 16 layers (6.9 GB): no L2 hits
+    # decode layers: the 40-layer stack of config 2 (17 GB); the single-layer decode leg cycles
+    # through them (no L2 hits)
+    n_dec_layers = 0 if only_prefill else CONFIG2_LAYERS
     c3_tokens = CONFIG3_M // world
     arena_bytes = ((n_dec_layers + 1) * sh.expert_bytes * (E + 1)
                    + (0 if only_prefill else 2 * sh.expert_bytes * (E + 1))
@@ -339,7 +344,7 @@ def main():
                 "layer_frac": layer_bytes / (ms / 1e3) / 1e9 / hbm,
                 "stage_ms": {k: round(v, 4) for k, v in stage_ms.items()}}
 
-    e2e, decode, cpu, config3 = None, None, None, None
+    e2e, decode, cpu, config3, config2, config4 = None, None, None, None, None, None
     if not only_prefill:
         # ---- end to end through the public API: pinned host buffers, copies inside --------------
         hx = [torch.from_numpy(x).pin_memory() for x in xs[:4]]
@@ -410,8 +415,63 @@ def main():
                   "layer_achieved_gbs": dec_bytes / (dms / 1e3) / 1e9,
                   "layer_frac": dec_bytes / (dms / 1e3) / 1e9 / hbm,
                   "alg_bytes_per_token": dec_bytes, "stage_us": {k: round(v * 1e3, 2) for k, v in dstages.items()},
-                  "l2": "16 layers (6.9 GB) cycled, a fresh token per step",
+                  "l2": f"{n_dec_layers} layers ({n_dec_layers * sh.expert_bytes * (E + 1) / 1e9:.1f} GB) cycled, a fresh token per step",
                   "parallelism": "one GPU per replica" if world > 1 else "single GPU"}
+
+        # ---- config 2: 40-layer stack, x <- x + MoE(RMSNorm(x)) per layer, one token per step,
+        # 256 steps; one token step (40 x (RMSNorm + fused decode layer)) is a captured CUDA graph
+        x2, xn2 = ctx.alloc(H * 4), ctx.alloc(H * 4)
+        xt = [ctx.put(synth.tokens(SEED + 11, rank * 1000 + i, 1, H)) for i in range(CONFIG2_STEPS)]
+
+        def token_step():
+            for lid in dec_ids:
+                ctx.rms_norm(x2, xn2, 1, H, 1e-6)
+                ctx.forward(lid, xn2, x2, x2, 1)
+        arena[x2:x2 + H * 4].copy_(arena[xt[0]:xt[0] + H * 4])
+        token_step()  # eager first step (workspace)
+        torch.cuda.synchronize()
+        g2 = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g2, stream=stream):
+            token_step()
+        torch.cuda.synchronize()
+        ev0.record(stream)
+        for i in range(CONFIG2_STEPS):
+            arena[x2:x2 + H * 4].copy_(arena[xt[i]:xt[i] + H * 4])
+            g2.replay()
+        ev1.record(stream)
+        torch.cuda.synchronize()
+        us2 = ev0.elapsed_time(ev1) / CONFIG2_STEPS * 1e3
+        step_bytes = n_dec_layers * dec_bytes
+        config2 = {"layers": n_dec_layers, "steps": CONFIG2_STEPS, "tok_s": 1e6 / us2, "us_per_token": us2,
+                   "hbm_gbs": step_bytes / (us2 / 1e6) / 1e9, "hbm_frac": step_bytes / (us2 / 1e6) / 1e9 / hbm,
+                   "expert_bytes_resident_gb": n_dec_layers * sh.expert_bytes * (E + 1) / 1e9,
+                   "step": "CUDA graph of 40 x (RMSNorm, fused decode layer); fresh token copied in per step"}
+        del g2
+
+        # ---- config 4: batched decode, 64 independent tokens, both expert kernels ----------------
+        m4 = CONFIG4_M
+        x4 = [ctx.put(synth.tokens(SEED + 13, rank * 1000 + i, m4, H)) for i in range(4)]
+        o4 = ctx.alloc(m4 * H * 4)
+        lid4 = dec_ids[0]
+        routed4 = ctx.do_route(lid4, x4[0], m4, sh.top_k)[0]
+        d4 = len(np.unique(routed4)) + 1
+        config4 = {"tokens": m4, "distinct_experts_plus_shared": d4, "auto_choice": "tcgen05 (M > 8)"}
+        for name, path in (("gemv", 1), ("tcgen05", 3)):
+            ctx.set_path(path)
+            for i in range(3):
+                ctx.forward(lid4, x4[i % 4], x4[i % 4], o4, m4)
+            torch.cuda.synchronize()
+            k4 = 20
+            ev0.record(stream)
+            for i in range(k4):
+                ctx.forward(lid4, x4[i % 4], x4[i % 4], o4, m4)
+            ev1.record(stream)
+            torch.cuda.synchronize()
+            ms4 = ev0.elapsed_time(ev1) / k4
+            b4 = d4 * sh.expert_bytes
+            config4[name] = {"ms_per_step": ms4, "tok_s": m4 / (ms4 / 1e3), "hbm_gbs": b4 / (ms4 / 1e3) / 1e9,
+                             "hbm_frac": b4 / (ms4 / 1e3) / 1e9 / hbm}
+        ctx.set_path(args.path)
 
         # ---- CPU baseline (rank 0, N=1 only) ------------------------------------------------------
         if rank == 0 and world == 1 and not args.no_cpu:
@@ -436,7 +496,8 @@ def main():
                            "ep_step": ep_graphs[0] if ep_graphs else None,
                            "l2": "weights 430 MB per layer exceed the 126 MB L2; fresh tokens per step"},
                 "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches,
-                "clocks": clk.summary(), "decode": decode, "config3": config3}
+                "clocks": clk.summary(), "decode": decode, "config2": config2, "config3": config3,
+                "config4": config4}
         print(json.dumps(line), flush=True)
     torch.cuda.synchronize()
     ep_caps.clear()  # captured NCCL work must be released before the process group

@@ -515,7 +515,14 @@ void launch_decode(const Layer& L, const Workspace& ws, int* sync, int sm_count,
     a.h = ws.h;
     a.counter = reinterpret_cast<unsigned long long*>(sync);
     a.status = ws.status;
-    cudaFuncSetAttribute(decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kDecodeSmem));
+    // once per device (not during a stream capture that may follow the first call)
+    static bool attr_set[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64 || !attr_set[dev]) {
+        cudaFuncSetAttribute(decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kDecodeSmem));
+        if (dev >= 0 && dev < 64) attr_set[dev] = true;
+    }
     decode_kernel<<<sm_count, kDThreads, kDecodeSmem, s>>>(a);
 }
 
