@@ -548,7 +548,7 @@ int moe_sync(moe_ctx* c) {
     MOE_CUDA(c, cudaMemcpy(&st, c->ws.status, sizeof(int), cudaMemcpyDeviceToHost));
     if (st != 0) {
         cudaMemset(c->ws.status, 0, sizeof(int));
-        cudaMemset(c->ws.status + 16, 0, 64);  // the decode kernel's grid counter
+        cudaMemset(c->ws.status + 16, 0, 96);  // the decode kernel's grid counter and h maxima
         const char* what = st == moe::kDevBadExpert ? "expert id out of range"
                          : st == moe::kDevBadToken ? "token index out of range"
                          : st == moe::kDevOverflow ? "chunk list overflow" : "device error";

@@ -17,12 +17,14 @@
 // from global memory touches each line with several partial requests and is limited by the
 // SM's outstanding-request capacity.
 //
-// Gate/up dot products are integer: the IQ4_XS codes are exact bytes (kvalue + 128), x is
-// rounded to 16-bit fixed point with a power-of-two scale chosen from its largest magnitude,
-// and dp2a accumulates code x activation products of a 32-weight sub-block exactly in int32.
-// Each sub-block sum is then converted to f32, multiplied by its scale d*(ls-32) and
-// accumulated in f32 in a fixed order.  The only rounding besides f32 accumulation is the
-// 16-bit grid of x (relative step 2^-15 of max |x|).  The down projection is f32 throughout.
+// Expert dot products are integer: the IQ4_XS codes are exact bytes (kvalue + 128), the
+// activation row (x, or one slot of h) is rounded to 16-bit fixed point with a power-of-two
+// scale chosen from its largest magnitude, and dp2a accumulates code x activation products of a
+// 32-weight sub-block exactly in int32.  Each sub-block sum is then converted to f32, multiplied
+// by its scale d*(ls-32) and accumulated in f32 in a fixed order.  The only rounding besides
+// f32 accumulation is the 16-bit activation grid (relative step 2^-15 of the row maximum).  The
+// max |h| of a slot is gathered during phase 2 (per CTA, then one 64-bit atomicMax per slot
+// whose high word is the launch's epoch, so stale values of earlier launches always lose).
 //
 // Grid synchronisation uses one 64-bit counter that only grows: every CTA adds 1 at each of the
 // two arrival points, so a launch of G CTAs adds 2G and a launch finds its base by rounding the
@@ -59,7 +61,7 @@ constexpr int kDThreads = 32 * kDWarps;
 constexpr int kRouteWarp = kDWarps - 1;  // its units come last in the unit order
 constexpr uint64_t kSpinLimitNs = 100000000ull;  // 100 ms
 constexpr int kMaxH = 2048;                      // decode_supported limits
-constexpr int kMaxI = 1024;
+constexpr int kMaxI = 512;
 // 16-bit activation pairs in shared memory: sub-block sb (32 values) occupies words
 // [sb*kQW, sb*kQW+16); word 4w+i holds values 4w+i (low half) and 16+4w+i (high half), the
 // pairing of one IQ4_XS qs word's low and high nibbles.  Word 16 holds 128 * (sum of the 32
@@ -69,7 +71,7 @@ constexpr int kQW = 20;
 constexpr int kMaxRow13 = kMaxH / kQK * kBlockBytes;  // bytes of one W1/W3 row
 constexpr int kMaxRow2 = kMaxI / kQK * kBlockBytes;   // bytes of one W2 row
 constexpr size_t kDecodeSmem = sizeof(float) * padded_len(kMaxH) + sizeof(uint32_t) * (kMaxH / 32) * kQW +
-                               sizeof(float) * (kMaxTopK + 1) * padded_len(kMaxI) +
+                               sizeof(uint32_t) * (kMaxTopK + 1) * (kMaxI / 32) * kQW +
                                size_t(kDWarps) * 4 * kMaxRow13 + size_t(kDWarps) * (kMaxTopK + 1) * kMaxRow2;
 
 __device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
@@ -104,6 +106,7 @@ struct DecodeArgs {
     uint2* topk;          // [k+1] records (written by CTA 0 for inspection)
     float* h;             // [k+1][I]
     unsigned long long* counter;
+    unsigned long long* hmax;  // [k+1]: (launch epoch << 32) | bits of max |h| per slot
     int* status;
 };
 
@@ -120,7 +123,7 @@ __device__ __forceinline__ int dp2a_hi(uint32_t a, uint32_t b, int c) {
 
 // Exact integer dot of one IQ4_XS sub-block with 32 packed 16-bit activations (kQW layout):
 // sum over j of kv(code_j) * a_j.
-__device__ __forceinline__ int dot_subblk_i16(const SubBlk& s, const uint32_t* aq) {
+__device__ __noinline__ int dot_subblk_i16(const SubBlk& s, const uint32_t* aq) {
     const uint4* a4 = reinterpret_cast<const uint4*>(aq);
     const uint32_t w[4] = {s.q01.x, s.q01.y, s.q23.x, s.q23.y};
     int acc = -static_cast<int>(aq[16]);
@@ -176,14 +179,16 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const DecodeArgs a
     extern __shared__ __align__(16) float sm[];
     float* xs = sm;                                                      // padded f32 x (router)
     uint32_t* xq = reinterpret_cast<uint32_t*>(sm + padded_len(kMaxH));  // [H/32][kQW]
-    float* hs = reinterpret_cast<float*>(xq + kMaxH / 32 * kQW);         // padded f32 h [k+1][I]
-    uint8_t* st13 = reinterpret_cast<uint8_t*>(hs + (kMaxTopK + 1) * padded_len(kMaxI));  // W1/W3 rows
+    uint32_t* hq = xq + kMaxH / 32 * kQW;                                // [k+1][I/32][kQW]
+    uint8_t* st13 = reinterpret_cast<uint8_t*>(hq + (kMaxTopK + 1) * (kMaxI / 32) * kQW);  // W1/W3 rows
     uint8_t* st2 = st13 + kDWarps * 4 * kMaxRow13;                       // W2 rows
     __shared__ const uint8_t* tw[3][kMaxExperts + 1];  // expert weight pointers W1, W3, W2
     __shared__ unsigned long long base;
     __shared__ float red[kDWarps];
     __shared__ float wgt[kMaxTopK + 1];
     __shared__ int slot_e[kMaxTopK + 1];
+    __shared__ uint32_t s_hmax[kMaxTopK + 1];  // bits of max |h| per slot over this CTA's units
+    __shared__ float hscale[kMaxTopK + 1], hw[kMaxTopK + 1];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int gwarp = blockIdx.x * kDWarps + warp, nwarps = gridDim.x * kDWarps;
     const float* x = a.io->x;
@@ -243,6 +248,7 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const DecodeArgs a
         base = v - v % (2 * G);
         if (a.has_shared) slot_e[k] = E;
     }
+    if (tid <= kMaxTopK) s_hmax[tid] = 0u;
     float mx = 0.f;
 #pragma unroll
     for (int t = 0; t < kMaxH / (4 * kDThreads); ++t) {
@@ -325,7 +331,11 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const DecodeArgs a
         if (!x_finite) gt = up = __int_as_float(0x7fc00000);
         const int g = pw + t * nwarps;
         const int slot = g < g_sh ? k : (g - g_sh) / I, j = g < g_sh ? g : (g - g_sh) % I;
-        if (lane == 0) a.h[static_cast<size_t>(slot) * I + j] = silu_f(gt) * up;
+        if (lane == 0) {
+            const float hv = silu_f(gt) * up;
+            a.h[static_cast<size_t>(slot) * I + j] = hv;
+            atomicMax(&s_hmax[slot], __float_as_uint(fabsf(hv)));  // NaN bits exceed inf's
+        }
     };
     // runs units [t0, t1) of this warp; units t0 and t0+1 were issued (or committed empty)
     auto run_units = [&](int t0, int t1, auto&& issue) {
@@ -447,16 +457,49 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const DecodeArgs a
     if (pw < H) issue_row(pw);
     __syncthreads();  // this CTA's h rows are written
     DEC_TRACE(5);
+    // per-slot maxima of |h| from every CTA, tagged with this launch's epoch so that values
+    // left by earlier launches lose (no reset needed); released by the barrier arrival
+    const unsigned long long epoch = (base / (2 * G) + 1) << 32;
+    if (tid < ns) atomicMax(a.hmax + tid, epoch | s_hmax[tid]);
+    __syncthreads();
     if (tid == 0) {
         grid_arrive(a.counter);
         grid_wait(a.counter, base + 2 * G, a.status);
     }
     __syncthreads();
     DEC_TRACE(6);
-    for (int i = tid * 4; i < ns * I; i += kDThreads * 4) {
-        const int s = i / I, c = i - s * I;
-        *reinterpret_cast<float4*>(hs + s * padded_len(I) + padded_idx(c)) =
-            __ldcg(reinterpret_cast<const float4*>(a.h + i));
+    constexpr int kPairIt = ((kMaxTopK + 1) * kMaxI / 2 + kDThreads - 1) / kDThreads;
+    float hlo[kPairIt], hhi[kPairIt];
+#pragma unroll
+    for (int it = 0; it < kPairIt; ++it) {  // every load issued before any is used
+        const int q = tid + it * kDThreads;
+        if (q < ns * I / 2) {
+            const int j = (q >> 4) * 32 + ((q & 15) >> 2) * 4 + (q & 3);
+            hlo[it] = __ldcg(a.h + j);
+            hhi[it] = __ldcg(a.h + j + 16);
+        }
+    }
+    // h as 16-bit pairs per slot (kQW layout), scale from the slot's max |h|
+    if (tid < ns) {
+        const unsigned long long v = __ldcg(a.hmax + tid);
+        const float m = (v & ~0xFFFFFFFFull) == epoch ? __uint_as_float(static_cast<uint32_t>(v)) : __int_as_float(0x7fc00000);
+        const float sc = q16_scale(m);
+        hscale[tid] = sc;
+        hw[tid] = isfinite(m) ? wgt[tid] / sc : __int_as_float(0x7fc00000);
+    }
+    __syncthreads();
+#pragma unroll
+    for (int it = 0; it < kPairIt; ++it) {  // 16 consecutive lanes per sub-block
+        const int q = tid + it * kDThreads;
+        if (q >= ns * I / 2) break;
+        const int gsb = q >> 4, wi = q & 15;           // gsb = slot * (I/32) + sub-block
+        const float sc = hscale[gsb / (I / 32)];
+        const int lo = q16(hlo[it], sc), hi = q16(hhi[it], sc);
+        hq[gsb * kQW + wi] = (static_cast<uint32_t>(lo) & 0xFFFFu) | (static_cast<uint32_t>(hi) << 16);
+        int s16 = lo + hi;
+#pragma unroll
+        for (int o = 8; o > 0; o >>= 1) s16 += __shfl_xor_sync(0xffffffffu, s16, o);
+        if (wi == 0) hq[gsb * kQW + 16] = static_cast<uint32_t>(128 * s16);
     }
     __syncthreads();
     DEC_TRACE(7);
@@ -475,8 +518,8 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const DecodeArgs a
             if (s < ns) {
                 const SubBlk b = lds_subblk(st_d + s * kMaxRow2, sb);
                 const float d = iq4_subscale(b.hdr.x, b.hdr.y, sb & 7) *
-                                dot_subblk(b, hs + s * padded_len(I) + sb * 36);
-                y = fmaf(wgt[s], d, y);
+                                static_cast<float>(dot_subblk_i16(b, hq + (s * spr + sb) * kQW));
+                y = fmaf(hw[s], d, y);
             }
         }
         __syncwarp();  // staging free
@@ -514,6 +557,7 @@ void launch_decode(const Layer& L, const Workspace& ws, int* sync, int sm_count,
     a.topk = ws.topk;
     a.h = ws.h;
     a.counter = reinterpret_cast<unsigned long long*>(sync);
+    a.hmax = a.counter + 1;
     a.status = ws.status;
     // once per device (not during a stream capture that may follow the first call)
     static bool attr_set[64] = {};
