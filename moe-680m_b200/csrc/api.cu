@@ -304,7 +304,7 @@ int run_experts(Ctx* c, const Layer& L, uint32_t M, bool routed, bool shared, fl
         const int items13 = moe::max_tiles_for(static_cast<int>(M), slots, E, moe::tc_max_n(13)) * (2 * I / 128);
         moe::launch_tc13(L, ws.xmap, ws, items13, c->sm_count, a_tmem, c->stream);
         stage(c, "tc13", 1);
-        moe::launch_convert_h(ws.h, static_cast<int>(S), I, ws.h16, ws.hexp, c->stream);
+        moe::launch_convert_h(ws.h, static_cast<int>(S), ws.ranges + E + 1, I, ws.h16, ws.hexp, c->stream);
         stage(c, "convert_h", 1);
         const int items2 = moe::max_tiles_for(static_cast<int>(M), slots, E, moe::tc_max_n(2)) * (H / 128);
         moe::launch_tc2(L, ws.hmap, ws, items2, c->sm_count, a_tmem, c->stream);

@@ -700,12 +700,12 @@ convert_x_kernel(const IoArgs* __restrict__ io, const int* __restrict__ slot_pos
 // gu[p] = [g (I) | u (I)] f32 -> h = silu(g) * u -> dst[p][perm(k)] = fp16(h * 2^-e); sexp[p] = e.
 // One warp per slot; h is staged in shared memory (I <= 1024).
 __global__ void __launch_bounds__(256)
-convert_h_kernel(const float* __restrict__ gu, int n_rows, int I, __half* __restrict__ dst,
-                 int* __restrict__ sexp) {
+convert_h_kernel(const float* __restrict__ gu, int n_rows, const int* __restrict__ n_used, int I,
+                 __half* __restrict__ dst, int* __restrict__ sexp) {
     __shared__ __align__(16) float hs[8][1024];
     const int wib = threadIdx.x >> 5;
     const int p = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
-    if (p >= n_rows) return;
+    if (p >= n_rows || p >= *n_used) return;  // slot rows past the buckets' total are unused
     const float* g = gu + static_cast<size_t>(p) * 2 * I;
     const float* u = g + I;
     float* h = hs[wib];
@@ -764,9 +764,9 @@ void launch_convert_x(const IoArgs* x, const int* slot_pos, int M, int ns, int l
     convert_x_kernel<<<(M * 32 + 255) / 256, 256, 0, s>>>(x, slot_pos, M, ns, len, dst, sexp);
 }
 
-void launch_convert_h(const float* gu, int n_rows, int inter, __half* dst, int* sexp,
+void launch_convert_h(const float* gu, int n_rows, const int* n_used, int inter, __half* dst, int* sexp,
                       cudaStream_t s) {
-    convert_h_kernel<<<(n_rows * 32 + 255) / 256, 256, 0, s>>>(gu, n_rows, inter, dst, sexp);
+    convert_h_kernel<<<(n_rows * 32 + 255) / 256, 256, 0, s>>>(gu, n_rows, n_used, inter, dst, sexp);
 }
 
 void launch_tc13(const Layer& L, const BMaps& xmap, const Workspace& ws, int max_items,

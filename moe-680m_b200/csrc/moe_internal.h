@@ -183,7 +183,7 @@ int tc_max_n(int mode);
 bool tc_supported(int hidden, int inter);
 void launch_convert_x(const IoArgs* io, const int* slot_pos, int M, int ns, int len, __half* dst,
                       int* sexp, cudaStream_t s);
-void launch_convert_h(const float* gu, int n_rows, int inter, __half* dst, int* sexp,
+void launch_convert_h(const float* gu, int n_rows, const int* n_used, int inter, __half* dst, int* sexp,
                       cudaStream_t s);
 bool make_iq4_tmap(CUtensorMap* m, const void* base, uint64_t rows, uint64_t row_bytes);
 bool make_f32_tmap(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows);
