@@ -238,6 +238,12 @@ int moe_launch_count(moe_ctx* ctx, uint64_t* n);
  * dequant_iq4_xs primitive of shaders/common.glsl:59-86 for the GGUF block format). */
 int moe_dequant_iq4xs(moe_ctx* ctx, uint64_t src_off, uint64_t n_blocks, uint64_t dst_off);
 
+/* Decode n_blocks of the reference's own 36-byte weight blocks (shaders/common.glsl:59-86:
+ * 32 weights, f16 scales for weights 0-15 and 16-31, 5-bit codes, w = (q - 8) * d, subnormal
+ * scales flushed to zero) into f32 at dst_off (128 bytes per block), bit-exact with the shipped
+ * shaders' decode.  For checking or converting weights stored in that format. */
+int moe_dequant_ref36(moe_ctx* ctx, uint64_t src_off, uint64_t n_blocks, uint64_t dst_off);
+
 /* Fill n_blocks synthetic IQ4_XS blocks at dst_off (seeded counter-based generator: block b
  * is 17 little-endian words splitmix64(key + 17*(block_start+b) + i), then its f16 d is
  * replaced by f16(0.005 + 0.015*u), u = (word0 >> 40) * 2^-24).  Benchmark/test input only. */

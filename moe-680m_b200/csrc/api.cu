@@ -968,6 +968,16 @@ int moe_dequant_iq4xs(moe_ctx* c, uint64_t src_off, uint64_t n_blocks, uint64_t 
     return check_launch(c, "dequant");
 }
 
+int moe_dequant_ref36(moe_ctx* c, uint64_t src_off, uint64_t n_blocks, uint64_t dst_off) {
+    if (!c) return fail(c, MOE_E_INVALID, "NULL context");
+    if (n_blocks == 0) return MOE_OK;
+    if (!off_ok(c, src_off, n_blocks * 36, 4) || !off_ok(c, dst_off, n_blocks * 128, 4))
+        return fail(c, MOE_E_INVALID, "dequant_ref36 offsets invalid");
+    DeviceGuard g(c->device);
+    moe::launch_dequant_ref36(c->base + src_off, n_blocks, at<float>(c, dst_off), c->stream);
+    return check_launch(c, "dequant_ref36");
+}
+
 int moe_synth_iq4xs(moe_ctx* c, uint64_t dst_off, uint64_t key, uint64_t block_start,
                     uint64_t n_blocks) {
     if (!c) return fail(c, MOE_E_INVALID, "NULL context");

@@ -217,6 +217,7 @@ void launch_ep_combine(EpPlan plan, int M, int n_ranks, int H, const float* y_ba
                        float scale, float* out, cudaStream_t s);
 void launch_rms_norm(const float* x, float* y, int M, int H, float eps, cudaStream_t s);
 void launch_dequant(const uint8_t* src, uint64_t n_blocks, float* dst, cudaStream_t s);
+void launch_dequant_ref36(const uint8_t* src, uint64_t n_blocks, float* dst, cudaStream_t s);
 void launch_synth(uint8_t* dst, uint64_t key, uint64_t block_start, uint64_t n_blocks,
                   cudaStream_t s);
 

@@ -88,6 +88,35 @@ rms_norm_kernel(const float* __restrict__ x, float* __restrict__ y, int H, float
 
 }  // namespace
 
+// The reference's own 36-byte weight block (shaders/common.glsl:59-86, "IQ4_XS" there): 32
+// weights, f16 scales d0 (weights 0-15) and d2 (16-31) at bytes 0 and 2, low 4 bits of weight p
+// in byte 4 + p/2 (low nibble for even p), bit 4 in byte 20 + p/8, bit p%8; w = (q - 8) * d in
+// f32.  The shader's f16 -> f32 conversion flushes subnormals to signed zero and keeps inf/NaN;
+// this decoder does the same, so it reproduces the shipped shaders' weights bit for bit.
+__device__ __forceinline__ float ref_f16_to_f32(uint32_t b) {
+    const uint32_t sgn = (b & 0x8000u) << 16, e = (b & 0x7C00u) >> 10, m = b & 0x03FFu;
+    if (e == 0u) return __uint_as_float(sgn);
+    const uint32_t e32 = e == 31u ? 255u : e + 112u;
+    return __uint_as_float(sgn | (e32 << 23) | (m << 13));
+}
+
+__global__ void dequant_ref36_kernel(const uint8_t* __restrict__ src, uint64_t n_blocks,
+                                     float* __restrict__ dst) {
+    const uint64_t i = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x;  // weight
+    if (i >= n_blocks * 32) return;
+    const uint8_t* b = src + (i >> 5) * 36;
+    const uint32_t p = static_cast<uint32_t>(i & 31);
+    const uint32_t dbits = p < 16 ? (b[0] | (b[1] << 8)) : (b[2] | (b[3] << 8));
+    uint32_t q = (b[4 + (p >> 1)] >> ((p & 1) * 4)) & 0xFu;
+    q |= ((b[20 + (p >> 3)] >> (p & 7)) & 1u) << 4;
+    dst[i] = (static_cast<float>(q) - 8.0f) * ref_f16_to_f32(dbits);
+}
+
+void launch_dequant_ref36(const uint8_t* src, uint64_t n_blocks, float* dst, cudaStream_t s) {
+    const uint64_t n = n_blocks * 32;
+    dequant_ref36_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, s>>>(src, n_blocks, dst);
+}
+
 void launch_dequant(const uint8_t* src, uint64_t n_blocks, float* dst, cudaStream_t s) {
     const uint64_t threads = n_blocks * 32;
     dequant_kernel<<<static_cast<unsigned>((threads + 255) / 256), 256, 0, s>>>(src, n_blocks, dst);

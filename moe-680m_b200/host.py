@@ -34,7 +34,7 @@ EXPORTS = (
     "moe_bucket", "moe_forward", "moe_forward_routed", "moe_rms_norm", "moe_dequant_iq4xs",
     "moe_synth_iq4xs", "moe_profile", "moe_profile_read", "moe_launch_count", "moe_set_path",
     "moe_bucket_static", "moe_forward_topk", "moe_ep_plan_bytes", "moe_ep_dispatch",
-    "moe_ep_combine",
+    "moe_ep_combine", "moe_dequant_ref36",
 )
 
 PATH_AUTO, PATH_GEMV, PATH_TC_SMEM_A, PATH_TC_TMEM_A = 0, 1, 2, 3
@@ -98,6 +98,7 @@ def lib():
         "moe_forward_routed": (i32, [vp, u32, u64, u64, u64, u32, P(C.c_uint16), P(f32), P(f32)]),
         "moe_rms_norm": (i32, [vp, u64, u64, u32, u32, f32]),
         "moe_dequant_iq4xs": (i32, [vp, u64, u64, u64]),
+        "moe_dequant_ref36": (i32, [vp, u64, u64, u64]),
         "moe_synth_iq4xs": (i32, [vp, u64, u64, u64, u64]),
         "moe_profile": (i32, [vp, i32]),
         "moe_profile_read": (i32, [vp, P(StageStatC), i32, P(i32)]),
@@ -268,6 +269,9 @@ class Context:
 
     def dequant(self, src_off, n_blocks, dst_off):
         self._check(lib().moe_dequant_iq4xs(self.h, src_off, n_blocks, dst_off))
+
+    def dequant_ref36(self, src_off, n_blocks, dst_off):
+        self._check(lib().moe_dequant_ref36(self.h, src_off, n_blocks, dst_off))
 
     def synth_iq4xs(self, dst_off, key, block_start, n_blocks):
         self._check(lib().moe_synth_iq4xs(self.h, dst_off, key, block_start, n_blocks))

@@ -58,6 +58,33 @@ def dequant_iq4xs(blocks: np.ndarray) -> np.ndarray:
     return (dl[:, :, None] * kv).reshape(n, QK_K).astype(np.float32)
 
 
+def ref36_f16_to_f32(bits: np.ndarray) -> np.ndarray:
+    """The reference shaders' f16 -> f32 conversion (shaders/common.glsl:20-36): subnormals
+    flush to signed zero, exponent 31 maps to 255 (inf / NaN), otherwise exponent + 112."""
+    b = bits.astype(np.uint32)
+    s = (b & 0x8000) << 16
+    e = (b & 0x7C00) >> 10
+    m = b & 0x03FF
+    e32 = np.where(e == 31, 255, e + 112)
+    out = np.where(e == 0, s, s | (e32 << 23) | (m << 13)).astype(np.uint32)
+    return out.view(np.float32)
+
+
+def dequant_ref36(blocks: np.ndarray) -> np.ndarray:
+    """The reference's own 36-byte block (shaders/common.glsl:66-86) -> f32 [n x 32]: d0 @0
+    (weights 0-15), d2 @2 (16-31), low nibble of weight p in byte 4 + p/2 (even p: low half),
+    fifth bit in byte 20 + p/8 bit p%8; w = (q - 8) * d in f32."""
+    b = np.ascontiguousarray(blocks, dtype=np.uint8).reshape(-1, 36)
+    n = b.shape[0]
+    d0 = ref36_f16_to_f32(b[:, 0].astype(np.uint32) | (b[:, 1].astype(np.uint32) << 8))
+    d2 = ref36_f16_to_f32(b[:, 2].astype(np.uint32) | (b[:, 3].astype(np.uint32) << 8))
+    p = np.arange(32)
+    q = (b[:, 4 + (p >> 1)] >> ((p & 1) * 4)) & 0xF
+    q = q.astype(np.uint32) | (((b[:, 20 + (p >> 3)] >> (p & 7)) & 1).astype(np.uint32) << 4)
+    d = np.where(p[None, :] < 16, d0[:, None], d2[:, None]).astype(np.float32)
+    return ((q.astype(np.float32) - np.float32(8.0)) * d).astype(np.float32)
+
+
 def dequant_matrix(raw: np.ndarray, rows: int, cols: int) -> np.ndarray:
     return dequant_iq4xs(raw.reshape(-1, BLOCK_BYTES)).reshape(rows, cols)
 

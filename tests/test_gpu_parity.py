@@ -264,3 +264,23 @@ def test_decode_single_token_small(ctx, name):
         out, _ = run_forward(ctx, lid, x, x)
         ref = coracle.moe_forward(hl, x, x, acc64=True)
         check_close(out, ref["out64"], f"decode {name} t={t}")
+
+
+def test_dequant_ref36_bit_exact(ctx):
+    """The reference's own 36-byte block decode (shaders/common.glsl:59-86) on the device,
+    bit-exact against the oracle restatement, over random blocks including subnormal, inf and
+    NaN scales."""
+    rng = np.random.default_rng(36)
+    n = 50000
+    blk = rng.integers(0, 256, size=(n, 36), dtype=np.uint8)
+    special = np.array([0x0001, 0x8001, 0x7C00, 0xFC00, 0x7E00, 0x0400, 0x3C00], np.uint16)
+    blk[:len(special), 0:2] = special.view(np.uint8).reshape(-1, 2)
+    src = ctx.put(blk)
+    dst = ctx.alloc(n * 128)
+    ctx.dequant_ref36(src, n, dst)
+    ctx.sync()
+    got = ctx.download(dst, (n, 32))
+    ref = O.dequant_ref36(blk)
+    nan = np.isnan(ref)
+    assert np.array_equal(np.isnan(got), nan)  # NaN payloads are not compared
+    assert np.array_equal(got[~nan].view(np.uint32), ref[~nan].view(np.uint32))

@@ -138,3 +138,20 @@ def test_bucket_numpy_vs_c():
     ids2 = np.tile(np.arange(k, dtype=np.int32), (5, 1))
     r3, t3, _, _ = coracle.bucket(ids2, np.ones((5, k), np.float32), None, E, False)
     assert r3[k] == r3[E + 1] == 5 * k
+
+
+def test_ref36_decode_known_answers():
+    """The reference's 36-byte block: hand-built known answers (scales 1.0 / -0.5, a subnormal
+    scale flushed to zero, codes 0, 8, 31 through the fifth-bit byte)."""
+    blk = np.zeros((2, 36), np.uint8)
+    blk[0, 0:2] = np.array([1.0], np.float16).view(np.uint8)
+    blk[0, 2:4] = np.array([-0.5], np.float16).view(np.uint8)
+    blk[0, 4] = 0x80          # weight 0: low nibble 0; weight 1: high nibble 8
+    blk[0, 4 + 8] = 0x0F      # weight 16: low nibble 15
+    blk[0, 20 + 2] = 0x01     # weight 16: fifth bit -> q = 31
+    blk[1, 0:2] = np.array([1], np.uint16).view(np.uint8)  # subnormal f16: flushed
+    blk[1, 4] = 0x33
+    w = O.dequant_ref36(blk)
+    assert w[0, 0] == -8.0 and w[0, 1] == 0.0 and w[0, 16] == (31 - 8) * -0.5
+    assert w[0, 2] == -8.0 and w[0, 17] == 4.0    # q = 0 under both scales
+    assert np.all(w[1, :16] == 0.0)
