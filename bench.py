@@ -420,13 +420,13 @@ def main():
 
         # ---- config 2: 40-layer stack, x <- x + MoE(RMSNorm(x)) per layer, one token per step,
         # 256 steps; one token step (40 x (RMSNorm + fused decode layer)) is a captured CUDA graph
-        x2, xn2 = ctx.alloc(H * 4), ctx.alloc(H * 4)
+        x2, xb2 = ctx.alloc(H * 4), ctx.alloc(H * 4)
         xt = [ctx.put(synth.tokens(SEED + 11, rank * 1000 + i, 1, H)) for i in range(CONFIG2_STEPS)]
 
-        def token_step():
-            for lid in dec_ids:
-                ctx.rms_norm(x2, xn2, 1, H, 1e-6)
-                ctx.forward(lid, xn2, x2, x2, 1)
+        def token_step():  # moe_forward_norm: RMSNorm + layer + residual in one launch per layer
+            for li, lid in enumerate(dec_ids):
+                src, dst = (x2, xb2) if li % 2 == 0 else (xb2, x2)
+                ctx.forward_norm(lid, src, dst, 1, 1e-6)
         arena[x2:x2 + H * 4].copy_(arena[xt[0]:xt[0] + H * 4])
         token_step()  # eager first step (workspace)
         torch.cuda.synchronize()
@@ -445,7 +445,7 @@ def main():
         config2 = {"layers": n_dec_layers, "steps": CONFIG2_STEPS, "tok_s": 1e6 / us2, "us_per_token": us2,
                    "hbm_gbs": step_bytes / (us2 / 1e6) / 1e9, "hbm_frac": step_bytes / (us2 / 1e6) / 1e9 / hbm,
                    "expert_bytes_resident_gb": n_dec_layers * sh.expert_bytes * (E + 1) / 1e9,
-                   "step": "CUDA graph of 40 x (RMSNorm, fused decode layer); fresh token copied in per step"}
+                   "step": "CUDA graph of 40 fused (RMSNorm + decode layer + residual) launches; fresh token copied in per step"}
         del g2
 
         # ---- config 4: batched decode, 64 independent tokens, both expert kernels ----------------

@@ -155,6 +155,14 @@ int moe_bucket_static(uint32_t n_experts, uint32_t top_k, int has_shared, const 
 int moe_forward(moe_ctx* ctx, uint32_t layer_id, uint64_t x_off, uint64_t resid_off,
                 uint64_t out_off, uint32_t M);
 
+/* The layer with its pre-norm and residual, as one step of the reference's layer loop
+ * (src/inference.rs:474-482, 588-596 with attention replaced by identity):
+ *   out = x + scale * MoE(RMSNorm(x)),  RMSNorm(x) = x / sqrt(mean(x^2) + eps) (no gain).
+ * For one token the normalisation runs inside the fused decode kernel (one launch); otherwise
+ * an RMSNorm launch precedes the layer.  out_off must differ from x_off. */
+int moe_forward_norm(moe_ctx* ctx, uint32_t layer_id, uint64_t x_off, uint64_t out_off, uint32_t M,
+                     float eps);
+
 /* record_and_submit_moe with host routing (RoutingOutput rows as returned by moe_do_route):
  * experts and combine only; routed[M][k] ids, weights[M][k], shared_gate[M] (NULL: 1.0). */
 int moe_forward_routed(moe_ctx* ctx, uint32_t layer_id, uint64_t x_off, uint64_t resid_off,

@@ -102,6 +102,7 @@ int ensure_ws(Ctx* c, uint32_t M, uint32_t E, uint32_t k, uint32_t slots, uint32
     const size_t o_io = take(sizeof(moe::IoArgs));
     const size_t o_xh = take(sizeof(float) * M * H);
     const size_t o_xl = take(sizeof(float) * M * H);
+    const size_t o_xn = take(sizeof(float) * M * H);
     const size_t total = off;
     int* status = ws.status;
     ws.status = nullptr;
@@ -142,6 +143,7 @@ int ensure_ws(Ctx* c, uint32_t M, uint32_t E, uint32_t k, uint32_t slots, uint32
     ws.io = reinterpret_cast<moe::IoArgs*>(b + o_io);
     ws.xh = reinterpret_cast<float*>(b + o_xh);
     ws.xl = reinterpret_cast<float*>(b + o_xl);
+    ws.xn = reinterpret_cast<float*>(b + o_xn);
     ws.max_chunks = static_cast<uint32_t>(max_chunks);
     ws.status = status;
     return MOE_OK;
@@ -759,6 +761,40 @@ int moe_forward(moe_ctx* c, uint32_t layer_id, uint64_t x_off, uint64_t resid_of
         return graph_forward(c, layer_id, *L, M, x, resid, out);
     prof_begin(c);
     rc = record_forward(c, *L, M, x, resid, out);
+    prof_end(c);
+    return rc;
+}
+
+int moe_forward_norm(moe_ctx* c, uint32_t layer_id, uint64_t x_off, uint64_t out_off, uint32_t M,
+                     float eps) {
+    if (!c) return fail(c, MOE_E_INVALID, "NULL context");
+    Layer* L;
+    int rc = get_layer(c, layer_id, &L);
+    if (rc) return rc;
+    if (L->subset())
+        return fail(c, MOE_E_UNSUPPORTED, "expert-subset layer: route with moe_route and run moe_forward_topk");
+    if (!(eps >= 0.f)) return fail(c, MOE_E_INVALID, "eps must be >= 0");
+    if (M == 0) return MOE_OK;
+    if ((rc = check_tokens(c, *L, x_off, M, "x"))) return rc;
+    if ((rc = check_tokens(c, *L, out_off, M, "out"))) return rc;
+    DeviceGuard g(c->device);
+    if ((rc = ensure_layer_ws(c, *L, M))) return rc;
+    const float* x = at<float>(c, x_off);
+    float* out = at<float>(c, out_off);
+    if (M == 1 && (c->path == moe::kPathAuto || c->path == moe::kPathGemv) && moe::decode_supported(*L) &&
+        out != x) {
+        // one launch: normalisation inside the fused decode kernel, direct pointers
+        moe::launch_decode(*L, c->ws, c->ws.status + 16, c->sm_count, c->stream, x, x, out, eps);
+        stage(c, "decode", 1);
+        return check_launch(c, "decode");
+    }
+    moe::launch_rms_norm(x, c->ws.xn, static_cast<int>(M), static_cast<int>(L->spec.hidden), eps, c->stream);
+    stage(c, "rms_norm", 1);
+    if ((rc = check_launch(c, "rms_norm"))) return rc;
+    if (c->use_graphs && !c->prof && !stream_capturing(c))
+        return graph_forward(c, layer_id, *L, M, c->ws.xn, x, out);
+    prof_begin(c);
+    rc = record_forward(c, *L, M, c->ws.xn, x, out);
     prof_end(c);
     return rc;
 }

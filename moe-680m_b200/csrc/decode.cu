@@ -94,7 +94,11 @@ __device__ __forceinline__ SubBlk lds_subblk(const uint8_t* row, int sb) {
 }
 
 struct DecodeArgs {
-    const IoArgs* io;
+    const IoArgs* io;     // activation pointers in device memory (graph replay), or null:
+    const float* x_direct;       // ... then these (a direct launch)
+    const float* resid_direct;
+    float* out_direct;
+    float norm_eps;       // >= 0: the layer input is RMSNorm(x) (no gain), the residual x
     const float* wr;      // [E][H]
     const float* bias;    // [E] or null
     const float* gate_w;  // [H] or null (gate 1.0)
@@ -191,7 +195,7 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const DecodeArgs a
     __shared__ float hscale[kMaxTopK + 1], hw[kMaxTopK + 1];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int gwarp = blockIdx.x * kDWarps + warp, nwarps = gridDim.x * kDWarps;
-    const float* x = a.io->x;
+    const float* x = a.io ? a.io->x : a.x_direct;
     const int H = a.H, I = a.I, E = a.E, k = a.k;
     const int ns = k + (a.has_shared ? 1 : 0);
     const unsigned long long G = gridDim.x;
@@ -249,6 +253,32 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const DecodeArgs a
         if (a.has_shared) slot_e[k] = E;
     }
     if (tid <= kMaxTopK) s_hmax[tid] = 0u;
+    if (a.norm_eps >= 0.f) {
+        // RMSNorm of the layer input (rms_norm.comp: x / sqrt(mean(x^2) + eps), no gain), the
+        // sum of squares reduced in a fixed order in every CTA
+        float ss = 0.f;
+#pragma unroll
+        for (int t = 0; t < kMaxH / (4 * kDThreads); ++t) {
+            const int i = (tid + t * kDThreads) * 4;
+            if (i < H) {
+                const float4 v = xv4[t];
+                ss = fmaf(v.x, v.x, ss); ss = fmaf(v.y, v.y, ss);
+                ss = fmaf(v.z, v.z, ss); ss = fmaf(v.w, v.w, ss);
+            }
+        }
+        ss = warp_sum(ss);
+        if (lane == 0) red[warp] = ss;
+        __syncthreads();
+        float tot = 0.f;
+#pragma unroll
+        for (int w = 0; w < kDWarps; ++w) tot += red[w];
+        const float r = 1.0f / sqrtf(tot / static_cast<float>(H) + a.norm_eps);
+        __syncthreads();  // red[] reused below
+#pragma unroll
+        for (int t = 0; t < kMaxH / (4 * kDThreads); ++t) {
+            xv4[t].x *= r; xv4[t].y *= r; xv4[t].z *= r; xv4[t].w *= r;
+        }
+    }
     float mx = 0.f;
 #pragma unroll
     for (int t = 0; t < kMaxH / (4 * kDThreads); ++t) {
@@ -506,8 +536,8 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const DecodeArgs a
     const int spr = I / 32, G2 = 32 / spr;
     const int gi = lane / spr, sb = lane - gi * spr;
     const int nslot = (ns + G2 - 1) / G2;
-    const float* resid = a.io->resid;
-    float* out = a.io->out;
+    const float* resid = a.io ? a.io->resid : a.resid_direct;
+    float* out = a.io ? a.io->out : a.out_direct;
     for (int n = pw; n < H; n += nwarps) {
         cp_wait<0>();
         __syncwarp();
@@ -540,9 +570,14 @@ bool decode_supported(const Layer& L) {
            L.spec.inter <= kMaxI && L.spec.inter % 512 == 0 && L.spec.n_experts <= kMaxExperts;
 }
 
-void launch_decode(const Layer& L, const Workspace& ws, int* sync, int sm_count, cudaStream_t s) {
+void launch_decode(const Layer& L, const Workspace& ws, int* sync, int sm_count, cudaStream_t s,
+                   const float* x, const float* resid, float* out, float norm_eps) {
     DecodeArgs a;
-    a.io = ws.io;
+    a.io = x ? nullptr : ws.io;
+    a.x_direct = x;
+    a.resid_direct = resid;
+    a.out_direct = out;
+    a.norm_eps = norm_eps;
     a.wr = reinterpret_cast<const float*>(L.router_w_ptr);
     a.bias = reinterpret_cast<const float*>(L.bias_ptr);
     a.gate_w = reinterpret_cast<const float*>(L.gate_ptr);

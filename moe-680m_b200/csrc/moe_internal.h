@@ -107,7 +107,8 @@ struct Workspace {
     __half* h16 = nullptr;        // [S][I]
     int* xexp = nullptr;          // [S] power-of-two exponent of x16's scale
     float* xh = nullptr;          // [M][H] TF32 part of x (tensor-core router)
-    float* xl = nullptr;          // [M][H] remainder
+    float* xl = nullptr;
+    float* xn = nullptr;  // [M][H] normalised layer input (moe_forward_norm)          // [M][H] remainder
     CUtensorMap xhmap, xlmap;
     const void* xh_base = nullptr;
     uint64_t xh_rows = 0, xh_cols = 0;
@@ -198,7 +199,11 @@ void launch_tc2(const Layer& L, const BMaps& hmap, const Workspace& ws, int max_
                 int sm_count, bool a_tmem, cudaStream_t s);
 bool make_fp16_tmaps(BMaps* m, const void* base, uint64_t rows, uint64_t cols);
 bool decode_supported(const Layer& L);
-void launch_decode(const Layer& L, const Workspace& ws, int* sync, int sm_count, cudaStream_t s);
+// x == nullptr: activation pointers from ws.io; otherwise direct pointers, and norm_eps >= 0
+// normalises x (RMSNorm) for the layer while x stays the residual when resid == x.
+void launch_decode(const Layer& L, const Workspace& ws, int* sync, int sm_count, cudaStream_t s,
+                   const float* x = nullptr, const float* resid = nullptr, float* out = nullptr,
+                   float norm_eps = -1.0f);
 void launch_combine(const Layer& L, const Workspace& ws, const IoArgs* io, int M, int ns,
                     float scale, cudaStream_t s);
 // Expert-parallel dispatch plan (arena or workspace memory): mask[M], pos[M][n_ranks],

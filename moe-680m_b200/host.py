@@ -34,7 +34,7 @@ EXPORTS = (
     "moe_bucket", "moe_forward", "moe_forward_routed", "moe_rms_norm", "moe_dequant_iq4xs",
     "moe_synth_iq4xs", "moe_profile", "moe_profile_read", "moe_launch_count", "moe_set_path",
     "moe_bucket_static", "moe_forward_topk", "moe_ep_plan_bytes", "moe_ep_dispatch",
-    "moe_ep_combine", "moe_dequant_ref36",
+    "moe_ep_combine", "moe_dequant_ref36", "moe_forward_norm",
 )
 
 PATH_AUTO, PATH_GEMV, PATH_TC_SMEM_A, PATH_TC_TMEM_A = 0, 1, 2, 3
@@ -99,6 +99,7 @@ def lib():
         "moe_rms_norm": (i32, [vp, u64, u64, u32, u32, f32]),
         "moe_dequant_iq4xs": (i32, [vp, u64, u64, u64]),
         "moe_dequant_ref36": (i32, [vp, u64, u64, u64]),
+        "moe_forward_norm": (i32, [vp, u32, u64, u64, u32, f32]),
         "moe_synth_iq4xs": (i32, [vp, u64, u64, u64, u64]),
         "moe_profile": (i32, [vp, i32]),
         "moe_profile_read": (i32, [vp, P(StageStatC), i32, P(i32)]),
@@ -241,6 +242,10 @@ class Context:
 
     def forward(self, layer: int, x_off: int, resid_off: int, out_off: int, m: int):
         self._check(lib().moe_forward(self.h, layer, x_off, resid_off, out_off, m))
+
+    def forward_norm(self, layer: int, x_off: int, out_off: int, m: int, eps: float = 1e-6):
+        """out = x + MoE(RMSNorm(x)) (one step of the layer stack)."""
+        self._check(lib().moe_forward_norm(self.h, layer, x_off, out_off, m, eps))
 
     def forward_routed(self, layer, x_off, resid_off, out_off, m, routed, weights, gate=None):
         r = np.ascontiguousarray(routed, np.uint16)

@@ -284,3 +284,26 @@ def test_dequant_ref36_bit_exact(ctx):
     nan = np.isnan(ref)
     assert np.array_equal(np.isnan(got), nan)  # NaN payloads are not compared
     assert np.array_equal(got[~nan].view(np.uint32), ref[~nan].view(np.uint32))
+
+
+@pytest.mark.parametrize("m", [1, 17])
+def test_forward_norm_matches_oracle(ctx, m):
+    """out = x + MoE(RMSNorm(x)) (one step of the config-2 layer stack): the fused decode kernel
+    for one token, RMSNorm + layer otherwise; against the f64 oracle and against the separate
+    moe_rms_norm + moe_forward calls."""
+    lid, hl = model(ctx, 21, FULL)
+    x = synth.tokens(21, 50 + m, m, FULL.hidden) * 3.0
+    xo = ctx.put(x)
+    out = ctx.alloc(x.nbytes)
+    ctx.forward_norm(lid, xo, out, m, 1e-6)
+    xn = ctx.alloc(x.nbytes)
+    out2 = ctx.alloc(x.nbytes)
+    ctx.rms_norm(xo, xn, m, FULL.hidden, 1e-6)
+    ctx.forward(lid, xn, xo, out2, m)
+    ctx.sync()
+    got = ctx.download(out, x.shape)
+    sep = ctx.download(out2, x.shape)
+    xn_ref = O.rms_norm(x, 1e-6)
+    ref = coracle.moe_forward(hl, xn_ref.astype(np.float32), x)["out64"]
+    check_close(got, ref, f"forward_norm m={m}")
+    assert O.rel_l2(got, sep) < 1e-5
