@@ -423,6 +423,9 @@ def main():
         x2, xb2 = ctx.alloc(H * 4), ctx.alloc(H * 4)
         xt = [ctx.put(synth.tokens(SEED + 11, rank * 1000 + i, 1, H)) for i in range(CONFIG2_STEPS)]
 
+        for li, lid in enumerate(dec_ids):  # layer l prefetches layer l+1's fixed weights
+            ctx.layer_set_next(lid, dec_ids[(li + 1) % len(dec_ids)])
+
         def token_step():  # moe_forward_norm: RMSNorm + layer + residual in one launch per layer
             for li, lid in enumerate(dec_ids):
                 src, dst = (x2, xb2) if li % 2 == 0 else (xb2, x2)

@@ -155,6 +155,12 @@ int moe_bucket_static(uint32_t n_experts, uint32_t top_k, int has_shared, const 
 int moe_forward(moe_ctx* ctx, uint32_t layer_id, uint64_t x_off, uint64_t resid_off,
                 uint64_t out_off, uint32_t M);
 
+/* Declare that layer next_id runs after layer_id (-1: none).  The single-token kernel of
+ * layer_id then prefetches next_id's router weight and shared expert into L2 while it finishes,
+ * so a layer stack decodes with those reads served from L2 (no counterpart in the reference,
+ * whose layers run as separate submissions).  Set it before capturing a CUDA graph. */
+int moe_layer_set_next(moe_ctx* ctx, uint32_t layer_id, int32_t next_id);
+
 /* The layer with its pre-norm and residual, as one step of the reference's layer loop
  * (src/inference.rs:474-482, 588-596 with attention replaced by identity):
  *   out = x + scale * MoE(RMSNorm(x)),  RMSNorm(x) = x / sqrt(mean(x^2) + eps) (no gain).

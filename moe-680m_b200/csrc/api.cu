@@ -765,6 +765,32 @@ int moe_forward(moe_ctx* c, uint32_t layer_id, uint64_t x_off, uint64_t resid_of
     return rc;
 }
 
+int moe_layer_set_next(moe_ctx* c, uint32_t layer_id, int32_t next_id) {
+    if (!c) return fail(c, MOE_E_INVALID, "NULL context");
+    Layer* L;
+    int rc = get_layer(c, layer_id, &L);
+    if (rc) return rc;
+    L->next_router = nullptr;
+    L->next_router_bytes = 0;
+    for (int i = 0; i < 3; ++i) { L->next_shared[i] = nullptr; L->next_shared_bytes[i] = 0; }
+    if (next_id < 0) return MOE_OK;
+    Layer* N;
+    if ((rc = get_layer(c, static_cast<uint32_t>(next_id), &N))) return rc;
+    const uint64_t H = N->spec.hidden, I = N->spec.inter, E = N->spec.n_experts;
+    L->next_router = N->router_w_ptr;
+    L->next_router_bytes = E * H * 4;
+    if (N->has_shared() && N->tab) {
+        std::vector<const uint8_t*> t(3 * (E + 1));
+        MOE_CUDA(c, cudaMemcpy(t.data(), N->tab, t.size() * sizeof(void*), cudaMemcpyDeviceToHost));
+        const uint64_t b13 = I * (H / 256) * 136, b2 = H * (I / 256) * 136;
+        for (int i = 0; i < 3; ++i) {
+            L->next_shared[i] = t[i * (E + 1) + E];
+            L->next_shared_bytes[i] = i == 2 ? b2 : b13;
+        }
+    }
+    return MOE_OK;
+}
+
 int moe_forward_norm(moe_ctx* c, uint32_t layer_id, uint64_t x_off, uint64_t out_off, uint32_t M,
                      float eps) {
     if (!c) return fail(c, MOE_E_INVALID, "NULL context");

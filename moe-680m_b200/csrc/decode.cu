@@ -99,6 +99,8 @@ struct DecodeArgs {
     const float* resid_direct;
     float* out_direct;
     float norm_eps;       // >= 0: the layer input is RMSNorm(x) (no gain), the residual x
+    const uint8_t* pf[4];  // next layer's router and shared W1, W3, W2 (L2 prefetch), or null
+    uint32_t pf_bytes[4];
     const float* wr;      // [E][H]
     const float* bias;    // [E] or null
     const float* gate_w;  // [H] or null (gate 1.0)
@@ -498,6 +500,16 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const DecodeArgs a
     }
     __syncthreads();
     DEC_TRACE(6);
+    if (pw >= H) {  // warps without an output row: pull the next layer's fixed weights into L2
+        const int idle = nwarps - H, me = pw - H;
+#pragma unroll 1
+        for (int r = 0; r < 4; ++r) {
+            if (!a.pf[r]) continue;
+            for (uint32_t o = (static_cast<uint32_t>(me) * 32 + lane) * 128; o < a.pf_bytes[r];
+                 o += static_cast<uint32_t>(idle) * 32 * 128)
+                asm volatile("prefetch.global.L2 [%0];" :: "l"(a.pf[r] + o));
+        }
+    }
     constexpr int kPairIt = ((kMaxTopK + 1) * kMaxI / 2 + kDThreads - 1) / kDThreads;
     float hlo[kPairIt], hhi[kPairIt];
 #pragma unroll
@@ -578,6 +590,12 @@ void launch_decode(const Layer& L, const Workspace& ws, int* sync, int sm_count,
     a.resid_direct = resid;
     a.out_direct = out;
     a.norm_eps = norm_eps;
+    a.pf[0] = L.next_router;
+    a.pf_bytes[0] = static_cast<uint32_t>(L.next_router_bytes);
+    for (int i = 0; i < 3; ++i) {
+        a.pf[1 + i] = L.next_shared[i];
+        a.pf_bytes[1 + i] = static_cast<uint32_t>(L.next_shared_bytes[i]);
+    }
     a.wr = reinterpret_cast<const float*>(L.router_w_ptr);
     a.bias = reinterpret_cast<const float*>(L.bias_ptr);
     a.gate_w = reinterpret_cast<const float*>(L.gate_ptr);

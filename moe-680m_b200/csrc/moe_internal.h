@@ -29,6 +29,12 @@ struct Layer {
     const uint8_t* router_w_ptr = nullptr;
     const uint8_t* bias_ptr = nullptr;  // may be null
     const uint8_t* gate_ptr = nullptr;  // may be null
+    // the layer that runs after this one (moe_layer_set_next): its router and shared expert are
+    // prefetched into L2 by the single-token kernel
+    const uint8_t* next_router = nullptr;
+    size_t next_router_bytes = 0;
+    const uint8_t* next_shared[3] = {nullptr, nullptr, nullptr};
+    size_t next_shared_bytes[3] = {0, 0, 0};
     CUtensorMap* wmaps = nullptr;       // device [3][E+1] raw IQ4_XS maps (W1, W3, W2), or null
                                         // when the shapes do not suit the tensor-core path
     float* wsplit = nullptr;            // device [2][E][H]: router weight split (TF32 hi, rest)

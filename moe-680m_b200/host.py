@@ -35,6 +35,7 @@ EXPORTS = (
     "moe_synth_iq4xs", "moe_profile", "moe_profile_read", "moe_launch_count", "moe_set_path",
     "moe_bucket_static", "moe_forward_topk", "moe_ep_plan_bytes", "moe_ep_dispatch",
     "moe_ep_combine", "moe_dequant_ref36", "moe_forward_norm",
+    "moe_layer_set_next",
 )
 
 PATH_AUTO, PATH_GEMV, PATH_TC_SMEM_A, PATH_TC_TMEM_A = 0, 1, 2, 3
@@ -100,6 +101,7 @@ def lib():
         "moe_dequant_iq4xs": (i32, [vp, u64, u64, u64]),
         "moe_dequant_ref36": (i32, [vp, u64, u64, u64]),
         "moe_forward_norm": (i32, [vp, u32, u64, u64, u32, f32]),
+        "moe_layer_set_next": (i32, [vp, u32, i32]),
         "moe_synth_iq4xs": (i32, [vp, u64, u64, u64, u64]),
         "moe_profile": (i32, [vp, i32]),
         "moe_profile_read": (i32, [vp, P(StageStatC), i32, P(i32)]),
@@ -219,6 +221,9 @@ class Context:
         self._check(lib().moe_layer_create(self.h, C.byref(c), _ptr(a1, C.c_uint64),
                                            _ptr(a3, C.c_uint64), _ptr(a2, C.c_uint64), C.byref(lid)))
         return lid.value
+
+    def layer_set_next(self, layer: int, next_layer: int):
+        self._check(lib().moe_layer_set_next(self.h, layer, next_layer))
 
     def reserve(self, layer: int, max_tokens: int):
         self._check(lib().moe_reserve(self.h, layer, max_tokens))

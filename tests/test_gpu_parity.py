@@ -307,3 +307,17 @@ def test_forward_norm_matches_oracle(ctx, m):
     ref = coracle.moe_forward(hl, xn_ref.astype(np.float32), x)["out64"]
     check_close(got, ref, f"forward_norm m={m}")
     assert O.rel_l2(got, sep) < 1e-5
+
+
+def test_layer_set_next_keeps_results(ctx):
+    """Prefetching the next layer's fixed weights into L2 changes no result bit."""
+    lid, _ = model(ctx, 21, FULL)
+    x = synth.tokens(21, 77, 1, FULL.hidden)
+    xo = ctx.put(x)
+    o1, o2 = ctx.alloc(x.nbytes), ctx.alloc(x.nbytes)
+    ctx.forward_norm(lid, xo, o1, 1)
+    ctx.layer_set_next(lid, lid)
+    ctx.forward_norm(lid, xo, o2, 1)
+    ctx.layer_set_next(lid, -1)
+    ctx.sync()
+    assert np.array_equal(ctx.download(o1, x.shape).view(np.uint32), ctx.download(o2, x.shape).view(np.uint32))
