@@ -327,15 +327,19 @@ void destroy_graph(moe::GraphEntry& g) {
     g.graph = nullptr;
 }
 
+bool use_decode(const Ctx* c, const Layer& L, uint32_t M) {
+    return M == 1 && (c->path == moe::kPathAuto || c->path == moe::kPathGemv) && moe::decode_supported(L);
+}
+
 int record_forward(Ctx* c, const Layer& L, uint32_t M, const float* x, const float* resid, float* out) {
-    run_set_io(c, x, resid, out);
-    if (M == 1 && (c->path == moe::kPathAuto || c->path == moe::kPathGemv) && moe::decode_supported(L)) {
-        // single token: the whole layer in one fused launch; its self-resetting grid-sync words
-        // live after the status word (zeroed at context creation)
-        moe::launch_decode(L, c->ws, c->ws.status + 16, c->sm_count, c->stream);
+    if (use_decode(c, L, M)) {
+        // single token: the whole layer in one fused launch with direct pointers (no graph or
+        // pointer block needed); its grid-sync words live after the status word
+        moe::launch_decode(L, c->ws, c->ws.status + 16, c->sm_count, c->stream, x, resid, out, -1.0f);
         stage(c, "decode", 1);
         return check_launch(c, "decode");
     }
+    run_set_io(c, x, resid, out);
     int rc = run_route(c, L, M);
     if (rc) return rc;
     return run_experts(c, L, M, true, L.has_shared(), L.spec.scale);
@@ -757,7 +761,7 @@ int moe_forward(moe_ctx* c, uint32_t layer_id, uint64_t x_off, uint64_t resid_of
     const float* x = at<float>(c, x_off);
     const float* resid = resid_off ? at<float>(c, resid_off) : nullptr;
     float* out = at<float>(c, out_off);
-    if (c->use_graphs && !c->prof && !stream_capturing(c))
+    if (c->use_graphs && !c->prof && !stream_capturing(c) && !use_decode(c, *L, M))
         return graph_forward(c, layer_id, *L, M, x, resid, out);
     prof_begin(c);
     rc = record_forward(c, *L, M, x, resid, out);
@@ -817,7 +821,7 @@ int moe_forward_norm(moe_ctx* c, uint32_t layer_id, uint64_t x_off, uint64_t out
     moe::launch_rms_norm(x, c->ws.xn, static_cast<int>(M), static_cast<int>(L->spec.hidden), eps, c->stream);
     stage(c, "rms_norm", 1);
     if ((rc = check_launch(c, "rms_norm"))) return rc;
-    if (c->use_graphs && !c->prof && !stream_capturing(c))
+    if (c->use_graphs && !c->prof && !stream_capturing(c) && !use_decode(c, *L, M))
         return graph_forward(c, layer_id, *L, M, c->ws.xn, x, out);
     prof_begin(c);
     rc = record_forward(c, *L, M, c->ws.xn, x, out);
