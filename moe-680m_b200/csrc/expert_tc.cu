@@ -86,7 +86,7 @@ constexpr int kRawRowBytes = 2 * kBlockBytes;      // 512 K of one weight row
 #define MOE_TC_RAW_TMAP 1   // 0: raw chunks with per-row bulk copies instead of tensor-map boxes
 #endif
 #ifndef MOE_TC_L2_AHEAD
-#define MOE_TC_L2_AHEAD 6   // raw chunks prefetched into L2 ahead of their tensor-map load
+#define MOE_TC_L2_AHEAD 0   // raw chunks prefetched into L2 ahead of their tensor-map load (0: none; measured fastest)
 #endif
 #ifndef MOE_TC_RAW_BOX
 #define MOE_TC_RAW_BOX 128
@@ -513,9 +513,8 @@ expert_tc_kernel(const __grid_constant__ BMaps bmap, const TcArgs a) {
         }
         asm volatile("cp.async.wait_all;" ::: "memory");
 #elif MOE_TC_RAW_TMAP
-        // The tensor-memory-access engine keeps only ~35 KB in flight per SM, which covers L2
-        // latency but not HBM latency; tiles are therefore prefetched into L2 MOE_TC_L2_AHEAD
-        // chunks before their load.
+        // Optionally, tiles are prefetched into L2 MOE_TC_L2_AHEAD chunks before their load
+        // (off by default: the prefetches compete with the loads and measured slower).
         if (lane == 0) {
             const int my_items = (n_items - static_cast<int>(blockIdx.x) + static_cast<int>(gridDim.x) - 1) /
                                  static_cast<int>(gridDim.x);
