@@ -43,14 +43,12 @@ namespace moe {
 __device__ unsigned long long g_dec_trace[160][16];
 __device__ volatile int g_route_done[160];  // per CTA: phase timestamps (debug builds)
 #define DEC_TRACE(i) do { if (blockIdx.x < 160 && threadIdx.x == 0) g_dec_trace[blockIdx.x][i] = tc::globaltimer_ns(); } while (0)
-#define DEC_CLK(i) do { if (blockIdx.x == 0 && threadIdx.x == 32 * kRouteWarp) g_dec_trace[159][i] = clock64(); } while (0)
 #define DEC_TRACE_R(i) do { if (blockIdx.x < 160 && threadIdx.x == 32 * kRouteWarp) g_dec_trace[blockIdx.x][i] = tc::globaltimer_ns(); } while (0)
 extern "C" int moe_debug_dec_trace(unsigned long long* out) {
     return cudaMemcpyFromSymbol(out, g_dec_trace, sizeof(g_dec_trace)) == cudaSuccess ? 0 : -2;
 }
 #else
 #define DEC_TRACE(i) do {} while (0)
-#define DEC_CLK(i) do {} while (0)
 #define DEC_TRACE_R(i) do {} while (0)
 #endif
 
@@ -393,7 +391,6 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const DecodeArgs a
         __syncwarp();
         DEC_TRACE_R(3);
         const float* lg = a.logits;
-        DEC_CLK(8);
         float pv[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) {  // unconditional (clamped) loads, so all issue at once
@@ -405,18 +402,14 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const DecodeArgs a
         float lmax = -INFINITY;
 #pragma unroll
         for (int i = 0; i < 8; ++i) if (lane + 32 * i < E) lmax = fmaxf(lmax, pv[i]);
-        DEC_CLK(9);
         lmax = warp_max(lmax);
-        DEC_CLK(10);
         float sum = 0.f;
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
             pv[i] = lane + 32 * i < E ? expf(pv[i] - lmax) : 0.f;
             sum += pv[i];
         }
-        DEC_CLK(11);
         sum = warp_sum(sum);
-        DEC_CLK(12);
         uint32_t key[8];
         uint32_t avail = 0;  // bit i: expert lane + 32 i exists and is not taken
 #pragma unroll
@@ -428,7 +421,6 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const DecodeArgs a
         }
         DEC_TRACE_R(9);
         for (int r = 0; r < k; ++r) {
-            DEC_CLK(r);
             uint32_t best = 0;
             int bi = -1;
 #pragma unroll
@@ -444,7 +436,6 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const DecodeArgs a
                 if (blockIdx.x == 0) a.topk[1 + r] = make_uint2(e, m);
             }
         }
-        DEC_CLK(13);
         if (lane == 0) {  // the shared-expert gate sigmoid(g . x), or 1 without a gate weight
             float gt = 1.0f;
             if (a.gate_w) {

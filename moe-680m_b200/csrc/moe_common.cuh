@@ -68,21 +68,10 @@ __device__ __forceinline__ float iq4_subscale(uint32_t h0, uint32_t h1, int ib) 
 }
 
 // Streaming 8-byte load that skips L1 allocation (weights are read once).
-#ifndef MOE_LDG_FLAVOR
-#define MOE_LDG_FLAVOR 0
-#endif
 __device__ __forceinline__ uint2 ldg_stream_u2(const void* p) {
     uint2 v;
-#if MOE_LDG_FLAVOR == 1
-    asm("ld.global.nc.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p));
-#elif MOE_LDG_FLAVOR == 2
-    asm("ld.global.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p));
-#elif MOE_LDG_FLAVOR == 3
-    asm("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p));
-#else
     asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];"
                  : "=r"(v.x), "=r"(v.y) : "l"(p));
-#endif
     return v;
 }
 
