@@ -41,6 +41,8 @@ CONFIG3_M = 8192
 CONFIG2_LAYERS = 40
 CONFIG2_STEPS = 256
 CONFIG4_M = 64
+VOCAB, VOCAB_HIDDEN = 248320, 2048  # the LM head (token_embd) of the reference model
+VOCAB_BYTES = VOCAB * VOCAB_HIDDEN // 256 * 136
 
 
 def load_pkg():
@@ -218,6 +220,7 @@ def main():
     c3_tokens = CONFIG3_M // world
     arena_bytes = ((n_dec_layers + 1) * sh.expert_bytes * (E + 1)
                    + (0 if only_prefill else 2 * sh.expert_bytes * (E + 1))
+                   + (0 if only_prefill else VOCAB_BYTES)
                    + (3 << 30))
     arena = torch.empty(arena_bytes, dtype=torch.uint8, device=torch.device("cuda", local))
     ctx = host.Context(local, arena_bytes, external_ptr=arena.data_ptr())
@@ -344,7 +347,7 @@ def main():
                 "layer_frac": layer_bytes / (ms / 1e3) / 1e9 / hbm,
                 "stage_ms": {k: round(v, 4) for k, v in stage_ms.items()}}
 
-    e2e, decode, cpu, config3, config2, config4 = None, None, None, None, None, None
+    e2e, decode, cpu, config3, config2, config4, lm_head = None, None, None, None, None, None, None
     if not only_prefill:
         # ---- end to end through the public API: pinned host buffers, copies inside --------------
         hx = [torch.from_numpy(x).pin_memory() for x in xs[:4]]
@@ -476,6 +479,29 @@ def main():
                              "hbm_frac": b4 / (ms4 / 1e3) / 1e9 / hbm}
         ctx.set_path(args.path)
 
+        # ---- LM head: 248,320 x 2048 IQ4_XS projection + greedy argmax (moe_vocab_logits) -----
+        wv = ctx.alloc(VOCAB_BYTES)
+        ctx.synth_iq4xs(wv, synth.tensor_key(SEED, 90, 0, 0), 0, VOCAB_BYTES // 136)
+        lm_head = {"vocab": VOCAB, "hidden": VOCAB_HIDDEN, "alg_bytes_per_launch": VOCAB_BYTES,
+                   "l2": "270 MB weight exceeds the 126 MB L2"}
+        for mv in (1, 8):
+            xv = [ctx.put(synth.tokens(SEED + 17, rank * 1000 + i, mv, VOCAB_HIDDEN)) for i in range(4)]
+            lv, iv = ctx.alloc(mv * VOCAB * 4), ctx.alloc(256)
+            for i in range(3):
+                ctx.vocab_logits(wv, VOCAB, VOCAB_HIDDEN, xv[i % 4], mv, lv, iv)
+            torch.cuda.synchronize()
+            kv = 50
+            ev0.record(stream)
+            for i in range(kv):
+                ctx.vocab_logits(wv, VOCAB, VOCAB_HIDDEN, xv[i % 4], mv, lv, iv)
+            ev1.record(stream)
+            torch.cuda.synchronize()
+            usv = ev0.elapsed_time(ev1) / kv * 1e3
+            ctx.sync()
+            gbs = VOCAB_BYTES / (usv / 1e6) / 1e9
+            lm_head[f"m{mv}"] = {"us_per_launch": usv, "hbm_gbs": gbs, "hbm_frac": gbs / hbm,
+                                 "outputs": "f32 logits + argmax ids"}
+
         # ---- CPU baseline (rank 0, N=1 only) ------------------------------------------------------
         if rank == 0 and world == 1 and not args.no_cpu:
             _, v, dt, n = cpu_baseline(sh, xs[0])
@@ -500,7 +526,7 @@ def main():
                            "l2": "weights 430 MB per layer exceed the 126 MB L2; fresh tokens per step"},
                 "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches,
                 "clocks": clk.summary(), "decode": decode, "config2": config2, "config3": config3,
-                "config4": config4}
+                "config4": config4, "lm_head": lm_head}
         print(json.dumps(line), flush=True)
     torch.cuda.synchronize()
     ep_caps.clear()  # captured NCCL work must be released before the process group

@@ -246,6 +246,23 @@ int moe_profile_read(moe_ctx* ctx, moe_stage_stat* out, int max, int* n);
 /* Number of kernels this context has launched since creation. */
 int moe_launch_count(moe_ctx* ctx, uint64_t* n);
 
+/* ---- vocabulary projection (LM head) -------------------------------------------------- */
+
+/* logits[m][n] = sum_h x[m][h] * W[n][h] for m < M, n < V: the LM head / MTP output-head
+ * projection of src/inference.rs:319-330 and :355-360 (shaders/attn_output.comp with
+ * M = 1, N = vocab), which the reference follows with a greedy argmax on the host
+ * (sampling::sample -> util::argmax, src/util.rs:66-76).
+ *   w_off      IQ4_XS matrix [V][H] in GGUF row layout (V rows of H/256 blocks), 16-byte aligned
+ *   x_off      f32 [M][H] activations (the final hidden state)
+ *   logits_off f32 [M][V] output, or 0 to skip writing logits
+ *   ids_off    u32 [M] output: per row the lowest index of the largest logit (NaN and -inf
+ *              never win; 0 when no logit exceeds -inf), or 0 to skip the argmax
+ * 1 <= M <= 8, 512 <= H <= 4096 with H % 512 == 0 (else MOE_E_UNSUPPORTED).  Activations are
+ * rounded to 16-bit fixed point per row (relative step 2^-15 of the row's largest magnitude);
+ * a row with a non-finite value gives NaN logits.  Stream-ordered on the context's stream. */
+int moe_vocab_logits(moe_ctx* ctx, uint64_t w_off, uint32_t V, uint32_t H, uint64_t x_off, uint32_t M,
+                     uint64_t logits_off, uint64_t ids_off);
+
 /* ---- weight utilities ------------------------------------------------------------------ */
 
 /* Decode n_blocks IQ4_XS blocks at src_off into f32 [n_blocks*256] at dst_off (exact; the

@@ -554,10 +554,12 @@ int moe_sync(moe_ctx* c) {
     MOE_CUDA(c, cudaMemcpy(&st, c->ws.status, sizeof(int), cudaMemcpyDeviceToHost));
     if (st != 0) {
         cudaMemset(c->ws.status, 0, sizeof(int));
-        cudaMemset(c->ws.status + 16, 0, 96);  // the decode kernel's grid counter and h maxima
+        // the decode kernel's grid counter and h maxima, the vocabulary argmax ticket and keys
+        cudaMemset(c->ws.status + 16, 0, 232 - 64);
         const char* what = st == moe::kDevBadExpert ? "expert id out of range"
                          : st == moe::kDevBadToken ? "token index out of range"
-                         : st == moe::kDevOverflow ? "chunk list overflow" : "device error";
+                         : st == moe::kDevOverflow ? "chunk list overflow"
+                         : st == moe::kDevTimeout ? "wait timed out" : "device error";
         return fail(c, MOE_E_DEVICE, "kernel reported status %d (%s)", st, what);
     }
     return MOE_OK;
@@ -1022,6 +1024,37 @@ int moe_rms_norm(moe_ctx* c, uint64_t x_off, uint64_t y_off, uint32_t M, uint32_
                          static_cast<int>(H), eps, c->stream);
     stage(c, "rms_norm", 1);
     return check_launch(c, "rms_norm");
+}
+
+int moe_vocab_logits(moe_ctx* c, uint64_t w_off, uint32_t V, uint32_t H, uint64_t x_off, uint32_t M,
+                     uint64_t logits_off, uint64_t ids_off) {
+    if (!c) return fail(c, MOE_E_INVALID, "NULL context");
+    if (M == 0 || V == 0) return MOE_OK;
+    if (!moe::vocab_supported(static_cast<int>(H), static_cast<int>(M)))
+        return fail(c, MOE_E_UNSUPPORTED, "vocab_logits: M=%u H=%u (need 1<=M<=8, H%%512==0, 512<=H<=4096)", M, H);
+    if (V > 0x7FFFFFF0u) return fail(c, MOE_E_UNSUPPORTED, "vocab_logits: V=%u too large", V);
+    if (logits_off == 0 && ids_off == 0) return fail(c, MOE_E_INVALID, "vocab_logits: no output");
+    const uint64_t wb = static_cast<uint64_t>(V) * (H / 256) * 136;
+    if (!off_ok(c, w_off, wb, 16)) return fail(c, MOE_E_INVALID, "vocab_logits weight offset invalid");
+    if (!off_ok(c, x_off, static_cast<uint64_t>(M) * H * 4, 4))
+        return fail(c, MOE_E_INVALID, "vocab_logits x offset invalid");
+    if (logits_off && !off_ok(c, logits_off, static_cast<uint64_t>(M) * V * 4, 4))
+        return fail(c, MOE_E_INVALID, "vocab_logits logits offset invalid");
+    if (ids_off && !off_ok(c, ids_off, static_cast<uint64_t>(M) * 4, 4))
+        return fail(c, MOE_E_INVALID, "vocab_logits ids offset invalid");
+    DeviceGuard g(c->device);
+    // argmax keys and the CTA ticket live in the status block, after the decode kernel's words
+    uint8_t* sb = reinterpret_cast<uint8_t*>(c->ws.status);
+    const int r = moe::launch_vocab(c->base + w_off, static_cast<int>(V), static_cast<int>(H),
+                                    at<float>(c, x_off), static_cast<int>(M),
+                                    logits_off ? at<float>(c, logits_off) : nullptr,
+                                    ids_off ? at<uint32_t>(c, ids_off) : nullptr,
+                                    reinterpret_cast<unsigned long long*>(sb + 168),
+                                    reinterpret_cast<unsigned int*>(sb + 160), c->ws.status, c->sm_count,
+                                    c->stream);
+    if (r != 0) return fail(c, MOE_E_UNSUPPORTED, "vocab_logits: H=%u does not fit shared memory", H);
+    stage(c, "vocab", 1);
+    return check_launch(c, "vocab_logits");
 }
 
 int moe_dequant_iq4xs(moe_ctx* c, uint64_t src_off, uint64_t n_blocks, uint64_t dst_off) {

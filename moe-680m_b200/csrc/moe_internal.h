@@ -229,6 +229,11 @@ void launch_ep_combine(EpPlan plan, int M, int n_ranks, int H, const float* y_ba
 void launch_rms_norm(const float* x, float* y, int M, int H, float eps, cudaStream_t s);
 void launch_dequant(const uint8_t* src, uint64_t n_blocks, float* dst, cudaStream_t s);
 void launch_dequant_ref36(const uint8_t* src, uint64_t n_blocks, float* dst, cudaStream_t s);
+bool vocab_supported(int H, int M);
+// Returns -1 when the shape does not fit the kernel's shared memory (nothing launched).
+int launch_vocab(const uint8_t* w, int V, int H, const float* x, int M, float* logits, uint32_t* ids,
+                 unsigned long long* keys, unsigned int* ticket, int* status, int sm_count,
+                 cudaStream_t s);
 void launch_synth(uint8_t* dst, uint64_t key, uint64_t block_start, uint64_t n_blocks,
                   cudaStream_t s);
 

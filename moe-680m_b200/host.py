@@ -34,7 +34,7 @@ EXPORTS = (
     "moe_bucket", "moe_forward", "moe_forward_routed", "moe_rms_norm", "moe_dequant_iq4xs",
     "moe_synth_iq4xs", "moe_profile", "moe_profile_read", "moe_launch_count", "moe_set_path",
     "moe_bucket_static", "moe_forward_topk", "moe_ep_plan_bytes", "moe_ep_dispatch",
-    "moe_ep_combine", "moe_dequant_ref36", "moe_forward_norm",
+    "moe_ep_combine", "moe_dequant_ref36", "moe_forward_norm", "moe_vocab_logits",
     "moe_layer_set_next",
 )
 
@@ -100,6 +100,7 @@ def lib():
         "moe_rms_norm": (i32, [vp, u64, u64, u32, u32, f32]),
         "moe_dequant_iq4xs": (i32, [vp, u64, u64, u64]),
         "moe_dequant_ref36": (i32, [vp, u64, u64, u64]),
+        "moe_vocab_logits": (i32, [vp, u64, u32, u32, u64, u32, u64, u64]),
         "moe_forward_norm": (i32, [vp, u32, u64, u64, u32, f32]),
         "moe_layer_set_next": (i32, [vp, u32, i32]),
         "moe_synth_iq4xs": (i32, [vp, u64, u64, u64, u64]),
@@ -282,6 +283,10 @@ class Context:
 
     def dequant_ref36(self, src_off, n_blocks, dst_off):
         self._check(lib().moe_dequant_ref36(self.h, src_off, n_blocks, dst_off))
+
+    def vocab_logits(self, w_off, vocab, hidden, x_off, m, logits_off=0, ids_off=0):
+        """LM-head projection (moe_vocab_logits): f32 logits [m][vocab] and/or argmax ids [m]."""
+        self._check(lib().moe_vocab_logits(self.h, w_off, vocab, hidden, x_off, m, logits_off, ids_off))
 
     def synth_iq4xs(self, dst_off, key, block_start, n_blocks):
         self._check(lib().moe_synth_iq4xs(self.h, dst_off, key, block_start, n_blocks))

@@ -222,3 +222,23 @@ def max_rel(a, b) -> float:
     a = np.asarray(a, np.float64)
     b = np.asarray(b, np.float64)
     return float(np.abs(a - b).max() / max(np.abs(b).max(), 1e-300))
+
+
+def vocab_logits(x: np.ndarray, w_raw: np.ndarray, vocab: int, hidden: int) -> np.ndarray:
+    """LM-head projection, f64: logits[m][n] = sum_h x[m][h] * W[n][h] with W an IQ4_XS matrix of
+    ``vocab`` rows in GGUF row layout.  The reference computes the same product on
+    shaders/attn_output.comp with M = 1, N = vocab, K = hidden (src/inference.rs:319-330), from
+    its own weight layout and f16 activations."""
+    w = dequant_matrix(np.asarray(w_raw, np.uint8), vocab, hidden).astype(np.float64)
+    return np.asarray(x, np.float64) @ w.T
+
+
+def argmax_first(v) -> int:
+    """Greedy sampling's argmax (src/util.rs:66-76): the first index whose value is strictly
+    greater than every earlier one, starting from -inf, so NaN and -inf never win and an input
+    with no value above -inf gives 0."""
+    best_i, best_v = 0, -np.inf
+    for i, x in enumerate(np.asarray(v, np.float32).tolist()):
+        if x > best_v:
+            best_i, best_v = i, x
+    return best_i

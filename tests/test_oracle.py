@@ -155,3 +155,22 @@ def test_ref36_decode_known_answers():
     assert w[0, 0] == -8.0 and w[0, 1] == 0.0 and w[0, 16] == (31 - 8) * -0.5
     assert w[0, 2] == -8.0 and w[0, 17] == 4.0    # q = 0 under both scales
     assert np.all(w[1, :16] == 0.0)
+
+
+def test_argmax_first_follows_the_reference():
+    """src/util.rs:66-76: strict '>' from -inf, so ties keep the first index, NaN and -inf never
+    win, and no value above -inf gives index 0."""
+    assert O.argmax_first([1.0, 3.0, 3.0, 2.0]) == 1
+    assert O.argmax_first([np.nan, 0.5, np.nan, 0.7]) == 3
+    assert O.argmax_first([-np.inf, -np.inf]) == 0
+    assert O.argmax_first([np.nan, np.nan]) == 0
+    assert O.argmax_first([-0.0, 0.0]) == 0
+    assert O.argmax_first([-5.0, -np.inf, -1.0]) == 2
+
+
+def test_vocab_logits_is_the_dequantised_product():
+    raw = synth.iq4xs_matrix(synth.tensor_key(1, 90, 0, 0), 37, 512)
+    x = np.random.default_rng(0).standard_normal((3, 512)).astype(np.float32)
+    w = O.dequant_matrix(raw, 37, 512)
+    ref = x.astype(np.float64) @ w.astype(np.float64).T
+    assert np.array_equal(O.vocab_logits(x, raw, 37, 512), ref)
