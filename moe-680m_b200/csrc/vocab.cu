@@ -6,11 +6,12 @@
 //
 // The pass is a single read of W (V * H/256 * 136 bytes; 270 MB for the 248,320 x 2048 head),
 // so it is bound by HBM bandwidth.  Layout of the work:
-//   * persistent grid, one CTA per SM; chunk c = rows [16c, 16c+16) is one contiguous byte
-//     range of W and is copied to shared memory by a single bulk copy (cp.async.bulk, completion
-//     counted on an mbarrier) issued by a producer warp into a ring of up to 8 stages;
-//   * 16 consumer warps take one row each per chunk: lane l decodes sub-blocks l, l+32, ... of
-//     the row once and applies them to every activation row;
+//   * persistent grid, one CTA per SM; a chunk of 16*R consecutive rows (R = 4 for one
+//     activation row, else 2) is one contiguous byte range of W and is copied to shared memory
+//     by a single bulk copy (cp.async.bulk, completion counted on an mbarrier) issued by a
+//     producer warp into a ring of up to 8 stages;
+//   * 16 consumer warps take R rows each per chunk: lane l decodes sub-blocks l, l+32, ... of
+//     each row once and applies them to every activation row;
 //   * the products are integer, as in the single-token layer kernel: activations are rounded to
 //     16-bit fixed point with a power-of-two scale per row (from its largest magnitude), dp2a
 //     sums code x activation over a 32-weight sub-block exactly, and the sub-block sums are
@@ -33,7 +34,11 @@ namespace moe {
 
 namespace {
 
-constexpr int kVWarps = 16;                    // consumer warps = rows per chunk
+constexpr int kVWarps = 16;                    // consumer warps
+// rows per warp per chunk: independent rows give the decode/dot chains instruction-level
+// parallelism (measured at M=1 on 248,320 x 2048: 1 row 110 us, 2 rows 94 us, 4 rows 90 us)
+template <int MT>
+constexpr int vocab_rows() { return MT == 1 ? 4 : 2; }
 constexpr int kVThreads = 32 * (kVWarps + 1);  // + the producer warp
 constexpr int kVMaxStages = 8;
 constexpr int kVQW = 20;  // words per 32-value group of packed 16-bit activations (see below)
@@ -81,6 +86,33 @@ __device__ __forceinline__ float q16_scale(float max_abs) {
     return ldexpf(1.f, 15 - e);
 }
 
+// Sub-block sb of a row staged in shared memory: its 32 codes as kv+128 bytes in r (byte order
+// of kv_lookup8 for the four qs words) and its scale d*(ls-32).
+__device__ __forceinline__ float decode_subblk(const uint8_t* row, int sb, uint32_t (&r)[8]) {
+    const uint8_t* blk = row + (sb >> 3) * kBlockBytes;
+    const uint2 hdr = *reinterpret_cast<const uint2*>(blk);
+    const uint2* qp = reinterpret_cast<const uint2*>(blk + 8 + (sb & 7) * 16);
+    const uint2 q01 = qp[0], q23 = qp[1];
+    kv_lookup8(q01.x, r[0], r[1]);
+    kv_lookup8(q01.y, r[2], r[3]);
+    kv_lookup8(q23.x, r[4], r[5]);
+    kv_lookup8(q23.y, r[6], r[7]);
+    return iq4_subscale(hdr.x, hdr.y, sb & 7);
+}
+
+// Exact sum over the sub-block of kv(code_j) * a_j, a in the packed 17-word layout.
+__device__ __forceinline__ int dot_codes(const uint32_t (&aw)[17], const uint32_t (&r)[8]) {
+    int d = -static_cast<int>(aw[16]);
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+        d = dp2a_lo(aw[4 * w], r[2 * w], d);
+        d = dp2a_hi(aw[4 * w + 1], r[2 * w], d);
+        d = dp2a_lo(aw[4 * w + 2], r[2 * w + 1], d);
+        d = dp2a_hi(aw[4 * w + 3], r[2 * w + 1], d);
+    }
+    return d;
+}
+
 // Order-preserving argmax key: larger value first, then lower index; 0 = no candidate.  -0 is
 // folded into +0 (the reference compares with >, so equal values keep the first index), and
 // NaN and -inf never win (v > -inf fails for both).
@@ -92,8 +124,10 @@ __device__ __forceinline__ unsigned long long argmax_key(float v, uint32_t idx) 
     return (static_cast<unsigned long long>(o) << 32) | (0xFFFFFFFFu - idx);
 }
 
-template <int MT>
+template <int MT, int NL>
 __global__ void __launch_bounds__(kVThreads, 1) vocab_kernel(const VocabArgs a) {
+    constexpr int kVRows = vocab_rows<MT>();
+    constexpr int kVChunkRows = kVWarps * kVRows;
     extern __shared__ __align__(128) uint8_t sm[];
     uint64_t* full = reinterpret_cast<uint64_t*>(sm);
     uint64_t* empty = full + kVMaxStages;
@@ -104,7 +138,7 @@ __global__ void __launch_bounds__(kVThreads, 1) vocab_kernel(const VocabArgs a) 
     const int nsb = a.H / 32;
     const size_t xq_bytes = static_cast<size_t>(MT) * nsb * kVQW * 4;
     uint8_t* stage0 = sm + ((kVHeader + xq_bytes + 127) / 128) * 128;
-    const uint32_t chunk_bytes = a.row_bytes * kVWarps;
+    const uint32_t chunk_bytes = a.row_bytes * kVChunkRows;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int S = a.stages, M = a.M;
 
@@ -126,7 +160,7 @@ __global__ void __launch_bounds__(kVThreads, 1) vocab_kernel(const VocabArgs a) 
                 const int s = issued % S;
                 if (issued >= S && !tc::mbar_wait(&empty[s], ((issued / S) & 1) ^ 1, abort_flag, kVSpinNs))
                     break;
-                const int rows = min(kVWarps, a.V - c * kVWarps);
+                const int rows = min(kVChunkRows, a.V - c * kVChunkRows);
                 const uint32_t bytes = static_cast<uint32_t>(rows) * a.row_bytes;
                 tc::mbar_arrive_expect_tx(&full[s], bytes);
                 tc::bulk_load(stage0 + static_cast<size_t>(s) * chunk_bytes,
@@ -173,55 +207,83 @@ __global__ void __launch_bounds__(kVThreads, 1) vocab_kernel(const VocabArgs a) 
         float inv[MT];
 #pragma unroll
         for (int t = 0; t < MT; ++t) inv[t] = t < M ? xinv[t] : 0.f;
+        // NL > 0: lane l always takes sub-blocks l, l+32, ..., so its packed activations stay in
+        // registers (NL*17 words per row); shared-memory reads of them bound the rate otherwise
+        uint32_t xreg[NL > 0 ? MT : 1][NL > 0 ? NL : 1][17];
+        if constexpr (NL > 0) {
+#pragma unroll
+            for (int t = 0; t < MT; ++t)
+#pragma unroll
+                for (int n = 0; n < NL; ++n)
+#pragma unroll
+                    for (int w = 0; w < 17; ++w)
+                        xreg[t][n][w] = t < M ? xq[(static_cast<size_t>(t) * nsb + lane + 32 * n) * kVQW + w] : 0u;
+        }
         unsigned long long best = 0ull;  // lane t: activation row t
         int i = 0;
         for (int c = blockIdx.x; c < a.n_chunks; c += gridDim.x, ++i) {
             const int s = i % S;
             if (!tc::mbar_wait_warp(&full[s], (i / S) & 1, abort_flag)) break;
-            const int row = c * kVWarps + warp;
-            if (row < a.V) {
+            const int row0 = (c * kVWarps + warp) * kVRows;
+            if (row0 < a.V) {
+                // rows row0 .. row0+kVRows-1 (rows past V in the last chunk are computed from stale
+                // shared memory and not stored)
                 const uint8_t* rp = stage0 + static_cast<size_t>(s) * chunk_bytes +
-                                    static_cast<size_t>(warp) * a.row_bytes;
-                float acc[MT];
+                                    static_cast<size_t>(warp) * kVRows * a.row_bytes;
+                float acc[kVRows][MT];
 #pragma unroll
-                for (int t = 0; t < MT; ++t) acc[t] = 0.f;
-                for (int sb = lane; sb < nsb; sb += 32) {
-                    const uint8_t* blk = rp + (sb >> 3) * kBlockBytes;
-                    const uint2 hdr = *reinterpret_cast<const uint2*>(blk);
-                    const uint2* qp = reinterpret_cast<const uint2*>(blk + 8 + (sb & 7) * 16);
-                    const uint2 q01 = qp[0], q23 = qp[1];
-                    const float dl = iq4_subscale(hdr.x, hdr.y, sb & 7);
-                    uint32_t r[8];
-                    kv_lookup8(q01.x, r[0], r[1]);
-                    kv_lookup8(q01.y, r[2], r[3]);
-                    kv_lookup8(q23.x, r[4], r[5]);
-                    kv_lookup8(q23.y, r[6], r[7]);
+                for (int rr = 0; rr < kVRows; ++rr)
 #pragma unroll
-                    for (int t = 0; t < MT; ++t) {
-                        if (t < M) {
-                            const uint32_t* aq = xq + (static_cast<size_t>(t) * nsb + sb) * kVQW;
-                            const uint4* a4 = reinterpret_cast<const uint4*>(aq);
-                            int d = -static_cast<int>(aq[16]);
+                    for (int t = 0; t < MT; ++t) acc[rr][t] = 0.f;
+                if constexpr (NL > 0) {
 #pragma unroll
-                            for (int w = 0; w < 4; ++w) {
-                                const uint4 av = a4[w];
-                                d = dp2a_lo(av.x, r[2 * w], d);
-                                d = dp2a_hi(av.y, r[2 * w], d);
-                                d = dp2a_lo(av.z, r[2 * w + 1], d);
-                                d = dp2a_hi(av.w, r[2 * w + 1], d);
+                    for (int n = 0; n < NL; ++n) {
+#pragma unroll
+                        for (int rr = 0; rr < kVRows; ++rr) {
+                            uint32_t r[8];
+                            const float dl = decode_subblk(rp + rr * a.row_bytes, lane + 32 * n, r);
+#pragma unroll
+                            for (int t = 0; t < MT; ++t)
+                                if (t < M)
+                                    acc[rr][t] = fmaf(dl, static_cast<float>(dot_codes(xreg[t][n], r)), acc[rr][t]);
+                        }
+                    }
+                } else {
+                    for (int sb = lane; sb < nsb; sb += 32) {
+#pragma unroll
+                        for (int rr = 0; rr < kVRows; ++rr) {
+                            uint32_t r[8];
+                            const float dl = decode_subblk(rp + rr * a.row_bytes, sb, r);
+#pragma unroll
+                            for (int t = 0; t < MT; ++t) {
+                                if (t < M) {
+                                    const uint32_t* aq = xq + (static_cast<size_t>(t) * nsb + sb) * kVQW;
+                                    const uint4* a4 = reinterpret_cast<const uint4*>(aq);
+                                    uint32_t aw[17];
+#pragma unroll
+                                    for (int w = 0; w < 4; ++w) {
+                                        const uint4 av = a4[w];
+                                        aw[4 * w] = av.x; aw[4 * w + 1] = av.y; aw[4 * w + 2] = av.z; aw[4 * w + 3] = av.w;
+                                    }
+                                    aw[16] = aq[16];
+                                    acc[rr][t] = fmaf(dl, static_cast<float>(dot_codes(aw, r)), acc[rr][t]);
+                                }
                             }
-                            acc[t] = fmaf(dl, static_cast<float>(d), acc[t]);
                         }
                     }
                 }
 #pragma unroll
-                for (int t = 0; t < MT; ++t) {
-                    if (t < M) {
-                        const float v = warp_sum(acc[t]) * inv[t];
-                        if (lane == t) {
-                            if (a.logits) a.logits[static_cast<size_t>(t) * a.V + row] = v;
-                            const unsigned long long k = argmax_key(v, static_cast<uint32_t>(row));
-                            best = k > best ? k : best;
+                for (int rr = 0; rr < kVRows; ++rr) {
+                    const int row = row0 + rr;
+#pragma unroll
+                    for (int t = 0; t < MT; ++t) {
+                        if (t < M) {
+                            const float v = warp_sum(acc[rr][t]) * inv[t];
+                            if (lane == t && row < a.V) {
+                                if (a.logits) a.logits[static_cast<size_t>(t) * a.V + row] = v;
+                                const unsigned long long k = argmax_key(v, static_cast<uint32_t>(row));
+                                best = k > best ? k : best;
+                            }
                         }
                     }
                 }
@@ -253,14 +315,17 @@ __global__ void __launch_bounds__(kVThreads, 1) vocab_kernel(const VocabArgs a) 
 
 template <int MT>
 size_t vocab_smem(int H, int stages, uint32_t row_bytes) {
+    constexpr int kVChunkRows = kVWarps * vocab_rows<MT>();
     const size_t xq = static_cast<size_t>(MT) * (H / 32) * kVQW * 4;
-    return (kVHeader + xq + 127) / 128 * 128 + static_cast<size_t>(stages) * row_bytes * kVWarps;
+    return (kVHeader + xq + 127) / 128 * 128 + static_cast<size_t>(stages) * row_bytes * kVChunkRows;
 }
 
-template <int MT>
+template <int MT, int NL>
 int launch_vocab_t(VocabArgs a, int sm_count, cudaStream_t s) {
+    constexpr int kVChunkRows = kVWarps * vocab_rows<MT>();
+    a.n_chunks = (a.V + kVChunkRows - 1) / kVChunkRows;
     const size_t base = vocab_smem<MT>(a.H, 0, a.row_bytes);
-    const size_t chunk = static_cast<size_t>(a.row_bytes) * kVWarps;
+    const size_t chunk = static_cast<size_t>(a.row_bytes) * kVChunkRows;
     if (base + 2 * chunk > static_cast<size_t>(kVSmemMax)) return -1;
     a.stages = static_cast<int>(std::min<size_t>(kVMaxStages, (kVSmemMax - base) / chunk));
     const size_t smem = vocab_smem<MT>(a.H, a.stages, a.row_bytes);
@@ -268,11 +333,11 @@ int launch_vocab_t(VocabArgs a, int sm_count, cudaStream_t s) {
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 64 && !attr_set[dev]) {
-        cudaFuncSetAttribute(vocab_kernel<MT>, cudaFuncAttributeMaxDynamicSharedMemorySize, kVSmemMax);
+        cudaFuncSetAttribute(vocab_kernel<MT, NL>, cudaFuncAttributeMaxDynamicSharedMemorySize, kVSmemMax);
         attr_set[dev] = true;
     }
     const int grid = std::min(a.n_chunks, sm_count);
-    vocab_kernel<MT><<<grid, kVThreads, smem, s>>>(a);
+    vocab_kernel<MT, NL><<<grid, kVThreads, smem, s>>>(a);
     return 0;
 }
 
@@ -289,11 +354,14 @@ int launch_vocab(const uint8_t* w, int V, int H, const float* x, int M, float* l
     a.w = w; a.x = x; a.logits = logits; a.ids = ids; a.keys = keys; a.ticket = ticket;
     a.status = status; a.V = V; a.H = H; a.M = M;
     a.row_bytes = static_cast<uint32_t>(H / kQK * kBlockBytes);
-    a.n_chunks = (V + kVWarps - 1) / kVWarps;
-    if (M <= 1) return launch_vocab_t<1>(a, sm_count, s);
-    if (M <= 2) return launch_vocab_t<2>(a, sm_count, s);
-    if (M <= 4) return launch_vocab_t<4>(a, sm_count, s);
-    return launch_vocab_t<8>(a, sm_count, s);
+    // activations in registers when each lane's share is small (H = 1024 or 2048, M <= 2)
+    const int nl = (H == 1024 || H == 2048) ? H / 1024 : 0;
+    if (M <= 1) return nl == 2 ? launch_vocab_t<1, 2>(a, sm_count, s)
+                     : nl == 1 ? launch_vocab_t<1, 1>(a, sm_count, s) : launch_vocab_t<1, 0>(a, sm_count, s);
+    if (M <= 2) return nl == 2 ? launch_vocab_t<2, 2>(a, sm_count, s)
+                     : nl == 1 ? launch_vocab_t<2, 1>(a, sm_count, s) : launch_vocab_t<2, 0>(a, sm_count, s);
+    if (M <= 4) return launch_vocab_t<4, 0>(a, sm_count, s);
+    return launch_vocab_t<8, 0>(a, sm_count, s);
 }
 
 }  // namespace moe

@@ -50,8 +50,9 @@ def check(lg, ids, ref):
         assert ref[t, ids[t]] >= ref[t].max() - 1e-3 * np.abs(ref[t]).max()
 
 
-@pytest.mark.parametrize("vocab,hidden,m", [(1000, 2048, 1), (4099, 2048, 3), (2053, 1024, 8),
-                                            (16, 512, 2), (777, 4096, 5), (1, 2048, 1)])
+@pytest.mark.parametrize("vocab,hidden,m", [(1000, 2048, 1), (999, 2048, 2), (4099, 2048, 3),
+                                            (1500, 1024, 1), (1501, 1024, 2), (2053, 1024, 8),
+                                            (16, 512, 2), (777, 4096, 5), (300, 4096, 1), (1, 2048, 1)])
 def test_logits_and_argmax(ctx, vocab, hidden, m):
     raw = head(7, vocab, hidden)
     x = synth.tokens(7, vocab % 97, m, hidden)
