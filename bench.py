@@ -182,6 +182,36 @@ def _barrier(world: int):
         dist.barrier()
 
 
+def lm_head_leg(ctx, synth, stream, hbm, rank):
+    """LM head: the 248,320 x 2048 IQ4_XS projection + greedy argmax (moe_vocab_logits), M = 1
+    and 8, 50 timed launches each with CUDA events on the library's stream (the 270 MB weight
+    exceeds the L2, so every launch reads it from HBM)."""
+    import torch
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    wv = ctx.alloc(VOCAB_BYTES)
+    ctx.synth_iq4xs(wv, synth.tensor_key(SEED, 90, 0, 0), 0, VOCAB_BYTES // 136)
+    out = {"vocab": VOCAB, "hidden": VOCAB_HIDDEN, "alg_bytes_per_launch": VOCAB_BYTES,
+           "l2": "270 MB weight exceeds the 126 MB L2"}
+    for mv in (1, 8):
+        xv = [ctx.put(synth.tokens(SEED + 17, rank * 1000 + i, mv, VOCAB_HIDDEN)) for i in range(4)]
+        lv, iv = ctx.alloc(mv * VOCAB * 4), ctx.alloc(256)
+        for i in range(3):
+            ctx.vocab_logits(wv, VOCAB, VOCAB_HIDDEN, xv[i % 4], mv, lv, iv)
+        torch.cuda.synchronize()
+        kv = 50
+        ev0.record(stream)
+        for i in range(kv):
+            ctx.vocab_logits(wv, VOCAB, VOCAB_HIDDEN, xv[i % 4], mv, lv, iv)
+        ev1.record(stream)
+        torch.cuda.synchronize()
+        ctx.sync()
+        usv = ev0.elapsed_time(ev1) / kv * 1e3
+        gbs = VOCAB_BYTES / (usv / 1e6) / 1e9
+        out[f"m{mv}"] = {"us_per_launch": usv, "hbm_gbs": gbs, "hbm_frac": gbs / hbm,
+                         "outputs": "f32 logits + argmax ids"}
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -189,8 +219,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
-    ap.add_argument("--only", default="all", choices=["all", "prefill"],
-                    help="prefill: skip the decode, config-3, end-to-end and CPU legs (profiling runs)")
+    ap.add_argument("--only", default="all", choices=["all", "prefill", "lm_head"],
+                    help="prefill: skip the decode, config-3, end-to-end and CPU legs; lm_head: only "
+                         "the LM-head leg, 0.3 GB on the device (profiling runs)")
     ap.add_argument("--path", type=int, default=0,
                     help="expert kernels: 0 auto, 1 CUDA-core GEMV, 2 tcgen05 (A in smem), 3 tcgen05 (A in TMEM)")
     args = ap.parse_args()
@@ -207,6 +238,20 @@ def main():
         dist.init_process_group("nccl", device_id=torch.device("cuda", local))
     load_pkg()
     from moe680m_b200 import ep, host, synth
+
+    if args.only == "lm_head":  # the LM-head leg alone, on each rank's GPU
+        arena = torch.empty(VOCAB_BYTES + (64 << 20), dtype=torch.uint8, device=torch.device("cuda", local))
+        ctx = host.Context(local, arena.numel(), external_ptr=arena.data_ptr())
+        stream = torch.cuda.Stream()
+        torch.cuda.set_stream(stream)
+        ctx.set_stream(stream.cuda_stream)
+        res = lm_head_leg(ctx, synth, stream, peaks()[0], rank)
+        if rank == 0:
+            print(json.dumps({"lm_head": res}), flush=True)
+        ctx.close()
+        if world > 1:
+            dist.destroy_process_group()
+        return
 
     sh = synth.LayerShapes()
     E, H = sh.n_experts, sh.hidden
@@ -479,28 +524,7 @@ def main():
                              "hbm_frac": b4 / (ms4 / 1e3) / 1e9 / hbm}
         ctx.set_path(args.path)
 
-        # ---- LM head: 248,320 x 2048 IQ4_XS projection + greedy argmax (moe_vocab_logits) -----
-        wv = ctx.alloc(VOCAB_BYTES)
-        ctx.synth_iq4xs(wv, synth.tensor_key(SEED, 90, 0, 0), 0, VOCAB_BYTES // 136)
-        lm_head = {"vocab": VOCAB, "hidden": VOCAB_HIDDEN, "alg_bytes_per_launch": VOCAB_BYTES,
-                   "l2": "270 MB weight exceeds the 126 MB L2"}
-        for mv in (1, 8):
-            xv = [ctx.put(synth.tokens(SEED + 17, rank * 1000 + i, mv, VOCAB_HIDDEN)) for i in range(4)]
-            lv, iv = ctx.alloc(mv * VOCAB * 4), ctx.alloc(256)
-            for i in range(3):
-                ctx.vocab_logits(wv, VOCAB, VOCAB_HIDDEN, xv[i % 4], mv, lv, iv)
-            torch.cuda.synchronize()
-            kv = 50
-            ev0.record(stream)
-            for i in range(kv):
-                ctx.vocab_logits(wv, VOCAB, VOCAB_HIDDEN, xv[i % 4], mv, lv, iv)
-            ev1.record(stream)
-            torch.cuda.synchronize()
-            usv = ev0.elapsed_time(ev1) / kv * 1e3
-            ctx.sync()
-            gbs = VOCAB_BYTES / (usv / 1e6) / 1e9
-            lm_head[f"m{mv}"] = {"us_per_launch": usv, "hbm_gbs": gbs, "hbm_frac": gbs / hbm,
-                                 "outputs": "f32 logits + argmax ids"}
+        lm_head = lm_head_leg(ctx, synth, stream, hbm, rank)
 
         # ---- CPU baseline (rank 0, N=1 only) ------------------------------------------------------
         if rank == 0 and world == 1 and not args.no_cpu:
