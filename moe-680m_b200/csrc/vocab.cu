@@ -7,7 +7,7 @@
 // The pass is a single read of W (V * H/256 * 136 bytes; 270 MB for the 248,320 x 2048 head),
 // so it is bound by HBM bandwidth.  Layout of the work:
 //   * persistent grid, one CTA per SM; a chunk of 16*R consecutive rows (R = 4 for one
-//     activation row, else 2) is one contiguous byte range of W and is copied to shared memory
+//     activation row with H <= 2048, else 2) is one contiguous byte range of W and is copied to shared memory
 //     by a single bulk copy (cp.async.bulk, completion counted on an mbarrier) issued by a
 //     producer warp into a ring of up to 8 stages;
 //   * 16 consumer warps take R rows each per chunk: lane l decodes sub-blocks l, l+32, ... of
@@ -37,8 +37,9 @@ namespace {
 constexpr int kVWarps = 16;                    // consumer warps
 // rows per warp per chunk: independent rows give the decode/dot chains instruction-level
 // parallelism (measured at M=1 on 248,320 x 2048: 1 row 110 us, 2 rows 94 us, 4 rows 90 us)
-template <int MT>
-constexpr int vocab_rows() { return MT == 1 ? 4 : 2; }
+// (4 rows only with the register-held activations, H <= 2048, so that two or more stages fit)
+template <int MT, int NL>
+constexpr int vocab_rows() { return MT == 1 && NL > 0 ? 4 : 2; }
 constexpr int kVThreads = 32 * (kVWarps + 1);  // + the producer warp
 constexpr int kVMaxStages = 8;
 constexpr int kVQW = 20;  // words per 32-value group of packed 16-bit activations (see below)
@@ -126,7 +127,7 @@ __device__ __forceinline__ unsigned long long argmax_key(float v, uint32_t idx) 
 
 template <int MT, int NL>
 __global__ void __launch_bounds__(kVThreads, 1) vocab_kernel(const VocabArgs a) {
-    constexpr int kVRows = vocab_rows<MT>();
+    constexpr int kVRows = vocab_rows<MT, NL>();
     constexpr int kVChunkRows = kVWarps * kVRows;
     extern __shared__ __align__(128) uint8_t sm[];
     uint64_t* full = reinterpret_cast<uint64_t*>(sm);
@@ -142,29 +143,35 @@ __global__ void __launch_bounds__(kVThreads, 1) vocab_kernel(const VocabArgs a) 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int S = a.stages, M = a.M;
 
-    if (tid == 0) {
-        for (int s = 0; s < S; ++s) {
-            tc::mbar_init(&full[s], 1);
-            tc::mbar_init(&empty[s], kVWarps);
-        }
-        tc::fence_mbar_init();
-        *abort_flag = 0;
-    }
     if (tid < 8) bkey[tid] = 0ull;
     if (warp == kVWarps) {
-        // producer: one elected lane streams the CTA's chunks through the ring
+        // producer: one lane initialises the ring, issues the first S chunks before the CTA-wide
+        // barrier (overlapping the activation packing), then streams the rest
+        int issued = 0;
+        int c = blockIdx.x;
+        auto issue = [&](int s) {
+            const int rows = min(kVChunkRows, a.V - c * kVChunkRows);
+            const uint32_t bytes = static_cast<uint32_t>(rows) * a.row_bytes;
+            tc::mbar_arrive_expect_tx(&full[s], bytes);
+            tc::bulk_load(stage0 + static_cast<size_t>(s) * chunk_bytes,
+                          a.w + static_cast<size_t>(c) * chunk_bytes, bytes, &full[s]);
+        };
+        if (lane == 0) {
+            for (int s = 0; s < S; ++s) {
+                tc::mbar_init(&full[s], 1);
+                tc::mbar_init(&empty[s], kVWarps);
+            }
+            tc::fence_mbar_init();
+            *abort_flag = 0;
+            for (; c < a.n_chunks && issued < S; c += gridDim.x, ++issued) issue(issued);
+        }
+        __syncwarp();
         __syncthreads();
         if (lane == 0) {
-            int issued = 0;
-            for (int c = blockIdx.x; c < a.n_chunks; c += gridDim.x, ++issued) {
+            for (; c < a.n_chunks; c += gridDim.x, ++issued) {
                 const int s = issued % S;
-                if (issued >= S && !tc::mbar_wait(&empty[s], ((issued / S) & 1) ^ 1, abort_flag, kVSpinNs))
-                    break;
-                const int rows = min(kVChunkRows, a.V - c * kVChunkRows);
-                const uint32_t bytes = static_cast<uint32_t>(rows) * a.row_bytes;
-                tc::mbar_arrive_expect_tx(&full[s], bytes);
-                tc::bulk_load(stage0 + static_cast<size_t>(s) * chunk_bytes,
-                              a.w + static_cast<size_t>(c) * chunk_bytes, bytes, &full[s]);
+                if (!tc::mbar_wait(&empty[s], ((issued / S) & 1) ^ 1, abort_flag, kVSpinNs)) break;
+                issue(s);
             }
             // drain: the copies still in flight land before the CTA's shared memory goes away
             for (int i = max(0, issued - S); i < issued; ++i) {
@@ -313,22 +320,22 @@ __global__ void __launch_bounds__(kVThreads, 1) vocab_kernel(const VocabArgs a) 
     }
 }
 
-template <int MT>
+template <int MT, int NL>
 size_t vocab_smem(int H, int stages, uint32_t row_bytes) {
-    constexpr int kVChunkRows = kVWarps * vocab_rows<MT>();
+    constexpr int kVChunkRows = kVWarps * vocab_rows<MT, NL>();
     const size_t xq = static_cast<size_t>(MT) * (H / 32) * kVQW * 4;
     return (kVHeader + xq + 127) / 128 * 128 + static_cast<size_t>(stages) * row_bytes * kVChunkRows;
 }
 
 template <int MT, int NL>
 int launch_vocab_t(VocabArgs a, int sm_count, cudaStream_t s) {
-    constexpr int kVChunkRows = kVWarps * vocab_rows<MT>();
+    constexpr int kVChunkRows = kVWarps * vocab_rows<MT, NL>();
     a.n_chunks = (a.V + kVChunkRows - 1) / kVChunkRows;
-    const size_t base = vocab_smem<MT>(a.H, 0, a.row_bytes);
+    const size_t base = vocab_smem<MT, NL>(a.H, 0, a.row_bytes);
     const size_t chunk = static_cast<size_t>(a.row_bytes) * kVChunkRows;
     if (base + 2 * chunk > static_cast<size_t>(kVSmemMax)) return -1;
     a.stages = static_cast<int>(std::min<size_t>(kVMaxStages, (kVSmemMax - base) / chunk));
-    const size_t smem = vocab_smem<MT>(a.H, a.stages, a.row_bytes);
+    const size_t smem = vocab_smem<MT, NL>(a.H, a.stages, a.row_bytes);
     static bool attr_set[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
