@@ -213,6 +213,26 @@ int moe_ep_dispatch(moe_ctx* ctx, uint32_t n_experts, uint32_t top_k, uint32_t n
 int moe_ep_combine(moe_ctx* ctx, uint32_t n_ranks, uint32_t capacity, uint32_t H, uint32_t M,
                    uint64_t plan_off, uint64_t y_back_off, uint64_t resid_off, uint64_t out_off, float scale);
 
+/* ---- expert parallelism over NCCL, no Python (one process per GPU) ---------------------- *
+ * The C-level form of the expert-parallel layer: rank r of N holds routed experts
+ * [r*E/N, (r+1)*E/N) (a layer created with MOE_F_EXPERT_SUBSET, or a full layer), the router and
+ * the shared expert, and its own M_r tokens.  NCCL is loaded at run time (libnccl.so.2; the copy
+ * already in the process when there is one).  Not thread-safe, like the rest of the context. */
+
+/* Write a new NCCL unique id (128 bytes) to out[0..n); rank 0 makes it and the caller passes it
+ * to every rank out of band. */
+int moe_ep_unique_id(void* out, size_t n);
+/* Join the n_ranks-rank group (blocks until every rank has called it; 1 <= n_ranks <= 8).
+ * Replaces an earlier group of this context. */
+int moe_ep_init(moe_ctx* ctx, const void* unique_id, uint32_t n_ranks, uint32_t rank);
+/* out = resid + scale * MoE(x) for this rank's M tokens (M may be 0) through the group: route,
+ * per-rank blocks of `capacity` rows, NCCL all-to-all, this rank's experts, all-to-all back,
+ * combine.  Every rank must call it with the same layer shape and the same capacity
+ * (>= the largest M of any rank).  Stream-ordered on the context's stream; capturable in a CUDA
+ * graph after one eager call (which sizes the buffers). */
+int moe_forward_ep(moe_ctx* ctx, uint32_t layer_id, uint64_t x_off, uint64_t resid_off, uint64_t out_off,
+                   uint32_t M, uint32_t capacity);
+
 /* Expert-product kernels used by moe_forward / moe_forward_routed (a tuning and diagnostic
  * knob; the default picks by batch size: CUDA-core grouped GEMV for M <= 8, tcgen05 grouped
  * GEMM otherwise). */

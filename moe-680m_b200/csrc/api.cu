@@ -486,6 +486,8 @@ int moe_ctx_create_external(int device, void* base, uint64_t bytes, moe_ctx** ou
     return MOE_OK;
 }
 
+static void ep_release(Ctx* c);
+
 void moe_ctx_destroy(moe_ctx* c) {
     if (!c) return;
     cudaSetDevice(c->device);
@@ -496,6 +498,7 @@ void moe_ctx_destroy(moe_ctx* c) {
         if (L.wsplit) cudaFree(L.wsplit);
     }
     for (auto& g : c->graphs) destroy_graph(g);
+    ep_release(c);
     int* status = c->ws.status;
     free_ws(c->ws);
     if (status) cudaFree(status);
@@ -977,6 +980,184 @@ int moe_ep_combine(moe_ctx* c, uint32_t n_ranks, uint32_t capacity, uint32_t H, 
                            resid_off ? at<float>(c, resid_off) : nullptr, scale, at<float>(c, out_off), c->stream);
     stage(c, "ep_combine", 1);
     return check_launch(c, "ep_combine");
+}
+
+// ---- expert parallelism over NCCL ----------------------------------------------------------
+
+static int nccl_fail(Ctx* c, const moe::NcclApi* api, ncclResult_t r, const char* what) {
+    return fail(c, MOE_E_CUDA, "%s: %s", what, api->error_string ? api->error_string(r) : "NCCL error");
+}
+
+// Per-peer blocks of `count` elements: block d of `send` goes to rank d, block d of `recv` comes
+// from rank d (equal splits: nothing about the sizes is exchanged).
+static int ep_alltoall(Ctx* c, const moe::NcclApi* api, const void* send, void* recv, size_t count,
+                       ncclDataType_t type, size_t elem, const char* what) {
+    const moe::EpState& ep = c->ep;
+    ncclResult_t r = api->group_start();
+    if (r != ncclSuccess) return nccl_fail(c, api, r, what);
+    for (uint32_t d = 0; d < ep.n_ranks && r == ncclSuccess; ++d) {
+        r = api->send(static_cast<const uint8_t*>(send) + d * count * elem, count, type, static_cast<int>(d),
+                      ep.comm, c->stream);
+        if (r == ncclSuccess)
+            r = api->recv(static_cast<uint8_t*>(recv) + d * count * elem, count, type, static_cast<int>(d),
+                          ep.comm, c->stream);
+    }
+    const ncclResult_t r2 = api->group_end();
+    if (r != ncclSuccess) return nccl_fail(c, api, r, what);
+    if (r2 != ncclSuccess) return nccl_fail(c, api, r2, what);
+    return MOE_OK;
+}
+
+static moe::EpPlan ep_plan_ptr(uint8_t* base, uint32_t M, uint32_t n_ranks) {
+    const uint64_t a = (4ull * M + 255) / 256 * 256;
+    const uint64_t b = (4ull * M * n_ranks + 255) / 256 * 256;
+    return moe::EpPlan{reinterpret_cast<uint32_t*>(base), reinterpret_cast<int*>(base + a),
+                       reinterpret_cast<int*>(base + a + b)};
+}
+
+// Exchange buffers for n_ranks x capacity rows of width H with (k+1)-entry records.
+static int ensure_ep_buffers(Ctx* c, uint32_t capacity, uint32_t H, uint32_t k) {
+    moe::EpState& ep = c->ep;
+    if (ep.buf && capacity <= ep.capacity && H <= ep.hidden && k <= ep.top_k) return MOE_OK;
+    capacity = std::max(capacity, ep.capacity);
+    H = std::max(H, ep.hidden);
+    k = std::max(k, ep.top_k);
+    const uint64_t rows = static_cast<uint64_t>(ep.n_ranks) * capacity;
+    const uint64_t xb = rows * H * 4, rb = rows * (k + 1) * 8;
+    const uint64_t pb = (moe_ep_plan_bytes(capacity, ep.n_ranks) + 255) / 256 * 256;
+    MOE_CUDA(c, cudaStreamSynchronize(c->stream));
+    if (ep.buf) cudaFree(ep.buf);
+    ep.buf = nullptr;
+    void* p = nullptr;
+    cudaError_t e = cudaMalloc(&p, pb + 4 * xb + 2 * rb);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        ep.capacity = ep.hidden = ep.top_k = 0;
+        return fail(c, MOE_E_OOM, "expert-parallel buffers for %u x %u rows: %s", ep.n_ranks, capacity,
+                    cudaGetErrorString(e));
+    }
+    uint8_t* b = static_cast<uint8_t*>(p);
+    ep.buf = b;
+    ep.plan = b;
+    ep.send_x = reinterpret_cast<float*>(b + pb);
+    ep.recv_x = reinterpret_cast<float*>(b + pb + xb);
+    ep.y_send = reinterpret_cast<float*>(b + pb + 2 * xb);
+    ep.y_recv = reinterpret_cast<float*>(b + pb + 3 * xb);
+    ep.send_rec = reinterpret_cast<uint2*>(b + pb + 4 * xb);
+    ep.recv_rec = reinterpret_cast<uint2*>(b + pb + 4 * xb + rb);
+    ep.capacity = capacity;
+    ep.hidden = H;
+    ep.top_k = k;
+    return MOE_OK;
+}
+
+static void ep_release(Ctx* c) {
+    moe::EpState& ep = c->ep;
+    if (ep.comm) {
+        const moe::NcclApi* api = moe::nccl_api(nullptr);
+        if (api) api->comm_destroy(ep.comm);
+    }
+    if (ep.buf) cudaFree(ep.buf);
+    ep = moe::EpState{};
+}
+
+int moe_ep_unique_id(void* out, size_t n) {
+    if (!out || n < sizeof(ncclUniqueId)) return fail(nullptr, MOE_E_INVALID, "unique id buffer below %zu bytes",
+                                                       sizeof(ncclUniqueId));
+    std::string err;
+    const moe::NcclApi* api = moe::nccl_api(&err);
+    if (!api) return fail(nullptr, MOE_E_UNSUPPORTED, "%s", err.c_str());
+    ncclUniqueId id;
+    const ncclResult_t r = api->get_unique_id(&id);
+    if (r != ncclSuccess) return fail(nullptr, MOE_E_CUDA, "ncclGetUniqueId: %s", api->error_string(r));
+    std::memcpy(out, &id, sizeof(id));
+    return MOE_OK;
+}
+
+int moe_ep_init(moe_ctx* c, const void* unique_id, uint32_t n_ranks, uint32_t rank) {
+    if (!c || !unique_id) return fail(c, MOE_E_INVALID, "NULL argument");
+    if (n_ranks == 0 || n_ranks > static_cast<uint32_t>(moe::kMaxEpRanks) || rank >= n_ranks)
+        return fail(c, MOE_E_UNSUPPORTED, "n_ranks %u (1..%d) / rank %u", n_ranks, moe::kMaxEpRanks, rank);
+    std::string err;
+    const moe::NcclApi* api = moe::nccl_api(&err);
+    if (!api) return fail(c, MOE_E_UNSUPPORTED, "%s", err.c_str());
+    DeviceGuard g(c->device);
+    MOE_CUDA(c, cudaStreamSynchronize(c->stream));
+    ep_release(c);
+    ncclUniqueId id;
+    std::memcpy(&id, unique_id, sizeof(id));
+    ncclComm_t comm = nullptr;
+    const ncclResult_t r = api->comm_init_rank(&comm, static_cast<int>(n_ranks), id, static_cast<int>(rank));
+    if (r != ncclSuccess) return nccl_fail(c, api, r, "ncclCommInitRank");
+    c->ep.comm = comm;
+    c->ep.n_ranks = n_ranks;
+    c->ep.rank = rank;
+    return MOE_OK;
+}
+
+int moe_forward_ep(moe_ctx* c, uint32_t layer_id, uint64_t x_off, uint64_t resid_off, uint64_t out_off,
+                   uint32_t M, uint32_t capacity) {
+    if (!c) return fail(c, MOE_E_INVALID, "NULL context");
+    moe::EpState& ep = c->ep;
+    if (!ep.comm) return fail(c, MOE_E_INVALID, "moe_ep_init has not been called on this context");
+    Layer* L;
+    int rc = get_layer(c, layer_id, &L);
+    if (rc) return rc;
+    const uint32_t n = ep.n_ranks, E = L->spec.n_experts, k = L->spec.top_k, H = L->spec.hidden;
+    if (E % n != 0) return fail(c, MOE_E_UNSUPPORTED, "%u experts do not split over %u ranks", E, n);
+    if (capacity == 0 || capacity < M)
+        return fail(c, MOE_E_INVALID, "capacity %u must be >= 1 and >= the %u local tokens", capacity, M);
+    if (M) {
+        if ((rc = check_tokens(c, *L, x_off, M, "x"))) return rc;
+        if (resid_off && (rc = check_tokens(c, *L, resid_off, M, "resid"))) return rc;
+        if ((rc = check_tokens(c, *L, out_off, M, "out"))) return rc;
+    }
+    const moe::NcclApi* api = moe::nccl_api(nullptr);
+    DeviceGuard g(c->device);
+    if ((rc = ensure_ep_buffers(c, capacity, H, k))) return rc;
+    const uint32_t rows = n * capacity;
+    if ((rc = ensure_layer_ws(c, *L, std::max(rows, M)))) return rc;
+    const size_t rec = static_cast<size_t>(k + 1) * 8;
+    const moe::EpPlan plan = ep_plan_ptr(ep.plan, std::max(M, 1u), n);
+    const int epr = static_cast<int>(E / n);
+    prof_begin(c);
+    // 1-2. route the local tokens, build the rank blocks (empty records pad every block)
+    MOE_CUDA(c, cudaMemsetAsync(ep.send_rec, 0xFF, rows * rec, c->stream));
+    if (M) {
+        run_set_io(c, at<float>(c, x_off), nullptr, nullptr);
+        if ((rc = run_route(c, *L, M))) return rc;
+        moe::launch_ep_plan(c->ws.topk, static_cast<int>(M), static_cast<int>(k), epr, static_cast<int>(n),
+                            static_cast<int>(ep.rank), static_cast<int>(capacity), plan, c->ws.status, c->stream);
+        moe::launch_ep_gather(at<float>(c, x_off), c->ws.topk, plan, static_cast<int>(M), static_cast<int>(H),
+                              static_cast<int>(k), epr, static_cast<int>(n), static_cast<int>(ep.rank), ep.send_x,
+                              ep.send_rec, c->stream);
+        stage(c, "ep_dispatch", 3);
+    }
+    // 3. rows and records to their expert ranks
+    if ((rc = ep_alltoall(c, api, ep.send_x, ep.recv_x, static_cast<size_t>(capacity) * H, ncclFloat32, 4,
+                          "dispatch all-to-all")))
+        return rc;
+    if ((rc = ep_alltoall(c, api, ep.send_rec, ep.recv_rec, capacity * rec, ncclUint8, 1, "record all-to-all")))
+        return rc;
+    stage(c, "ep_alltoall", 0);
+    // 4. this rank's experts (and the shared expert for its own tokens) on every received row
+    MOE_CUDA(c, cudaMemcpyAsync(c->ws.topk, ep.recv_rec, rows * rec, cudaMemcpyDeviceToDevice, c->stream));
+    run_set_io(c, ep.recv_x, nullptr, ep.y_send);
+    if ((rc = run_experts(c, *L, rows, true, L->has_shared(), 1.0f))) return rc;
+    // 5. partial rows back to their owners
+    if ((rc = ep_alltoall(c, api, ep.y_send, ep.y_recv, static_cast<size_t>(capacity) * H, ncclFloat32, 4,
+                          "combine all-to-all")))
+        return rc;
+    stage(c, "ep_alltoall", 0);
+    // 6. out = resid + scale * sum of the partials in rank order
+    if (M) {
+        moe::launch_ep_combine(plan, static_cast<int>(M), static_cast<int>(n), static_cast<int>(H), ep.y_recv,
+                               resid_off ? at<float>(c, resid_off) : nullptr, L->spec.scale, at<float>(c, out_off),
+                               c->stream);
+        stage(c, "ep_combine", 1);
+    }
+    prof_end(c);
+    return check_launch(c, "forward_ep");
 }
 
 int moe_set_path(moe_ctx* c, int path) {

@@ -3,6 +3,7 @@
 #include <cuda.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
+#include <nccl.h>
 
 #include <cstdint>
 #include <string>
@@ -148,6 +149,37 @@ struct GraphEntry {
     uint64_t last_use = 0;
 };
 
+// NCCL entry points used by the expert-parallel layer (resolved at run time, nccl_dl.cu).
+struct NcclApi {
+    bool ok = false;
+    ncclResult_t (*get_unique_id)(ncclUniqueId*) = nullptr;
+    ncclResult_t (*comm_init_rank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
+    ncclResult_t (*comm_destroy)(ncclComm_t) = nullptr;
+    ncclResult_t (*group_start)() = nullptr;
+    ncclResult_t (*group_end)() = nullptr;
+    ncclResult_t (*send)(const void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
+    ncclResult_t (*recv)(void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
+    const char* (*error_string)(ncclResult_t) = nullptr;
+};
+// Null (with *err set) when NCCL cannot be loaded.
+const NcclApi* nccl_api(std::string* err);
+
+// Expert-parallel state of a context (moe_ep_init / moe_forward_ep): the communicator and the
+// exchange buffers, sized for n_ranks x capacity rows.
+struct EpState {
+    ncclComm_t comm = nullptr;
+    uint32_t n_ranks = 0, rank = 0;
+    uint32_t capacity = 0, hidden = 0, top_k = 0;  // buffer sizes
+    uint8_t* buf = nullptr;
+    uint8_t* plan = nullptr;
+    float* send_x = nullptr;
+    float* recv_x = nullptr;
+    float* y_send = nullptr;
+    float* y_recv = nullptr;
+    uint2* send_rec = nullptr;
+    uint2* recv_rec = nullptr;
+};
+
 struct Ctx {
     // CUDA graphs of moe_forward, keyed by (layer, M, path, stream)
     bool use_graphs = true;
@@ -170,6 +202,7 @@ struct Ctx {
     std::string err;
     std::vector<Layer> layers;
     Workspace ws;
+    EpState ep;
 };
 
 // Kernel launchers (stream-ordered, no synchronisation).

@@ -35,6 +35,7 @@ EXPORTS = (
     "moe_synth_iq4xs", "moe_profile", "moe_profile_read", "moe_launch_count", "moe_set_path",
     "moe_bucket_static", "moe_forward_topk", "moe_ep_plan_bytes", "moe_ep_dispatch",
     "moe_ep_combine", "moe_dequant_ref36", "moe_forward_norm", "moe_vocab_logits",
+    "moe_ep_unique_id", "moe_ep_init", "moe_forward_ep",
     "moe_layer_set_next",
 )
 
@@ -101,6 +102,9 @@ def lib():
         "moe_dequant_iq4xs": (i32, [vp, u64, u64, u64]),
         "moe_dequant_ref36": (i32, [vp, u64, u64, u64]),
         "moe_vocab_logits": (i32, [vp, u64, u32, u32, u64, u32, u64, u64]),
+        "moe_ep_unique_id": (i32, [vp, C.c_size_t]),
+        "moe_ep_init": (i32, [vp, vp, u32, u32]),
+        "moe_forward_ep": (i32, [vp, u32, u64, u64, u64, u32, u32]),
         "moe_forward_norm": (i32, [vp, u32, u64, u64, u32, f32]),
         "moe_layer_set_next": (i32, [vp, u32, i32]),
         "moe_synth_iq4xs": (i32, [vp, u64, u64, u64, u64]),
@@ -287,6 +291,23 @@ class Context:
     def vocab_logits(self, w_off, vocab, hidden, x_off, m, logits_off=0, ids_off=0):
         """LM-head projection (moe_vocab_logits): f32 logits [m][vocab] and/or argmax ids [m]."""
         self._check(lib().moe_vocab_logits(self.h, w_off, vocab, hidden, x_off, m, logits_off, ids_off))
+
+    # -- expert parallelism over NCCL (C level) --------------------------------------------------
+    @staticmethod
+    def ep_unique_id() -> bytes:
+        """A new NCCL unique id (128 bytes) for moe_ep_init; made by rank 0, shared out of band."""
+        buf = C.create_string_buffer(128)
+        rc = lib().moe_ep_unique_id(buf, 128)
+        if rc != 0:
+            raise MoeError(rc, _err(None))
+        return buf.raw
+
+    def ep_init(self, unique_id: bytes, n_ranks: int, rank: int):
+        buf = C.create_string_buffer(bytes(unique_id), 128)
+        self._check(lib().moe_ep_init(self.h, buf, n_ranks, rank))
+
+    def forward_ep(self, layer_id, x_off, resid_off, out_off, m, capacity):
+        self._check(lib().moe_forward_ep(self.h, layer_id, x_off, resid_off, out_off, m, capacity))
 
     def synth_iq4xs(self, dst_off, key, block_start, n_blocks):
         self._check(lib().moe_synth_iq4xs(self.h, dst_off, key, block_start, n_blocks))

@@ -66,3 +66,14 @@ def test_registry_and_layer_weights():
     w1, w3, w2 = lw.expert_tables(1)
     assert w1[2] == reg.lookup("blk.1.experts.2.w1.weight")
     assert len(w3) == 4 and len(w2) == 4
+
+
+def test_ep_unique_id_without_gpu():
+    """moe_ep_unique_id loads NCCL at run time and needs no device; a short buffer is rejected."""
+    try:
+        a = host.Context.ep_unique_id()
+    except host.MoeError as e:
+        pytest.skip(f"NCCL not loadable here: {e}")
+    assert len(a) == 128 and a != host.Context.ep_unique_id()
+    import ctypes
+    assert host.lib().moe_ep_unique_id(ctypes.create_string_buffer(64), 64) == -1  # MOE_E_INVALID
