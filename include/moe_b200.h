@@ -233,6 +233,19 @@ int moe_ep_init(moe_ctx* ctx, const void* unique_id, uint32_t n_ranks, uint32_t 
 int moe_forward_ep(moe_ctx* ctx, uint32_t layer_id, uint64_t x_off, uint64_t resid_off, uint64_t out_off,
                    uint32_t M, uint32_t capacity);
 
+/* How the rank blocks travel (set identically on every rank, before moe_forward_ep):
+ *   MOE_EP_TRANSPORT_PEER (default): the dispatch kernel stores rows and records straight into
+ *     the owner ranks' receive buffers and the combine kernel reads the partial rows from the
+ *     expert ranks' output buffers, over NVLink through CUDA IPC mappings of the context's
+ *     exchange buffers, with per-step flags (bounded waits) in place of collectives; falls back
+ *     to NCCL on every rank when any rank cannot map its peers;
+ *   MOE_EP_TRANSPORT_NCCL: grouped ncclSend/ncclRecv all-to-alls of whole capacity blocks. */
+#define MOE_EP_TRANSPORT_NCCL 0
+#define MOE_EP_TRANSPORT_PEER 1
+int moe_ep_set_transport(moe_ctx* ctx, int transport);
+/* The transport of the current exchange buffers (-1 before the first moe_forward_ep). */
+int moe_ep_transport(moe_ctx* ctx, int* transport);
+
 /* Expert-product kernels used by moe_forward / moe_forward_routed (a tuning and diagnostic
  * knob; the default picks by batch size: CUDA-core grouped GEMV for M <= 8, tcgen05 grouped
  * GEMM otherwise). */

@@ -1015,21 +1015,96 @@ static moe::EpPlan ep_plan_ptr(uint8_t* base, uint32_t M, uint32_t n_ranks) {
                        reinterpret_cast<int*>(base + a + b)};
 }
 
-// Exchange buffers for n_ranks x capacity rows of width H with (k+1)-entry records.
-static int ensure_ep_buffers(Ctx* c, uint32_t capacity, uint32_t H, uint32_t k) {
+static void ep_close_peers(moe::EpState& ep) {
+    for (uint32_t d = 0; d < 8; ++d) {
+        if (ep.peer_base[d]) cudaIpcCloseMemHandle(ep.peer_base[d]);
+        ep.peer_base[d] = nullptr;
+    }
+    ep.peer = false;
+}
+
+// Maps every other rank's exchange buffer (CUDA IPC handles all-gathered over the group).  The
+// outcome is agreed by all ranks (an all-reduce of the local result), so either every rank uses
+// the peer transport or none does.
+static int ep_map_peers(Ctx* c, const moe::NcclApi* api) {
     moe::EpState& ep = c->ep;
-    if (ep.buf && capacity <= ep.capacity && H <= ep.hidden && k <= ep.top_k) return MOE_OK;
+    const uint32_t n = ep.n_ranks;
+    int ok = 1;
+    cudaIpcMemHandle_t mine;
+    if (n > 1 && cudaIpcGetMemHandle(&mine, ep.buf) != cudaSuccess) {
+        cudaGetLastError();
+        ok = 0;
+        std::memset(&mine, 0, sizeof(mine));
+    }
+    std::vector<cudaIpcMemHandle_t> all(n);
+    void* tmp = nullptr;
+    MOE_CUDA(c, cudaMalloc(&tmp, sizeof(cudaIpcMemHandle_t) * (n + 1) + 16));
+    uint8_t* t = static_cast<uint8_t*>(tmp);
+    int* flag = reinterpret_cast<int*>(t + sizeof(cudaIpcMemHandle_t) * (n + 1));
+    int rc = MOE_OK;
+    ncclResult_t r = ncclSuccess;
+    if (n > 1) {
+        cudaMemcpy(t + sizeof(cudaIpcMemHandle_t) * n, &mine, sizeof(mine), cudaMemcpyHostToDevice);
+        r = api->all_gather(t + sizeof(cudaIpcMemHandle_t) * n, t, sizeof(mine), ncclUint8, ep.comm, c->stream);
+        if (r == ncclSuccess) {
+            cudaStreamSynchronize(c->stream);
+            cudaMemcpy(all.data(), t, sizeof(cudaIpcMemHandle_t) * n, cudaMemcpyDeviceToHost);
+            for (uint32_t d = 0; d < n && ok; ++d) {
+                if (d == ep.rank) continue;
+                void* p = nullptr;
+                if (cudaIpcOpenMemHandle(&p, all[d], cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+                    cudaGetLastError();
+                    ok = 0;
+                } else {
+                    ep.peer_base[d] = static_cast<uint8_t*>(p);
+                }
+            }
+        }
+    }
+    if (r == ncclSuccess) {
+        cudaMemcpy(flag, &ok, sizeof(int), cudaMemcpyHostToDevice);
+        r = api->all_reduce(flag, flag, 1, ncclInt32, ncclMin, ep.comm, c->stream);
+        if (r == ncclSuccess) {
+            cudaStreamSynchronize(c->stream);
+            cudaMemcpy(&ok, flag, sizeof(int), cudaMemcpyDeviceToHost);
+        }
+    }
+    cudaFree(tmp);
+    if (r != ncclSuccess) rc = nccl_fail(c, api, r, "peer handle exchange");
+    if (!ok || rc != MOE_OK) ep_close_peers(ep);
+    else ep.peer = true;
+    return rc;
+}
+
+// Exchange buffers for n_ranks x capacity rows of width H with (k+1)-entry records, the step
+// flags and epoch, and (peer transport) the mappings of the other ranks' buffers.  Collective
+// when it reallocates: every rank calls it with the same sizes.
+static int ensure_ep_buffers(Ctx* c, const moe::NcclApi* api, uint32_t capacity, uint32_t H, uint32_t k) {
+    moe::EpState& ep = c->ep;
+    const bool want_peer = ep.transport == MOE_EP_TRANSPORT_PEER;
+    if (ep.buf && capacity <= ep.capacity && H <= ep.hidden && k <= ep.top_k && ep.peer == (want_peer && ep.peer))
+        return MOE_OK;
     capacity = std::max(capacity, ep.capacity);
     H = std::max(H, ep.hidden);
     k = std::max(k, ep.top_k);
     const uint64_t rows = static_cast<uint64_t>(ep.n_ranks) * capacity;
-    const uint64_t xb = rows * H * 4, rb = rows * (k + 1) * 8;
+    const uint64_t xb = (rows * H * 4 + 255) / 256 * 256, rb = (rows * (k + 1) * 8 + 255) / 256 * 256;
     const uint64_t pb = (moe_ep_plan_bytes(capacity, ep.n_ranks) + 255) / 256 * 256;
     MOE_CUDA(c, cudaStreamSynchronize(c->stream));
+    if (ep.peer) {
+        // every rank stops using the old mappings before any rank frees its buffer
+        ep_close_peers(ep);
+        int* one = nullptr;
+        MOE_CUDA(c, cudaMalloc(&one, sizeof(int)));
+        const ncclResult_t r = api->all_reduce(one, one, 1, ncclInt32, ncclSum, ep.comm, c->stream);
+        cudaStreamSynchronize(c->stream);
+        cudaFree(one);
+        if (r != ncclSuccess) return nccl_fail(c, api, r, "exchange buffer release");
+    }
     if (ep.buf) cudaFree(ep.buf);
     ep.buf = nullptr;
     void* p = nullptr;
-    cudaError_t e = cudaMalloc(&p, pb + 4 * xb + 2 * rb);
+    cudaError_t e = cudaMalloc(&p, pb + 4 * xb + 2 * rb + 256);
     if (e != cudaSuccess) {
         cudaGetLastError();
         ep.capacity = ep.hidden = ep.top_k = 0;
@@ -1040,25 +1115,71 @@ static int ensure_ep_buffers(Ctx* c, uint32_t capacity, uint32_t H, uint32_t k) 
     ep.buf = b;
     ep.plan = b;
     ep.send_x = reinterpret_cast<float*>(b + pb);
-    ep.recv_x = reinterpret_cast<float*>(b + pb + xb);
-    ep.y_send = reinterpret_cast<float*>(b + pb + 2 * xb);
+    ep.off_recv_x = pb + xb;
+    ep.recv_x = reinterpret_cast<float*>(b + ep.off_recv_x);
+    ep.off_y_send = pb + 2 * xb;
+    ep.y_send = reinterpret_cast<float*>(b + ep.off_y_send);
     ep.y_recv = reinterpret_cast<float*>(b + pb + 3 * xb);
     ep.send_rec = reinterpret_cast<uint2*>(b + pb + 4 * xb);
-    ep.recv_rec = reinterpret_cast<uint2*>(b + pb + 4 * xb + rb);
+    ep.off_recv_rec = pb + 4 * xb + rb;
+    ep.recv_rec = reinterpret_cast<uint2*>(b + ep.off_recv_rec);
+    ep.off_flags = pb + 4 * xb + 2 * rb;
+    ep.flags = reinterpret_cast<unsigned long long*>(b + ep.off_flags);
+    ep.epoch = ep.flags + 16;
+    MOE_CUDA(c, cudaMemsetAsync(b + ep.off_flags, 0, 256, c->stream));
+    MOE_CUDA(c, cudaStreamSynchronize(c->stream));
     ep.capacity = capacity;
     ep.hidden = H;
     ep.top_k = k;
+    if (want_peer) return ep_map_peers(c, api);
     return MOE_OK;
 }
 
 static void ep_release(Ctx* c) {
     moe::EpState& ep = c->ep;
+    ep_close_peers(ep);
     if (ep.comm) {
         const moe::NcclApi* api = moe::nccl_api(nullptr);
         if (api) api->comm_destroy(ep.comm);
     }
     if (ep.buf) cudaFree(ep.buf);
+    const int transport = ep.transport;
     ep = moe::EpState{};
+    ep.transport = transport;
+}
+
+// Peer addresses of this rank's blocks at every rank (see EpPeers).
+static moe::EpPeers ep_peers(const moe::EpState& ep) {
+    moe::EpPeers P{};
+    const uint64_t rb = static_cast<uint64_t>(ep.rank) * ep.capacity;
+    for (uint32_t d = 0; d < ep.n_ranks; ++d) {
+        uint8_t* base = d == ep.rank ? ep.buf : ep.peer_base[d];
+        P.x[d] = reinterpret_cast<float*>(base + ep.off_recv_x) + rb * ep.hidden;
+        P.rec[d] = reinterpret_cast<uint2*>(base + ep.off_recv_rec) + rb * (ep.top_k + 1);
+        P.y[d] = reinterpret_cast<const float*>(base + ep.off_y_send) + rb * ep.hidden;
+        for (int s = 0; s < 2; ++s)
+            P.flag[s][d] = reinterpret_cast<unsigned long long*>(base + ep.off_flags) + s * 8 + ep.rank;
+    }
+    return P;
+}
+
+int moe_ep_set_transport(moe_ctx* c, int transport) {
+    if (!c) return fail(c, MOE_E_INVALID, "NULL context");
+    if (transport != MOE_EP_TRANSPORT_NCCL && transport != MOE_EP_TRANSPORT_PEER)
+        return fail(c, MOE_E_INVALID, "unknown transport %d", transport);
+    if (c->ep.transport != transport) {
+        DeviceGuard g(c->device);
+        MOE_CUDA(c, cudaStreamSynchronize(c->stream));
+        c->ep.transport = transport;
+        c->ep.capacity = 0;  // the next moe_forward_ep re-creates the buffers (collectively)
+    }
+    return MOE_OK;
+}
+
+int moe_ep_transport(moe_ctx* c, int* transport) {
+    if (!c || !transport) return fail(c, MOE_E_INVALID, "NULL argument");
+    *transport = c->ep.buf ? (c->ep.peer ? MOE_EP_TRANSPORT_PEER : MOE_EP_TRANSPORT_NCCL) : -1;
+    return MOE_OK;
 }
 
 int moe_ep_unique_id(void* out, size_t n) {
@@ -1114,47 +1235,74 @@ int moe_forward_ep(moe_ctx* c, uint32_t layer_id, uint64_t x_off, uint64_t resid
     }
     const moe::NcclApi* api = moe::nccl_api(nullptr);
     DeviceGuard g(c->device);
-    if ((rc = ensure_ep_buffers(c, capacity, H, k))) return rc;
+    if ((rc = ensure_ep_buffers(c, api, capacity, H, k))) return rc;
     const uint32_t rows = n * capacity;
     if ((rc = ensure_layer_ws(c, *L, std::max(rows, M)))) return rc;
     const size_t rec = static_cast<size_t>(k + 1) * 8;
     const moe::EpPlan plan = ep_plan_ptr(ep.plan, std::max(M, 1u), n);
     const int epr = static_cast<int>(E / n);
     prof_begin(c);
-    // 1-2. route the local tokens, build the rank blocks (empty records pad every block)
-    MOE_CUDA(c, cudaMemsetAsync(ep.send_rec, 0xFF, rows * rec, c->stream));
     if (M) {
         run_set_io(c, at<float>(c, x_off), nullptr, nullptr);
         if ((rc = run_route(c, *L, M))) return rc;
         moe::launch_ep_plan(c->ws.topk, static_cast<int>(M), static_cast<int>(k), epr, static_cast<int>(n),
                             static_cast<int>(ep.rank), static_cast<int>(capacity), plan, c->ws.status, c->stream);
-        moe::launch_ep_gather(at<float>(c, x_off), c->ws.topk, plan, static_cast<int>(M), static_cast<int>(H),
-                              static_cast<int>(k), epr, static_cast<int>(n), static_cast<int>(ep.rank), ep.send_x,
-                              ep.send_rec, c->stream);
-        stage(c, "ep_dispatch", 3);
+        stage(c, "ep_plan", 2);
     }
-    // 3. rows and records to their expert ranks
-    if ((rc = ep_alltoall(c, api, ep.send_x, ep.recv_x, static_cast<size_t>(capacity) * H, ncclFloat32, 4,
-                          "dispatch all-to-all")))
-        return rc;
-    if ((rc = ep_alltoall(c, api, ep.send_rec, ep.recv_rec, capacity * rec, ncclUint8, 1, "record all-to-all")))
-        return rc;
-    stage(c, "ep_alltoall", 0);
-    // 4. this rank's experts (and the shared expert for its own tokens) on every received row
-    MOE_CUDA(c, cudaMemcpyAsync(c->ws.topk, ep.recv_rec, rows * rec, cudaMemcpyDeviceToDevice, c->stream));
-    run_set_io(c, ep.recv_x, nullptr, ep.y_send);
-    if ((rc = run_experts(c, *L, rows, true, L->has_shared(), 1.0f))) return rc;
-    // 5. partial rows back to their owners
-    if ((rc = ep_alltoall(c, api, ep.y_send, ep.y_recv, static_cast<size_t>(capacity) * H, ncclFloat32, 4,
-                          "combine all-to-all")))
-        return rc;
-    stage(c, "ep_alltoall", 0);
-    // 6. out = resid + scale * sum of the partials in rank order
-    if (M) {
-        moe::launch_ep_combine(plan, static_cast<int>(M), static_cast<int>(n), static_cast<int>(H), ep.y_recv,
-                               resid_off ? at<float>(c, resid_off) : nullptr, L->spec.scale, at<float>(c, out_off),
-                               c->stream);
-        stage(c, "ep_combine", 1);
+    const float* resid = resid_off ? at<float>(c, resid_off) : nullptr;
+    if (ep.peer) {
+        // rows and records stored into every owner's receive block over NVLink, then the
+        // rank's experts, then each owner reads its partial rows from the expert ranks
+        const moe::EpPeers P = ep_peers(ep);
+        moe::launch_ep_push(at<float>(c, x_off), c->ws.topk, plan, static_cast<int>(M), static_cast<int>(H),
+                            static_cast<int>(k), epr, static_cast<int>(n), static_cast<int>(ep.rank),
+                            static_cast<int>(capacity), P, c->stream);
+        moe::launch_ep_signal(ep.epoch, true, static_cast<int>(n), P, 0, c->stream);
+        moe::launch_ep_wait(ep.flags, ep.epoch, static_cast<int>(n), c->ws.status, c->stream);
+        stage(c, "ep_push", M ? 4 : 3);
+        MOE_CUDA(c, cudaMemcpyAsync(c->ws.topk, ep.recv_rec, rows * rec, cudaMemcpyDeviceToDevice, c->stream));
+        run_set_io(c, ep.recv_x, nullptr, ep.y_send);
+        if ((rc = run_experts(c, *L, rows, true, L->has_shared(), 1.0f))) return rc;
+        moe::launch_ep_signal(ep.epoch, false, static_cast<int>(n), P, 1, c->stream);
+        moe::launch_ep_wait(ep.flags + 8, ep.epoch, static_cast<int>(n), c->ws.status, c->stream);
+        stage(c, "ep_sync", 2);
+        if (M) {
+            moe::launch_ep_pull_combine(plan, static_cast<int>(M), static_cast<int>(n), static_cast<int>(H), P,
+                                        resid, L->spec.scale, at<float>(c, out_off), c->stream);
+            stage(c, "ep_combine", 1);
+        }
+    } else {
+        // 1-2. the rank blocks (empty records pad every block)
+        MOE_CUDA(c, cudaMemsetAsync(ep.send_rec, 0xFF, rows * rec, c->stream));
+        if (M) {
+            moe::launch_ep_gather(at<float>(c, x_off), c->ws.topk, plan, static_cast<int>(M), static_cast<int>(H),
+                                  static_cast<int>(k), epr, static_cast<int>(n), static_cast<int>(ep.rank), ep.send_x,
+                                  ep.send_rec, c->stream);
+            stage(c, "ep_dispatch", 1);
+        }
+        // 3. rows and records to their expert ranks
+        if ((rc = ep_alltoall(c, api, ep.send_x, ep.recv_x, static_cast<size_t>(capacity) * H, ncclFloat32, 4,
+                              "dispatch all-to-all")))
+            return rc;
+        if ((rc = ep_alltoall(c, api, ep.send_rec, ep.recv_rec, capacity * rec, ncclUint8, 1,
+                              "record all-to-all")))
+            return rc;
+        stage(c, "ep_alltoall", 0);
+        // 4. this rank's experts (and the shared expert for its own tokens) on every received row
+        MOE_CUDA(c, cudaMemcpyAsync(c->ws.topk, ep.recv_rec, rows * rec, cudaMemcpyDeviceToDevice, c->stream));
+        run_set_io(c, ep.recv_x, nullptr, ep.y_send);
+        if ((rc = run_experts(c, *L, rows, true, L->has_shared(), 1.0f))) return rc;
+        // 5. partial rows back to their owners
+        if ((rc = ep_alltoall(c, api, ep.y_send, ep.y_recv, static_cast<size_t>(capacity) * H, ncclFloat32, 4,
+                              "combine all-to-all")))
+            return rc;
+        stage(c, "ep_alltoall", 0);
+        // 6. out = resid + scale * sum of the partials in rank order
+        if (M) {
+            moe::launch_ep_combine(plan, static_cast<int>(M), static_cast<int>(n), static_cast<int>(H), ep.y_recv,
+                                   resid, L->spec.scale, at<float>(c, out_off), c->stream);
+            stage(c, "ep_combine", 1);
+        }
     }
     prof_end(c);
     return check_launch(c, "forward_ep");

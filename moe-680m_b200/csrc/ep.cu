@@ -161,7 +161,132 @@ __global__ void ep_combine_kernel(const uint32_t* __restrict__ mask, const int* 
     *reinterpret_cast<float4*>(out + row) = r;
 }
 
+// ---- peer transport: rows and records stored straight into the owner ranks' receive blocks,
+// partial rows read straight from the expert ranks' output blocks (NVLink loads/stores through
+// CUDA IPC mappings; plain loads and stores only) --------------------------------------------
+
+// Warp per token: its row and reduced record to block my_rank of every rank it visits.
+__global__ void ep_push_kernel(const float* __restrict__ x, const uint2* __restrict__ topk,
+                               const uint32_t* __restrict__ mask, const int* __restrict__ pos, int M, int H,
+                               int k, int epr, int n_ranks, int my_rank, EpPeers P) {
+    const int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    if (t < M) {
+        const uint32_t m = mask[t];
+        const float4* src = reinterpret_cast<const float4*>(x + static_cast<size_t>(t) * H);
+        const uint2* rec = topk + static_cast<size_t>(t) * (k + 1);
+        const uint2 r = lane <= k ? rec[lane] : make_uint2(0, 0);
+        for (int d = 0; d < n_ranks; ++d) {
+            if (!((m >> d) & 1u)) continue;
+            const size_t p = static_cast<size_t>(pos[static_cast<size_t>(t) * n_ranks + d]);
+            float4* dst = reinterpret_cast<float4*>(P.x[d] + p * H);
+            for (int i = lane; i < H / 4; i += 32) dst[i] = src[i];
+            if (lane <= k) {
+                uint2 o = r;
+                if (lane > 0) {
+                    const uint32_t e = r.x;
+                    o.x = (e != kNoExpert && e / static_cast<uint32_t>(epr) == static_cast<uint32_t>(d))
+                              ? e : kNoExpert;
+                } else if (d != my_rank) {
+                    o.x = kNoExpert;
+                }
+                P.rec[d][p * (k + 1) + lane] = o;
+            }
+        }
+    }
+    __threadfence_system();
+}
+
+// Empty records for the rows [used_d, capacity) of block my_rank at every rank d (used_d from the
+// scan's counts, or 0 when this rank has no tokens).
+__global__ void ep_fill_kernel(const int* __restrict__ counts, int n_ranks, int capacity, int k, EpPeers P) {
+    const int per = capacity * (k + 1);
+    for (int d = 0; d < n_ranks; ++d) {
+        const int used = counts ? counts[d] * (k + 1) : 0;
+        for (int i = used + blockIdx.x * blockDim.x + threadIdx.x; i < per; i += gridDim.x * blockDim.x)
+            P.rec[d][i] = make_uint2(kNoExpert, kNoExpert);
+    }
+    __threadfence_system();
+}
+
+// Publish step progress to every rank: flag[d] (this rank's slot at rank d) = epoch, after
+// bumping the local epoch when `bump` (one bump per layer step).
+__global__ void ep_signal_kernel(unsigned long long* epoch, int bump, int n_ranks, EpPeers P, int slot) {
+    if (threadIdx.x != 0) return;
+    __threadfence_system();
+    const unsigned long long e = *epoch + static_cast<unsigned long long>(bump);
+    if (bump) *epoch = e;
+    for (int d = 0; d < n_ranks; ++d)
+        asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(P.flag[slot][d]), "l"(e) : "memory");
+}
+
+// Wait until every rank has published this step to slot `slot` of this rank's flags (bounded:
+// gives up after 1 s, records kDevTimeout and returns).
+__global__ void ep_wait_kernel(const unsigned long long* flags, const unsigned long long* epoch, int n_ranks,
+                               int* status) {
+    const int d = threadIdx.x;
+    if (d >= n_ranks) return;
+    const unsigned long long e = *epoch;
+    unsigned long long v, t0, now;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+    for (uint32_t i = 0;; ++i) {
+        asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(flags + d) : "memory");
+        if (v >= e) break;
+        if ((i & 255u) == 255u) {
+            asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(now));
+            if (now - t0 > 1000000000ull) { set_dev_error(status, kDevTimeout); break; }
+        }
+    }
+}
+
+// out[t] = resid[t] + scale * sum over the ranks d in mask (ascending) of the partial row that
+// rank d computed for t, read from rank d's output block.
+__global__ void ep_pull_combine_kernel(const uint32_t* __restrict__ mask, const int* __restrict__ pos,
+                                       int n_ranks, int H, EpPeers P, const float* __restrict__ resid,
+                                       float scale, float* __restrict__ out) {
+    const int t = blockIdx.x;
+    const int c = (blockIdx.y * blockDim.x + threadIdx.x) * 4;
+    if (c >= H) return;
+    const uint32_t m = mask[t];
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int d = 0; d < n_ranks; ++d) {
+        if (!((m >> d) & 1u)) continue;
+        const size_t p = static_cast<size_t>(pos[static_cast<size_t>(t) * n_ranks + d]);
+        const float4 y = *reinterpret_cast<const float4*>(P.y[d] + p * H + c);
+        acc.x += y.x; acc.y += y.y; acc.z += y.z; acc.w += y.w;
+    }
+    const size_t row = static_cast<size_t>(t) * H + c;
+    float4 r = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (resid) r = *reinterpret_cast<const float4*>(resid + row);
+    r.x = fmaf(scale, acc.x, r.x); r.y = fmaf(scale, acc.y, r.y);
+    r.z = fmaf(scale, acc.z, r.z); r.w = fmaf(scale, acc.w, r.w);
+    *reinterpret_cast<float4*>(out + row) = r;
+}
+
 }  // namespace
+
+void launch_ep_push(const float* x, const uint2* topk, EpPlan plan, int M, int H, int k, int epr, int n_ranks,
+                    int my_rank, int capacity, const EpPeers& P, cudaStream_t s) {
+    if (M > 0)
+        ep_push_kernel<<<(M * 32 + 255) / 256, 256, 0, s>>>(x, topk, plan.mask, plan.pos, M, H, k, epr, n_ranks,
+                                                            my_rank, P);
+    ep_fill_kernel<<<32, 256, 0, s>>>(M > 0 ? plan.offsets + n_ranks : nullptr, n_ranks, capacity, k, P);
+}
+
+void launch_ep_signal(unsigned long long* epoch, bool bump, int n_ranks, const EpPeers& P, int slot,
+                      cudaStream_t s) {
+    ep_signal_kernel<<<1, 32, 0, s>>>(epoch, bump ? 1 : 0, n_ranks, P, slot);
+}
+
+void launch_ep_wait(const unsigned long long* flags, const unsigned long long* epoch, int n_ranks, int* status,
+                    cudaStream_t s) {
+    ep_wait_kernel<<<1, 32, 0, s>>>(flags, epoch, n_ranks, status);
+}
+
+void launch_ep_pull_combine(EpPlan plan, int M, int n_ranks, int H, const EpPeers& P, const float* resid,
+                            float scale, float* out, cudaStream_t s) {
+    dim3 grid(M, (H / 4 + 255) / 256);
+    ep_pull_combine_kernel<<<grid, 256, 0, s>>>(plan.mask, plan.pos, n_ranks, H, P, resid, scale, out);
+}
 
 void launch_ep_plan(const uint2* topk, int M, int k, int epr, int n_ranks, int my_rank, int capacity,
                     EpPlan plan, int* status, cudaStream_t s) {

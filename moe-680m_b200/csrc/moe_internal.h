@@ -159,6 +159,9 @@ struct NcclApi {
     ncclResult_t (*group_end)() = nullptr;
     ncclResult_t (*send)(const void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
     ncclResult_t (*recv)(void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
+    ncclResult_t (*all_gather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
+    ncclResult_t (*all_reduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
+                               cudaStream_t) = nullptr;
     const char* (*error_string)(ncclResult_t) = nullptr;
 };
 // Null (with *err set) when NCCL cannot be loaded.
@@ -178,6 +181,13 @@ struct EpState {
     float* y_recv = nullptr;
     uint2* send_rec = nullptr;
     uint2* recv_rec = nullptr;
+    unsigned long long* flags = nullptr;  // [2][8]: per slot, the step each rank has published
+    unsigned long long* epoch = nullptr;  // steps started by this rank
+    // peer transport: the other ranks' exchange buffers mapped through CUDA IPC
+    int transport = 1;                    // MOE_EP_TRANSPORT_PEER / _NCCL as requested
+    bool peer = false;                    // the peer transport is active for the current buffers
+    uint8_t* peer_base[8] = {};
+    uint64_t off_recv_x = 0, off_recv_rec = 0, off_y_send = 0, off_flags = 0;
 };
 
 struct Ctx {
@@ -253,6 +263,22 @@ struct EpPlan {
     int* pos;
     int* offsets;
 };
+// Peer-transport addresses of one rank (device pointers valid on this rank's GPU: local or CUDA
+// IPC mappings of the other ranks' exchange buffers).
+struct EpPeers {
+    float* x[kMaxEpRanks];      // block my_rank of rank d's receive rows
+    uint2* rec[kMaxEpRanks];    // block my_rank of rank d's receive records
+    const float* y[kMaxEpRanks];  // block my_rank of rank d's partial-row output
+    unsigned long long* flag[2][kMaxEpRanks];  // this rank's slot in rank d's flags (dispatch, outputs)
+};
+void launch_ep_push(const float* x, const uint2* topk, EpPlan plan, int M, int H, int k, int epr, int n_ranks,
+                    int my_rank, int capacity, const EpPeers& P, cudaStream_t s);
+void launch_ep_signal(unsigned long long* epoch, bool bump, int n_ranks, const EpPeers& P, int slot,
+                      cudaStream_t s);
+void launch_ep_wait(const unsigned long long* flags, const unsigned long long* epoch, int n_ranks, int* status,
+                    cudaStream_t s);
+void launch_ep_pull_combine(EpPlan plan, int M, int n_ranks, int H, const EpPeers& P, const float* resid,
+                            float scale, float* out, cudaStream_t s);
 void launch_ep_plan(const uint2* topk, int M, int k, int epr, int n_ranks, int my_rank, int capacity,
                     EpPlan plan, int* status, cudaStream_t s);
 void launch_ep_gather(const float* x, const uint2* topk, EpPlan plan, int M, int H, int k, int epr,

@@ -40,6 +40,8 @@ const NcclApi* nccl_api(std::string* err) {
         api.group_end = reinterpret_cast<decltype(api.group_end)>(sym("ncclGroupEnd"));
         api.send = reinterpret_cast<decltype(api.send)>(sym("ncclSend"));
         api.recv = reinterpret_cast<decltype(api.recv)>(sym("ncclRecv"));
+        api.all_gather = reinterpret_cast<decltype(api.all_gather)>(sym("ncclAllGather"));
+        api.all_reduce = reinterpret_cast<decltype(api.all_reduce)>(sym("ncclAllReduce"));
         api.error_string = reinterpret_cast<decltype(api.error_string)>(sym("ncclGetErrorString"));
         api.ok = ok;
     });

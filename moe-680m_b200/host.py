@@ -25,6 +25,7 @@ MOE_F_SHARED_GATE = 2
 MOE_F_EXPERT_SUBSET = 4
 MOE_NO_EXPERT = 0xFFFFFFFF
 MOE_FT_NO_SHARED, MOE_FT_SHARED_ONLY, MOE_FT_UNSCALED = 1, 2, 4
+MOE_EP_TRANSPORT_NCCL, MOE_EP_TRANSPORT_PEER = 0, 1
 
 # Every symbol include/moe_b200.h declares.
 EXPORTS = (
@@ -35,7 +36,7 @@ EXPORTS = (
     "moe_synth_iq4xs", "moe_profile", "moe_profile_read", "moe_launch_count", "moe_set_path",
     "moe_bucket_static", "moe_forward_topk", "moe_ep_plan_bytes", "moe_ep_dispatch",
     "moe_ep_combine", "moe_dequant_ref36", "moe_forward_norm", "moe_vocab_logits",
-    "moe_ep_unique_id", "moe_ep_init", "moe_forward_ep",
+    "moe_ep_unique_id", "moe_ep_init", "moe_forward_ep", "moe_ep_set_transport", "moe_ep_transport",
     "moe_layer_set_next",
 )
 
@@ -105,6 +106,8 @@ def lib():
         "moe_ep_unique_id": (i32, [vp, C.c_size_t]),
         "moe_ep_init": (i32, [vp, vp, u32, u32]),
         "moe_forward_ep": (i32, [vp, u32, u64, u64, u64, u32, u32]),
+        "moe_ep_set_transport": (i32, [vp, i32]),
+        "moe_ep_transport": (i32, [vp, P(i32)]),
         "moe_forward_norm": (i32, [vp, u32, u64, u64, u32, f32]),
         "moe_layer_set_next": (i32, [vp, u32, i32]),
         "moe_synth_iq4xs": (i32, [vp, u64, u64, u64, u64]),
@@ -305,6 +308,14 @@ class Context:
     def ep_init(self, unique_id: bytes, n_ranks: int, rank: int):
         buf = C.create_string_buffer(bytes(unique_id), 128)
         self._check(lib().moe_ep_init(self.h, buf, n_ranks, rank))
+
+    def ep_set_transport(self, transport: int):
+        self._check(lib().moe_ep_set_transport(self.h, transport))
+
+    def ep_transport(self) -> int:
+        v = C.c_int(0)
+        self._check(lib().moe_ep_transport(self.h, C.byref(v)))
+        return v.value
 
     def forward_ep(self, layer_id, x_off, resid_off, out_off, m, capacity):
         self._check(lib().moe_forward_ep(self.h, layer_id, x_off, resid_off, out_off, m, capacity))

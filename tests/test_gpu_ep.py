@@ -225,31 +225,35 @@ def test_ep_two_ranks_match_single_gpu():
 
 # ---- the C-level expert-parallel layer (moe_ep_init / moe_forward_ep, NCCL inside the library) --
 
-def test_c_abi_ep_one_rank(full):
+@pytest.mark.parametrize("transport", [host.MOE_EP_TRANSPORT_PEER, host.MOE_EP_TRANSPORT_NCCL])
+def test_c_abi_ep_one_rank(full, transport):
     ctx, lid = full
+    ctx.ep_set_transport(transport)
     ctx.ep_init(host.Context.ep_unique_id(), 1, 0)
     m = 260
     x = synth.tokens(SEED, 5, m, FULL.hidden)
     xo = ctx.put(x)
     ref_o, ep_o = ctx.alloc(x.nbytes), ctx.alloc(x.nbytes)
     ctx.forward(lid, xo, xo, ref_o, m)
-    for cap in (m, 300):  # a second call with a larger capacity regrows the exchange buffers
+    for cap in (m, 300, 300):  # a larger capacity regrows the exchange buffers; then a reuse
         ctx.forward_ep(lid, xo, xo, ep_o, m, cap)
         ctx.sync()
         got = ctx.download(ep_o, (m, FULL.hidden))
         assert O.rel_l2(got, ctx.download(ref_o, (m, FULL.hidden))) < 1e-6
+    assert ctx.ep_transport() == transport
     ctx.forward_ep(lid, xo, xo, ep_o, 0, 8)  # a rank without tokens still takes part
     ctx.sync()
     with pytest.raises(host.MoeError):
         ctx.forward_ep(lid, xo, xo, ep_o, m, m - 1)  # capacity below the local tokens
 
 
-def _c_ep_worker(rank, world, uid, tokens_per_rank, q):
+def _c_ep_worker(rank, world, uid, tokens_per_rank, transport, q):
     try:
         E, H = FULL.n_experts, FULL.hidden
         epr = E // world
         ctx = host.Context(rank, 1 << 30)
         _, _, ids = host.build_synthetic_model(ctx, SEED, 1, FULL, 1.1, experts=range(rank * epr, (rank + 1) * epr))
+        ctx.ep_set_transport(transport)
         ctx.ep_init(uid, world, rank)
         m = tokens_per_rank[rank]
         x_all = synth.tokens(SEED, 1, sum(tokens_per_rank), H)
@@ -257,25 +261,29 @@ def _c_ep_worker(rank, world, uid, tokens_per_rank, q):
         x = x_all[start:start + m]
         xo = ctx.put(x if m else np.zeros((1, H), np.float32))
         out = ctx.alloc(max(m, 1) * H * 4)
-        for _ in range(2):  # the second step reuses the exchange buffers
+        for _ in range(3):  # later steps reuse the exchange buffers and step flags
             ctx.forward_ep(ids[0], xo, xo, out, m, max(tokens_per_rank))
         ctx.sync()
         got = ctx.download(out, (m, H)) if m else np.zeros((0, H), np.float32)
+        used = ctx.ep_transport()
         ctx.close()
-        q.put((rank, x, got))
+        q.put((rank, x, (got, used)))
     except Exception as e:  # reported to the parent
         q.put((rank, None, repr(e)))
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-def test_c_abi_ep_two_ranks_match_single_gpu():
+@pytest.mark.parametrize("transport,tpr", [(host.MOE_EP_TRANSPORT_PEER, [300, 212]),
+                                           (host.MOE_EP_TRANSPORT_PEER, [0, 97]),
+                                           (host.MOE_EP_TRANSPORT_NCCL, [300, 212])])
+def test_c_abi_ep_two_ranks_match_single_gpu(transport, tpr):
     import torch.multiprocessing as mp
     os.environ["NCCL_NVLS_ENABLE"] = "0"
-    world, tpr = 2, [300, 212]
+    world = 2
     uid = host.Context.ep_unique_id()
     mpc = mp.get_context("spawn")
     q = mpc.Queue()
-    procs = [mpc.Process(target=_c_ep_worker, args=(r, world, uid, tpr, q)) for r in range(world)]
+    procs = [mpc.Process(target=_c_ep_worker, args=(r, world, uid, tpr, transport, q)) for r in range(world)]
     for p in procs:
         p.start()
     res = {}
@@ -289,6 +297,7 @@ def test_c_abi_ep_two_ranks_match_single_gpu():
             p.join(timeout=60)
             if p.is_alive():
                 p.kill()
+    assert res[0][1][1] == transport and res[1][1][1] == transport
     x = np.concatenate([res[0][0], res[1][0]])
-    got = np.concatenate([res[0][1], res[1][1]])
+    got = np.concatenate([res[0][1][0], res[1][1][0]])
     assert O.rel_l2(got, _single_gpu_reference(x)) < 1e-6
