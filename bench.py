@@ -222,6 +222,10 @@ def main():
     ap.add_argument("--only", default="all", choices=["all", "prefill", "lm_head"],
                     help="prefill: skip the decode, config-3, end-to-end and CPU legs; lm_head: only "
                          "the LM-head leg, 0.3 GB on the device (profiling runs)")
+    ap.add_argument("--ep", default="peer", choices=["peer", "nccl", "torch"],
+                    help="expert-parallel exchange at N>1: peer = moe_forward_ep over NVLink peer memory "
+                         "(default), nccl = moe_forward_ep over NCCL all-to-all, torch = ep.py over "
+                         "torch.distributed")
     ap.add_argument("--path", type=int, default=0,
                     help="expert kernels: 0 auto, 1 CUDA-core GEMV, 2 tcgen05 (A in smem), 3 tcgen05 (A in TMEM)")
     args = ap.parse_args()
@@ -273,6 +277,12 @@ def main():
     torch.cuda.set_stream(stream)
     ctx.set_stream(stream.cuda_stream)
     ctx.set_path(args.path)
+    c_ep = ep_mode and args.ep != "torch"
+    if c_ep:  # the library's own expert-parallel group (NCCL id from rank 0)
+        uid = [host.Context.ep_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        ctx.ep_set_transport(host.MOE_EP_TRANSPORT_PEER if args.ep == "peer" else host.MOE_EP_TRANSPORT_NCCL)
+        ctx.ep_init(uid[0], world, rank)
     pre = host.build_synthetic_model(ctx, SEED, 1, sh, ZIPF, experts=my_experts)[2][0]
     dec_ids = host.build_synthetic_model(ctx, SEED + 1, n_dec_layers, sh, None)[2] if n_dec_layers else []
     K, W = args.steps, args.warmup
@@ -284,7 +294,40 @@ def main():
     ep_graphs, ep_caps = [], []
 
     def make_step(lid, m, out):
-        if ep_mode:
+        if c_ep:
+            xin_ep = ctx.alloc(m * H * 4)  # the captured step's fixed input rows
+            nb = m * H * 4
+            arena[xin_ep:xin_ep + nb].zero_()
+            ctx.forward_ep(lid, xin_ep, xin_ep, out, m, m)  # eager first step: buffers, workspace
+            torch.cuda.synchronize()
+            g = torch.cuda.CUDAGraph()
+            try:
+                with torch.cuda.graph(g, stream=stream):
+                    ctx.forward_ep(lid, xin_ep, xin_ep, out, m, m)
+                ok = 1
+            except Exception as e:  # noqa: BLE001 - reported in the JSON line
+                ok, why = 0, type(e).__name__
+            flag = torch.tensor([ok], device=arena.device)
+            dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+            captured = bool(int(flag.item()))
+            if captured:
+                ep_caps.append(g)
+            ep_graphs.append(("captured" if captured else "eager" + ("" if ok else f" ({why})"))
+                             + ", transport " + {0: "nccl", 1: "peer"}.get(ctx.ep_transport(), "?"))
+
+            def step(x_off):
+                if x_off != xin_ep:
+                    arena[xin_ep:xin_ep + nb].copy_(arena[x_off:x_off + nb])
+                if captured:
+                    g.replay()
+                else:
+                    ctx.forward_ep(lid, xin_ep, xin_ep, out, m, m)
+
+            def eager(x_off):
+                arena[xin_ep:xin_ep + nb].copy_(arena[x_off:x_off + nb])
+                ctx.forward_ep(lid, xin_ep, xin_ep, out, m, m)
+            step.eager = eager
+        elif ep_mode:
             xin_ep = ctx.alloc(m * H * 4)  # the captured step's fixed input rows
             ops = ep.LibraryEpOps(ctx, arena, lid, ep.EpShape(H, E, sh.top_k, world, m), rank,
                                   xin_ep, xin_ep, out)
@@ -541,8 +584,10 @@ def main():
                 "config": {"workload": "config1: prefill 512 tok per GPU, Zipf(1.1) router bias, 1 MoE layer "
                                        "(H=2048, I=512, E=256, top-8 + gated shared, IQ4_XS)",
                            "tokens_per_step": PREFILL_M * world,
-                           "parallelism": (f"ep{world}: {epr} experts per GPU, NCCL all-to-all dispatch "
-                                           "and combine") if ep_mode else "single GPU",
+                           "parallelism": (f"ep{world}: {epr} experts per GPU, " + {
+                               "peer": "dispatch stores / combine loads over NVLink peer memory (moe_forward_ep)",
+                               "nccl": "NCCL all-to-all inside moe_forward_ep",
+                               "torch": "torch.distributed all-to-all (ep.py)"}[args.ep]) if ep_mode else "single GPU",
                            "expert_kernels": {0: "auto (tcgen05, A in TMEM)", 1: "CUDA-core GEMV",
                                               2: "tcgen05, A in smem", 3: "tcgen05, A in TMEM"}[args.path],
                            "distinct_experts_per_gpu": round(statistics.mean(distinct), 1),

@@ -228,8 +228,10 @@ int moe_ep_init(moe_ctx* ctx, const void* unique_id, uint32_t n_ranks, uint32_t 
 /* out = resid + scale * MoE(x) for this rank's M tokens (M may be 0) through the group: route,
  * per-rank blocks of `capacity` rows, NCCL all-to-all, this rank's experts, all-to-all back,
  * combine.  Every rank must call it with the same layer shape and the same capacity
- * (>= the largest M of any rank).  Stream-ordered on the context's stream; capturable in a CUDA
- * graph after one eager call (which sizes the buffers). */
+ * (>= the largest M of any rank).  The exchange buffers keep the largest capacity asked for;
+ * buffers replaced by a larger request stay allocated until the context is destroyed, so a
+ * graph captured earlier stays valid.  Stream-ordered on the context's stream; capturable in a
+ * CUDA graph after one eager call (which sizes the buffers). */
 int moe_forward_ep(moe_ctx* ctx, uint32_t layer_id, uint64_t x_off, uint64_t resid_off, uint64_t out_off,
                    uint32_t M, uint32_t capacity);
 

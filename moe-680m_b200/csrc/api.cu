@@ -1082,26 +1082,21 @@ static int ep_map_peers(Ctx* c, const moe::NcclApi* api) {
 static int ensure_ep_buffers(Ctx* c, const moe::NcclApi* api, uint32_t capacity, uint32_t H, uint32_t k) {
     moe::EpState& ep = c->ep;
     const bool want_peer = ep.transport == MOE_EP_TRANSPORT_PEER;
-    if (ep.buf && capacity <= ep.capacity && H <= ep.hidden && k <= ep.top_k && ep.peer == (want_peer && ep.peer))
-        return MOE_OK;
-    capacity = std::max(capacity, ep.capacity);
-    H = std::max(H, ep.hidden);
-    k = std::max(k, ep.top_k);
+    // rows are laid out with the layer's own width and record length, so those must match
+    const bool same_shape = H == ep.hidden && k == ep.top_k;
+    if (ep.buf && same_shape && capacity <= ep.capacity && ep.peer == (want_peer && ep.peer)) return MOE_OK;
+    if (same_shape) capacity = std::max(capacity, ep.capacity);
     const uint64_t rows = static_cast<uint64_t>(ep.n_ranks) * capacity;
     const uint64_t xb = (rows * H * 4 + 255) / 256 * 256, rb = (rows * (k + 1) * 8 + 255) / 256 * 256;
     const uint64_t pb = (moe_ep_plan_bytes(capacity, ep.n_ranks) + 255) / 256 * 256;
     MOE_CUDA(c, cudaStreamSynchronize(c->stream));
-    if (ep.peer) {
-        // every rank stops using the old mappings before any rank frees its buffer
-        ep_close_peers(ep);
-        int* one = nullptr;
-        MOE_CUDA(c, cudaMalloc(&one, sizeof(int)));
-        const ncclResult_t r = api->all_reduce(one, one, 1, ncclInt32, ncclSum, ep.comm, c->stream);
-        cudaStreamSynchronize(c->stream);
-        cudaFree(one);
-        if (r != ncclSuccess) return nccl_fail(c, api, r, "exchange buffer release");
+    if (ep.buf) {  // retired, not freed: graphs captured against it may still be replayed
+        moe::EpState::Retired r{ep.buf, {}};
+        for (int d = 0; d < 8; ++d) r.peer_base[d] = ep.peer_base[d];
+        ep.retired.push_back(r);
+        for (int d = 0; d < 8; ++d) ep.peer_base[d] = nullptr;
+        ep.peer = false;
     }
-    if (ep.buf) cudaFree(ep.buf);
     ep.buf = nullptr;
     void* p = nullptr;
     cudaError_t e = cudaMalloc(&p, pb + 4 * xb + 2 * rb + 256);
@@ -1138,6 +1133,11 @@ static int ensure_ep_buffers(Ctx* c, const moe::NcclApi* api, uint32_t capacity,
 static void ep_release(Ctx* c) {
     moe::EpState& ep = c->ep;
     ep_close_peers(ep);
+    for (auto& r : ep.retired) {
+        for (int d = 0; d < 8; ++d)
+            if (r.peer_base[d]) cudaIpcCloseMemHandle(r.peer_base[d]);
+        cudaFree(r.buf);
+    }
     if (ep.comm) {
         const moe::NcclApi* api = moe::nccl_api(nullptr);
         if (api) api->comm_destroy(ep.comm);
@@ -1236,6 +1236,7 @@ int moe_forward_ep(moe_ctx* c, uint32_t layer_id, uint64_t x_off, uint64_t resid
     const moe::NcclApi* api = moe::nccl_api(nullptr);
     DeviceGuard g(c->device);
     if ((rc = ensure_ep_buffers(c, api, capacity, H, k))) return rc;
+    capacity = ep.capacity;  // rank blocks are laid out with the buffers' capacity
     const uint32_t rows = n * capacity;
     if ((rc = ensure_layer_ws(c, *L, std::max(rows, M)))) return rc;
     const size_t rec = static_cast<size_t>(k + 1) * 8;

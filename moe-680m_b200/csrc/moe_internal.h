@@ -188,6 +188,13 @@ struct EpState {
     bool peer = false;                    // the peer transport is active for the current buffers
     uint8_t* peer_base[8] = {};
     uint64_t off_recv_x = 0, off_recv_rec = 0, off_y_send = 0, off_flags = 0;
+    // earlier buffer generations (replaced when a larger capacity was asked for): kept with their
+    // mappings until the context is destroyed, so CUDA graphs captured against them stay valid
+    struct Retired {
+        uint8_t* buf;
+        uint8_t* peer_base[8];
+    };
+    std::vector<Retired> retired;
 };
 
 struct Ctx {
