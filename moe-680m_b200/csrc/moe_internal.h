@@ -114,8 +114,8 @@ struct Workspace {
     __half* h16 = nullptr;        // [S][I]
     int* xexp = nullptr;          // [S] power-of-two exponent of x16's scale
     float* xh = nullptr;          // [M][H] TF32 part of x (tensor-core router)
-    float* xl = nullptr;
-    float* xn = nullptr;  // [M][H] normalised layer input (moe_forward_norm)          // [M][H] remainder
+    float* xl = nullptr;          // [M][H] remainder x - xh
+    float* xn = nullptr;          // [M][H] normalised layer input (moe_forward_norm)
     CUtensorMap xhmap, xlmap;
     const void* xh_base = nullptr;
     uint64_t xh_rows = 0, xh_cols = 0;
