@@ -154,6 +154,11 @@ int ensure_layer_ws(Ctx* c, const Layer& L, uint32_t M) {
                      L.spec.hidden, L.spec.inter);
 }
 
+// The decode kernel's grid-synchronisation words in the status block.
+int* decode_sync(Ctx* c) {
+    return reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(c->ws.status) + moe::kStatusDecodeOff);
+}
+
 struct DeviceGuard {
     explicit DeviceGuard(int dev) { cudaSetDevice(dev); }
 };
@@ -335,7 +340,7 @@ int record_forward(Ctx* c, const Layer& L, uint32_t M, const float* x, const flo
     if (use_decode(c, L, M)) {
         // single token: the whole layer in one fused launch with direct pointers (no graph or
         // pointer block needed); its grid-sync words live after the status word
-        moe::launch_decode(L, c->ws, c->ws.status + 16, c->sm_count, c->stream, x, resid, out, -1.0f);
+        moe::launch_decode(L, c->ws, decode_sync(c), c->sm_count, c->stream, x, resid, out, -1.0f);
         stage(c, "decode", 1);
         return check_launch(c, "decode");
     }
@@ -431,8 +436,8 @@ static int ctx_init(int device, moe_ctx* c) {
     const char* ng = std::getenv("MOE_B200_NO_GRAPHS");
     c->use_graphs = !(ng && ng[0] == '1');
     void* st = nullptr;
-    MOE_CUDA(c, cudaMalloc(&st, 256));
-    MOE_CUDA(c, cudaMemset(st, 0, 256));
+    MOE_CUDA(c, cudaMalloc(&st, moe::kStatusBlockBytes));
+    MOE_CUDA(c, cudaMemset(st, 0, moe::kStatusBlockBytes));
     c->ws.status = static_cast<int*>(st);
     return MOE_OK;
 }
@@ -558,7 +563,7 @@ int moe_sync(moe_ctx* c) {
     if (st != 0) {
         cudaMemset(c->ws.status, 0, sizeof(int));
         // the decode kernel's grid counter and h maxima, the vocabulary argmax ticket and keys
-        cudaMemset(c->ws.status + 16, 0, 232 - 64);
+        cudaMemset(decode_sync(c), 0, moe::kStatusKernelEnd - moe::kStatusDecodeOff);
         const char* what = st == moe::kDevBadExpert ? "expert id out of range"
                          : st == moe::kDevBadToken ? "token index out of range"
                          : st == moe::kDevOverflow ? "chunk list overflow"
@@ -819,7 +824,7 @@ int moe_forward_norm(moe_ctx* c, uint32_t layer_id, uint64_t x_off, uint64_t out
     if (M == 1 && (c->path == moe::kPathAuto || c->path == moe::kPathGemv) && moe::decode_supported(*L) &&
         out != x) {
         // one launch: normalisation inside the fused decode kernel, direct pointers
-        moe::launch_decode(*L, c->ws, c->ws.status + 16, c->sm_count, c->stream, x, x, out, eps);
+        moe::launch_decode(*L, c->ws, decode_sync(c), c->sm_count, c->stream, x, x, out, eps);
         stage(c, "decode", 1);
         return check_launch(c, "decode");
     }
@@ -1379,8 +1384,8 @@ int moe_vocab_logits(moe_ctx* c, uint64_t w_off, uint32_t V, uint32_t H, uint64_
                                     at<float>(c, x_off), static_cast<int>(M),
                                     logits_off ? at<float>(c, logits_off) : nullptr,
                                     ids_off ? at<uint32_t>(c, ids_off) : nullptr,
-                                    reinterpret_cast<unsigned long long*>(sb + 168),
-                                    reinterpret_cast<unsigned int*>(sb + 160), c->ws.status, c->sm_count,
+                                    reinterpret_cast<unsigned long long*>(sb + moe::kStatusVocabKeysOff),
+                                    reinterpret_cast<unsigned int*>(sb + moe::kStatusVocabTicketOff), c->ws.status, c->sm_count,
                                     c->stream);
     if (r != 0) return fail(c, MOE_E_UNSUPPORTED, "vocab_logits: H=%u does not fit shared memory", H);
     stage(c, "vocab", 1);

@@ -13,6 +13,18 @@
 
 namespace moe {
 
+// Layout of the context's 256-byte status block (zeroed at creation; moe_sync clears the kernel
+// words after an error):
+//   [0, 4)      int status word (first device error code)
+//   [64, 160)   decode kernel: 64-bit grid counter, then per-slot 64-bit |h| maxima
+//   [160, 164)  LM-head kernel: CTA completion ticket
+//   [168, 232)  LM-head kernel: 8 64-bit argmax keys
+constexpr size_t kStatusBlockBytes = 256;
+constexpr size_t kStatusDecodeOff = 64;
+constexpr size_t kStatusVocabTicketOff = 160;
+constexpr size_t kStatusVocabKeysOff = 168;
+constexpr size_t kStatusKernelEnd = 232;
+
 // Tokens per chunk of the CUDA-core grouped GEMV kernels.
 constexpr int kGemvTok = 8;
 
