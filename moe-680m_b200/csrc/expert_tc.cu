@@ -8,20 +8,21 @@
 // up to kNMax tokens.  The gate/up product is one GEMM over W1 and W3 stacked ([2I][H]: feature
 // tiles 0..I/128-1 read W1, the rest W3); SiLU(g)*u is applied by the next conversion kernel.
 //
-// One persistent CTA per SM (480 threads, warp-specialised), looping over work items
-// (token tile of one bucket x 128-row feature tile):
-//   warp 10     TMA: raw IQ4_XS bytes of the item's 128 weight rows, 512 K (two 136-byte
-//               blocks per row) per load, into a 4-deep shared-memory ring;
-//   producer warps (8 or 16) dequantise from that ring (kvalues_iq4nl lookup by byte
-//               permutes, fp16 scale per 32-weight sub-block) and store the fp16 A operand, 64 K
-//               per stage, into TMEM (tcgen05.st) or 128-byte-swizzled shared memory; the warps
-//               of one 32-row quarter take turns by stage;
-//   warp 9      TMA: B operand (fp16 activations of the tile's slots, pre-scaled per slot by a
-//               power of two, K permuted as below), one 16/32/64/128-row box per stage;
-//   warp 8      allocates TMEM; one elected lane issues tcgen05.mma (M=128, N=16..kNMax, K=16) and
-//               tcgen05.commit;
-//   warps 11-14 epilogue: TMEM -> registers, undo the activation scale, store f32
-//               out[slot][feature] (gate/up pre-activations, or the unweighted down output).
+// One persistent CTA per SM (warp-specialised; 27 warps with the default 16 producer warps),
+// looping over work items (token tile of one bucket x 128-row feature tile):
+//   TMA-A warp  raw IQ4_XS bytes of the item's 128 weight rows, 512 K (two 136-byte blocks per
+//               row) per tensor-map load, into a 2-deep shared-memory ring;
+//   producer warps (16, or 8 with MOE_B200_TC_PRODUCER_WARPS=8) dequantise from that ring
+//               (kvalues_iq4nl lookup by byte permutes, fp16 scale per 32-weight sub-block) and
+//               store the fp16 A operand, 64 K per stage, into TMEM (tcgen05.st) or 128-byte-
+//               swizzled shared memory; the warps of one 32-row quarter take turns by stage;
+//   TMA-B warp  fp16 activations of the tile's slots (pre-scaled per slot by a power of two, K
+//               permuted as below), one 16/32/64/128-row box per stage, 6 stages in flight;
+//   MMA warp    allocates TMEM; one elected lane issues tcgen05.mma (M=128, N=16..kNMax, K=16)
+//               and tcgen05.commit;
+//   8 epilogue warps (two per TMEM lane quarter): TMEM -> registers, undo the activation
+//               scale, store f32 out[slot][feature] (gate/up pre-activations, or the unweighted
+//               down output).
 // The accumulators are double-buffered in TMEM so the epilogue of one item overlaps the main
 // loop of the next.  Every mbarrier wait is bounded: on timeout the CTA records an error
 // status, stops issuing work, lets in-flight operations drain and frees its TMEM.
@@ -62,7 +63,7 @@ namespace {
 
 using namespace tc;
 
-// Warp roles: producers 0..PW-1, then MMA, TMA-B, TMA-A, and four epilogue warps.
+// Warp roles: producers 0..PW-1, then MMA, TMA-B, TMA-A, and eight epilogue warps.
 template <int PW>
 struct Roles {
     static constexpr int kProd = PW;
@@ -76,15 +77,6 @@ constexpr int kNMax = 128;          // tokens per tile
 constexpr int kAccStride = 128;     // TMEM columns per accumulator buffer
 constexpr int kACol0 = 256;         // TMEM column of A stage 0 (32 columns per stage)
 constexpr int kRawRowBytes = 2 * kBlockBytes;      // 512 K of one weight row
-#ifndef MOE_TC_RAW_LDG
-#define MOE_TC_RAW_LDG 0    // 1: raw weights by the producers' own global loads
-#endif
-#ifndef MOE_TC_RAW_CPASYNC
-#define MOE_TC_RAW_CPASYNC 0  // 1: raw chunks by the raw-A warp's coalesced 16-byte cp.async
-#endif
-#ifndef MOE_TC_RAW_TMAP
-#define MOE_TC_RAW_TMAP 1   // 0: raw chunks with per-row bulk copies instead of tensor-map boxes
-#endif
 #ifndef MOE_TC_L2_AHEAD
 #define MOE_TC_L2_AHEAD 0   // raw chunks prefetched into L2 ahead of their tensor-map load (0: none; measured fastest)
 #endif
@@ -218,7 +210,7 @@ expert_tc_kernel(const __grid_constant__ BMaps bmap, const TcArgs a) {
             mbar_init(&empty[i], 1);
         }
         for (int i = 0; i < kRaw; ++i) {
-            mbar_init(&rfull[i], MOE_TC_RAW_CPASYNC == 2 ? kProdWarps * 32 : MOE_TC_RAW_CPASYNC ? 32 : 1);
+            mbar_init(&rfull[i], 1);
             mbar_init(&rempty[i], kProdWarps * 32);
         }
         for (int i = 0; i < 2; ++i) {
@@ -228,22 +220,6 @@ expert_tc_kernel(const __grid_constant__ BMaps bmap, const TcArgs a) {
         *abort = 0;
         fence_mbar_init();
     }
-#if MOE_TC_RAW_CPASYNC == 2
-    // weight tile base of each of this CTA's items (row tile start, chunk 0), looked up once
-    // here so that issuing a chunk's copies involves no dependent global loads
-    constexpr int kMaxItemsCached = 128;
-    __shared__ const uint8_t* item_src[kMaxItemsCached];
-    {
-        const int my = (n_items - static_cast<int>(blockIdx.x) + static_cast<int>(gridDim.x) - 1) /
-                       static_cast<int>(gridDim.x);
-        for (int it = threadIdx.x; it < my && it < kMaxItemsCached; it += blockDim.x) {
-            const Item x = get_item(a, static_cast<int>(blockIdx.x) + it * static_cast<int>(gridDim.x));
-            const int mat = a.mat0 + x.rt / a.rt_per_mat;
-            item_src[it] = (mat == 0 ? a.tabs.w1 : mat == 1 ? a.tabs.w3 : a.tabs.w2)[x.bucket] +
-                           static_cast<size_t>((x.rt % a.rt_per_mat) * 128) * a.row_bytes;
-        }
-    }
-#endif
     if (warp == kMmaWarp) tmem_alloc(tmem_base_p, kTmemCols);
     if (warp == kTmaBWarp && lane < 4) tma_prefetch_desc(&bmap.m[lane]);
     tc_fence_before();
@@ -267,22 +243,12 @@ expert_tc_kernel(const __grid_constant__ BMaps bmap, const TcArgs a) {
             uint32_t v[32];
             const __half2 s0 = subscale_h2(hdr.x, hdr.y, ib0);
             const __half2 s1 = subscale_h2(hdr.x, hdr.y, ib0 + 1);
-#if defined(MOE_TC_DIAG) && MOE_TC_DIAG == 2
-#pragma unroll
-            for (int i = 0; i < 32; ++i) v[i] = qw[i & 7] ^ hdr.x;  // diagnostic: no dequant
-#else
 #pragma unroll
             for (int i = 0; i < 8; ++i) word_f16(qw[i], i < 4 ? s0 : s1, v + 4 * i);
-#endif
             if (warp == 0 && lane == 0) TC_TRACE(7, g);
             if (!mbar_wait(&empty[slot], ((g / kStages) & 1) ^ 1, abort)) return false;
             if (warp == 0 && lane == 0) TC_TRACE(1, g);
-#if defined(MOE_TC_DIAG) && MOE_TC_DIAG == 1
-            if (v[0] == 0x12345678u && v[31] == 0x9abcdef0u) g_tc_trace[1][7][0] = v[5];  // keep work
-            if constexpr (false) {
-#else
             if constexpr (A_TMEM) {
-#endif
                 tmem_st32(tmem + (static_cast<uint32_t>(q * 32) << 16) + kACol0 + slot * 32, v);
                 tmem_wait_st();
                 tc_fence_before();
@@ -297,100 +263,11 @@ expert_tc_kernel(const __grid_constant__ BMaps bmap, const TcArgs a) {
             mbar_arrive(&full[slot]);
             return true;
         };
-#if MOE_TC_RAW_LDG
-        // Raw weights straight from global memory into registers (streaming 8-byte loads),
-        // kPre own stages ahead: the load/store path keeps far more bytes in flight per SM than
-        // the tensor-memory-access engine did for these short row segments.
-        struct RawRegs { uint2 hdr; uint32_t qw[8]; };
-        const int my_items = (n_items - static_cast<int>(blockIdx.x) + static_cast<int>(gridDim.x) - 1) /
-                             static_cast<int>(gridDim.x);
-        const int total_st = my_items > 0 ? my_items * nst : 0;
-        int cached_it = -1;
-        const uint8_t* cached_row = nullptr;  // this thread's weight row of item cached_it
-        auto load = [&](int g, RawRegs& r) {
-            if (g >= total_st) return;
-            const int it = g / nst, st = g - it * nst;
-            if (it != cached_it) {  // loads run in increasing g: one cached item suffices
-                const Item x = get_item(a, static_cast<int>(blockIdx.x) + it * static_cast<int>(gridDim.x));
-                const int mat = a.mat0 + x.rt / a.rt_per_mat;
-                const uint8_t* w = (mat == 0 ? a.tabs.w1 : mat == 1 ? a.tabs.w3 : a.tabs.w2)[x.bucket];
-                cached_row = w + static_cast<size_t>((x.rt % a.rt_per_mat) * 128 + row) * a.row_bytes;
-                cached_it = it;
-            }
-            const uint8_t* blk = cached_row + (st >> 2) * kBlockBytes;
-            r.hdr = ldg_stream_u2(blk);
-            const uint8_t* qp = blk + 8 + (st & 3) * 32;
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const uint2 v = ldg_stream_u2(qp + 8 * i);
-                r.qw[2 * i] = v.x;
-                r.qw[2 * i + 1] = v.y;
-            }
-        };
-        // a register ring of kPre+1 stages, rotated by value (no dynamic register indexing)
-        RawRegs r0, r1, r2, r3, r4;
-        load(part, r0);
-        load(part + kParts, r1);
-        load(part + 2 * kParts, r2);
-        load(part + 3 * kParts, r3);
-        for (int g = part; g < total_st; g += kParts) {
-            load(g + 4 * kParts, r4);
-            const int st = g % nst;
-            if (!produce(g, r0.hdr, r0.qw, (st & 3) * 2)) break;
-            r0 = r1;
-            r1 = r2;
-            r2 = r3;
-            r3 = r4;
-        }
-#else
         int g = 0, rc = 0;
-#if MOE_TC_RAW_CPASYNC == 2
-        // The producers themselves copy raw chunks ahead with coalesced 16-byte cp.async
-        // (512 threads, ~4 copies each per chunk), so many more bytes are in flight per SM than
-        // one copy engine or one warp keeps.
-        const int my_items = (n_items - static_cast<int>(blockIdx.x) + static_cast<int>(gridDim.x) - 1) /
-                             static_cast<int>(gridDim.x);
-        const int total_rc = my_items > 0 ? my_items * nchunk : 0;
-        const int ptid = warp * 32 + lane;
-        // one cp.async group per chunk (empty past the end), so wait_group(kRaw - 2) before a
-        // chunk's plain rfull arrival means "this thread's copies of that chunk have landed"
-        auto issue_chunk = [&](int c) -> bool {
-            if (c >= total_rc) { asm volatile("cp.async.commit_group;" ::: "memory"); return true; }
-            const int slot = c % kRaw;
-            if (!mbar_wait(&rempty[slot], ((c / kRaw) & 1) ^ 1, abort)) return false;
-            const int it = c / nchunk, kc = c - it * nchunk;
-            const uint8_t* base;
-            if (it < kMaxItemsCached) {
-                base = item_src[it];
-            } else {
-                const Item x = get_item(a, static_cast<int>(blockIdx.x) + it * static_cast<int>(gridDim.x));
-                const int mat = a.mat0 + x.rt / a.rt_per_mat;
-                base = (mat == 0 ? a.tabs.w1 : mat == 1 ? a.tabs.w3 : a.tabs.w2)[x.bucket] +
-                       static_cast<size_t>((x.rt % a.rt_per_mat) * 128) * a.row_bytes;
-            }
-            const uint8_t* src = base + kc * kRawRowBytes;
-            uint8_t* dst = rst + slot * kRawBytes;
-            constexpr int kPieces = kRawRowBytes / 16;
-            for (int pc = ptid; pc < 128 * kPieces; pc += kProdWarps * 32) {
-                const int r = pc / kPieces, o = (pc - r * kPieces) * 16;
-                cp_async16_cg(dst + r * kRawRowBytes + o, src + static_cast<size_t>(r) * a.row_bytes + o);
-            }
-            asm volatile("cp.async.commit_group;" ::: "memory");
-            return true;
-        };
-        // kRaw-2 chunks ahead: the slot of chunk c+kRaw-2 was released by chunk c-2, long done,
-        // so issuing never waits for the slowest producer of the previous chunk
-        for (int c = 0; c < kRaw - 2; ++c) issue_chunk(c);
-#endif
         for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
             bool ok = true;
             for (int kc = 0; kc < nchunk && ok; ++kc, ++rc) {
                 const int rs = rc % kRaw;
-#if MOE_TC_RAW_CPASYNC == 2
-                if (!issue_chunk(rc + kRaw - 2)) { ok = false; break; }
-                asm volatile("cp.async.wait_group %0;" :: "n"(kRaw - 2) : "memory");
-                mbar_arrive(&rfull[rs]);
-#endif
                 if (!mbar_wait(&rfull[rs], (rc / kRaw) & 1, abort)) { ok = false; break; }
                 if (warp == 0 && lane == 0) TC_TRACE(5, 512 + rc);
                 const uint8_t* raw = rst + rs * kRawBytes + row * kRawRowBytes;
@@ -412,10 +289,6 @@ expert_tc_kernel(const __grid_constant__ BMaps bmap, const TcArgs a) {
             }
             if (!ok) break;
         }
-#if MOE_TC_RAW_CPASYNC == 2
-        asm volatile("cp.async.wait_all;" ::: "memory");
-#endif
-#endif
     } else if (warp == kMmaWarp) {
         // ---------------- MMA issuer (whole warp loops, one elected lane issues) ----------------
         int g = 0, it = 0;
@@ -469,50 +342,15 @@ expert_tc_kernel(const __grid_constant__ BMaps bmap, const TcArgs a) {
                     const int slot = g % kStages;
                     if (!mbar_wait(&empty[slot], ((g / kStages) & 1) ^ 1, abort)) { ok = false; break; }
                     TC_TRACE(2, g);
-#if defined(MOE_TC_DIAG) && MOE_TC_DIAG == 4
-                    (void)bm; (void)bbytes;
-                    mbar_arrive(&full[slot]);  // diagnostic: no B traffic (results wrong)
-#else
                     mbar_arrive_expect_tx(&full[slot], bbytes);
                     tma_load_2d(bst + slot * kBStageBytes, bm, s * 64, x.p0, &full[slot]);
-#endif
                 }
                 if (!ok) break;
             }
         }
         __syncwarp();
     } else if (warp == kTmaAWarp) {
-        // ---------------- raw A loads (tensor-map variant only) ----------------
-#if MOE_TC_RAW_LDG || MOE_TC_RAW_CPASYNC == 2
-#elif MOE_TC_RAW_CPASYNC
-        // Rows of the chunk (272 bytes = 17 x 16 bytes, 16-byte aligned) by 16-byte cp.async
-        // from all 32 lanes: consecutive lanes copy consecutive 16-byte pieces, so one warp
-        // instruction covers 512 contiguous-ish bytes; each lane's copies complete on rfull.
-        int rc = 0;
-        constexpr int kPieces = kRawRowBytes / 16;
-        for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
-            const Item x = get_item(a, item);
-            const int mat = a.mat0 + x.rt / a.rt_per_mat;
-            const int row0 = (x.rt % a.rt_per_mat) * 128;
-            const uint8_t* w = (mat == 0 ? a.tabs.w1 : mat == 1 ? a.tabs.w3 : a.tabs.w2)[x.bucket] +
-                               static_cast<size_t>(row0) * a.row_bytes;
-            bool ok = true;
-            for (int kc = 0; kc < nchunk; ++kc, ++rc) {
-                const int rs = rc % kRaw;
-                if (!mbar_wait_warp(&rempty[rs], ((rc / kRaw) & 1) ^ 1, abort)) { ok = false; break; }
-                if (lane == 0) TC_TRACE(3, rc);
-                uint8_t* dst = rst + rs * kRawBytes;
-                const uint8_t* src = w + kc * kRawRowBytes;
-                for (int c = lane; c < 128 * kPieces; c += 32) {
-                    const int r = c / kPieces, o = (c - r * kPieces) * 16;
-                    cp_async16_cg(dst + r * kRawRowBytes + o, src + static_cast<size_t>(r) * a.row_bytes + o);
-                }
-                cp_async_mbar_arrive(&rfull[rs]);
-            }
-            if (!ok) break;
-        }
-        asm volatile("cp.async.wait_all;" ::: "memory");
-#elif MOE_TC_RAW_TMAP
+        // ---------------- raw A loads: tensor-map boxes into the raw ring ----------------
         // Optionally, tiles are prefetched into L2 MOE_TC_L2_AHEAD chunks before their load
         // (off by default: the prefetches compete with the loads and measured slower).
         if (lane == 0) {
@@ -551,35 +389,6 @@ expert_tc_kernel(const __grid_constant__ BMaps bmap, const TcArgs a) {
                                 row0 + r, &rfull[rs]);
             }
         }
-#else
-        // One 272-byte bulk copy per weight row (rows are contiguous and 16-byte aligned); the
-        // 32 lanes issue the chunk's 128 copies, which the copy engine serves in parallel.
-        int rc = 0;
-        for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
-            const Item x = get_item(a, item);
-            const int mat = a.mat0 + x.rt / a.rt_per_mat;
-            const int row0 = (x.rt % a.rt_per_mat) * 128;
-            const uint8_t* w = (mat == 0 ? a.tabs.w1 : mat == 1 ? a.tabs.w3 : a.tabs.w2)[x.bucket] +
-                               static_cast<size_t>(row0) * a.row_bytes;
-            bool ok = true;
-            for (int kc = 0; kc < nchunk; ++kc, ++rc) {
-                const int rs = rc % kRaw;
-                if (!mbar_wait_warp(&rempty[rs], ((rc / kRaw) & 1) ^ 1, abort)) { ok = false; break; }
-                if (lane == 0) {
-                    TC_TRACE(3, rc);
-                    mbar_arrive_expect_tx(&rfull[rs], kRawBytes);
-                }
-                __syncwarp();
-                uint8_t* dst = rst + rs * kRawBytes;
-                const uint8_t* src = w + kc * kRawRowBytes;
-#pragma unroll
-                for (int r = lane; r < 128; r += 32)
-                    bulk_load(dst + r * kRawRowBytes, src + static_cast<size_t>(r) * a.row_bytes,
-                              kRawRowBytes, &rfull[rs]);
-            }
-            if (!ok) break;
-        }
-#endif
         __syncwarp();
     } else {
         // ---------------- epilogue ----------------

@@ -33,19 +33,11 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
 
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     uint32_t ok;
-#if defined(MOE_TC_DIAG) && MOE_TC_DIAG == 3
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity) : "memory");
-#else
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
         "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}"
         : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity) : "memory");
-#endif
     return ok != 0;
 }
 
@@ -252,13 +244,5 @@ __host__ __device__ constexpr uint32_t idesc_f16(int M, int N) {
 }
 
 }  // namespace tc
-// 16-byte cp.async (L2 only) into shared memory, and an mbarrier arrival (without a pending
-// count increment) once all of this thread's earlier cp.async copies have landed.
-__device__ __forceinline__ void cp_async16_cg(void* smem, const void* gmem) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" :: "r"(tc::smem_u32(smem)), "l"(gmem) : "memory");
-}
-__device__ __forceinline__ void cp_async_mbar_arrive(uint64_t* bar) {
-    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" :: "r"(tc::smem_u32(bar)) : "memory");
-}
 
 }  // namespace moe
