@@ -298,6 +298,12 @@ int moe_launch_count(moe_ctx* ctx, uint64_t* n);
 int moe_vocab_logits(moe_ctx* ctx, uint64_t w_off, uint32_t V, uint32_t H, uint64_t x_off, uint32_t M,
                      uint64_t logits_off, uint64_t ids_off);
 
+/* y[i] = silu(g[i]) * u[i] for i < n (u_off 0: y = silu(g)), silu(v) = v / (1 + e^-v), f32, in place
+ * allowed (y_off == g_off): shaders/silu_mult.comp with gate and up at their own offsets; the
+ * MTP head (src/inference.rs:335-360) is moe_vocab_logits(w1, V = H) -> moe_silu_mul ->
+ * moe_vocab_logits(w2, V = vocab). */
+int moe_silu_mul(moe_ctx* ctx, uint64_t g_off, uint64_t u_off, uint64_t y_off, uint64_t n);
+
 /* ---- weight utilities ------------------------------------------------------------------ */
 
 /* Decode n_blocks IQ4_XS blocks at src_off into f32 [n_blocks*256] at dst_off (exact; the

@@ -1392,6 +1392,18 @@ int moe_vocab_logits(moe_ctx* c, uint64_t w_off, uint32_t V, uint32_t H, uint64_
     return check_launch(c, "vocab_logits");
 }
 
+int moe_silu_mul(moe_ctx* c, uint64_t g_off, uint64_t u_off, uint64_t y_off, uint64_t n) {
+    if (!c) return fail(c, MOE_E_INVALID, "NULL context");
+    if (n == 0) return MOE_OK;
+    if (!off_ok(c, g_off, n * 4, 4) || (u_off && !off_ok(c, u_off, n * 4, 4)) || !off_ok(c, y_off, n * 4, 4))
+        return fail(c, MOE_E_INVALID, "silu_mul offsets invalid");
+    DeviceGuard g(c->device);
+    moe::launch_silu_mul(at<float>(c, g_off), u_off ? at<float>(c, u_off) : nullptr, at<float>(c, y_off), n,
+                         c->sm_count, c->stream);
+    stage(c, "silu_mul", 1);
+    return check_launch(c, "silu_mul");
+}
+
 int moe_dequant_iq4xs(moe_ctx* c, uint64_t src_off, uint64_t n_blocks, uint64_t dst_off) {
     if (!c) return fail(c, MOE_E_INVALID, "NULL context");
     if (n_blocks == 0) return MOE_OK;

@@ -305,6 +305,7 @@ void launch_ep_gather(const float* x, const uint2* topk, EpPlan plan, int M, int
 void launch_ep_combine(EpPlan plan, int M, int n_ranks, int H, const float* y_back, const float* resid,
                        float scale, float* out, cudaStream_t s);
 void launch_rms_norm(const float* x, float* y, int M, int H, float eps, cudaStream_t s);
+void launch_silu_mul(const float* g, const float* u, float* y, uint64_t n, int sm_count, cudaStream_t s);
 void launch_dequant(const uint8_t* src, uint64_t n_blocks, float* dst, cudaStream_t s);
 void launch_dequant_ref36(const uint8_t* src, uint64_t n_blocks, float* dst, cudaStream_t s);
 bool vocab_supported(int H, int M);

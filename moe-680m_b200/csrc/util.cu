@@ -2,6 +2,8 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
+
 #include "moe_common.cuh"
 #include "moe_internal.h"
 
@@ -86,6 +88,17 @@ rms_norm_kernel(const float* __restrict__ x, float* __restrict__ y, int H, float
     }
 }
 
+// y[i] = silu(g[i]) * (u ? u[i] : 1), silu(v) = v / (1 + e^-v) (shaders/silu_mult.comp:21-38,
+// shaders/common.glsl:106-108).
+__global__ void silu_mul_kernel(const float* __restrict__ g, const float* __restrict__ u, float* __restrict__ y,
+                                uint64_t n) {
+    for (uint64_t i = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
+        const float v = silu_f(g[i]);
+        y[i] = u ? v * u[i] : v;
+    }
+}
+
 }  // namespace
 
 // The reference's own 36-byte weight block (shaders/common.glsl:59-86, "IQ4_XS" there): 32
@@ -131,6 +144,11 @@ void launch_synth(uint8_t* dst, uint64_t key, uint64_t block_start, uint64_t n_b
 
 void launch_rms_norm(const float* x, float* y, int M, int H, float eps, cudaStream_t s) {
     rms_norm_kernel<<<M, 256, 0, s>>>(x, y, H, eps);
+}
+
+void launch_silu_mul(const float* g, const float* u, float* y, uint64_t n, int sm_count, cudaStream_t s) {
+    const uint64_t blocks = std::min<uint64_t>((n + 255) / 256, static_cast<uint64_t>(sm_count) * 8);
+    silu_mul_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(g, u, y, n);
 }
 
 }  // namespace moe

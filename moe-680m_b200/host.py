@@ -36,7 +36,7 @@ EXPORTS = (
     "moe_synth_iq4xs", "moe_profile", "moe_profile_read", "moe_launch_count", "moe_set_path",
     "moe_bucket_static", "moe_forward_topk", "moe_ep_plan_bytes", "moe_ep_dispatch",
     "moe_ep_combine", "moe_dequant_ref36", "moe_forward_norm", "moe_vocab_logits",
-    "moe_ep_unique_id", "moe_ep_init", "moe_forward_ep", "moe_ep_set_transport", "moe_ep_transport",
+    "moe_ep_unique_id", "moe_ep_init", "moe_forward_ep", "moe_ep_set_transport", "moe_ep_transport", "moe_silu_mul",
     "moe_layer_set_next",
 )
 
@@ -107,6 +107,7 @@ def lib():
         "moe_ep_init": (i32, [vp, vp, u32, u32]),
         "moe_forward_ep": (i32, [vp, u32, u64, u64, u64, u32, u32]),
         "moe_ep_set_transport": (i32, [vp, i32]),
+        "moe_silu_mul": (i32, [vp, u64, u64, u64, u64]),
         "moe_ep_transport": (i32, [vp, P(i32)]),
         "moe_forward_norm": (i32, [vp, u32, u64, u64, u32, f32]),
         "moe_layer_set_next": (i32, [vp, u32, i32]),
@@ -319,6 +320,10 @@ class Context:
 
     def forward_ep(self, layer_id, x_off, resid_off, out_off, m, capacity):
         self._check(lib().moe_forward_ep(self.h, layer_id, x_off, resid_off, out_off, m, capacity))
+
+    def silu_mul(self, g_off, u_off, y_off, n):
+        """y = silu(g) * u (u_off 0: y = silu(g)), n f32 values."""
+        self._check(lib().moe_silu_mul(self.h, g_off, u_off, y_off, n))
 
     def synth_iq4xs(self, dst_off, key, block_start, n_blocks):
         self._check(lib().moe_synth_iq4xs(self.h, dst_off, key, block_start, n_blocks))

@@ -145,3 +145,33 @@ def test_full_vocab_sampled_rows(ctx):
     assert O.rel_l2(lg[:, rows], ref) <= REL_L2 and O.max_rel(lg[:, rows], ref) <= MAX_REL
     for t in range(m):
         assert int(ids[t]) == O.argmax_first(lg[t])
+
+
+def test_silu_mul(ctx):
+    rng = np.random.default_rng(3)
+    g = (rng.standard_normal(5000) * 4).astype(np.float32)
+    u = rng.standard_normal(5000).astype(np.float32)
+    go, uo, yo = ctx.put(g), ctx.put(u), ctx.alloc(g.nbytes)
+    ctx.silu_mul(go, uo, yo, g.size)
+    ctx.silu_mul(go, 0, go, g.size)  # in place, no up operand
+    ctx.sync()
+    ref = O.silu(g.astype(np.float64))
+    assert O.max_rel(ctx.download(yo, g.shape), ref * u) <= 1e-6
+    assert O.max_rel(ctx.download(go, g.shape), ref) <= 1e-6
+
+
+def test_mtp_head_chain(ctx):
+    """MTP head (src/inference.rs:335-360): z = W1 . h (V = H), a = silu(z), draft = argmax(W2 . a)."""
+    hidden, vocab = 2048, 5003
+    w1 = synth.iq4xs_matrix(synth.tensor_key(14, 92, 0, 0), hidden, hidden)
+    w2 = synth.iq4xs_matrix(synth.tensor_key(14, 93, 0, 0), vocab, hidden)
+    x = synth.tokens(14, 0, 1, hidden)
+    w1o, w2o, xo = ctx.put(w1), ctx.put(w2), ctx.put(x)
+    zo, lo, io = ctx.alloc(hidden * 4), ctx.alloc(vocab * 4), ctx.alloc(256)
+    ctx.vocab_logits(w1o, hidden, hidden, xo, 1, zo, 0)
+    ctx.silu_mul(zo, 0, zo, hidden)
+    ctx.vocab_logits(w2o, vocab, hidden, zo, 1, lo, io)
+    ctx.sync()
+    a = O.silu(O.vocab_logits(x, w1, hidden, hidden))
+    ref = O.vocab_logits(a, w2, vocab, hidden)
+    check(ctx.download(lo, (1, vocab)), ctx.download(io, (1,), np.uint32), ref)
