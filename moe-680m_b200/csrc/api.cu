@@ -1031,6 +1031,34 @@ static void ep_close_peers(moe::EpState& ep) {
 // Maps every other rank's exchange buffer (CUDA IPC handles all-gathered over the group).  The
 // outcome is agreed by all ranks (an all-reduce of the local result), so either every rank uses
 // the peer transport or none does.
+// Every rank's buffer layout (capacity, width, record length) must be the same, or rank blocks
+// would land at different offsets (and, with the peer transport, past a smaller peer buffer):
+// checked whenever the buffers are (re)created, by an all-gather of the layouts.
+static int ep_check_layout(Ctx* c, const moe::NcclApi* api) {
+    moe::EpState& ep = c->ep;
+    const uint32_t n = ep.n_ranks;
+    if (n == 1) return MOE_OK;
+    const uint32_t mine[4] = {ep.capacity, ep.hidden, ep.top_k, n};
+    uint32_t* d = nullptr;
+    MOE_CUDA(c, cudaMalloc(&d, sizeof(mine) * (n + 1)));
+    cudaMemcpy(d + 4 * n, mine, sizeof(mine), cudaMemcpyHostToDevice);
+    const ncclResult_t r = api->all_gather(d + 4 * n, d, 4, ncclUint32, ep.comm, c->stream);
+    std::vector<uint32_t> all(4 * n);
+    if (r == ncclSuccess) {
+        cudaStreamSynchronize(c->stream);
+        cudaMemcpy(all.data(), d, sizeof(mine) * n, cudaMemcpyDeviceToHost);
+    }
+    cudaFree(d);
+    if (r != ncclSuccess) return nccl_fail(c, api, r, "layout exchange");
+    for (uint32_t q = 0; q < n; ++q)
+        if (std::memcmp(&all[4 * q], mine, sizeof(mine)) != 0)
+            return fail(c, MOE_E_INVALID,
+                        "expert-parallel ranks disagree: rank %u has capacity %u, hidden %u, top_k %u; rank %u "
+                        "capacity %u, hidden %u, top_k %u (every rank must pass the same capacity and layer shape)",
+                        ep.rank, mine[0], mine[1], mine[2], q, all[4 * q], all[4 * q + 1], all[4 * q + 2]);
+    return MOE_OK;
+}
+
 static int ep_map_peers(Ctx* c, const moe::NcclApi* api) {
     moe::EpState& ep = c->ep;
     const uint32_t n = ep.n_ranks;
@@ -1131,6 +1159,11 @@ static int ensure_ep_buffers(Ctx* c, const moe::NcclApi* api, uint32_t capacity,
     ep.capacity = capacity;
     ep.hidden = H;
     ep.top_k = k;
+    int rc = ep_check_layout(c, api);
+    if (rc != MOE_OK) {
+        ep.capacity = ep.hidden = ep.top_k = 0;  // the next call re-creates (and re-checks) them
+        return rc;
+    }
     if (want_peer) return ep_map_peers(c, api);
     return MOE_OK;
 }

@@ -301,3 +301,46 @@ def test_c_abi_ep_two_ranks_match_single_gpu(transport, tpr):
     x = np.concatenate([res[0][0], res[1][0]])
     got = np.concatenate([res[0][1][0], res[1][1][0]])
     assert O.rel_l2(got, _single_gpu_reference(x)) < 1e-6
+
+
+def _c_ep_mismatch_worker(rank, world, uid, caps, q):
+    try:
+        E, H = FULL.n_experts, FULL.hidden
+        epr = E // world
+        ctx = host.Context(rank, 1 << 30)
+        _, _, ids = host.build_synthetic_model(ctx, SEED, 1, FULL, 1.1, experts=range(rank * epr, (rank + 1) * epr))
+        ctx.ep_init(uid, world, rank)
+        xo = ctx.put(synth.tokens(SEED, 9, 8, H))
+        out = ctx.alloc(8 * H * 4)
+        try:
+            ctx.forward_ep(ids[0], xo, xo, out, 8, caps[rank])
+            q.put((rank, "no error"))
+        except host.MoeError as e:
+            q.put((rank, str(e)))
+        ctx.close()
+    except Exception as e:  # reported to the parent
+        q.put((rank, "worker failed: " + repr(e)))
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_c_abi_ep_two_ranks_reject_different_capacities():
+    """Ranks that pass different capacities get an error on every rank, before any exchange."""
+    import torch.multiprocessing as mp
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    uid = host.Context.ep_unique_id()
+    mpc = mp.get_context("spawn")
+    q = mpc.Queue()
+    procs = [mpc.Process(target=_c_ep_mismatch_worker, args=(r, 2, uid, [64, 96], q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = {}
+    try:
+        for _ in range(2):
+            r, msg = q.get(timeout=300)
+            res[r] = msg
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.kill()
+    assert all("disagree" in m for m in res.values()), res
