@@ -119,3 +119,72 @@ def test_load_and_forward_matches_oracle(tmp_path, router_dtype):
         assert O.rel_l2(got, ref) <= 1e-3 and O.max_rel(got, ref) <= 2e-3
     finally:
         ctx.close()
+
+
+class _ArenaStandIn:
+    """Host-memory stand-in for host.Context with the three calls load_moe_layers makes (put,
+    layer_create) so the tensor-name mapping is checked without a GPU."""
+
+    def __init__(self):
+        self.mem = bytearray(256)
+        self.layers = []
+
+    def put(self, arr):
+        off = (len(self.mem) + 255) // 256 * 256
+        data = np.ascontiguousarray(arr).view(np.uint8).reshape(-1).tobytes()
+        self.mem.extend(b"\0" * (off - len(self.mem)))
+        self.mem.extend(data)
+        return off
+
+    def layer_create(self, spec, w1, w3, w2):
+        self.layers.append((spec, list(w1), list(w3), list(w2)))
+        return len(self.layers) - 1
+
+
+@pytest.mark.parametrize("router_dtype", ["f32", "f16"])
+def test_load_maps_tensor_names_without_gpu(model_file, tmp_path, router_dtype):
+    """Every expert's W1/W3/W2 offset points at its own slice of the stacked tensor, the shared
+    expert and gate are wired with their flags, the router lands as f32."""
+    p = model_file
+    if router_dtype == "f16":
+        p = tmp_path / "f16.gguf"
+        write_model(p, router_dtype="f16")
+    g = gguf_io.read_gguf(p)
+    arena = _ArenaStandIn()
+    reg, ids = gguf_io.load_moe_layers(arena, g, scale=0.5)
+    assert ids == [0, 1]
+    E, H, I = SH.n_experts, SH.hidden, SH.inter
+    b13, b2 = I * (H // 256) * 136, H * (I // 256) * 136
+    for l, (spec, w1, w3, w2) in enumerate(arena.layers):
+        assert (spec.hidden, spec.inter, spec.n_experts, spec.top_k) == (H, I, E, SH.top_k)
+        assert spec.flags == host.MOE_F_SHARED | host.MOE_F_SHARED_GATE and spec.scale == 0.5
+        wr, gate, ex = _weights(l)
+        if router_dtype == "f16":
+            wr = wr.astype(np.float16).astype(np.float32)
+        got_wr = np.frombuffer(bytes(arena.mem[spec.router_w:spec.router_w + wr.nbytes]), np.float32)
+        assert np.array_equal(got_wr, wr.reshape(-1))
+        assert reg.lookup(f"blk.{l}.ffn_gate_inp.weight") == spec.router_w
+        for e in range(E):
+            for offs, m, nb in ((w1, 0, b13), (w3, 1, b13), (w2, 2, b2)):
+                assert bytes(arena.mem[offs[e]:offs[e] + nb]) == ex[e][m].tobytes()
+        for off, m, nb in ((spec.shared_w1, 0, b13), (spec.shared_w3, 1, b13), (spec.shared_w2, 2, b2)):
+            assert bytes(arena.mem[off:off + nb]) == ex[E][m].tobytes()
+        got_g = np.frombuffer(bytes(arena.mem[spec.shared_gate:spec.shared_gate + gate.nbytes]), np.float32)
+        assert np.array_equal(got_g, gate.reshape(-1))
+
+
+def test_load_rejects_missing_expert_tensor(tmp_path):
+    p = tmp_path / "bad.gguf"
+    w = gguf.GGUFWriter(str(p), arch=ARCH)
+    w.add_block_count(1)
+    w.add_uint32(f"{ARCH}.expert_count", SH.n_experts)
+    w.add_uint32(f"{ARCH}.expert_used_count", SH.top_k)
+    wr, _, _ = _weights(0)
+    w.add_tensor("blk.0.ffn_gate_inp.weight", wr)
+    w.add_tensor("blk.0.ffn_gate_exps.weight", np.zeros((SH.n_experts, SH.inter, SH.hidden), np.float32))
+    w.write_header_to_file()
+    w.write_kv_data_to_file()
+    w.write_tensors_to_file()
+    w.close()
+    with pytest.raises(gguf_io.GgufError):
+        gguf_io.load_moe_layers(_ArenaStandIn(), gguf_io.read_gguf(p))
