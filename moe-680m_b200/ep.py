@@ -16,10 +16,13 @@ counterpart):
   5. all-to-all of the partial rows back to their owners (same layout);
   6. out = resid + scale * (sum of the returned partials in rank order).
 
-The per-rank compute goes through an ``ops`` object: ``LibraryEpOps`` (the CUDA library,
-tensors aliasing the context's arena) is the product; a test stand-in with the same methods
-drives the same exchange on CPU ranks over gloo.  With no host synchronisation inside, a step
-of LibraryEpOps can be captured in a CUDA graph together with the NCCL collectives.
+This module runs the exchange with the caller's own process group, for callers that already
+have one; the library runs the same steps by itself in ``moe_forward_ep`` (its own NCCL group,
+or stores and loads over NVLink peer memory).  The per-rank compute goes through an ``ops``
+object: ``LibraryEpOps`` (the CUDA library, tensors aliasing the context's arena); a test
+stand-in with the same methods drives the same exchange on CPU ranks over gloo.  With no host
+synchronisation inside, a step of LibraryEpOps can be captured in a CUDA graph together with
+the NCCL collectives.
 """
 from __future__ import annotations
 
