@@ -294,7 +294,8 @@ int moe_launch_count(moe_ctx* ctx, uint64_t* n);
  *              never win; 0 when no logit exceeds -inf), or 0 to skip the argmax
  * 1 <= M <= 8, 512 <= H <= 4096 with H % 512 == 0 (else MOE_E_UNSUPPORTED).  Activations are
  * rounded to 16-bit fixed point per row (relative step 2^-15 of the row's largest magnitude);
- * a row with a non-finite value gives NaN logits.  Stream-ordered on the context's stream. */
+ * a row with a non-finite value gives NaN logits.  Stream-ordered on the context's stream;
+ * capturable in a CUDA graph after one eager call on the device. */
 int moe_vocab_logits(moe_ctx* ctx, uint64_t w_off, uint32_t V, uint32_t H, uint64_t x_off, uint32_t M,
                      uint64_t logits_off, uint64_t ids_off);
 
