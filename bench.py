@@ -111,6 +111,28 @@ def distinct_experts(routed: np.ndarray) -> int:
     return len(np.unique(routed))
 
 
+NVLINK_GBS = 770.0  # measured peer-copy bandwidth per direction per GPU on this pool's B200s
+
+
+def ep_exchange_bytes(routed_all: np.ndarray, world: int, m: int, epr: int, hidden: int, k: int) -> np.ndarray:
+    """Bytes each rank moves over NVLink in one expert-parallel step, [world][2] (out, in).
+
+    routed_all: [world*m, k] expert ids, rank r's tokens at rows r*m..(r+1)*m.  A token visits
+    the ranks owning its experts; the visits to other ranks cross NVLink twice: the row and its
+    record (hidden*4 + (k+1)*8 bytes) to the expert rank, the partial row (hidden*4 bytes) back."""
+    n = world * m
+    owner = np.repeat(np.arange(world), m)
+    visits = np.zeros((n, world), bool)
+    visits[np.arange(n)[:, None], routed_all.astype(np.int64) // epr] = True
+    visits[np.arange(n), owner] = False
+    sent = np.array([visits[owner == r].sum() for r in range(world)], np.int64)  # rows r dispatches
+    recv = visits.sum(axis=0).astype(np.int64)                                     # rows r serves
+    row_in, row_back = hidden * 4 + (k + 1) * 8, hidden * 4
+    out = sent * row_in + recv * row_back
+    inn = recv * row_in + sent * row_back
+    return np.stack([out, inn], axis=1)
+
+
 def cpu_baseline(shapes, x: np.ndarray, min_seconds: float = 10.0, threads: int = 0):
     """C restatement of the reference's MoE layer (f32 accumulation) on the host cores: whole
     512-token prefills repeated until ``min_seconds`` of CPU time have passed."""
@@ -434,6 +456,19 @@ def main():
                 "layer_achieved_gbs": layer_bytes / (ms / 1e3) / 1e9,
                 "layer_frac": layer_bytes / (ms / 1e3) / 1e9 / hbm,
                 "stage_ms": {k: round(v, 4) for k, v in stage_ms.items()}}
+    if ep_mode:
+        # the expert-parallel step against its two floors: this GPU's expert weights from HBM and
+        # the rows crossing NVLink (the larger direction of the busiest GPU, at the measured
+        # peer bandwidth)
+        try:
+            nv = max(float(ep_exchange_bytes(routed[i], world, PREFILL_M, epr, H, sh.top_k).max())
+                     for i in range(K))
+            t_nv, t_hbm = nv / (NVLINK_GBS * 1e3), layer_bytes / (hbm * 1e3)
+            roofline["ep_step"] = {"nvlink_bytes_max": nv, "nvlink_us": t_nv, "hbm_us": t_hbm,
+                                   "target_us": max(t_nv, t_hbm), "step_us": ms * 1e3,
+                                   "frac": max(t_nv, t_hbm) / (ms * 1e3), "nvlink_gbs": NVLINK_GBS}
+        except Exception as e:  # noqa: BLE001 - reported, never fatal to the bench
+            roofline["ep_step"] = {"error": repr(e)}
 
     e2e, decode, cpu, config3, config2, config4, lm_head = None, None, None, None, None, None, None
     if not only_prefill:

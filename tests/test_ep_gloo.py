@@ -166,3 +166,23 @@ def test_exchange_matches_single_process(world, counts):
     assert got.shape == ref.shape
     # partial rows travel as f32: agreement to f32 rounding of the partial sums
     assert orc.rel_l2(got, ref) < 1e-6
+
+
+def test_bench_ep_exchange_bytes():
+    """The NVLink byte count the bench's expert-parallel roofline uses, on a hand-checked case:
+    2 ranks, 4 experts each, 2 tokens per rank, top-2."""
+    import importlib.util
+    from pathlib import Path
+    spec = importlib.util.spec_from_file_location("bench_mod", Path(__file__).resolve().parent.parent / "bench.py")
+    bench = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(bench)
+    routed = np.array([[0, 1],    # rank 0 token: own experts only
+                       [2, 5],    # rank 0 token: visits rank 1
+                       [6, 7],    # rank 1 token: own experts only
+                       [0, 4]])   # rank 1 token: visits rank 0
+    b = bench.ep_exchange_bytes(routed, world=2, m=2, epr=4, hidden=8, k=2)
+    row_in, row_back = 8 * 4 + 3 * 8, 8 * 4
+    assert b.tolist() == [[row_in + row_back, row_in + row_back], [row_in + row_back, row_in + row_back]]
+    routed[3] = [6, 7]  # now only rank 0 sends
+    b = bench.ep_exchange_bytes(routed, world=2, m=2, epr=4, hidden=8, k=2)
+    assert b.tolist() == [[row_in, row_back], [row_back, row_in]]
