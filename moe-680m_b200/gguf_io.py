@@ -8,8 +8,10 @@ with 256-weight / 136-byte blocks, the tensor data section starts at the next mu
 ``general.alignment`` (32 when absent), and hyper-parameters are read under
 ``<general.architecture>.``.
 
-``load_moe_layers`` maps the Qwen-MoE tensor names of llama.cpp files onto the library's layer
-description (the registry shape of src/memory.rs:120-290):
+``load_moe_layers`` maps MoE tensors onto the library's layer description (the registry shape of
+src/memory.rs:120-290), under the reference registry's own names (``blk.L.ffn_gate``,
+``blk.L.experts.E.w1/w3/w2``, ``blk.L.shared_expert.w1/w3/w2``) or the Qwen-MoE names of
+llama.cpp files:
 
   blk.L.ffn_gate_inp.weight        router [E][H]           (F32; F16 / BF16 converted to f32)
   blk.L.ffn_gate_exps.weight       W1 of all experts [E][I][H]   IQ4_XS, stacked
@@ -173,13 +175,36 @@ def _router_f32(g: GgufFile, t: TensorInfo) -> np.ndarray:
     raise GgufError(f"{t.name}: router type {GGML_NAMES.get(t.ggml_type, t.ggml_type)} not supported")
 
 
+def _moe_blocks(g: GgufFile) -> list:
+    """Blocks with MoE experts under either naming: llama.cpp's stacked ``ffn_*_exps`` tensors or
+    the reference registry's per-expert ``experts.E.w1`` tensors (src/memory.rs:159-175)."""
+    out = set()
+    for n in g.tensors:
+        parts = n.split(".")
+        if len(parts) > 2 and parts[0] == "blk" and (n.endswith("ffn_gate_exps.weight") or
+                                                    n.endswith(".experts.0.w1.weight")):
+            out.add(int(parts[1]))
+    return sorted(out)
+
+
 def load_moe_layers(ctx: host.Context, g: GgufFile, layers=None, scale: float = 1.0):
     """Upload the MoE tensors of ``layers`` (default: every block with experts) into the
-    context's arena and create one library layer each.  Returns (TensorRegistry, [layer ids])."""
+    context's arena and create one library layer each.  Returns (TensorRegistry, [layer ids]).
+
+    Two tensor namings are read:
+      * llama.cpp (Qwen-MoE): ``blk.L.ffn_gate_inp`` router, stacked ``ffn_{gate,up,down}_exps``,
+        ``ffn_{gate,up,down}_shexp`` shared expert, optional ``ffn_gate_inp_shexp`` gate;
+      * the reference's registry (src/memory.rs:147-175, :236-262): ``blk.L.ffn_gate`` router,
+        ``blk.L.experts.E.w1/w3/w2`` per expert, ``blk.L.shared_expert.w1/w3/w2``, no shared
+        gate (the reference weights routed experts p/9 and the shared expert 1/9: pass
+        ``scale=1/9``).
+    The router may be F32, F16, BF16 (converted on the host) or IQ4_XS (decoded to f32 on the
+    device with moe_dequant_iq4xs)."""
     reg = host.TensorRegistry()
-    blocks = sorted({int(n.split(".")[1]) for n in g.tensors if n.endswith("ffn_gate_exps.weight")})
-    layers = blocks if layers is None else list(layers)
+    layers = _moe_blocks(g) if layers is None else list(layers)
     k = g.arch_int("expert_used_count")
+    if k is None and "llama.expert_used_count" in g.metadata:  # the key the reference reads
+        k = int(g.metadata["llama.expert_used_count"])
     if k is None:
         raise GgufError("expert_used_count missing from the metadata")
     ids = []
@@ -193,39 +218,66 @@ def load_moe_layers(ctx: host.Context, g: GgufFile, layers=None, scale: float = 
         reg.add(name, off, data.nbytes, t.ggml_type if arr is None else host.GGML_F32)
         return off, t
 
+    def iq4(name, shape=None):
+        off, t = put(name)
+        if t is None or t.ggml_type != 23:
+            raise GgufError(f"{name} missing or not IQ4_XS")
+        if shape is not None and tuple(t.shape) != tuple(shape):
+            raise GgufError(f"{name} has shape {t.shape}, expected {tuple(shape)}")
+        return off, t
+
+    def router(name):
+        t = g.tensors.get(name)
+        if t is None:
+            raise GgufError(f"{name} missing")
+        if t.ggml_type == 23:  # IQ4_XS router: decoded on the device into an f32 [E][H] tensor
+            src, _ = put(name)
+            E_, H_ = t.shape
+            dst = ctx.alloc(E_ * H_ * 4)
+            ctx.dequant(src, E_ * H_ // 256, dst)
+            reg.add(name + ".f32", dst, E_ * H_ * 4, host.GGML_F32)
+            return dst, t
+        return put(name, _router_f32(g, t))[0], t
+
     for l in layers:
         p = f"blk.{l}."
-        rt = g.tensors.get(p + "ffn_gate_inp.weight")
-        if rt is None:
-            raise GgufError(f"{p}ffn_gate_inp.weight missing")
+        stacked = p + "ffn_gate_exps.weight" in g.tensors
+        if not stacked and p + "experts.0.w1.weight" not in g.tensors:
+            raise GgufError(f"{p}: no expert tensors (ffn_gate_exps or experts.0.w1)")
+        router_off, rt = router(p + ("ffn_gate_inp.weight" if stacked else "ffn_gate.weight"))
         E, H = rt.shape
-        router_off, _ = put(p + "ffn_gate_inp.weight", _router_f32(g, rt))
-        offs, shapes = {}, {}
-        for key in ("ffn_gate_exps", "ffn_up_exps", "ffn_down_exps"):
-            off, t = put(p + key + ".weight")
-            if t is None or t.ggml_type != 23:
-                raise GgufError(f"{p}{key}.weight missing or not IQ4_XS")
-            if t.shape[0] != E:
-                raise GgufError(f"{p}{key}.weight has {t.shape[0]} experts, router {E}")
-            offs[key], shapes[key] = off, t.shape
-        I = shapes["ffn_gate_exps"][1]
-        if shapes["ffn_gate_exps"][2] != H or shapes["ffn_down_exps"][1:] != (H, I):
-            raise GgufError(f"{p}: expert shapes {shapes} do not match hidden {H}")
-        b13 = I * (H // 256) * 136
-        b2 = H * (I // 256) * 136
-        w1 = [offs["ffn_gate_exps"] + e * b13 for e in range(E)]
-        w3 = [offs["ffn_up_exps"] + e * b13 for e in range(E)]
-        w2 = [offs["ffn_down_exps"] + e * b2 for e in range(E)]
         flags = 0
         sh = [0, 0, 0]
-        if p + "ffn_gate_shexp.weight" in g.tensors:
-            for i, key in enumerate(("ffn_gate_shexp", "ffn_up_shexp", "ffn_down_shexp")):
-                off, t = put(p + key + ".weight")
-                if t is None or t.ggml_type != 23:
-                    raise GgufError(f"{p}{key}.weight missing or not IQ4_XS")
-                sh[i] = off
-            flags |= host.MOE_F_SHARED
         gate_off = 0
+        if stacked:
+            offs, shapes = {}, {}
+            for key in ("ffn_gate_exps", "ffn_up_exps", "ffn_down_exps"):
+                off, t = iq4(p + key + ".weight")
+                if t.shape[0] != E:
+                    raise GgufError(f"{p}{key}.weight has {t.shape[0]} experts, router {E}")
+                offs[key], shapes[key] = off, t.shape
+            I = shapes["ffn_gate_exps"][1]
+            if shapes["ffn_gate_exps"][2] != H or shapes["ffn_down_exps"][1:] != (H, I):
+                raise GgufError(f"{p}: expert shapes {shapes} do not match hidden {H}")
+            b13 = I * (H // 256) * 136
+            b2 = H * (I // 256) * 136
+            w1 = [offs["ffn_gate_exps"] + e * b13 for e in range(E)]
+            w3 = [offs["ffn_up_exps"] + e * b13 for e in range(E)]
+            w2 = [offs["ffn_down_exps"] + e * b2 for e in range(E)]
+            shared = ("ffn_gate_shexp", "ffn_up_shexp", "ffn_down_shexp")
+        else:
+            t1 = g.tensors.get(p + "experts.0.w1.weight")
+            I = t1.shape[0]
+            w1, w3, w2 = [], [], []
+            for e in range(E):
+                w1.append(iq4(f"{p}experts.{e}.w1.weight", (I, H))[0])
+                w3.append(iq4(f"{p}experts.{e}.w3.weight", (I, H))[0])
+                w2.append(iq4(f"{p}experts.{e}.w2.weight", (H, I))[0])
+            shared = ("shared_expert.w1", "shared_expert.w3", "shared_expert.w2")
+        if p + shared[0] + ".weight" in g.tensors:
+            for i, key in enumerate(shared):
+                sh[i] = iq4(p + key + ".weight", (H, I) if i == 2 else (I, H))[0]
+            flags |= host.MOE_F_SHARED
         gt = g.tensors.get(p + "ffn_gate_inp_shexp.weight")
         if gt is not None and flags & host.MOE_F_SHARED:
             gate_off, _ = put(p + "ffn_gate_inp_shexp.weight", _router_f32(g, gt).reshape(-1))

@@ -136,6 +136,14 @@ class _ArenaStandIn:
         self.mem.extend(data)
         return off
 
+    def alloc(self, nbytes):
+        return self.put(np.zeros(nbytes, np.uint8))
+
+    def dequant(self, src, n_blocks, dst):  # moe_dequant_iq4xs, here by the oracle
+        raw = np.frombuffer(bytes(self.mem[src:src + n_blocks * 136]), np.uint8).reshape(n_blocks, 136)
+        f = O.dequant_iq4xs(raw).astype(np.float32).tobytes()
+        self.mem[dst:dst + len(f)] = f
+
     def layer_create(self, spec, w1, w3, w2):
         self.layers.append((spec, list(w1), list(w3), list(w2)))
         return len(self.layers) - 1
@@ -188,3 +196,56 @@ def test_load_rejects_missing_expert_tensor(tmp_path):
     w.close()
     with pytest.raises(gguf_io.GgufError):
         gguf_io.load_moe_layers(_ArenaStandIn(), gguf_io.read_gguf(p))
+
+
+def write_reference_named(path, router="f32"):
+    """One block under the reference registry's names (src/memory.rs:147-175): ffn_gate router,
+    experts.E.w1/w3/w2 per expert, shared_expert.w1/w3/w2, and the llama.* expert keys the
+    reference reads whatever the architecture."""
+    w = gguf.GGUFWriter(str(path), arch="qwen35moe")
+    w.add_uint32("llama.expert_count", SH.n_experts)
+    w.add_uint32("llama.expert_used_count", SH.top_k)
+    wr, _, ex = _weights(0)
+    IQ = gguf.GGMLQuantizationType.IQ4_XS
+    if router == "iq4":
+        raw = synth.iq4xs_matrix(synth.tensor_key(SEED, 50, 0, 0), SH.n_experts, SH.hidden)
+        w.add_tensor("blk.0.ffn_gate.weight", raw.reshape(SH.n_experts, -1), raw_dtype=IQ)
+    else:
+        w.add_tensor("blk.0.ffn_gate.weight", wr)
+    for e in range(SH.n_experts + 1):
+        pre = f"blk.0.experts.{e}." if e < SH.n_experts else "blk.0.shared_expert."
+        for m, name in ((0, "w1"), (1, "w3"), (2, "w2")):
+            a = ex[e][m]
+            w.add_tensor(pre + name + ".weight", a.reshape(a.shape[0], -1), raw_dtype=IQ)
+    w.write_header_to_file()
+    w.write_kv_data_to_file()
+    w.write_tensors_to_file()
+    w.close()
+
+
+@pytest.mark.parametrize("router", ["f32", "iq4"])
+def test_load_reference_registry_names(tmp_path, router):
+    p = tmp_path / "ref.gguf"
+    write_reference_named(p, router)
+    g = gguf_io.read_gguf(p)
+    arena = _ArenaStandIn()
+    reg, ids = gguf_io.load_moe_layers(arena, g, scale=1.0 / 9.0)
+    assert ids == [0]
+    spec, w1, w3, w2 = arena.layers[0]
+    E, H, I = SH.n_experts, SH.hidden, SH.inter
+    assert (spec.hidden, spec.inter, spec.n_experts, spec.top_k) == (H, I, E, SH.top_k)
+    assert spec.flags == host.MOE_F_SHARED and spec.shared_gate == 0  # reference: no shared gate
+    assert abs(spec.scale - 1.0 / 9.0) < 1e-7
+    wr, _, ex = _weights(0)
+    if router == "iq4":
+        raw = synth.iq4xs_matrix(synth.tensor_key(SEED, 50, 0, 0), E, H)
+        wr = O.dequant_matrix(raw, E, H).astype(np.float32)
+    got = np.frombuffer(bytes(arena.mem[spec.router_w:spec.router_w + wr.nbytes]), np.float32)
+    assert np.array_equal(got, wr.reshape(-1))
+    b13, b2 = I * (H // 256) * 136, H * (I // 256) * 136
+    for e in range(E):
+        for offs, m, nb in ((w1, 0, b13), (w3, 1, b13), (w2, 2, b2)):
+            assert bytes(arena.mem[offs[e]:offs[e] + nb]) == ex[e][m].tobytes()
+            assert reg.lookup(f"blk.0.experts.{e}.{('w1', 'w3', 'w2')[m]}.weight") == offs[e]
+    for off, m, nb in ((spec.shared_w1, 0, b13), (spec.shared_w3, 1, b13), (spec.shared_w2, 2, b2)):
+        assert bytes(arena.mem[off:off + nb]) == ex[E][m].tobytes()
