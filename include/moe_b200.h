@@ -139,10 +139,12 @@ int moe_bucket(moe_ctx* ctx, uint32_t n_experts, uint32_t top_k, int has_shared,
  * launched on `stream` (a cudaStream_t, NULL = legacy default stream).  Its scratch is a fixed
  * file-scope device array of about 190 KB that every GPU loading the library keeps until exit;
  * M is limited to 8192 tokens (larger M returns MOE_E_UNSUPPORTED), E to 256, top_k to 8.
- * The first call on a device looks up the array's device address; make that first call before
- * any stream capture.  All calls on a device share the array: calls that may run concurrently on
- * the GPU race and must be ordered by the caller.  Asynchronous; failures are reported only by
- * the return code. */
+ * The first call in a CUDA context looks up the array's device address in that context; make
+ * that first call before any stream capture.  All calls on a device share the array: calls that
+ * may run concurrently on the GPU race and must be ordered by the caller.  Asynchronous;
+ * argument failures are reported only by the return code.  Nothing is checked on the device:
+ * a routed expert id outside [0, E) (other than MOE_NO_EXPERT) is dropped -- its slot gets
+ * slot_pos -1 and no bucket position -- and no error is reported. */
 int moe_bucket_static(uint32_t n_experts, uint32_t top_k, int has_shared, const void* topk,
                       uint32_t M, int32_t* ranges, int32_t* tokens, float* weights,
                       int32_t* slot_pos, void* stream);
@@ -228,12 +230,24 @@ int moe_ep_init(moe_ctx* ctx, const void* unique_id, uint32_t n_ranks, uint32_t 
 /* out = resid + scale * MoE(x) for this rank's M tokens (M may be 0) through the group: route,
  * per-rank blocks of `capacity` rows, NCCL all-to-all, this rank's experts, all-to-all back,
  * combine.  Every rank must call it with the same layer shape and the same capacity
- * (>= the largest M of any rank).  The exchange buffers keep the largest capacity asked for;
+ * (>= the largest M of any rank).  A rank whose own token arguments are invalid (offsets, or
+ * M > capacity) still completes the exchange as a rank without tokens, serving its experts to
+ * the others, and then returns MOE_E_INVALID; a rank that cannot grow its workspace returns NaN
+ * partial rows to the others and MOE_E_OOM, so one rank's bad call never leaves the others
+ * waiting.  The exchange buffers keep the largest capacity asked for;
  * buffers replaced by a larger request stay allocated until the context is destroyed, so a
  * graph captured earlier stays valid.  Stream-ordered on the context's stream; capturable in a
  * CUDA graph after one eager call (which sizes the buffers). */
 int moe_forward_ep(moe_ctx* ctx, uint32_t layer_id, uint64_t x_off, uint64_t resid_off, uint64_t out_off,
                    uint32_t M, uint32_t capacity);
+
+/* Abort the group's NCCL communicator (ncclCommAbort), from any thread: a host watchdog that
+ * finds a peer rank dead or stuck calls it so that this rank's blocked NCCL work ends with an
+ * error instead of waiting forever (NCCL's GPU-side waits have no time limit; the peer
+ * transport's waits give up after 1 s on their own).  Afterwards moe_forward_ep fails with
+ * MOE_E_CUDA until moe_ep_init forms a new group.  Like the reference's Vulkan fence wait
+ * (src/inference.rs:169-182) there is no counterpart for a lost peer in the reference. */
+int moe_ep_abort(moe_ctx* ctx);
 
 /* How the rank blocks travel (set identically on every rank, before moe_forward_ep):
  *   MOE_EP_TRANSPORT_PEER (default): the dispatch kernel stores rows and records straight into

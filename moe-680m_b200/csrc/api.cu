@@ -5,6 +5,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cstdarg>
 #include <cstdio>
 #include <cstdlib>
@@ -1135,6 +1136,10 @@ static int ensure_ep_buffers(Ctx* c, const moe::NcclApi* api, uint32_t capacity,
     cudaError_t e = cudaMalloc(&p, pb + 4 * xb + 2 * rb + 256);
     if (e != cudaSuccess) {
         cudaGetLastError();
+        // the other ranks are entering the layout exchange: take part with an empty layout, so
+        // every rank fails (on the disagreement) instead of waiting for this one
+        ep.capacity = ep.hidden = ep.top_k = 0;
+        ep_check_layout(c, api);
         ep.capacity = ep.hidden = ep.top_k = 0;
         return fail(c, MOE_E_OOM, "expert-parallel buffers for %u x %u rows: %s", ep.n_ranks, capacity,
                     cudaGetErrorString(e));
@@ -1176,13 +1181,13 @@ static void ep_release(Ctx* c) {
             if (r.peer_base[d]) cudaIpcCloseMemHandle(r.peer_base[d]);
         cudaFree(r.buf);
     }
-    if (ep.comm) {
+    if (ep.comm && !ep.aborted.load()) {  // an aborted communicator is already freed
         const moe::NcclApi* api = moe::nccl_api(nullptr);
         if (api) api->comm_destroy(ep.comm);
     }
     if (ep.buf) cudaFree(ep.buf);
     const int transport = ep.transport;
-    ep = moe::EpState{};
+    ep.reset();
     ep.transport = transport;
 }
 
@@ -1254,40 +1259,83 @@ int moe_ep_init(moe_ctx* c, const void* unique_id, uint32_t n_ranks, uint32_t ra
     return MOE_OK;
 }
 
+int moe_ep_abort(moe_ctx* c) {
+    if (!c) return fail(c, MOE_E_INVALID, "NULL context");
+    moe::EpState& ep = c->ep;
+    if (!ep.comm) return MOE_OK;
+    if (ep.aborted.exchange(true)) return MOE_OK;
+    const moe::NcclApi* api = moe::nccl_api(nullptr);
+    if (api && api->comm_abort) api->comm_abort(ep.comm);
+    return MOE_OK;
+}
+
 int moe_forward_ep(moe_ctx* c, uint32_t layer_id, uint64_t x_off, uint64_t resid_off, uint64_t out_off,
                    uint32_t M, uint32_t capacity) {
     if (!c) return fail(c, MOE_E_INVALID, "NULL context");
     moe::EpState& ep = c->ep;
     if (!ep.comm) return fail(c, MOE_E_INVALID, "moe_ep_init has not been called on this context");
+    if (ep.aborted.load()) return fail(c, MOE_E_CUDA, "the expert-parallel group was aborted (moe_ep_abort)");
     Layer* L;
     int rc = get_layer(c, layer_id, &L);
     if (rc) return rc;
     const uint32_t n = ep.n_ranks, E = L->spec.n_experts, k = L->spec.top_k, H = L->spec.hidden;
     if (E % n != 0) return fail(c, MOE_E_UNSUPPORTED, "%u experts do not split over %u ranks", E, n);
+    // A rank whose own per-call arguments are bad must still take part in the exchange: the
+    // other ranks are already waiting for its blocks (NCCL waits without a time limit).  It
+    // joins as a rank with no tokens, serves its experts to the others, and reports the error.
+    int local_rc = MOE_OK;
     if (capacity == 0 || capacity < M)
-        return fail(c, MOE_E_INVALID, "capacity %u must be >= 1 and >= the %u local tokens", capacity, M);
-    if (M) {
-        if ((rc = check_tokens(c, *L, x_off, M, "x"))) return rc;
-        if (resid_off && (rc = check_tokens(c, *L, resid_off, M, "resid"))) return rc;
-        if ((rc = check_tokens(c, *L, out_off, M, "out"))) return rc;
+        local_rc = fail(c, MOE_E_INVALID, "capacity %u must be >= 1 and >= the %u local tokens", capacity, M);
+    if (M && local_rc == MOE_OK) {
+        if ((rc = check_tokens(c, *L, x_off, M, "x")) ||
+            (resid_off && (rc = check_tokens(c, *L, resid_off, M, "resid"))) ||
+            (rc = check_tokens(c, *L, out_off, M, "out")))
+            local_rc = rc;
+    }
+    if (local_rc != MOE_OK) {
+        M = 0;
+        capacity = std::max(capacity, 1u);
     }
     const moe::NcclApi* api = moe::nccl_api(nullptr);
     DeviceGuard g(c->device);
-    if ((rc = ensure_ep_buffers(c, api, capacity, H, k))) return rc;
+    if ((rc = ensure_ep_buffers(c, api, capacity, H, k))) return rc;  // collective, agreed outcome
     capacity = ep.capacity;  // rank blocks are laid out with the buffers' capacity
     const uint32_t rows = n * capacity;
-    if ((rc = ensure_layer_ws(c, *L, std::max(rows, M)))) return rc;
+    // Without a workspace this rank cannot run its experts; it still completes the exchange and
+    // returns NaN partial rows, so the tokens it should have served come out NaN on their ranks
+    // instead of the group hanging.
+    bool serve = true;
+    if ((rc = ensure_layer_ws(c, *L, std::max(rows, M)))) {
+        if (local_rc == MOE_OK) local_rc = rc;
+        serve = false;
+        M = 0;
+    }
     const size_t rec = static_cast<size_t>(k + 1) * 8;
     const moe::EpPlan plan = ep_plan_ptr(ep.plan, std::max(M, 1u), n);
     const int epr = static_cast<int>(E / n);
     prof_begin(c);
     if (M) {
         run_set_io(c, at<float>(c, x_off), nullptr, nullptr);
-        if ((rc = run_route(c, *L, M))) return rc;
-        moe::launch_ep_plan(c->ws.topk, static_cast<int>(M), static_cast<int>(k), epr, static_cast<int>(n),
-                            static_cast<int>(ep.rank), static_cast<int>(capacity), plan, c->ws.status, c->stream);
-        stage(c, "ep_plan", 2);
+        if ((rc = run_route(c, *L, M))) {
+            if (local_rc == MOE_OK) local_rc = rc;
+            M = 0;
+        } else {
+            moe::launch_ep_plan(c->ws.topk, static_cast<int>(M), static_cast<int>(k), epr, static_cast<int>(n),
+                                static_cast<int>(ep.rank), static_cast<int>(capacity), plan, c->ws.status,
+                                c->stream);
+            stage(c, "ep_plan", 2);
+        }
     }
+    // this rank's experts on the received rows (or NaN rows when it cannot run them)
+    auto run_local = [&]() -> int {
+        if (!serve) {
+            MOE_CUDA(c, cudaMemsetAsync(ep.y_send, 0xFF, static_cast<size_t>(rows) * H * 4, c->stream));
+            return MOE_OK;
+        }
+        MOE_CUDA(c, cudaMemcpyAsync(c->ws.topk, ep.recv_rec, rows * rec, cudaMemcpyDeviceToDevice, c->stream));
+        run_set_io(c, ep.recv_x, nullptr, ep.y_send);
+        return run_experts(c, *L, rows, true, L->has_shared(), 1.0f);
+    };
     const float* resid = resid_off ? at<float>(c, resid_off) : nullptr;
     if (ep.peer) {
         // rows and records stored into every owner's receive block over NVLink, then the
@@ -1299,9 +1347,7 @@ int moe_forward_ep(moe_ctx* c, uint32_t layer_id, uint64_t x_off, uint64_t resid
         moe::launch_ep_signal(ep.epoch, true, static_cast<int>(n), P, 0, c->stream);
         moe::launch_ep_wait(ep.flags, ep.epoch, static_cast<int>(n), c->ws.status, c->stream);
         stage(c, "ep_push", M ? 4 : 3);
-        MOE_CUDA(c, cudaMemcpyAsync(c->ws.topk, ep.recv_rec, rows * rec, cudaMemcpyDeviceToDevice, c->stream));
-        run_set_io(c, ep.recv_x, nullptr, ep.y_send);
-        if ((rc = run_experts(c, *L, rows, true, L->has_shared(), 1.0f))) return rc;
+        if ((rc = run_local())) return rc;
         moe::launch_ep_signal(ep.epoch, false, static_cast<int>(n), P, 1, c->stream);
         moe::launch_ep_wait(ep.flags + 8, ep.epoch, static_cast<int>(n), c->ws.status, c->stream);
         stage(c, "ep_sync", 2);
@@ -1328,9 +1374,7 @@ int moe_forward_ep(moe_ctx* c, uint32_t layer_id, uint64_t x_off, uint64_t resid
             return rc;
         stage(c, "ep_alltoall", 0);
         // 4. this rank's experts (and the shared expert for its own tokens) on every received row
-        MOE_CUDA(c, cudaMemcpyAsync(c->ws.topk, ep.recv_rec, rows * rec, cudaMemcpyDeviceToDevice, c->stream));
-        run_set_io(c, ep.recv_x, nullptr, ep.y_send);
-        if ((rc = run_experts(c, *L, rows, true, L->has_shared(), 1.0f))) return rc;
+        if ((rc = run_local())) return rc;
         // 5. partial rows back to their owners
         if ((rc = ep_alltoall(c, api, ep.y_send, ep.y_recv, static_cast<size_t>(capacity) * H, ncclFloat32, 4,
                               "combine all-to-all")))
@@ -1344,7 +1388,8 @@ int moe_forward_ep(moe_ctx* c, uint32_t layer_id, uint64_t x_off, uint64_t resid
         }
     }
     prof_end(c);
-    return check_launch(c, "forward_ep");
+    rc = check_launch(c, "forward_ep");
+    return local_rc != MOE_OK ? local_rc : rc;
 }
 
 int moe_set_path(moe_ctx* c, int path) {

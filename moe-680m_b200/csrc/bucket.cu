@@ -139,8 +139,12 @@ bucket_scan_kernel(int* __restrict__ tilecnt, int n_tiles, int E, int* __restric
         ranges[nb] = total.x;
         int c = total.y, a13 = total.z, a2 = total.w;
         if (c > max_chunks) { set_dev_error(status, kDevOverflow); c = max_chunks; }
-        if (a13 > lists.max13) { set_dev_error(status, kDevOverflow); a13 = lists.max13; }
-        if (a2 > lists.max2) { set_dev_error(status, kDevOverflow); a2 = lists.max2; }
+        if (lists.t13) {  // without tile lists (moe_bucket_static) there is nothing to overflow
+            if (a13 > lists.max13) { set_dev_error(status, kDevOverflow); a13 = lists.max13; }
+            if (a2 > lists.max2) { set_dev_error(status, kDevOverflow); a2 = lists.max2; }
+        } else {
+            a13 = a2 = 0;
+        }
         counters[0] = c;
         counters[1] = a13;
         counters[2] = a2;

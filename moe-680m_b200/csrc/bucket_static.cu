@@ -3,17 +3,19 @@
 // arena it sized up front, code running where cudaMalloc is forbidden or would stall other
 // streams, or a host that only hands over pre-allocated buffers); moe_bucket needs a context
 // whose workspace it grows with cudaMalloc.  This variant keeps its scratch (per-tile expert
-// counts, the chunk list, counters and an error word) in one file-scope device array of fixed
-// size, so it never allocates.
+// counts, the chunk list and counters) in one file-scope device array of fixed size, so it
+// never allocates.
 //
 // Limits and sharing: up to kStaticMaxTokens tokens, 256 experts, top-8.  The array lives on
 // every GPU that loads this library until the process exits, and every call on that GPU uses
 // the same array: calls whose work overlaps on the GPU (different streams, no ordering between
 // them) race on it and must be serialised by the caller.
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <atomic>
 #include <cstdint>
+#include <mutex>
 
 #include "moe_common.cuh"
 #include "moe_internal.h"
@@ -28,24 +30,53 @@ constexpr uint32_t kStaticMaxChunks = (kStaticMaxTokens * (kMaxTopK + 1) + kGemv
                                       kMaxExperts + 1;
 constexpr size_t kChunkOff = (kTileCntBytes + 255) / 256 * 256;
 constexpr size_t kCounterOff = kChunkOff + (sizeof(Chunk) * kStaticMaxChunks + 255) / 256 * 256;
-constexpr size_t kStatusOff = kCounterOff + 256;
-constexpr size_t kScratchBytes = kStatusOff + 256;  // about 190 KB
+constexpr size_t kScratchBytes = kCounterOff + 256;  // about 190 KB
 
 static __device__ __align__(256) uint8_t g_bucket_scratch[kScratchBytes];
 
-// Device address of g_bucket_scratch per device (looked up once, with that device current).
-std::atomic<uint8_t*> g_scratch_addr[64];
+// Device address of g_bucket_scratch in the current CUDA context.  The address is looked up
+// with that context current and cached per context (a primary context recreated after
+// cudaDeviceReset, or a second context on the same device, gets its own lookup), so a stale
+// address of a destroyed context is never reused.
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
 
-uint8_t* scratch_for_device(int dev) {
-    if (dev < 0 || dev >= 64) return nullptr;
-    uint8_t* p = g_scratch_addr[dev].load(std::memory_order_acquire);
-    if (p) return p;
+CUcontext current_context() {
+    static std::atomic<CtxGetCurrentFn> fn{nullptr};
+    CtxGetCurrentFn f = fn.load(std::memory_order_acquire);
+    if (!f) {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess || !p)
+            return nullptr;
+        f = reinterpret_cast<CtxGetCurrentFn>(p);
+        fn.store(f, std::memory_order_release);
+    }
+    CUcontext c = nullptr;
+    return f(&c) == CUDA_SUCCESS ? c : nullptr;
+}
+
+constexpr int kCacheSlots = 64;
+std::mutex g_cache_mu;
+CUcontext g_cache_ctx[kCacheSlots];
+uint8_t* g_cache_ptr[kCacheSlots];
+int g_cache_n = 0;
+
+uint8_t* scratch_for_current_context() {
+    const CUcontext c = current_context();
+    if (!c) return nullptr;
+    std::lock_guard<std::mutex> lk(g_cache_mu);
+    for (int i = 0; i < g_cache_n; ++i)
+        if (g_cache_ctx[i] == c) return g_cache_ptr[i];
     void* q = nullptr;
     if (cudaGetSymbolAddress(&q, g_bucket_scratch) != cudaSuccess || !q) {
         cudaGetLastError();
         return nullptr;
     }
-    g_scratch_addr[dev].store(static_cast<uint8_t*>(q), std::memory_order_release);
+    // a full cache recycles the oldest slot (contexts that old are normally gone)
+    const int slot = g_cache_n < kCacheSlots ? g_cache_n++ : 0;
+    g_cache_ctx[slot] = c;
+    g_cache_ptr[slot] = static_cast<uint8_t*>(q);
     return static_cast<uint8_t*>(q);
 }
 
@@ -69,14 +100,13 @@ int moe_bucket_static(uint32_t n_experts, uint32_t top_k, int has_shared, const 
     if (M > kStaticMaxTokens)
         return static_fail(MOE_E_UNSUPPORTED,
                            "moe_bucket_static: M exceeds the fixed scratch limit of 8192 tokens");
-    int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess) return static_fail(MOE_E_CUDA, "moe_bucket_static: no current device");
-    uint8_t* base = scratch_for_device(dev);
-    if (!base) return static_fail(MOE_E_CUDA, "moe_bucket_static: cudaGetSymbolAddress failed");
+    uint8_t* base = scratch_for_current_context();
+    if (!base) return static_fail(MOE_E_CUDA, "moe_bucket_static: no current context or cudaGetSymbolAddress failed");
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    // the error word must start at zero; everything else is fully written before it is read
-    if (cudaMemsetAsync(base + kStatusOff, 0, sizeof(int), s) != cudaSuccess)
-        return static_fail(MOE_E_CUDA, "moe_bucket_static: cudaMemsetAsync failed");
+    // Nothing has to start at zero: the tile counts, the chunk list and the counters are fully
+    // written by one launch before the next reads them.  There is no status word: nothing could
+    // read it back without synchronising, so a routed id outside [0, E) is dropped (its slot_pos
+    // is -1) and reported nowhere.
     Workspace ws;  // a view of the static array; nothing is allocated
     ws.tilecnt = reinterpret_cast<int*>(base);
     ws.chunks = reinterpret_cast<Chunk*>(base + kChunkOff);
@@ -86,7 +116,7 @@ int moe_bucket_static(uint32_t n_experts, uint32_t top_k, int has_shared, const 
     ws.tiles2 = nullptr;
     launch_bucket(static_cast<int>(n_experts), static_cast<int>(top_k), true, has_shared != 0,
                   static_cast<const uint2*>(topk), static_cast<int>(M), ws, ranges, tokens, weights,
-                  slot_pos, reinterpret_cast<int*>(base + kStatusOff), s);
+                  slot_pos, nullptr, s);
     const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return static_fail(MOE_E_CUDA, cudaGetErrorString(e));
     return MOE_OK;

@@ -5,6 +5,7 @@
 #include <cuda_runtime.h>
 #include <nccl.h>
 
+#include <atomic>
 #include <cstdint>
 #include <string>
 #include <vector>
@@ -167,6 +168,7 @@ struct NcclApi {
     ncclResult_t (*get_unique_id)(ncclUniqueId*) = nullptr;
     ncclResult_t (*comm_init_rank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
     ncclResult_t (*comm_destroy)(ncclComm_t) = nullptr;
+    ncclResult_t (*comm_abort)(ncclComm_t) = nullptr;
     ncclResult_t (*group_start)() = nullptr;
     ncclResult_t (*group_end)() = nullptr;
     ncclResult_t (*send)(const void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
@@ -207,6 +209,23 @@ struct EpState {
         uint8_t* peer_base[8];
     };
     std::vector<Retired> retired;
+    // set by moe_ep_abort (possibly from another thread): the communicator was aborted and freed
+    std::atomic<bool> aborted{false};
+    // back to the state of a context without a group (keeps nothing)
+    void reset() {
+        comm = nullptr;
+        n_ranks = rank = capacity = hidden = top_k = 0;
+        buf = plan = nullptr;
+        send_x = recv_x = y_send = y_recv = nullptr;
+        send_rec = recv_rec = nullptr;
+        flags = epoch = nullptr;
+        transport = 1;
+        peer = false;
+        for (auto& p : peer_base) p = nullptr;
+        off_recv_x = off_recv_rec = off_y_send = off_flags = 0;
+        retired.clear();
+        aborted.store(false);
+    }
 };
 
 struct Ctx {

@@ -36,6 +36,7 @@ const NcclApi* nccl_api(std::string* err) {
         api.get_unique_id = reinterpret_cast<decltype(api.get_unique_id)>(sym("ncclGetUniqueId"));
         api.comm_init_rank = reinterpret_cast<decltype(api.comm_init_rank)>(sym("ncclCommInitRank"));
         api.comm_destroy = reinterpret_cast<decltype(api.comm_destroy)>(sym("ncclCommDestroy"));
+        api.comm_abort = reinterpret_cast<decltype(api.comm_abort)>(sym("ncclCommAbort"));
         api.group_start = reinterpret_cast<decltype(api.group_start)>(sym("ncclGroupStart"));
         api.group_end = reinterpret_cast<decltype(api.group_end)>(sym("ncclGroupEnd"));
         api.send = reinterpret_cast<decltype(api.send)>(sym("ncclSend"));

@@ -37,7 +37,7 @@ EXPORTS = (
     "moe_bucket_static", "moe_forward_topk", "moe_ep_plan_bytes", "moe_ep_dispatch",
     "moe_ep_combine", "moe_dequant_ref36", "moe_forward_norm", "moe_vocab_logits",
     "moe_ep_unique_id", "moe_ep_init", "moe_forward_ep", "moe_ep_set_transport", "moe_ep_transport", "moe_silu_mul",
-    "moe_layer_set_next",
+    "moe_layer_set_next", "moe_ep_abort",
 )
 
 PATH_AUTO, PATH_GEMV, PATH_TC_SMEM_A, PATH_TC_TMEM_A = 0, 1, 2, 3
@@ -107,6 +107,7 @@ def lib():
         "moe_ep_init": (i32, [vp, vp, u32, u32]),
         "moe_forward_ep": (i32, [vp, u32, u64, u64, u64, u32, u32]),
         "moe_ep_set_transport": (i32, [vp, i32]),
+        "moe_ep_abort": (i32, [vp]),
         "moe_silu_mul": (i32, [vp, u64, u64, u64, u64]),
         "moe_ep_transport": (i32, [vp, P(i32)]),
         "moe_forward_norm": (i32, [vp, u32, u64, u64, u32, f32]),
@@ -317,6 +318,10 @@ class Context:
         v = C.c_int(0)
         self._check(lib().moe_ep_transport(self.h, C.byref(v)))
         return v.value
+
+    def ep_abort(self):
+        """Abort the group's communicator (a watchdog's call when a peer rank is lost)."""
+        self._check(lib().moe_ep_abort(self.h))
 
     def forward_ep(self, layer_id, x_off, resid_off, out_off, m, capacity):
         self._check(lib().moe_forward_ep(self.h, layer_id, x_off, resid_off, out_off, m, capacity))

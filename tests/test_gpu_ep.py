@@ -344,3 +344,74 @@ def test_c_abi_ep_two_ranks_reject_different_capacities():
             if p.is_alive():
                 p.kill()
     assert all("disagree" in m for m in res.values()), res
+
+
+def test_c_abi_ep_abort_one_rank(full):
+    """moe_ep_abort ends the group: later moe_forward_ep calls fail; a new moe_ep_init recovers."""
+    ctx, lid = full
+    ctx.ep_init(host.Context.ep_unique_id(), 1, 0)
+    m = 64
+    x = synth.tokens(SEED, 6, m, FULL.hidden)
+    xo = ctx.put(x)
+    ref_o, ep_o = ctx.alloc(x.nbytes), ctx.alloc(x.nbytes)
+    ctx.forward(lid, xo, xo, ref_o, m)
+    ctx.forward_ep(lid, xo, xo, ep_o, m, m)
+    ctx.sync()
+    ctx.ep_abort()
+    ctx.ep_abort()  # idempotent
+    with pytest.raises(host.MoeError):
+        ctx.forward_ep(lid, xo, xo, ep_o, m, m)
+    ctx.ep_init(host.Context.ep_unique_id(), 1, 0)
+    ctx.forward_ep(lid, xo, xo, ep_o, m, m)
+    ctx.sync()
+    assert O.rel_l2(ctx.download(ep_o, (m, FULL.hidden)), ctx.download(ref_o, (m, FULL.hidden))) < 1e-6
+
+
+def _c_ep_bad_rank_worker(rank, world, uid, m, cap, q):
+    try:
+        E, H = FULL.n_experts, FULL.hidden
+        epr = E // world
+        ctx = host.Context(rank, 1 << 30)
+        _, _, ids = host.build_synthetic_model(ctx, SEED, 1, FULL, 1.1, experts=range(rank * epr, (rank + 1) * epr))
+        ctx.ep_init(uid, world, rank)
+        x = synth.tokens(SEED, 11 + rank, m, H)
+        xo = ctx.put(x)
+        out = ctx.alloc(m * H * 4)
+        try:
+            # rank 1 passes more tokens than the capacity: it must fail without stalling rank 0
+            ctx.forward_ep(ids[0], xo, xo, out, m if rank == 0 else cap + 5, cap)
+            ctx.sync()
+            q.put((rank, x, ctx.download(out, (m, H))))
+        except host.MoeError as e:
+            q.put((rank, None, str(e)))
+        ctx.close()
+    except Exception as e:  # reported to the parent
+        q.put((rank, None, "worker failed: " + repr(e)))
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_c_abi_ep_bad_rank_does_not_stall_the_group():
+    """A rank with invalid token arguments reports its error; the other rank's step completes
+    with results equal to the single-GPU layer (the bad rank served its experts)."""
+    import torch.multiprocessing as mp
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    uid = host.Context.ep_unique_id()
+    mpc = mp.get_context("spawn")
+    q = mpc.Queue()
+    procs = [mpc.Process(target=_c_ep_bad_rank_worker, args=(r, 2, uid, 96, 128, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = {}
+    try:
+        for _ in range(2):
+            r, x, got = q.get(timeout=300)
+            res[r] = (x, got)
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.kill()
+    assert res[1][0] is None and "capacity" in res[1][1], res[1]
+    x0, got0 = res[0]
+    assert x0 is not None, got0
+    assert O.rel_l2(got0, _single_gpu_reference(x0)) < 1e-6

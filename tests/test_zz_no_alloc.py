@@ -43,6 +43,24 @@ def test_bucket_static_matches_bucket():
                 a = ctx.download(ro, n, dt)
                 b = ctx.download(go, n, dt)
                 assert np.array_equal(a.view(np.uint32), b.view(np.uint32)), f"call {call}"
+        # an out-of-range routed id is dropped (slot_pos -1), the rest bucketed as usual
+        m = 3
+        rec = np.zeros((m, k + 1, 2), np.uint32)
+        rec[:, 0, 0] = E
+        rec[:, 0, 1] = np.float32(1.0).view(np.uint32)
+        rec[:, 1:, 0] = np.arange(k)[None, :]
+        rec[:, 1:, 1] = np.float32(0.125).view(np.uint32)
+        rec[1, 3, 0] = E + 7  # bad id in token 1, slot 2
+        ro = ctx.put(rec)
+        S = m * (k + 1)
+        outs = [ctx.alloc((E + 2) * 4), ctx.alloc(S * 4), ctx.alloc(S * 4), ctx.alloc(S * 4)]
+        assert L.moe_bucket_static(E, k, 1, C.c_void_p(ctx.ptr(ro)), m,
+                                   *[C.c_void_p(ctx.ptr(o)) for o in outs], None) == 0
+        torch.cuda.synchronize()
+        ranges = ctx.download(outs[0], (E + 2,), np.int32)
+        sp = ctx.download(outs[3], (m, k + 1), np.int32)
+        assert sp[1, 2] == -1 and (np.delete(sp.ravel(), 1 * (k + 1) + 2) >= 0).all()
+        assert ranges[E + 1] == S - 1 and ranges[2] - ranges[1] == 2  # expert 2 lost token 1
         # sizes beyond the fixed scratch are refused, not overrun
         assert L.moe_bucket_static(E, k, 1, C.c_void_p(ctx.ptr(topk)), 9000,
                                    *[C.c_void_p(ctx.ptr(o)) for o in got], None) == -4
