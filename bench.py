@@ -37,6 +37,9 @@ SEED = 20240601
 PREFILL_M = 512
 ZIPF = 1.1
 CPU_SAMPLE_TOKENS = 512
+PREFILL_LAYERS = 4  # independently seeded config-1 layers, cycled step by step (no L2 reuse)
+WORKLOAD = ("config1: prefill 512 tok per GPU, Zipf(1.1) router bias, 1 MoE layer "
+            "(H=2048, I=512, E=256, top-8 + gated shared, IQ4_XS)")
 CONFIG3_M = 8192
 CONFIG2_LAYERS = 40
 CONFIG2_STEPS = 256
@@ -54,6 +57,18 @@ def load_pkg():
     sys.modules["moe680m_b200"] = mod
     spec.loader.exec_module(mod)
     return mod
+
+
+def ncu_traffic(kernel_stage: str):
+    """DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum) of a stage's kernel
+    from the committed ncu summaries: a line ``ncu_dram_bytes[<stage>]: <bytes> (<file note>)``."""
+    import re
+    for f in sorted((ROOT / "profiles").glob("*.md")):
+        for line in f.read_text().splitlines():
+            m = re.match(r"\s*ncu_dram_bytes\[(\w+)\]:\s*(\d+)", line)
+            if m and m.group(1) == kernel_stage:
+                return int(m.group(2)), f"profiles/{f.name}"
+    return None, None
 
 
 def peaks():
@@ -114,7 +129,8 @@ def distinct_experts(routed: np.ndarray) -> int:
 NVLINK_GBS = 770.0  # measured peer-copy bandwidth per direction per GPU on this pool's B200s
 
 
-def ep_exchange_bytes(routed_all: np.ndarray, world: int, m: int, epr: int, hidden: int, k: int) -> np.ndarray:
+def ep_exchange_bytes(routed_all: np.ndarray, world: int, m: int, epr: int, hidden: int, k: int,
+                      transport: str = "peer", capacity: int | None = None) -> np.ndarray:
     """Bytes each rank moves over NVLink in one expert-parallel step, [world][2] (out, in).
 
     routed_all: [world*m, k] expert ids, rank r's tokens at rows r*m..(r+1)*m.  A token visits
@@ -128,6 +144,12 @@ def ep_exchange_bytes(routed_all: np.ndarray, world: int, m: int, epr: int, hidd
     sent = np.array([visits[owner == r].sum() for r in range(world)], np.int64)  # rows r dispatches
     recv = visits.sum(axis=0).astype(np.int64)                                     # rows r serves
     row_in, row_back = hidden * 4 + (k + 1) * 8, hidden * 4
+    if transport != "peer":
+        # the NCCL all-to-alls move whole fixed-capacity blocks to and from every other rank,
+        # used rows or not
+        cap = capacity if capacity is not None else m
+        blk = (world - 1) * cap * (row_in + row_back)
+        return np.full((world, 2), blk, np.int64)
     out = sent * row_in + recv * row_back
     inn = recv * row_in + sent * row_back
     return np.stack([out, inn], axis=1)
@@ -138,7 +160,7 @@ def cpu_baseline(shapes, x: np.ndarray, min_seconds: float = 10.0, threads: int 
     512-token prefills repeated until ``min_seconds`` of CPU time have passed."""
     sys.path.insert(0, str(ROOT / "oracle"))
     import coracle
-    layer = coracle.synthetic_layer(SEED, 0, shapes, ZIPF)
+    layer = host_layer(shapes)
     xs = np.ascontiguousarray(x)
     coracle.moe_forward(layer, xs[:4], xs[:4], acc64=False, nthreads=threads)  # warm
     n, t0 = 0, time.perf_counter()
@@ -162,30 +184,57 @@ def run_reference(args):
     sh = synth.LayerShapes()
     layer = coracle.synthetic_layer(SEED, 0, sh, ZIPF)
     x = synth.tokens(SEED, 0, PREFILL_M, sh.hidden)
-    cores = os.cpu_count() or 1
+    # every host thread, explicitly: torchrun exports OMP_NUM_THREADS=1, which the OpenMP
+    # default of the C restatement would otherwise honour
+    cores = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
     n = CPU_SAMPLE_TOKENS
     for i in range(args.warmup):
-        coracle.moe_forward(layer, x[:n], x[:n], acc64=False)
+        coracle.moe_forward(layer, x[:n], x[:n], acc64=False, nthreads=cores)
     times = []
     for i in range(args.steps):
         xs = np.ascontiguousarray(np.roll(x, -n * i, axis=0)[:n])
         t0 = time.perf_counter()
-        coracle.moe_forward(layer, xs, xs, acc64=False)
+        coracle.moe_forward(layer, xs, xs, acc64=False, nthreads=cores)
         times.append(time.perf_counter() - t0)
     ms = 1e3 * sum(times) / len(times)
     v = n / (ms / 1e3)
     line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "tok/s", "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded)",
-            "config": {"workload": "config1: prefill 512 tok, Zipf(1.1) router bias, 1 MoE layer "
-                                   "(H=2048, E=256, top-8 + gated shared, IQ4_XS)",
-                       "sample_tokens_per_step": n},
+            "config": {"workload": WORKLOAD, "sample_tokens_per_step": n,
+                       "omp_threads": cores},
             "cpu_baseline": {"value": v, "unit": "tok/s", "cores": cores, "kind": "port",
                              "sample": f"{n} of the 512 prefill tokens per step; the reference "
                                        "(Rust+Vulkan) cannot be built here, so its algorithm runs "
-                                       "as the C restatement in oracle/ (f32 accumulation, OpenMP)"},
+                                       f"as the C restatement in oracle/ (f32 accumulation, OpenMP, "
+                                       f"{cores} threads)"},
             "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
+
+
+_HOST_LAYER = {}
+
+
+def host_layer(shapes):
+    """Host copy of config-1 layer 0 for the C restatement (built once)."""
+    if "l" not in _HOST_LAYER:
+        sys.path.insert(0, str(ROOT / "oracle"))
+        import coracle
+        _HOST_LAYER["l"] = coracle.synthetic_layer(SEED, 0, shapes, ZIPF)
+    return _HOST_LAYER["l"]
+
+
+def oracle_rows_check(shapes, x: np.ndarray, got: np.ndarray, n_rows: int = 48) -> dict:
+    """Sampled rows of a timed step's output against the f64 C oracle (the checker only)."""
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import coracle
+    rows = np.random.default_rng(7).choice(x.shape[0], size=min(n_rows, x.shape[0]), replace=False)
+    rows.sort()
+    xr = np.ascontiguousarray(x[rows])
+    ref = coracle.moe_forward(host_layer(shapes), xr, xr, acc64=True, nthreads=os.cpu_count() or 0)["out64"]
+    g = got[rows].astype(np.float64)
+    return {"rows": int(len(rows)), "rel_l2": float(np.linalg.norm(g - ref) / np.linalg.norm(ref)),
+            "max_rel": float(np.abs(g - ref).max() / np.abs(ref).max())}
 
 
 def _max_over_ranks(v: float, world: int) -> float:
@@ -196,6 +245,17 @@ def _max_over_ranks(v: float, world: int) -> float:
     t = torch.tensor([v], device="cuda")
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     return float(t.item())
+
+
+def _gather_floats(v: float, world: int) -> list:
+    if world == 1:
+        return [v]
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([v], device="cuda", dtype=torch.float64)
+    out = [torch.empty_like(t) for _ in range(world)]
+    dist.all_gather(out, t)
+    return [float(o.item()) for o in out]
 
 
 def _barrier(world: int):
@@ -241,6 +301,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--no-check", action="store_true", help="skip the parity check of the timed step")
     ap.add_argument("--only", default="all", choices=["all", "prefill", "lm_head"],
                     help="prefill: skip the decode, config-3, end-to-end and CPU legs; lm_head: only "
                          "the LM-head leg, 0.3 GB on the device (profiling runs)")
@@ -289,7 +350,8 @@ def main():
     # through them (no L2 hits)
     n_dec_layers = 0 if only_prefill else CONFIG2_LAYERS
     c3_tokens = CONFIG3_M // world
-    arena_bytes = ((n_dec_layers + 1) * sh.expert_bytes * (E + 1)
+    n_full_check = 1 if (ep_mode and rank == 0) else 0  # rank 0's full layer for the EP parity check
+    arena_bytes = ((n_dec_layers + PREFILL_LAYERS + n_full_check) * sh.expert_bytes * (E + 1)
                    + (0 if only_prefill else 2 * sh.expert_bytes * (E + 1))
                    + (0 if only_prefill else VOCAB_BYTES)
                    + (3 << 30))
@@ -305,7 +367,8 @@ def main():
         dist.broadcast_object_list(uid, src=0)
         ctx.ep_set_transport(host.MOE_EP_TRANSPORT_PEER if args.ep == "peer" else host.MOE_EP_TRANSPORT_NCCL)
         ctx.ep_init(uid[0], world, rank)
-    pre = host.build_synthetic_model(ctx, SEED, 1, sh, ZIPF, experts=my_experts)[2][0]
+    pre_ids = host.build_synthetic_model(ctx, SEED, PREFILL_LAYERS, sh, ZIPF, experts=my_experts)[2]
+    pre = pre_ids[0]
     dec_ids = host.build_synthetic_model(ctx, SEED + 1, n_dec_layers, sh, None)[2] if n_dec_layers else []
     K, W = args.steps, args.warmup
     n_x = K + W
@@ -392,12 +455,19 @@ def main():
                 ctx.forward(lid, x_off, x_off, out, m)
         return step
 
-    step = make_step(pre, PREFILL_M, out_off)
+    # one step per layer; timed step i runs layer i mod PREFILL_LAYERS, so consecutive steps
+    # stream different weights (4 layers x ~82 touched experts x 1.67 MB = 0.55 GB > the 126 MB L2)
+    layer_steps = [make_step(lid, PREFILL_M, out_off) for lid in pre_ids]
+
+    def step(x_off, i=0):
+        layer_steps[i % PREFILL_LAYERS](x_off)
+    step.eager = lambda x_off, i=0: getattr(layer_steps[i % PREFILL_LAYERS], "eager",
+                                            layer_steps[i % PREFILL_LAYERS])(x_off)
     torch.cuda.synchronize()
 
     # ---- prefill: inputs resident in HBM ----------------------------------------------------
     for i in range(W):
-        step(x_offs[i])
+        step(x_offs[i], i)
     ctx.sync()
     dev_uuid = None
     try:
@@ -412,28 +482,60 @@ def main():
     with ClockSampler(dev_uuid) as clk:
         ev0.record(stream)
         for i in range(K):
-            step(x_offs[W + i])
+            step(x_offs[W + i], i)
         ev1.record(stream)
         torch.cuda.synchronize()
     launches = ctx.launch_count() - l0
     if ep_caps:  # graph replays do not pass through the library's launch counter
         l1 = ctx.launch_count()
-        step.eager(x_offs[W])
+        step.eager(x_offs[W], 0)
         torch.cuda.synchronize()
         launches = (ctx.launch_count() - l1) * K
-    ms = _max_over_ranks(ev0.elapsed_time(ev1) / K, world)
+    my_ms = ev0.elapsed_time(ev1) / K
+    ms = _max_over_ranks(my_ms, world)
     _barrier(world)
     value = world * PREFILL_M / (ms / 1e3)
+    rank_ms = _gather_floats(my_ms, world)
+
+    # ---- parity of the timed step: the output of step 0's layer on fixed tokens ------------
+    parity = None
+    if not args.no_check:
+        step(x_offs[W], 0)
+        torch.cuda.synchronize()
+        nb = PREFILL_M * H * 4
+        got_t = arena[out_off:out_off + nb].view(torch.float32).view(PREFILL_M, H).clone()
+        x_t = arena[x_offs[W]:x_offs[W] + nb].view(torch.float32).view(PREFILL_M, H).clone()
+        if ep_mode:
+            gx = [torch.empty_like(x_t) for _ in range(world)]
+            gy = [torch.empty_like(got_t) for _ in range(world)]
+            dist.all_gather(gx, x_t)
+            dist.all_gather(gy, got_t)
+            if rank == 0:
+                # the same tokens through the single-GPU layer (all 256 experts) on rank 0
+                full = host.build_synthetic_model(ctx, SEED, 1, sh, ZIPF)[2][0]
+                mt = world * PREFILL_M
+                xa = torch.cat(gx).cpu().numpy()
+                ya = torch.cat(gy).cpu().numpy()
+                xo_all, yo_all = ctx.put(xa), ctx.alloc(mt * H * 4)
+                ctx.forward(full, xo_all, xo_all, yo_all, mt)
+                ctx.sync()
+                ref = ctx.download(yo_all, (mt, H)).astype(np.float64)
+                parity = {"ep_parity": {"tokens": mt, "vs": "single-GPU moe_forward of the same tokens",
+                                        "rel_l2": float(np.linalg.norm(ya - ref) / np.linalg.norm(ref)),
+                                        "max_rel": float(np.abs(ya - ref).max() / np.abs(ref).max())},
+                          "oracle": oracle_rows_check(sh, xa, ya)}
+        else:
+            parity = {"oracle": oracle_rows_check(sh, x_t.cpu().numpy(), got_t.cpu().numpy())}
 
     # ---- per-stage device times (profiling pass, not the timed run) -------------------------
     ctx.profile(True)
     for i in range(K):
-        getattr(step, "eager", step)(x_offs[W + i])
+        step.eager(x_offs[W + i], i)
     stages = ctx.profile_read()
     ctx.profile(False)
     # distinct experts whose weights this GPU streams (all ranks' tokens reach a rank's experts)
-    routed = np.concatenate([ctx.do_route(pre, x_offs[W + i], PREFILL_M, sh.top_k)[0][None]
-                             for i in range(K)])  # [K, M, k]
+    routed = np.concatenate([ctx.do_route(pre_ids[i % PREFILL_LAYERS], x_offs[W + i], PREFILL_M,
+                                          sh.top_k)[0][None] for i in range(K)])  # [K, M, k]
     if ep_mode:
         t = torch.from_numpy(routed.astype(np.int64)).cuda()
         allr = [torch.empty_like(t) for _ in range(world)]
@@ -450,8 +552,10 @@ def main():
     dom = max(stage_ms, key=stage_ms.get)
     layer_bytes = n_mats * sh.expert_bytes
     ach = alg_bytes.get(dom, 0.0) / (stage_ms[dom] / 1e3) / 1e9 if dom in alg_bytes else None
+    traffic, traffic_src = ncu_traffic(dom)
     roofline = {"bound": "hbm", "kernel": dom, "achieved": ach, "peak": hbm, "unit": "GB/s",
-                "frac": ach / hbm if ach else None, "traffic": None, "peak_kind": peak_kind,
+                "frac": ach / hbm if ach else None, "traffic": traffic, "traffic_source": traffic_src,
+                "peak_kind": peak_kind,
                 "alg_bytes_per_launch": alg_bytes.get(dom),
                 "layer_achieved_gbs": layer_bytes / (ms / 1e3) / 1e9,
                 "layer_frac": layer_bytes / (ms / 1e3) / 1e9 / hbm,
@@ -461,12 +565,14 @@ def main():
         # the rows crossing NVLink (the larger direction of the busiest GPU, at the measured
         # peer bandwidth)
         try:
-            nv = max(float(ep_exchange_bytes(routed[i], world, PREFILL_M, epr, H, sh.top_k).max())
-                     for i in range(K))
+            tr = {0: "nccl", 1: "peer"}.get(ctx.ep_transport(), "nccl") if c_ep else "torch"
+            nv = max(float(ep_exchange_bytes(routed[i], world, PREFILL_M, epr, H, sh.top_k, tr,
+                                             PREFILL_M).max()) for i in range(K))
             t_nv, t_hbm = nv / (NVLINK_GBS * 1e3), layer_bytes / (hbm * 1e3)
             roofline["ep_step"] = {"nvlink_bytes_max": nv, "nvlink_us": t_nv, "hbm_us": t_hbm,
                                    "target_us": max(t_nv, t_hbm), "step_us": ms * 1e3,
-                                   "frac": max(t_nv, t_hbm) / (ms * 1e3), "nvlink_gbs": NVLINK_GBS}
+                                   "frac": max(t_nv, t_hbm) / (ms * 1e3), "nvlink_gbs": NVLINK_GBS,
+                                   "transport": tr}
         except Exception as e:  # noqa: BLE001 - reported, never fatal to the bench
             roofline["ep_step"] = {"error": repr(e)}
 
@@ -480,7 +586,7 @@ def main():
 
         def e2e_step(i):
             ctx.upload_ptr(xin, hx[i % 4].data_ptr(), nbytes)
-            step(xin)
+            step(xin, i)
             ctx.download_ptr(out_off, hout.data_ptr(), nbytes)
         for i in range(2):
             e2e_step(i)
@@ -512,9 +618,11 @@ def main():
                 step3(xc[i % 4])
             ev1.record(stream)
             torch.cuda.synchronize()
-            ms3 = _max_over_ranks(ev0.elapsed_time(ev1) / k3, world)
+            my3 = ev0.elapsed_time(ev1) / k3
+            ms3 = _max_over_ranks(my3, world)
             flops = CONFIG3_M * (sh.top_k + 1) * 6 * sh.inter * H
             config3[name] = {"ms_per_step": ms3, "tok_s": CONFIG3_M / (ms3 / 1e3),
+                             "rank_ms": [round(v, 4) for v in _gather_floats(my3, world)],
                              "tensor_tflops_per_gpu": flops / (ms3 / 1e3) / 1e12 / world,
                              "tensor_frac": flops / (ms3 / 1e3) / 1e12 / world / tfl}
 
@@ -584,7 +692,14 @@ def main():
         lid4 = dec_ids[0]
         routed4 = ctx.do_route(lid4, x4[0], m4, sh.top_k)[0]
         d4 = len(np.unique(routed4)) + 1
-        config4 = {"tokens": m4, "distinct_experts_plus_shared": d4, "auto_choice": "tcgen05 (M > 8)"}
+        ctx.set_path(0)  # what the library picks by itself at M=64: read from its stage names
+        ctx.profile(True)
+        ctx.forward(lid4, x4[0], x4[0], o4, m4)
+        auto_st = ctx.profile_read()
+        ctx.profile(False)
+        auto = "tcgen05" if "tc13" in auto_st else "gemv" if "gemv13" in auto_st else "?"
+        config4 = {"tokens": m4, "distinct_experts_plus_shared": d4,
+                   "auto_choice": auto, "auto_stages": sorted(auto_st)}
         for name, path in (("gemv", 1), ("tcgen05", 3)):
             ctx.set_path(path)
             for i in range(3):
@@ -606,8 +721,9 @@ def main():
 
         # ---- CPU baseline (rank 0, N=1 only) ------------------------------------------------------
         if rank == 0 and world == 1 and not args.no_cpu:
-            _, v, dt, n = cpu_baseline(sh, xs[0])
-            cpu = {"value": v, "unit": "tok/s", "cores": os.cpu_count(), "kind": "port",
+            ncpu = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
+            _, v, dt, n = cpu_baseline(sh, xs[0], threads=ncpu)
+            cpu = {"value": v, "unit": "tok/s", "cores": ncpu, "kind": "port",
                    "sample": f"{n} tokens = repeated config-1 512-token prefills ({dt:.1f} s), C "
                              "restatement of the reference MoE layer (oracle/, f32, OpenMP all cores)"}
 
@@ -616,8 +732,7 @@ def main():
                 "warmup": W, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
                 "vs_baseline": None, "dtype": "f32" if args.path == 1 else "f16 (f32 accumulate)",
                 "data": "synthetic (seeded IQ4_XS weights generated on device, N(0,1) tokens)",
-                "config": {"workload": "config1: prefill 512 tok per GPU, Zipf(1.1) router bias, 1 MoE layer "
-                                       "(H=2048, I=512, E=256, top-8 + gated shared, IQ4_XS)",
+                "config": {"workload": WORKLOAD,
                            "tokens_per_step": PREFILL_M * world,
                            "parallelism": (f"ep{world}: {epr} experts per GPU, " + {
                                "peer": "dispatch stores / combine loads over NVLink peer memory (moe_forward_ep)",
@@ -627,8 +742,12 @@ def main():
                                               2: "tcgen05, A in smem", 3: "tcgen05, A in TMEM"}[args.path],
                            "distinct_experts_per_gpu": round(statistics.mean(distinct), 1),
                            "ep_step": ep_graphs[0] if ep_graphs else None,
-                           "l2": "weights 430 MB per layer exceed the 126 MB L2; fresh tokens per step"},
-                "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches,
+                           "l2": (f"{PREFILL_LAYERS} independently seeded layers cycled step by step "
+                                  f"(~{n_mats * sh.expert_bytes / 1e6:.0f} MB of touched weights per step, "
+                                  f"{PREFILL_LAYERS * n_mats * sh.expert_bytes / 1e6:.0f} MB per cycle vs the "
+                                  "126 MB L2); fresh tokens per step; no L2 flush"),
+                           "rank_ms": [round(v, 4) for v in rank_ms]},
+                "parity": parity, "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches,
                 "clocks": clk.summary(), "decode": decode, "config2": config2, "config3": config3,
                 "config4": config4, "lm_head": lm_head}
         print(json.dumps(line), flush=True)
