@@ -9,7 +9,8 @@ ABI against the CPU oracle:
   free-running oracle chain;
 * config 4: the CUDA-core GEMV expert path forced at M=64 against the oracle.
 
-Tolerances: relative L2 <= 1e-3 and max|d| / max|ref| <= 2e-3 per layer output (the contract's).
+Tolerances: relative L2 <= 1e-3 and max|d| / max|ref| <= 2e-3 per layer output (the contract's);
+the 40-layer chain's final state within relative L2 1e-2 of the free-running oracle chain.
 """
 import numpy as np
 import pytest
@@ -22,6 +23,7 @@ pytestmark = pytest.mark.gpu
 
 REL_L2 = 1e-3
 MAX_REL = 2e-3
+STACK_REL_L2 = 1e-2  # final state of the 40-layer chain against the free-running oracle chain
 FULL = synth.LayerShapes(2048, 512, 256, 8, 512)
 
 
@@ -117,8 +119,9 @@ def test_config2_layer_stack_two_steps():
                 check_close(xs[li + 1], ref["out64"], f"step {t} layer {li}")
                 free = coracle.moe_forward(hl, fn, free, acc64=True)["out64"].astype(np.float32)
             finals.append(xs[-1])
-            # the free-running oracle chain ends where the stack does
-            check_close(xs[-1], free, f"step {t} final state")
+            # the free-running oracle chain ends where the stack does: 40 residual layers compound
+            # the per-layer differences, so the stack's bound is looser than one layer's
+            assert O.rel_l2(xs[-1], free) <= STACK_REL_L2, (t, O.rel_l2(xs[-1], free))
         assert not np.array_equal(finals[0], finals[1])
     finally:
         ctx.close()
