@@ -104,6 +104,8 @@ int ensure_ws(Ctx* c, uint32_t M, uint32_t E, uint32_t k, uint32_t slots, uint32
     const size_t o_xh = take(sizeof(float) * M * H);
     const size_t o_xl = take(sizeof(float) * M * H);
     const size_t o_xn = take(sizeof(float) * M * H);
+    const size_t dx_bytes = sizeof(unsigned long long) * moe::decode_exchange_words(E, slots - 1, I);
+    const size_t o_dx = take(dx_bytes);
     const size_t total = off;
     int* status = ws.status;
     ws.status = nullptr;
@@ -145,6 +147,12 @@ int ensure_ws(Ctx* c, uint32_t M, uint32_t E, uint32_t k, uint32_t slots, uint32
     ws.xh = reinterpret_cast<float*>(b + o_xh);
     ws.xl = reinterpret_cast<float*>(b + o_xl);
     ws.xn = reinterpret_cast<float*>(b + o_xn);
+    ws.dx = reinterpret_cast<unsigned long long*>(b + o_dx);
+    ws.dx_bytes = dx_bytes;
+    // no stale epoch may match a later launch: the exchange entries start at zero (epoch 0 is
+    // never used)
+    e = cudaMemset(b + o_dx, 0, dx_bytes);
+    if (e != cudaSuccess) return cuda_fail(c, e, "workspace exchange clear");
     ws.max_chunks = static_cast<uint32_t>(max_chunks);
     ws.status = status;
     return MOE_OK;
@@ -334,14 +342,15 @@ void destroy_graph(moe::GraphEntry& g) {
 }
 
 bool use_decode(const Ctx* c, const Layer& L, uint32_t M) {
-    return M == 1 && (c->path == moe::kPathAuto || c->path == moe::kPathGemv) && moe::decode_supported(L);
+    return M == 1 && (c->path == moe::kPathAuto || c->path == moe::kPathGemv) && moe::decode_supported(L, c->sm_count);
 }
 
 int record_forward(Ctx* c, const Layer& L, uint32_t M, const float* x, const float* resid, float* out) {
     if (use_decode(c, L, M)) {
         // single token: the whole layer in one fused launch with direct pointers (no graph or
-        // pointer block needed); its grid-sync words live after the status word
-        moe::launch_decode(L, c->ws, decode_sync(c), c->sm_count, c->stream, x, resid, out, -1.0f);
+        // pointer block needed); its launch counter lives after the status word
+        if (moe::launch_decode(L, c->ws, decode_sync(c), c->sm_count, c->stream, x, resid, out, -1.0f))
+            return check_launch(c, "decode (cooperative launch refused)");
         stage(c, "decode", 1);
         return check_launch(c, "decode");
     }
@@ -565,6 +574,7 @@ int moe_sync(moe_ctx* c) {
         cudaMemset(c->ws.status, 0, sizeof(int));
         // the decode kernel's grid counter and h maxima, the vocabulary argmax ticket and keys
         cudaMemset(decode_sync(c), 0, moe::kStatusKernelEnd - moe::kStatusDecodeOff);
+        if (c->ws.dx) cudaMemset(c->ws.dx, 0, c->ws.dx_bytes);  // stale epochs go with the counter
         const char* what = st == moe::kDevBadExpert ? "expert id out of range"
                          : st == moe::kDevBadToken ? "token index out of range"
                          : st == moe::kDevOverflow ? "chunk list overflow"
@@ -622,6 +632,7 @@ int moe_layer_create(moe_ctx* c, const moe_layer_spec* spec, const uint64_t* w1,
     Layer L;
     L.spec = s;
     L.tab = static_cast<const uint8_t**>(d);
+    L.host_tab = tab;
     L.tab_aligned16 = true;
     for (const uint8_t* q : tab)
         if (q && reinterpret_cast<uintptr_t>(q) % 16 != 0) L.tab_aligned16 = false;
@@ -822,10 +833,11 @@ int moe_forward_norm(moe_ctx* c, uint32_t layer_id, uint64_t x_off, uint64_t out
     if ((rc = ensure_layer_ws(c, *L, M))) return rc;
     const float* x = at<float>(c, x_off);
     float* out = at<float>(c, out_off);
-    if (M == 1 && (c->path == moe::kPathAuto || c->path == moe::kPathGemv) && moe::decode_supported(*L) &&
+    if (M == 1 && (c->path == moe::kPathAuto || c->path == moe::kPathGemv) && moe::decode_supported(*L, c->sm_count) &&
         out != x) {
         // one launch: normalisation inside the fused decode kernel, direct pointers
-        moe::launch_decode(*L, c->ws, decode_sync(c), c->sm_count, c->stream, x, x, out, eps);
+        if (moe::launch_decode(*L, c->ws, decode_sync(c), c->sm_count, c->stream, x, x, out, eps))
+            return check_launch(c, "decode (cooperative launch refused)");
         stage(c, "decode", 1);
         return check_launch(c, "decode");
     }

@@ -3,34 +3,43 @@
 // moe-680m's router.comp + router_topk.comp + do_route + the 18 w1_w3_fused / w2_scatter
 // dispatches of record_and_submit_moe's decode branch (src/inference.rs:734-762).
 //
-// One CTA per SM, 16 warps.  Phases:
-//   1. every warp computes router-row quarters (x . Wr[e], f32; row E = the shared-expert gate
-//      g . x) and each CTA arrives on a grid counter;
-//   2. gate/up work units (expert slot, row j): h[slot][j] = silu(W1[j].x) * (W3[j].x), slots
-//      0..k-1 routed, slot k shared.  Warps first run the shared expert's units, which need no
-//      routing; then every CTA waits for all router rows, computes softmax + top-k itself from
-//      the logits (identically in every CTA) and runs its routed units;
-//   3. after a second arrival on the counter: out[n] = resid[n] + scale * sum_s w_s (W2_s[n].h_s),
-//      one warp per output row.
-// Expert rows are copied to shared memory with coalesced 16-byte cp.async (a 32-lane load then
-// covers 4 whole 128-byte lines) and decoded from there; loading the sub-block layout directly
-// from global memory touches each line with several partial requests and is limited by the
-// SM's outstanding-request capacity.
+// One CTA per SM (cooperative launch, so every CTA is resident), 16 warps.  Each CTA owns fixed
+// slices of the work:
+//   * router half-rows t = c, c + G, ... of the 2 (E + 1) halves (row E: the shared-expert gate
+//     g . x), f32 dot products of the f32 router weight with x;
+//   * a contiguous range of the shared expert's gate/up units (unit j: rows j of W1 and W3,
+//     h[j] = silu(W1[j] . x) * (W3[j] . x)), ~I/G units;
+//   * a contiguous range of the k * I routed units (slot s = u / I, row j = u % I), ~k I / G;
+//   * a contiguous range of output rows n, over which it computes
+//     out[n] = resid[n] + scale * sum_s w_s (W2_s[n] . h_s) for all k + 1 slots.
+// Work of other CTAs is consumed through two exchanges in global memory whose entries carry the
+// launch's epoch in their high 32 bits (64-bit stores and loads are single-copy atomic): a
+// reader polls the entries it needs until every one shows the current epoch.  The data itself is
+// the barrier, so a consumer starts as soon as the entries it reads are complete, one L2 round
+// trip after the last producer, instead of a counter barrier followed by a second round trip
+// for the data.  Exchanges: the half-row logits (every CTA then computes softmax + top-k itself,
+// identically: fixed reduction order, ties to the lower index) and h (every CTA needs all of h
+// for its output rows).
 //
-// Expert dot products are integer: the IQ4_XS codes are exact bytes (kvalue + 128), the
-// activation row (x, or one slot of h) is rounded to 16-bit fixed point with a power-of-two
-// scale chosen from its largest magnitude, and dp2a accumulates code x activation products of a
-// 32-weight sub-block exactly in int32.  Each sub-block sum is then converted to f32, multiplied
-// by its scale d*(ls-32) and accumulated in f32 in a fixed order.  The only rounding besides
-// f32 accumulation is the 16-bit activation grid (relative step 2^-15 of the row maximum).  The
-// max |h| of a slot is gathered during phase 2 (per CTA, then one 64-bit atomicMax per slot
-// whose high word is the launch's epoch, so stale values of earlier launches always lose).
+// Weights move by bulk copies (cp.async.bulk, completion counted on mbarriers): the CTA's
+// shared-expert rows and the shared expert's W2 rows are requested at entry; right after the
+// routing step one warp requests the routed rows (two copies per warp: its units' W1 rows and
+// W3 rows are contiguous) and every routed expert's W2 rows of this CTA's output rows, which are
+// in shared memory long before h is complete.
 //
-// Grid synchronisation uses one 64-bit counter that only grows: every CTA adds 1 at each of the
-// two arrival points, so a launch of G CTAs adds 2G and a launch finds its base by rounding the
-// value it reads at entry down to a multiple of 2G.  Nothing has to be reset between launches
-// (CUDA-graph replay is safe).  Every spin wait gives up after 100 ms, records kDevTimeout and
-// continues; moe_sync then clears the counter along with the status word.
+// Dot products are integer: IQ4_XS codes are exact bytes (kvalue + 128); activations (x, and
+// each slot of h) are rounded to 16-bit fixed point with a power-of-two scale per 32-value
+// sub-block, chosen from that sub-block's largest magnitude (relative step 2^-15 of it); dp2a
+// accumulates a sub-block's code x activation products exactly in int32, which is then scaled
+// by d * (ls - 32) / activation scale and accumulated in f32 in a fixed order.
+//
+// Epochs: thread 0 of every CTA reads a 64-bit counter at entry, and increments it by one as
+// the CTA's last act, so a launch of G CTAs adds G.  No CTA can finish before every CTA of its
+// launch has produced its h entries, each of which it does after reading the counter, so all
+// CTAs of a launch read the same value v and use epoch v / G + 1.  Nothing is reset between
+// launches (CUDA-graph replay is safe).  Every wait gives up after 100 ms, records kDevTimeout
+// and lets the CTA finish (in-flight bulk copies are drained first); moe_sync then clears the
+// counter and the exchange entries.
 #include <cuda_runtime.h>
 
 #include "moe_common.cuh"
@@ -41,76 +50,83 @@ namespace moe {
 
 #ifdef MOE_TC_TRACE
 __device__ unsigned long long g_dec_trace[160][16];
-__device__ volatile int g_route_done[160];  // per CTA: phase timestamps (debug builds)
 #define DEC_TRACE(i) do { if (blockIdx.x < 160 && threadIdx.x == 0) g_dec_trace[blockIdx.x][i] = tc::globaltimer_ns(); } while (0)
-#define DEC_TRACE_R(i) do { if (blockIdx.x < 160 && threadIdx.x == 32 * kRouteWarp) g_dec_trace[blockIdx.x][i] = tc::globaltimer_ns(); } while (0)
+#define DEC_TRACE_W(i, w) do { if (blockIdx.x < 160 && threadIdx.x == 32 * (w)) g_dec_trace[blockIdx.x][i] = tc::globaltimer_ns(); } while (0)
+#define DEC_CLOCK_W(i, w) do { if (blockIdx.x < 160 && threadIdx.x == 32 * (w)) g_dec_trace[blockIdx.x][i] = clock64(); } while (0)
+__device__ unsigned long long g_dec_clk0[160][16];  // warp 0's own clock (sub-partition counter)
+#define DEC_CLK0(i) do { if (blockIdx.x < 160 && threadIdx.x == 0) g_dec_clk0[blockIdx.x][i] = clock64(); } while (0)
+extern "C" int moe_debug_dec_clk0(unsigned long long* out) {
+    return cudaMemcpyFromSymbol(out, g_dec_clk0, sizeof(g_dec_clk0)) == cudaSuccess ? 0 : -2;
+}
 extern "C" int moe_debug_dec_trace(unsigned long long* out) {
     return cudaMemcpyFromSymbol(out, g_dec_trace, sizeof(g_dec_trace)) == cudaSuccess ? 0 : -2;
 }
 #else
 #define DEC_TRACE(i) do {} while (0)
-#define DEC_TRACE_R(i) do {} while (0)
+#define DEC_TRACE_W(i, w) do {} while (0)
+#define DEC_CLOCK_W(i, w) do {} while (0)
+#define DEC_CLK0(i) do {} while (0)
 #endif
 
 namespace {
 
 constexpr int kDWarps = 16;
 constexpr int kDThreads = 32 * kDWarps;
-constexpr int kRouteWarp = kDWarps - 1;  // its units come last in the unit order
+constexpr int kRouteWarp = kDWarps - 1;
 constexpr uint64_t kSpinLimitNs = 100000000ull;  // 100 ms
 constexpr int kMaxH = 2048;                      // decode_supported limits
 constexpr int kMaxI = 512;
-// 16-bit activation pairs in shared memory: sub-block sb (32 values) occupies words
-// [sb*kQW, sb*kQW+16); word 4w+i holds values 4w+i (low half) and 16+4w+i (high half), the
-// pairing of one IQ4_XS qs word's low and high nibbles.  Word 16 holds 128 * (sum of the 32
-// values), the correction for codes stored as kvalue + 128.  The stride of 20 words keeps the
-// 16-byte loads of 8 consecutive lanes on distinct banks.
+constexpr int kMinGrid = 144;                    // per-CTA slices below are sized for G >= 144
+constexpr int kMaxShUnits = (kMaxI + kMinGrid - 1) / kMinGrid;                // 4
+constexpr int kMaxRoutedUnits = (kMaxTopK * kMaxI + kMinGrid - 1) / kMinGrid;  // 32 = 2 per warp
+constexpr int kMaxRows2 = (kMaxH + kMinGrid - 1) / kMinGrid;                  // 16 = 1 per warp
+static_assert(kMaxRoutedUnits <= 2 * kDWarps, "two routed units per warp");
+static_assert(kMaxRows2 <= kDWarps, "one output row per warp");
+static_assert(kMaxRoutedUnits <= 2 * kRouteWarp, "the routing warp itself has no routed units");
+// The routed rows arrive in chunks of 4 units (one bulk copy of 4 W1 rows and one of 4 W3 rows;
+// a chunk that straddles two slots takes two copies per matrix), each chunk on its own mbarrier:
+// few large copies (the bulk-copy unit takes ~70 cycles per request) that still let the warps of
+// early chunks start while later chunks land.
+constexpr int kChunkUnits = 4;
+constexpr int kMaxChunks = (kMaxRoutedUnits + kChunkUnits - 1) / kChunkUnits;  // 8
+static_assert(kMaxChunks * 2 * kChunkUnits <= 4 * kDWarps, "chunk staging fits the routed staging");
+// 16-bit activation pairs of one 32-value sub-block: word w (< 16) holds values w (low half) and
+// w + 16 (high half), the pairing of one IQ4_XS qs word's low and high nibbles; word 16 holds
+// 128 * (sum of the 32 values), the correction for codes stored as kvalue + 128; word 17 the f32
+// bits of 1 / scale.  The stride of 20 words keeps the 16-byte loads of 8 consecutive lanes on
+// distinct banks.
 constexpr int kQW = 20;
-constexpr int kMaxRow13 = kMaxH / kQK * kBlockBytes;  // bytes of one W1/W3 row
-constexpr int kMaxRow2 = kMaxI / kQK * kBlockBytes;   // bytes of one W2 row
-constexpr size_t kDecodeSmem = sizeof(float) * padded_len(kMaxH) + sizeof(uint32_t) * (kMaxH / 32) * kQW +
-                               sizeof(uint32_t) * (kMaxTopK + 1) * (kMaxI / 32) * kQW +
-                               size_t(kDWarps) * 4 * kMaxRow13 + size_t(kDWarps) * (kMaxTopK + 1) * kMaxRow2;
-
-__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
-    const uint32_t s = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" :: "r"(s), "l"(gmem) : "memory");
-}
-__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_wait() { asm volatile("cp.async.wait_group %0;" :: "n"(N) : "memory"); }
-
-// Sub-block `sb` of a row staged in shared memory (the layout of load_subblk).
-__device__ __forceinline__ SubBlk lds_subblk(const uint8_t* row, int sb) {
-    const uint8_t* blk = row + (sb >> 3) * kBlockBytes;
-    SubBlk s;
-    s.hdr = *reinterpret_cast<const uint2*>(blk);
-    const uint2* q = reinterpret_cast<const uint2*>(blk + 8 + (sb & 7) * 16);
-    s.q01 = q[0];
-    s.q23 = q[1];
-    return s;
-}
+constexpr int kRow13 = kMaxH / kQK * kBlockBytes;  // bytes of one W1/W3 row (1088)
+constexpr int kRow2 = kMaxI / kQK * kBlockBytes;   // bytes of one W2 row (272)
+constexpr size_t kStRouted = size_t(kDWarps) * 4 * kRow13;             // [warp][W1 a, W1 b, W3 a, W3 b]
+constexpr size_t kStShared = size_t(2) * kMaxShUnits * kRow13;         // [W1 rows][W3 rows]
+constexpr size_t kStW2 = size_t(kMaxTopK + 1) * kMaxRows2 * kRow2;      // [slot][row]
+constexpr size_t kW2Dec = size_t(kMaxRows2) * (kMaxTopK + 1) * (kMaxI / 32) * 32;  // decoded W2 codes
+static_assert(kW2Dec + size_t(kMaxRows2) * (kMaxTopK + 1) * (kMaxI / 32) * 4 <= kStRouted + kStShared,
+              "decoded W2 fits over the W1/W3 staging");
+constexpr size_t kDecodeSmem = kStRouted + kStShared + kStW2 + sizeof(float) * kMaxH +
+                               sizeof(uint32_t) * (kMaxH / 32) * kQW +
+                               sizeof(uint32_t) * (kMaxTopK + 1) * (kMaxI / 32) * kQW;
 
 struct DecodeArgs {
-    const IoArgs* io;     // activation pointers in device memory (graph replay), or null:
+    const IoArgs* io;            // activation pointers in device memory (graph replay), or null:
     const float* x_direct;       // ... then these (a direct launch)
     const float* resid_direct;
     float* out_direct;
-    float norm_eps;       // >= 0: the layer input is RMSNorm(x) (no gain), the residual x
-    const uint8_t* pf[4];  // next layer's router and shared W1, W3, W2 (L2 prefetch), or null
+    float norm_eps;              // >= 0: the layer input is RMSNorm(x) (no gain), the residual x
+    const uint8_t* pf[4];        // next layer's router and shared W1, W3, W2 (L2 prefetch), or null
     uint32_t pf_bytes[4];
-    const float* wr;      // [E][H]
-    const float* bias;    // [E] or null
-    const float* gate_w;  // [H] or null (gate 1.0)
-    ExpertTables tabs;
+    const float* wr;             // [E][H]
+    const float* bias;           // [E] or null
+    const float* gate_w;         // [H] or null (gate 1.0)
+    const uint8_t* tw[3][kMaxExperts + 1];  // expert weight pointers W1, W3, W2 (index E: shared)
     int H, I, E, k;
     int has_shared;
     float scale;
-    float* logits;        // [4][E+1] column-quarter partial logits
-    uint2* topk;          // [k+1] records (written by CTA 0 for inspection)
-    float* h;             // [k+1][I]
+    uint2* topk;                 // [k+1] records (written by CTA 0 for inspection)
+    unsigned long long* xlog;    // [2 (E+1)] tagged half-row logits
+    unsigned long long* xh;      // [k+1][I] tagged h
     unsigned long long* counter;
-    unsigned long long* hmax;  // [k+1]: (launch epoch << 32) | bits of max |h| per slot
     int* status;
 };
 
@@ -125,11 +141,24 @@ __device__ __forceinline__ int dp2a_hi(uint32_t a, uint32_t b, int c) {
     return d;
 }
 
-// Exact integer dot of one IQ4_XS sub-block with 32 packed 16-bit activations (kQW layout):
-// sum over j of kv(code_j) * a_j.
-__device__ __noinline__ int dot_subblk_i16(const SubBlk& s, const uint32_t* aq) {
+// Sub-block `sb` of a row staged in shared memory (the layout of load_subblk).
+__device__ __forceinline__ SubBlk lds_subblk(const uint8_t* row, int sb) {
+    const uint8_t* blk = row + (sb >> 3) * kBlockBytes;
+    SubBlk s;
+    s.hdr = *reinterpret_cast<const uint2*>(blk);
+    const uint2* q = reinterpret_cast<const uint2*>(blk + 8 + (sb & 7) * 16);
+    s.q01 = q[0];
+    s.q23 = q[1];
+    return s;
+}
+
+// Exact integer dot of one IQ4_XS sub-block (its four qs words) with 32 packed 16-bit
+// activations (kQW layout): sum over j of kv(code_j) * a_j.  Out of line (arguments in
+// registers): the kernel's code size matters more than the call.
+__device__ __noinline__ int dot_subblk_i16(uint32_t w0, uint32_t w1, uint32_t w2, uint32_t w3,
+                                           const uint32_t* aq) {
     const uint4* a4 = reinterpret_cast<const uint4*>(aq);
-    const uint32_t w[4] = {s.q01.x, s.q01.y, s.q23.x, s.q23.y};
+    const uint32_t w[4] = {w0, w1, w2, w3};
     int acc = -static_cast<int>(aq[16]);
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
@@ -144,437 +173,571 @@ __device__ __noinline__ int dot_subblk_i16(const SubBlk& s, const uint32_t* aq) 
     return acc;
 }
 
-// 16-bit fixed-point value of v at scale sc (a power of two), clamped to +-32767.
-__device__ __forceinline__ int q16(float v, float sc) {
-    return max(-32767, min(32767, __float2int_rn(v * sc)));
+// f32 contribution of one staged sub-block against packed activations: scale(d, ls) x
+// (1 / activation scale) x exact integer dot.
+__device__ __forceinline__ float subblk_dot(const uint8_t* row, int sb, const uint32_t* aq) {
+    const SubBlk b = lds_subblk(row, sb);
+    return iq4_subscale(b.hdr.x, b.hdr.y, sb & 7) * __uint_as_float(aq[17]) *
+           static_cast<float>(dot_subblk_i16(b.q01.x, b.q01.y, b.q23.x, b.q23.y, aq));
 }
 
-// Scale 2^e with max_abs * 2^e in [16384, 32768), or 1 for an all-zero row.
-__device__ __forceinline__ float q16_scale(float max_abs) {
-    if (!(max_abs > 0.f) || !isfinite(max_abs)) return 1.f;
-    int e;
-    frexpf(max_abs, &e);  // max_abs = m * 2^e, m in [0.5, 1)
-    return ldexpf(1.f, 15 - e);
+// Biased exponent field f of the power-of-two scale 2^(f - 127) that brings a sub-block's largest
+// magnitude m (bits mb, finite, > 0) into [16384, 32768): m = 1.x * 2^(E - 127) needs
+// 2^(141 - E), i.e. f = 268 - E, clamped to the normal range (sub-blocks below 2^-113 keep
+// fewer bits).  An all-zero sub-block gets scale 1 (f = 127).
+__device__ __forceinline__ uint32_t q16_scale_field(uint32_t mb) {
+    if (mb == 0u) return 127u;
+    const int e = static_cast<int>(mb >> 23);
+    return static_cast<uint32_t>(min(254, max(1, 268 - e)));
 }
 
+__device__ __forceinline__ unsigned long long ld_relaxed_u64(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
 __device__ __forceinline__ unsigned long long ld_acquire_u64(const unsigned long long* p) {
     unsigned long long v;
     asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
     return v;
 }
-
-// Thread 0, after a __syncthreads of its CTA: arrive on the counter (no return value needed).
-__device__ __forceinline__ void grid_arrive(unsigned long long* counter) {
-    __threadfence();
-    asm volatile("red.release.gpu.global.add.u64 [%0], 1;" :: "l"(counter) : "memory");
+__device__ __forceinline__ void st_relaxed_u64(unsigned long long* p, unsigned long long v) {
+    asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" :: "l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long tag(uint32_t epoch, float v) {
+    return (static_cast<unsigned long long>(epoch) << 32) | __float_as_uint(v);
 }
 
-// Thread 0: wait until the counter reaches `target` (bounded).
-__device__ __forceinline__ void grid_wait(const unsigned long long* counter, unsigned long long target,
-                                          int* status) {
-    if (ld_acquire_u64(counter) >= target) return;
+// Bounded wait on an mbarrier phase (a whole warp, or one thread); false on timeout.  Between
+// tests the warp sleeps, so waiting warps leave the issue slots to the warps still computing.
+__device__ __noinline__ bool bar_wait(uint64_t* bar, uint32_t parity) {
+    if (tc::mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = tc::globaltimer_ns();
-    while (ld_acquire_u64(counter) < target) {
-        if (tc::globaltimer_ns() - t0 > kSpinLimitNs) { set_dev_error(status, kDevTimeout); return; }
+    for (uint32_t i = 1;; ++i) {
+        __nanosleep(64);
+        if (tc::mbar_try_wait(bar, parity)) return true;
+        if ((i & 15u) == 0u && tc::globaltimer_ns() - t0 > kSpinLimitNs) return false;
     }
 }
 
-__global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const DecodeArgs a) {
-    extern __shared__ __align__(16) float sm[];
-    float* xs = sm;                                                      // padded f32 x (router)
-    uint32_t* xq = reinterpret_cast<uint32_t*>(sm + padded_len(kMaxH));  // [H/32][kQW]
-    uint32_t* hq = xq + kMaxH / 32 * kQW;                                // [k+1][I/32][kQW]
-    uint8_t* st13 = reinterpret_cast<uint8_t*>(hq + (kMaxTopK + 1) * (kMaxI / 32) * kQW);  // W1/W3 rows
-    uint8_t* st2 = st13 + kDWarps * 4 * kMaxRow13;                       // W2 rows
-    __shared__ const uint8_t* tw[3][kMaxExperts + 1];  // expert weight pointers W1, W3, W2
-    __shared__ unsigned long long base;
+// CTA named barrier 1 (barrier 0 is __syncthreads): warps park on it without issuing.
+__device__ __forceinline__ void named_sync(int n) { asm volatile("bar.sync 1, %0;" :: "r"(n) : "memory"); }
+__device__ __forceinline__ void named_arrive(int n) { asm volatile("bar.arrive 1, %0;" :: "r"(n) : "memory"); }
+
+// One warp packs N sub-blocks at once (the collectives of the N sub-blocks are independent, so
+// their latencies overlap): v[i] is lane's value of sub-block first + 16 i, written to
+// base + (first + 16 i) * kQW when that index is below nsb.  Each sub-block gets 16-bit fixed
+// point at its own power-of-two scale; a non-finite value makes its inverse scale NaN, so every
+// product with the sub-block is NaN.
+template <int N>
+__device__ __forceinline__ void pack_subblocks(const float (&v)[N], uint32_t* base, int first, int nsb, int lane) {
+    uint32_t mb[N];
+#pragma unroll
+    for (int i = 0; i < N; ++i) mb[i] = __reduce_max_sync(0xffffffffu, __float_as_uint(v[i]) & 0x7FFFFFFFu);
+    int q[N];
+    uint32_t f[N];
+#pragma unroll
+    for (int i = 0; i < N; ++i) {
+        f[i] = mb[i] < 0x7F800000u ? q16_scale_field(mb[i]) : 127u;
+        q[i] = max(-32767, min(32767, __float2int_rn(v[i] * __uint_as_float(f[i] << 23))));
+    }
+    int hi[N], sum[N];
+#pragma unroll
+    for (int i = 0; i < N; ++i) hi[i] = __shfl_down_sync(0xffffffffu, q[i], 16);
+#pragma unroll
+    for (int i = 0; i < N; ++i) sum[i] = __reduce_add_sync(0xffffffffu, q[i]);
+#pragma unroll
+    for (int i = 0; i < N; ++i) {
+        const int g = first + 16 * i;
+        if (g >= nsb) continue;
+        uint32_t* dst = base + g * kQW;
+        if (lane < 16) dst[lane] = (static_cast<uint32_t>(q[i]) & 0xFFFFu) | (static_cast<uint32_t>(hi[i]) << 16);
+        if (lane == 0) {
+            dst[16] = static_cast<uint32_t>(128 * sum[i]);
+            dst[17] = mb[i] < 0x7F800000u ? ((254u - f[i]) << 23) : 0x7fc00000u;  // 1 / scale, or NaN
+        }
+    }
+}
+
+// Order-preserving map of a float onto unsigned integers (NaN: 0, below every number).
+__device__ __forceinline__ uint32_t f2ord(float f) {
+    const uint32_t u = __float_as_uint(f);
+    if (f != f) return 0u;
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__device__ __forceinline__ float ord2f(uint32_t o) {
+    return __uint_as_float((o & 0x80000000u) ? (o & 0x7FFFFFFFu) : ~o);
+}
+
+// Compare-exchange of (key desc, index asc) pairs.
+__device__ __forceinline__ void cx(uint32_t& ka, uint32_t& ia, uint32_t& kb, uint32_t& ib) {
+    const bool sw = kb > ka || (kb == ka && ib < ia);
+    const uint32_t k0 = sw ? kb : ka, i0 = sw ? ib : ia;
+    kb = sw ? ka : kb;
+    ib = sw ? ia : ib;
+    ka = k0;
+    ia = i0;
+}
+
+// Routing of one token by one warp from the half-row logits (v0/v1: lane's experts lane + 32 i;
+// g0/g1: the gate row's halves): softmax over E (router_topk.comp:36-92) with max and sum
+// reduced in a fixed order, so that every CTA derives identical probabilities
+// p_e = exp(l_e - max) * (1 / sum), then the k largest p in descending order, ties to the lower
+// expert index.  Each lane sorts its 8 candidates once; a round then takes the warp maximum of
+// the lanes' heads (a tie between heads goes to the lower index) and the winning lane pops its
+// head, writing the slot's expert and probability.  Lane k writes the shared expert's slot
+// (gate sigmoid(g . x), or 1 without a gate weight).  CTA 0 also writes the routing record.
+__device__ __forceinline__ void route_warp(const unsigned long long (&v0)[8], const unsigned long long (&v1)[8],
+                                           unsigned long long g0, unsigned long long g1, const float* bias,
+                                           int E, int k, bool has_gate, bool has_shared, int* status,
+                                           int* slot_e, float* wgt, uint2* topk_rec) {
+    const int lane = threadIdx.x & 31;
+    float pv[8];
+    uint32_t om = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const int e = min(lane + 32 * i, E - 1);
+        pv[i] = (__uint_as_float(static_cast<uint32_t>(v0[i])) + __uint_as_float(static_cast<uint32_t>(v1[i]))) + bias[e];
+        if (lane + 32 * i < E) om = max(om, f2ord(pv[i]));
+    }
+    const float lmax = ord2f(__reduce_max_sync(0xffffffffu, om));
+    float sum = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        pv[i] = lane + 32 * i < E ? expf(pv[i] - lmax) : 0.f;
+        sum += pv[i];
+    }
+    sum = warp_sum(sum);
+    const float inv = sum > 0.f ? 1.0f / sum : 0.f;
+    uint32_t key[8], idx[8];
+    bool bad = false;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const float p = pv[i] * inv;
+        bad = bad || (p != p);
+        key[i] = (p == p) ? __float_as_uint(p) : 0u;  // NaN logits: reported, ranked as 0
+        idx[i] = lane + 32 * i < E ? static_cast<uint32_t>(lane + 32 * i) : 0xFFFFu;
+    }
+    if (bad) set_dev_error(status, kDevBadExpert);
+    // sorting network of 8 (19 compare-exchanges), descending by key, ascending index on ties
+    cx(key[0], idx[0], key[1], idx[1]); cx(key[2], idx[2], key[3], idx[3]);
+    cx(key[4], idx[4], key[5], idx[5]); cx(key[6], idx[6], key[7], idx[7]);
+    cx(key[0], idx[0], key[2], idx[2]); cx(key[1], idx[1], key[3], idx[3]);
+    cx(key[4], idx[4], key[6], idx[6]); cx(key[5], idx[5], key[7], idx[7]);
+    cx(key[1], idx[1], key[2], idx[2]); cx(key[5], idx[5], key[6], idx[6]);
+    cx(key[0], idx[0], key[4], idx[4]); cx(key[3], idx[3], key[7], idx[7]);
+    cx(key[1], idx[1], key[5], idx[5]); cx(key[2], idx[2], key[6], idx[6]);
+    cx(key[1], idx[1], key[4], idx[4]); cx(key[3], idx[3], key[6], idx[6]);
+    cx(key[2], idx[2], key[4], idx[4]); cx(key[3], idx[3], key[5], idx[5]);
+    cx(key[3], idx[3], key[4], idx[4]);
+#pragma unroll 1
+    for (int r = 0; r < k; ++r) {
+        const uint32_t m = __reduce_max_sync(0xffffffffu, key[0]);
+        const unsigned tie = __ballot_sync(0xffffffffu, key[0] == m);
+        uint32_t win;
+        if (__popc(tie) == 1) {
+            win = static_cast<uint32_t>(__ffs(tie) - 1);
+        } else {
+            win = __reduce_min_sync(0xffffffffu, key[0] == m ? idx[0] : 0xFFFFu) & 31u;
+        }
+        if (static_cast<uint32_t>(lane) == win) {
+            slot_e[r] = static_cast<int>(idx[0]);
+            wgt[r] = __uint_as_float(m);
+            if (topk_rec) topk_rec[1 + r] = make_uint2(idx[0], m);
+#pragma unroll
+            for (int i = 0; i < 7; ++i) {
+                key[i] = key[i + 1];
+                idx[i] = idx[i + 1];
+            }
+            key[7] = 0u;
+            idx[7] = 0xFFFFu;
+        }
+    }
+    if (lane == 0) {
+        float gt = 1.0f;
+        if (has_gate) {
+            const float z = __uint_as_float(static_cast<uint32_t>(g0)) + __uint_as_float(static_cast<uint32_t>(g1));
+            gt = 1.0f / (1.0f + expf(-z));
+        }
+        if (has_shared) {
+            slot_e[k] = E;
+            wgt[k] = gt;
+        }
+        if (topk_rec) topk_rec[0] = make_uint2(static_cast<uint32_t>(E), __float_as_uint(gt));
+    }
+}
+
+__global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const __grid_constant__ DecodeArgs a) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    uint8_t* st_r = smem;                         // routed W1/W3 rows, per warp (then decoded W2)
+    uint8_t* st_s = st_r + kStRouted;             // shared W1 rows, then W3 rows (then decoded W2)
+    uint8_t* st_2 = st_s + kStShared;             // raw W2 rows [slot][row]
+    float* xs = reinterpret_cast<float*>(st_2 + kStW2);                 // f32 x (router)
+    uint32_t* xq = reinterpret_cast<uint32_t*>(xs + kMaxH);             // [H/32][kQW]
+    uint32_t* hq = xq + (kMaxH / 32) * kQW;                             // [k+1][I/32][kQW]
+    // decoded W2 (after the units, over the W1/W3 staging): per (row, slot, sub-block) 8 words
+    // of kvalue + 128 bytes in dp2a pair order, and the sub-block scale d * (ls - 32)
+    uint32_t* w2q = reinterpret_cast<uint32_t*>(st_r);
+    float* w2s = reinterpret_cast<float*>(st_r + kW2Dec);
+    __shared__ __align__(8) uint64_t bar_sh, bar_w2, bar_c[kMaxChunks];
+    __shared__ unsigned long long s_base;
     __shared__ float red[kDWarps];
     __shared__ float wgt[kMaxTopK + 1];
     __shared__ int slot_e[kMaxTopK + 1];
-    __shared__ uint32_t s_hmax[kMaxTopK + 1];  // bits of max |h| per slot over this CTA's units
-    __shared__ float hscale[kMaxTopK + 1], hw[kMaxTopK + 1];
+    __shared__ float s_bias[kMaxExperts];
+    __shared__ int s_failed;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int gwarp = blockIdx.x * kDWarps + warp, nwarps = gridDim.x * kDWarps;
+    const int G = static_cast<int>(gridDim.x), c = static_cast<int>(blockIdx.x);
     const float* x = a.io ? a.io->x : a.x_direct;
     const int H = a.H, I = a.I, E = a.E, k = a.k;
     const int ns = k + (a.has_shared ? 1 : 0);
-    const unsigned long long G = gridDim.x;
+    const int rb13 = H / kQK * kBlockBytes, rb2 = I / kQK * kBlockBytes;
+    // this CTA's slices
+    const int sh0 = a.has_shared ? c * I / G : 0, sh1 = a.has_shared ? (c + 1) * I / G : 0;
+    const int U = k * I;
+    const int u0 = c * U / G, u1 = (c + 1) * U / G;
+    const int n0 = c * H / G, n1 = (c + 1) * H / G;
+    const int nrows = n1 - n0;
+    const int T = 2 * (E + (a.gate_w ? 1 : 0)), half = H / 2;
+    // router half-row task of this warp (warps 4..15; decode_supported bounds the count)
+    const int task = warp >= 4 ? c + G * (warp - 4) : T;
 
     DEC_TRACE(0);
-    // Warps are numbered with the CTAs interleaved (pw), so that the shared expert's units,
-    // which come first, spread over every SM instead of filling the first few.
-    const int pw = warp * static_cast<int>(G) + static_cast<int>(blockIdx.x);
-    const int g_sh = a.has_shared ? I : 0;
-    const int total = g_sh + k * I;
-    const int n_my = pw < total ? (total - pw + nwarps - 1) / nwarps : 0;  // this warp's units
-    const int n_sh = pw < g_sh ? (g_sh - pw + nwarps - 1) / nwarps : 0;    // ... of them shared
-    const int rb13 = H / kQK * kBlockBytes, nch13 = rb13 / 16;
-    uint8_t* st_w = st13 + warp * 4 * kMaxRow13;  // this warp's [2 units][W1, W3] row staging
-    // unit t of this warp: rows j of W1 and W3 of expert e into staging slot t & 1
-    auto issue_unit = [&](int t, const uint8_t* w1e, const uint8_t* w3e) {
-        const int g = pw + t * nwarps;
-        const size_t off = static_cast<size_t>(g < g_sh ? g : (g - g_sh) % I) * rb13;
-        uint8_t* dst = st_w + (t & 1) * 2 * kMaxRow13;
-        for (int c = lane; c < 2 * nch13; c += 32) {
-            const int m = c >= nch13 ? 1 : 0, o = (c - m * nch13) * 16;
-            cp_async16(dst + m * kMaxRow13 + o, (m ? w3e : w1e) + off + o);
-        }
-    };
-    const uint8_t* sh1 = nullptr;
-    const uint8_t* sh3 = nullptr;
-    if (n_sh > 0) {
-        sh1 = a.tabs.w1[E];
-        sh3 = a.tabs.w3[E];
-    }
-#pragma unroll
-    for (int t = 0; t < 2; ++t) {  // the first two shared units start loading at once
-        if (t < n_sh) issue_unit(t, sh1, sh3);
-        cp_commit();
-    }
-    // x, then the expert pointer tables into registers; the tables are stored to shared
-    // memory after the router rows, hiding their latency
-    float4 xv4[kMaxH / (4 * kDThreads)];
-#pragma unroll
-    for (int t = 0; t < kMaxH / (4 * kDThreads); ++t) {
-        const int i = (tid + t * kDThreads) * 4;
-        if (i < H) xv4[t] = *reinterpret_cast<const float4*>(x + i);
-    }
-    constexpr int kTabPerThread = (3 * (kMaxExperts + 1) + kDThreads - 1) / kDThreads;
-    const uint8_t* tv[kTabPerThread];
-#pragma unroll
-    for (int t = 0; t < kTabPerThread; ++t) {
-        const int i = tid + t * kDThreads;
-        const int m = i / (E + 1), e = i - m * (E + 1);
-        tv[t] = i < 3 * (E + 1) ? (m == 0 ? a.tabs.w1 : m == 1 ? a.tabs.w3 : a.tabs.w2)[e] : nullptr;
-    }
+    DEC_CLOCK_W(12, kRouteWarp);
+    DEC_CLK0(0);
+    // ---- every independent load first: x, this warp's router half-row, pointer tables, bias --
     if (tid == 0) {
-        const unsigned long long v = ld_acquire_u64(a.counter);
-        base = v - v % (2 * G);
-        if (a.has_shared) slot_e[k] = E;
+        s_failed = 0;
+        s_base = ld_relaxed_u64(a.counter);
+        tc::mbar_init(&bar_sh, 1);
+        tc::mbar_init(&bar_w2, 1);
+        for (int i = 0; i < kMaxChunks; ++i) tc::mbar_init(&bar_c[i], 1);
+        tc::fence_mbar_init();
+        // the shared expert needs no routing: its rows are requested first
+        if (sh1 > sh0) {
+            const uint32_t nb = static_cast<uint32_t>((sh1 - sh0) * rb13);
+            tc::mbar_arrive_expect_tx(&bar_sh, 2 * nb);
+            tc::bulk_load(st_s, a.tw[0][E] + static_cast<size_t>(sh0) * rb13, nb, &bar_sh);
+            tc::bulk_load(st_s + kMaxShUnits * kRow13, a.tw[1][E] + static_cast<size_t>(sh0) * rb13, nb, &bar_sh);
+        }
+        // W2 rows [n0, n1) of every slot land on bar_w2: all bytes expected now, the shared
+        // slot's copy issued now, the routed slots' after the routing step
+        tc::mbar_arrive_expect_tx(&bar_w2, static_cast<uint32_t>(ns * nrows * rb2));
+        if (a.has_shared)
+            tc::bulk_load(st_2 + static_cast<size_t>(k) * kMaxRows2 * kRow2,
+                          a.tw[2][E] + static_cast<size_t>(n0) * rb2, static_cast<uint32_t>(nrows * rb2), &bar_w2);
     }
-    if (tid <= kMaxTopK) s_hmax[tid] = 0u;
+    float4 xv = make_float4(0.f, 0.f, 0.f, 0.f);  // H <= 2048 = 4 x 512 threads
+    if (tid * 4 < H) xv = *reinterpret_cast<const float4*>(x + tid * 4);
+    float4 wv[kMaxH / 2 / 128];
+    const int hf = task & 1;
+    if (task < T) {
+        const int r = task >> 1;
+        const float* wrow = (r < E ? a.wr + static_cast<size_t>(r) * H : a.gate_w) + hf * half;
+#pragma unroll
+        for (int i = 0; i < kMaxH / 2 / 128; ++i)
+            if (lane * 4 + 128 * i < half) wv[i] = __ldg(reinterpret_cast<const float4*>(wrow + lane * 4 + 128 * i));
+    }
+    // the router bias is needed only at the routing step: loaded now, stored after the first
+    // barrier
+    const float bias_v = (a.bias && tid < E) ? a.bias[tid] : 0.f;
     if (a.norm_eps >= 0.f) {
         // RMSNorm of the layer input (rms_norm.comp: x / sqrt(mean(x^2) + eps), no gain), the
         // sum of squares reduced in a fixed order in every CTA
-        float ss = 0.f;
-#pragma unroll
-        for (int t = 0; t < kMaxH / (4 * kDThreads); ++t) {
-            const int i = (tid + t * kDThreads) * 4;
-            if (i < H) {
-                const float4 v = xv4[t];
-                ss = fmaf(v.x, v.x, ss); ss = fmaf(v.y, v.y, ss);
-                ss = fmaf(v.z, v.z, ss); ss = fmaf(v.w, v.w, ss);
-            }
-        }
+        float ss = fmaf(xv.x, xv.x, 0.f);
+        ss = fmaf(xv.y, xv.y, ss); ss = fmaf(xv.z, xv.z, ss); ss = fmaf(xv.w, xv.w, ss);
         ss = warp_sum(ss);
         if (lane == 0) red[warp] = ss;
         __syncthreads();
         float tot = 0.f;
-#pragma unroll
+#pragma unroll 1
         for (int w = 0; w < kDWarps; ++w) tot += red[w];
         const float r = 1.0f / sqrtf(tot / static_cast<float>(H) + a.norm_eps);
-        __syncthreads();  // red[] reused below
-#pragma unroll
-        for (int t = 0; t < kMaxH / (4 * kDThreads); ++t) {
-            xv4[t].x *= r; xv4[t].y *= r; xv4[t].z *= r; xv4[t].w *= r;
-        }
+        xv.x *= r; xv.y *= r; xv.z *= r; xv.w *= r;
     }
-    float mx = 0.f;
-#pragma unroll
-    for (int t = 0; t < kMaxH / (4 * kDThreads); ++t) {
-        const int i = (tid + t * kDThreads) * 4;
-        if (i < H) {
-            const float4 v = xv4[t];
-            *reinterpret_cast<float4*>(xs + padded_idx(i)) = v;
-            mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
-            if ((v.x * 0.f + v.y * 0.f) + (v.z * 0.f + v.w * 0.f) != 0.f) mx = INFINITY;  // NaN or inf
-        }
+    bool fin = true;
+    if (tid * 4 < H) {
+        *reinterpret_cast<float4*>(xs + tid * 4) = xv;
+        fin = isfinite(xv.x) && isfinite(xv.y) && isfinite(xv.z) && isfinite(xv.w);
     }
-    mx = warp_max(mx);
-    if (lane == 0) red[warp] = mx;
-    __syncthreads();  // xs complete
+    const bool x_finite = __syncthreads_and(fin) != 0;  // also: xs, barriers, s_base, tables
+    const unsigned long long base = s_base;
+    const uint32_t epoch = static_cast<uint32_t>(base / static_cast<unsigned long long>(G)) + 1u;
+    if (tid < E) s_bias[tid] = bias_v;
+    DEC_TRACE(1);
 
-    // ---- phase 1: router rows, each split in 4 column quarters ------------------------------
-    const int n_rows = E + (a.gate_w ? 1 : 0);
-    const int qlen = H / 4;
-    for (int w = gwarp; w < n_rows * 4; w += nwarps) {
-        const int r = w >> 2, part = w & 3;
-        const float* wrow = (r < E ? a.wr + static_cast<size_t>(r) * H : a.gate_w) + part * qlen;
+    // ---- router half-row of this warp (f32), published with the launch's epoch --------------
+    if (task < T) {
+        const float* xrow = xs + hf * half;
         float acc = 0.f;
-        for (int i = lane * 4; i < qlen; i += 128) {
-            const float4 wv = __ldg(reinterpret_cast<const float4*>(wrow + i));
-            const float4 xv = *reinterpret_cast<const float4*>(xs + padded_idx(part * qlen + i));
-            acc = fmaf(wv.x, xv.x, acc); acc = fmaf(wv.y, xv.y, acc);
-            acc = fmaf(wv.z, xv.z, acc); acc = fmaf(wv.w, xv.w, acc);
+#pragma unroll
+        for (int i = 0; i < kMaxH / 2 / 128; ++i) {
+            if (lane * 4 + 128 * i < half) {
+                const float4 xv4 = *reinterpret_cast<const float4*>(xrow + lane * 4 + 128 * i);
+                acc = fmaf(wv[i].x, xv4.x, acc); acc = fmaf(wv[i].y, xv4.y, acc);
+                acc = fmaf(wv[i].z, xv4.z, acc); acc = fmaf(wv[i].w, xv4.w, acc);
+            }
         }
         acc = warp_sum(acc);
-        if (lane == 0) a.logits[part * (E + 1) + r] = acc;
+        if (lane == 0) st_relaxed_u64(a.xlog + task, tag(epoch, acc));
     }
-    __syncthreads();  // this CTA's logits are written
-    DEC_TRACE(1);
-    if (tid == 0) grid_arrive(a.counter);
-    // x as 16-bit pairs for the experts (scale from the block maximum of |x|)
-    mx = red[0];
+    // x as 16-bit pairs per sub-block, for the experts
+    {
+        constexpr int kPerX = kMaxH / 32 / kDWarps;  // 4
+        float v[kPerX];
 #pragma unroll
-    for (int w = 1; w < kDWarps; ++w) mx = fmaxf(mx, red[w]);
-    const bool x_finite = isfinite(mx);
-    const float sx = q16_scale(mx), inv_sx = 1.f / sx;
-    for (int p = tid; p < H / 2; p += kDThreads) {  // 16 consecutive lanes per sub-block
-        const int sb = p >> 4, wi = p & 15;
-        const int j = sb * 32 + (wi >> 2) * 4 + (wi & 3);
-        const int lo = q16(xs[padded_idx(j)], sx), hi = q16(xs[padded_idx(j + 16)], sx);
-        xq[sb * kQW + wi] = (static_cast<uint32_t>(lo) & 0xFFFFu) | (static_cast<uint32_t>(hi) << 16);
-        int sum = lo + hi;
-#pragma unroll
-        for (int o = 8; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-        if (wi == 0) xq[sb * kQW + 16] = static_cast<uint32_t>(128 * sum);
+        for (int i = 0; i < kPerX; ++i) {
+            const int g = warp + kDWarps * i;
+            v[i] = g < H / 32 ? xs[g * 32 + lane] : 0.f;
+        }
+        pack_subblocks<kPerX>(v, xq, warp, H / 32, lane);
     }
-#pragma unroll
-    for (int t = 0; t < kTabPerThread; ++t) {
-        const int i = tid + t * kDThreads;
-        if (i < 3 * (E + 1)) tw[i / (E + 1)][i % (E + 1)] = tv[t];
-    }
-    __syncthreads();  // xq, tw, slot_e[k]
-
-    // ---- phase 2: gate/up units ------------------------------------------------------------
-    // Units g = 0 .. total-1 in one global sequence (the shared expert's I rows first), unit g
-    // on the warp with pw = g mod (warps in the grid).  A unit's two rows are copied into this
-    // warp's staging slot with 16-byte cp.async (coalesced: 4 full lines per instruction), two
-    // units in flight, and decoded from shared memory.
-    const int nsb_h = H / 32;  // <= 64: two sub-blocks per lane at most
-    auto compute_unit = [&](int t) {
-        const uint8_t* s1 = st_w + (t & 1) * 2 * kMaxRow13;
-        const uint8_t* s3 = s1 + kMaxRow13;
-        float gt = 0.f, up = 0.f;
-#pragma unroll 1
-        for (int i = 0; i < 2; ++i) {  // not unrolled: code size (instruction-cache misses) matters
-            const int sb = lane + 32 * i;
-            if (sb < nsb_h) {
-                const uint32_t* aq = xq + sb * kQW;
-                const SubBlk b1 = lds_subblk(s1, sb), b3 = lds_subblk(s3, sb);
-                gt = fmaf(iq4_subscale(b1.hdr.x, b1.hdr.y, sb & 7), static_cast<float>(dot_subblk_i16(b1, aq)), gt);
-                up = fmaf(iq4_subscale(b3.hdr.x, b3.hdr.y, sb & 7), static_cast<float>(dot_subblk_i16(b3, aq)), up);
-            }
-        }
-        gt = warp_sum(gt) * inv_sx;
-        up = warp_sum(up) * inv_sx;
-        if (!x_finite) gt = up = __int_as_float(0x7fc00000);
-        const int g = pw + t * nwarps;
-        const int slot = g < g_sh ? k : (g - g_sh) / I, j = g < g_sh ? g : (g - g_sh) % I;
-        if (lane == 0) {
-            const float hv = silu_f(gt) * up;
-            a.h[static_cast<size_t>(slot) * I + j] = hv;
-            atomicMax(&s_hmax[slot], __float_as_uint(fabsf(hv)));  // NaN bits exceed inf's
-        }
-    };
-    // runs units [t0, t1) of this warp; units t0 and t0+1 were issued (or committed empty)
-    auto run_units = [&](int t0, int t1, auto&& issue) {
-        for (int t = t0; t < t1; ++t) {
-            cp_wait<1>();
-            __syncwarp();
-            compute_unit(t);
-            __syncwarp();  // the slot is free again
-            if (t + 2 < t1) issue(t + 2);
-            cp_commit();
-        }
-    };
-    run_units(0, n_sh, [&](int t) { issue_unit(t, sh1, sh3); });
+    __syncthreads();  // xq complete
     DEC_TRACE(2);
 
-    // ---- routing, computed redundantly by every CTA by one warp from the published logits ---
-    // softmax over E (router_topk.comp:36-92) with max and sum reduced in a fixed order, so
-    // every CTA derives identical probabilities; then k rounds of selection: the largest
-    // probability (as its bit pattern, probabilities being non-negative) among the experts not
-    // taken yet, ties to the lower expert index.
+    // ---- routing (one warp per CTA), then the routed copies ----------------------------------
     if (warp == kRouteWarp) {
-        if (lane == 0) grid_wait(a.counter, base + G, a.status);
-        __syncwarp();
-        DEC_TRACE_R(3);
-        const float* lg = a.logits;
-        float pv[8];
+        unsigned long long v0[8], v1[8], g0 = 0, g1 = 0;
+        const uint64_t t0 = tc::globaltimer_ns();
+        for (;;) {
+            bool ok = true;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {  // unconditional (clamped) loads, so all issue at once
-            const int e = min(lane + 32 * i, E - 1);
-            const float b = a.bias ? a.bias[e] : 0.f;
-            pv[i] = (((__ldcg(lg + e) + __ldcg(lg + (E + 1) + e)) + __ldcg(lg + 2 * (E + 1) + e)) +
-                     __ldcg(lg + 3 * (E + 1) + e)) + b;
-        }
-        float lmax = -INFINITY;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) if (lane + 32 * i < E) lmax = fmaxf(lmax, pv[i]);
-        lmax = warp_max(lmax);
-        float sum = 0.f;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            pv[i] = lane + 32 * i < E ? expf(pv[i] - lmax) : 0.f;
-            sum += pv[i];
-        }
-        sum = warp_sum(sum);
-        uint32_t key[8];
-        uint32_t avail = 0;  // bit i: expert lane + 32 i exists and is not taken
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            const float p = sum > 0.f ? pv[i] / sum : 0.f;
-            key[i] = __float_as_uint(p);
-            if (p != p) { set_dev_error(a.status, kDevBadExpert); key[i] = 0; }  // NaN logits
-            if (lane + 32 * i < E) avail |= 1u << i;
-        }
-        DEC_TRACE_R(9);
-        for (int r = 0; r < k; ++r) {
-            uint32_t best = 0;
-            int bi = -1;
-#pragma unroll
-            for (int i = 0; i < 8; ++i)
-                if (((avail >> i) & 1u) && (bi < 0 || key[i] > best)) { best = key[i]; bi = i; }
-            const uint32_t m = __reduce_max_sync(0xffffffffu, bi >= 0 ? best : 0u);
-            const uint32_t cand = (bi >= 0 && best == m) ? static_cast<uint32_t>(lane + 32 * bi) : 0xFFFFu;
-            const uint32_t e = __reduce_min_sync(0xffffffffu, cand);
-            if (e == cand) avail &= ~(1u << bi);  // the winner lane drops it
-            if (lane == 0) {
-                slot_e[r] = static_cast<int>(e);
-                wgt[r] = __uint_as_float(m);
-                if (blockIdx.x == 0) a.topk[1 + r] = make_uint2(e, m);
+            for (int i = 0; i < 8; ++i) {
+                const int e = min(lane + 32 * i, E - 1);
+                v0[i] = ld_relaxed_u64(a.xlog + 2 * e);
+                v1[i] = ld_relaxed_u64(a.xlog + 2 * e + 1);
             }
-        }
-        if (lane == 0) {  // the shared-expert gate sigmoid(g . x), or 1 without a gate weight
-            float gt = 1.0f;
             if (a.gate_w) {
-                const float z = ((__ldcg(lg + E) + __ldcg(lg + (E + 1) + E)) + __ldcg(lg + 2 * (E + 1) + E)) +
-                                __ldcg(lg + 3 * (E + 1) + E);
-                gt = 1.0f / (1.0f + expf(-z));
+                g0 = ld_relaxed_u64(a.xlog + 2 * E);
+                g1 = ld_relaxed_u64(a.xlog + 2 * E + 1);
+                ok = (g0 >> 32) == epoch && (g1 >> 32) == epoch;
             }
-            if (a.has_shared) wgt[k] = gt;
-            if (blockIdx.x == 0) a.topk[0] = make_uint2(static_cast<uint32_t>(E), __float_as_uint(gt));
-        }
-    }
-    __syncthreads();
-    DEC_TRACE(4);
-
-    cp_wait<0>();  // only empty groups can be pending here
-    auto issue_routed = [&](int t) {
-        const int g = pw + t * nwarps;
-        const int e = slot_e[(g - g_sh) / I];
-        issue_unit(t, tw[0][e], tw[1][e]);
-    };
 #pragma unroll
-    for (int u = 0; u < 2; ++u) {
-        if (n_sh + u < n_my) issue_routed(n_sh + u);
-        cp_commit();
-    }
-    run_units(n_sh, n_my, issue_routed);
-
-    // ---- phase 3: down projection + weighted combine + residual ----------------------------
-    // warp per output row n (n = pw, pw + warps in the grid, ...); the row's W2 sub-blocks of
-    // every slot are staged in shared memory by cp.async, the first row's before the grid
-    // barrier.  Lane group gi (spr lanes, one per sub-block of the row) takes the slots
-    // s = gi, gi + G2, ...; partial sums are reduced across the warp in a fixed order.
-    const int rb2 = I / kQK * kBlockBytes, nch2 = rb2 / 16;
-    uint8_t* st_d = st2 + warp * (kMaxTopK + 1) * kMaxRow2;
-    auto issue_row = [&](int n) {
-        for (int c = lane; c < ns * nch2; c += 32) {
-            const int s = c / nch2, o = (c - s * nch2) * 16;
-            cp_async16(st_d + s * kMaxRow2 + o, tw[2][slot_e[s]] + static_cast<size_t>(n) * rb2 + o);
+            for (int i = 0; i < 8; ++i) ok = ok && (v0[i] >> 32) == epoch && (v1[i] >> 32) == epoch;
+            if (__all_sync(0xffffffffu, ok)) break;
+            if (tc::globaltimer_ns() - t0 > kSpinLimitNs) {
+                set_dev_error(a.status, kDevTimeout);
+                if (lane == 0) s_failed = 1;
+                break;
+            }
+            __nanosleep(64);
         }
-        cp_commit();
-    };
-    if (pw < H) issue_row(pw);
-    __syncthreads();  // this CTA's h rows are written
-    DEC_TRACE(5);
-    // per-slot maxima of |h| from every CTA, tagged with this launch's epoch so that values
-    // left by earlier launches lose (no reset needed); released by the barrier arrival
-    const unsigned long long epoch = (base / (2 * G) + 1) << 32;
-    if (tid < ns) atomicMax(a.hmax + tid, epoch | s_hmax[tid]);
-    __syncthreads();
-    if (tid == 0) {
-        grid_arrive(a.counter);
-        grid_wait(a.counter, base + 2 * G, a.status);
+        DEC_TRACE_W(3, kRouteWarp);
+        route_warp(v0, v1, g0, g1, s_bias, E, k, a.gate_w != nullptr, a.has_shared != 0, a.status, slot_e, wgt,
+                   c == 0 ? a.topk : nullptr);
+        __syncwarp();
+        DEC_CLOCK_W(13, kRouteWarp);
+        DEC_TRACE_W(9, kRouteWarp);
+        DEC_CLOCK_W(15, kRouteWarp);
+        {
+            // routed W1/W3 rows by chunks: lane (piece, chunk, matrix) = (l >> 4, (l & 15) >> 1,
+            // l & 1); piece 1 is the part of a chunk beyond its first slot
+            const int n_r = u1 - u0, nchk = (n_r + kChunkUnits - 1) / kChunkUnits;
+            const int piece = lane >> 4, ch = (lane & 15) >> 1, m = lane & 1;
+            const bool act = ch < nchk;
+            if (act && piece == 0 && m == 0)  // expected bytes posted before any copy is issued
+                tc::mbar_arrive_expect_tx(&bar_c[ch], static_cast<uint32_t>(2 * min(kChunkUnits, n_r - kChunkUnits * ch) * rb13));
+            __syncwarp();
+            if (act) {
+                const int ca = u0 + kChunkUnits * ch, cb = min(ca + kChunkUnits, u1);
+                const int send = (ca / I + 1) * I;
+                const int pa = piece == 0 ? ca : send, pb = piece == 0 ? min(cb, send) : cb;
+                if (pa < pb)
+                    tc::bulk_load(st_r + static_cast<size_t>(ch) * 2 * kChunkUnits * kRow13 + m * kChunkUnits * rb13 +
+                                      (pa - ca) * rb13,
+                                  a.tw[m][slot_e[pa / I]] + static_cast<size_t>(pa % I) * rb13,
+                                  static_cast<uint32_t>((pb - pa) * rb13), &bar_c[ch]);
+            }
+        }
+        __syncwarp();
+        named_arrive(kDThreads);  // the parked warps may read the routing now
+        if (lane < k)  // routed W2 rows [n0, n1) of slot `lane`
+            tc::bulk_load(st_2 + static_cast<size_t>(lane) * kMaxRows2 * kRow2,
+                          a.tw[2][slot_e[lane]] + static_cast<size_t>(n0) * rb2, static_cast<uint32_t>(nrows * rb2),
+                          &bar_w2);
+        DEC_CLOCK_W(14, kRouteWarp);
+        DEC_TRACE_W(4, kRouteWarp);
     }
+
+    // ---- gate/up units: the shared unit of warps 8.. (if any), then routed units 2w, 2w + 1 --
+    float* hx = reinterpret_cast<float*>(a.xh);  // h exchange, f32 [k+1][I]
+    {
+        // shared units on warps 8, 9, 10, 12: none on sub-partition 3, the routing warp's
+        const int wsh = warp == 12 ? 3 : (warp >= 8 && warp <= 10 ? warp - 8 : kMaxShUnits);
+        const bool has_sh = wsh < sh1 - sh0;
+        const int ua = u0 + 2 * warp;
+        const int nu = max(0, min(2, u1 - ua));  // routed units of this warp
+#pragma unroll 1
+        for (int q = 0; q < 3; ++q) {
+            if (q == 0 && !has_sh) continue;
+            // every warp but the routing warp parks on barrier 1 during the routing step (parked
+            // warps issue nothing)
+            if (q == 1 && warp != kRouteWarp) named_sync(kDThreads);
+            const uint8_t *s1, *s3;
+            int slot, j;
+            if (q == 0) {
+                if (!bar_wait(&bar_sh, 0)) { set_dev_error(a.status, kDevTimeout); if (lane == 0) s_failed = 1; }
+                s1 = st_s + wsh * rb13;
+                s3 = st_s + kMaxShUnits * kRow13 + wsh * rb13;
+                slot = k;
+                j = sh0 + wsh;
+            } else {
+                if (q > nu) break;
+                const int lu = 2 * warp + q - 1, ch = lu / kChunkUnits, iu = lu - ch * kChunkUnits;
+                if (q == 1 && !bar_wait(&bar_c[ch], 0)) {
+                    set_dev_error(a.status, kDevTimeout);
+                    if (lane == 0) s_failed = 1;
+                }
+                s1 = st_r + static_cast<size_t>(ch) * 2 * kChunkUnits * kRow13 + iu * rb13;
+                s3 = s1 + kChunkUnits * rb13;
+                slot = (u0 + lu) / I;
+                j = (u0 + lu) % I;
+            }
+            float gt = 0.f, up = 0.f;
+#pragma unroll 1
+            for (int sb = lane; sb < H / 32; sb += 32) {
+                const uint32_t* aq = xq + sb * kQW;
+                gt += subblk_dot(s1, sb, aq);
+                up += subblk_dot(s3, sb, aq);
+            }
+            gt = warp_sum(gt);
+            up = warp_sum(up);
+            float hv = silu_f(gt) * up;
+            if (!x_finite) hv = __int_as_float(0x7fc00000);
+            if (lane == 0) __stcg(hx + static_cast<size_t>(slot) * I + j, hv);
+        }
+    }
+    DEC_CLK0(1);
+    __syncthreads();  // this CTA's h entries are written; the W1/W3 staging is free
+    DEC_TRACE(5);
+    DEC_CLK0(2);
+    if (tid == 0) {   // arrive: the launch's G arrivals complete h
+        asm volatile("fence.acq_rel.gpu;\n\tred.relaxed.gpu.global.add.u64 [%0], 1;" :: "l"(a.counter) : "memory");
+    }
+    DEC_CLK0(3);
+
+    // ---- while h completes: decode this CTA's W2 rows into dp2a operands ---------------------
+    if (!bar_wait(&bar_w2, 0)) { set_dev_error(a.status, kDevTimeout); if (lane == 0) s_failed = 1; }
+    const int spr = I / 32;
+#pragma unroll 1
+    for (int q = tid; q < nrows * ns * spr; q += kDThreads) {
+        const int r = q / (ns * spr), rem = q - r * (ns * spr), s = rem / spr, sb = rem - s * spr;
+        const uint8_t* blk = st_2 + static_cast<size_t>(s) * kMaxRows2 * kRow2 + static_cast<size_t>(r) * rb2 +
+                             (sb >> 3) * kBlockBytes;
+        const uint2 hdr = *reinterpret_cast<const uint2*>(blk);
+        const uint32_t* qw = reinterpret_cast<const uint32_t*>(blk + 8 + (sb & 7) * 16);
+        uint2* d = reinterpret_cast<uint2*>(w2q + static_cast<size_t>(q) * 8);
+#pragma unroll 1
+        for (int i = 0; i < 4; ++i) {
+            uint2 o;
+            kv_lookup8(qw[i], o.x, o.y);
+            d[i] = o;
+        }
+        w2s[q] = iq4_subscale(hdr.x, hdr.y, sb & 7);
+    }
+    DEC_CLK0(4);
+    if (tid == 0) {  // wait for every CTA's arrival
+        const unsigned long long target = base + static_cast<unsigned long long>(G);
+        const uint64_t t0 = tc::globaltimer_ns();
+        while (ld_acquire_u64(a.counter) < target) {
+            if (tc::globaltimer_ns() - t0 > kSpinLimitNs) {
+                set_dev_error(a.status, kDevTimeout);
+                s_failed = 1;
+                break;
+            }
+            __nanosleep(20);
+        }
+    }
+    DEC_CLK0(5);
     __syncthreads();
     DEC_TRACE(6);
-    if (pw >= H) {  // warps without an output row: pull the next layer's fixed weights into L2
-        const int idle = nwarps - H, me = pw - H;
-#pragma unroll 1
-        for (int r = 0; r < 4; ++r) {
-            if (!a.pf[r]) continue;
-            for (uint32_t o = (static_cast<uint32_t>(me) * 32 + lane) * 128; o < a.pf_bytes[r];
-                 o += static_cast<uint32_t>(idle) * 32 * 128)
-                asm volatile("prefetch.global.L2 [%0];" :: "l"(a.pf[r] + o));
+    DEC_CLK0(6);
+    // h as 16-bit pairs per sub-block: warp w packs sub-blocks w, w + 16, ... of all slots
+    {
+        const int nsb = ns * spr;
+        constexpr int kPer = (kMaxTopK + 1) * (kMaxI / 32) / kDWarps;  // 9
+        float hv[kPer];
+#pragma unroll
+        for (int i = 0; i < kPer; ++i) {
+            const int g = warp + kDWarps * i;
+            hv[i] = g < nsb ? __ldcg(hx + g * 32 + lane) : 0.f;
         }
+        DEC_CLK0(7);
+        pack_subblocks<kPer>(hv, hq, warp, nsb, lane);
+        DEC_CLK0(8);
     }
-    constexpr int kPairIt = ((kMaxTopK + 1) * kMaxI / 2 + kDThreads - 1) / kDThreads;
-    float hlo[kPairIt], hhi[kPairIt];
-#pragma unroll
-    for (int it = 0; it < kPairIt; ++it) {  // every load issued before any is used
-        const int q = tid + it * kDThreads;
-        if (q < ns * I / 2) {
-            const int j = (q >> 4) * 32 + ((q & 15) >> 2) * 4 + (q & 3);
-            hlo[it] = __ldcg(a.h + j);
-            hhi[it] = __ldcg(a.h + j + 16);
-        }
-    }
-    // h as 16-bit pairs per slot (kQW layout), scale from the slot's max |h|
-    if (tid < ns) {
-        const unsigned long long v = __ldcg(a.hmax + tid);
-        const float m = (v & ~0xFFFFFFFFull) == epoch ? __uint_as_float(static_cast<uint32_t>(v)) : __int_as_float(0x7fc00000);
-        const float sc = q16_scale(m);
-        hscale[tid] = sc;
-        hw[tid] = isfinite(m) ? wgt[tid] / sc : __int_as_float(0x7fc00000);
-    }
-    __syncthreads();
-#pragma unroll
-    for (int it = 0; it < kPairIt; ++it) {  // 16 consecutive lanes per sub-block
-        const int q = tid + it * kDThreads;
-        if (q >= ns * I / 2) break;
-        const int gsb = q >> 4, wi = q & 15;           // gsb = slot * (I/32) + sub-block
-        const float sc = hscale[gsb / (I / 32)];
-        const int lo = q16(hlo[it], sc), hi = q16(hhi[it], sc);
-        hq[gsb * kQW + wi] = (static_cast<uint32_t>(lo) & 0xFFFFu) | (static_cast<uint32_t>(hi) << 16);
-        int s16 = lo + hi;
-#pragma unroll
-        for (int o = 8; o > 0; o >>= 1) s16 += __shfl_xor_sync(0xffffffffu, s16, o);
-        if (wi == 0) hq[gsb * kQW + 16] = static_cast<uint32_t>(128 * s16);
-    }
-    __syncthreads();
+    __syncthreads();  // hq, slot_e, wgt
     DEC_TRACE(7);
-    const int spr = I / 32, G2 = 32 / spr;
+    DEC_CLK0(9);
+
+    // ---- down projection + weighted combine + residual: warp w owns row n0 + w ----------------
+    const int G2 = 32 / spr;
     const int gi = lane / spr, sb = lane - gi * spr;
-    const int nslot = (ns + G2 - 1) / G2;
     const float* resid = a.io ? a.io->resid : a.resid_direct;
     float* out = a.io ? a.io->out : a.out_direct;
-    for (int n = pw; n < H; n += nwarps) {
-        cp_wait<0>();
-        __syncwarp();
+    if (warp < nrows) {
+        const int n = n0 + warp;
         float y = 0.f;
 #pragma unroll 1
-        for (int t = 0; t < nslot; ++t) {
-            const int s = gi + t * G2;
-            if (s < ns) {
-                const SubBlk b = lds_subblk(st_d + s * kMaxRow2, sb);
-                const float d = iq4_subscale(b.hdr.x, b.hdr.y, sb & 7) *
-                                static_cast<float>(dot_subblk_i16(b, hq + (s * spr + sb) * kQW));
-                y = fmaf(hw[s], d, y);
-            }
+        for (int s = gi; s < ns; s += G2) {
+            const int q = (warp * ns + s) * spr + sb;
+            const uint4* wq = reinterpret_cast<const uint4*>(w2q + static_cast<size_t>(q) * 8);
+            const uint32_t* aq = hq + (s * spr + sb) * kQW;
+            const uint4* a4 = reinterpret_cast<const uint4*>(aq);
+            const uint4 r0 = wq[0], r1 = wq[1];
+            const uint4 av0 = a4[0], av1 = a4[1], av2 = a4[2], av3 = a4[3];
+            int acc = -static_cast<int>(aq[16]);
+            acc = dp2a_lo(av0.x, r0.x, acc); acc = dp2a_hi(av0.y, r0.x, acc);
+            acc = dp2a_lo(av0.z, r0.y, acc); acc = dp2a_hi(av0.w, r0.y, acc);
+            acc = dp2a_lo(av1.x, r0.z, acc); acc = dp2a_hi(av1.y, r0.z, acc);
+            acc = dp2a_lo(av1.z, r0.w, acc); acc = dp2a_hi(av1.w, r0.w, acc);
+            acc = dp2a_lo(av2.x, r1.x, acc); acc = dp2a_hi(av2.y, r1.x, acc);
+            acc = dp2a_lo(av2.z, r1.y, acc); acc = dp2a_hi(av2.w, r1.y, acc);
+            acc = dp2a_lo(av3.x, r1.z, acc); acc = dp2a_hi(av3.y, r1.z, acc);
+            acc = dp2a_lo(av3.z, r1.w, acc); acc = dp2a_hi(av3.w, r1.w, acc);
+            y = fmaf(wgt[s], w2s[q] * __uint_as_float(aq[17]) * static_cast<float>(acc), y);
         }
-        __syncwarp();  // staging free
-        if (n + nwarps < H) issue_row(n + nwarps);
         y = warp_sum(y);
         if (!x_finite) y = __int_as_float(0x7fc00000);
         if (lane == 0) out[n] = (resid ? resid[n] : 0.f) + a.scale * y;
     }
-    cp_wait<0>();
+    DEC_CLK0(10);
     DEC_TRACE(8);
+    // pull this CTA's slice of the next layer's fixed weights into L2
+#pragma unroll 1
+    for (int r = 0; r < 4; ++r) {
+        if (!a.pf[r]) continue;
+        const uint32_t nl = (a.pf_bytes[r] + 127) / 128;
+        for (uint32_t l = static_cast<uint32_t>(c) + static_cast<uint32_t>(G) * tid; l < nl;
+             l += static_cast<uint32_t>(G) * kDThreads)
+            asm volatile("prefetch.global.L2 [%0];" :: "l"(a.pf[r] + static_cast<size_t>(l) * 128));
+    }
+    __syncthreads();
+    if (s_failed && tid == 0) {  // drain bulk copies still landing in this CTA's shared memory
+        bar_wait(&bar_sh, 0);
+        bar_wait(&bar_w2, 0);
+        for (int ch = 0; ch < (u1 - u0 + kChunkUnits - 1) / kChunkUnits; ++ch) bar_wait(&bar_c[ch], 0);
+    }
 }
 
 }  // namespace
 
-bool decode_supported(const Layer& L) {
-    // rows of whole 16-byte chunks (H and I multiples of 512) from 16-byte aligned experts
-    return L.tab_aligned16 && L.spec.hidden <= kMaxH && L.spec.hidden % 512 == 0 &&
-           L.spec.inter <= kMaxI && L.spec.inter % 512 == 0 && L.spec.n_experts <= kMaxExperts;
+size_t decode_exchange_words(int E, int k, int I) {
+    return static_cast<size_t>(2) * (E + 1) + static_cast<size_t>(k + 1) * I;
 }
 
-void launch_decode(const Layer& L, const Workspace& ws, int* sync, int sm_count, cudaStream_t s,
-                   const float* x, const float* resid, float* out, float norm_eps) {
+bool decode_supported(const Layer& L, int sm_count) {
+    // rows of whole 16-byte chunks (H and I multiples of 512) from 16-byte aligned experts, a
+    // grid large enough for the per-CTA slices of the shared memory plan, and at most one router
+    // half-row per warp 4..15
+    const int T = 2 * (static_cast<int>(L.spec.n_experts) + 1);
+    return L.tab_aligned16 && L.spec.hidden <= kMaxH && L.spec.hidden % 512 == 0 &&
+           L.spec.inter <= kMaxI && L.spec.inter % 512 == 0 && L.spec.n_experts <= kMaxExperts &&
+           sm_count >= kMinGrid && T <= (kDWarps - 4) * sm_count;
+}
+
+int launch_decode(const Layer& L, const Workspace& ws, int* sync, int sm_count, cudaStream_t s,
+                  const float* x, const float* resid, float* out, float norm_eps) {
     DecodeArgs a;
     a.io = x ? nullptr : ws.io;
     a.x_direct = x;
@@ -590,18 +753,18 @@ void launch_decode(const Layer& L, const Workspace& ws, int* sync, int sm_count,
     a.wr = reinterpret_cast<const float*>(L.router_w_ptr);
     a.bias = reinterpret_cast<const float*>(L.bias_ptr);
     a.gate_w = reinterpret_cast<const float*>(L.gate_ptr);
-    a.tabs = L.tables();
     a.H = static_cast<int>(L.spec.hidden);
     a.I = static_cast<int>(L.spec.inter);
     a.E = static_cast<int>(L.spec.n_experts);
+    for (int m = 0; m < 3; ++m)
+        for (int e = 0; e <= a.E; ++e) a.tw[m][e] = L.host_tab[static_cast<size_t>(m) * (a.E + 1) + e];
     a.k = static_cast<int>(L.spec.top_k);
     a.has_shared = L.has_shared() ? 1 : 0;
     a.scale = L.spec.scale;
-    a.logits = ws.logits;
     a.topk = ws.topk;
-    a.h = ws.h;
+    a.xlog = ws.dx;
+    a.xh = ws.dx + 2 * (a.E + 1);
     a.counter = reinterpret_cast<unsigned long long*>(sync);
-    a.hmax = a.counter + 1;
     a.status = ws.status;
     // once per device (not during a stream capture that may follow the first call)
     static bool attr_set[64] = {};
@@ -611,7 +774,18 @@ void launch_decode(const Layer& L, const Workspace& ws, int* sync, int sm_count,
         cudaFuncSetAttribute(decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kDecodeSmem));
         if (dev >= 0 && dev < 64) attr_set[dev] = true;
     }
-    decode_kernel<<<sm_count, kDThreads, kDecodeSmem, s>>>(a);
+    // cooperative: the CTAs wait on each other's exchange entries, so all must be resident
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(sm_count));
+    cfg.blockDim = dim3(kDThreads);
+    cfg.dynamicSmemBytes = kDecodeSmem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, decode_kernel, a) == cudaSuccess ? 0 : -1;
 }
 
 }  // namespace moe

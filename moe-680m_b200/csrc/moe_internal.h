@@ -17,7 +17,7 @@ namespace moe {
 // Layout of the context's 256-byte status block (zeroed at creation; moe_sync clears the kernel
 // words after an error):
 //   [0, 4)      int status word (first device error code)
-//   [64, 160)   decode kernel: 64-bit grid counter, then per-slot 64-bit |h| maxima
+//   [64, 72)    decode kernel: 64-bit launch counter (its epochs)
 //   [160, 164)  LM-head kernel: CTA completion ticket
 //   [168, 232)  LM-head kernel: 8 64-bit argmax keys
 constexpr size_t kStatusBlockBytes = 256;
@@ -39,6 +39,7 @@ struct ExpertTables {
 struct Layer {
     moe_layer_spec spec;
     const uint8_t** tab = nullptr;  // device [3][E+1]
+    std::vector<const uint8_t*> host_tab;  // the same pointers on the host (kernel parameters)
     bool tab_aligned16 = false;     // every expert weight pointer is 16-byte aligned
     const uint8_t* router_w_ptr = nullptr;
     const uint8_t* bias_ptr = nullptr;  // may be null
@@ -139,6 +140,9 @@ struct Workspace {
     const void* hmap_base = nullptr;
     uint64_t xmap_rows = 0, hmap_rows = 0, xmap_cols = 0, hmap_cols = 0;
     IoArgs* io = nullptr;         // device IoArgs of the current call
+    unsigned long long* dx = nullptr;  // single-token kernel's epoch-tagged exchange entries
+                                       // (decode_exchange_words), zeroed at allocation
+    size_t dx_bytes = 0;
     uint32_t max_chunks = 0;
 };
 
@@ -285,10 +289,13 @@ void launch_tc13(const Layer& L, const BMaps& xmap, const Workspace& ws, int max
 void launch_tc2(const Layer& L, const BMaps& hmap, const Workspace& ws, int max_items,
                 int sm_count, bool a_tmem, cudaStream_t s);
 bool make_fp16_tmaps(BMaps* m, const void* base, uint64_t rows, uint64_t cols);
-bool decode_supported(const Layer& L);
+bool decode_supported(const Layer& L, int sm_count);
+// 64-bit entries of the single-token kernel's exchange area: half-row logits and h.
+size_t decode_exchange_words(int E, int k, int I);
 // x == nullptr: activation pointers from ws.io; otherwise direct pointers, and norm_eps >= 0
-// normalises x (RMSNorm) for the layer while x stays the residual when resid == x.
-void launch_decode(const Layer& L, const Workspace& ws, int* sync, int sm_count, cudaStream_t s,
+// normalises x (RMSNorm) for the layer while x stays the residual when resid == x.  Returns 0,
+// or -1 when the launch was refused.
+int launch_decode(const Layer& L, const Workspace& ws, int* sync, int sm_count, cudaStream_t s,
                    const float* x = nullptr, const float* resid = nullptr, float* out = nullptr,
                    float norm_eps = -1.0f);
 void launch_combine(const Layer& L, const Workspace& ws, const IoArgs* io, int M, int ns,
