@@ -101,9 +101,6 @@ constexpr int kRow2 = kMaxI / kQK * kBlockBytes;   // bytes of one W2 row (272)
 constexpr size_t kStRouted = size_t(kDWarps) * 4 * kRow13;             // [warp][W1 a, W1 b, W3 a, W3 b]
 constexpr size_t kStShared = size_t(2) * kMaxShUnits * kRow13;         // [W1 rows][W3 rows]
 constexpr size_t kStW2 = size_t(kMaxTopK + 1) * kMaxRows2 * kRow2;      // [slot][row]
-constexpr size_t kW2Dec = size_t(kMaxRows2) * (kMaxTopK + 1) * (kMaxI / 32) * 32;  // decoded W2 codes
-static_assert(kW2Dec + size_t(kMaxRows2) * (kMaxTopK + 1) * (kMaxI / 32) * 4 <= kStRouted + kStShared,
-              "decoded W2 fits over the W1/W3 staging");
 constexpr size_t kDecodeSmem = kStRouted + kStShared + kStW2 + sizeof(float) * kMaxH +
                                sizeof(uint32_t) * (kMaxH / 32) * kQW +
                                sizeof(uint32_t) * (kMaxTopK + 1) * (kMaxI / 32) * kQW;
@@ -375,10 +372,6 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const __grid_const
     float* xs = reinterpret_cast<float*>(st_2 + kStW2);                 // f32 x (router)
     uint32_t* xq = reinterpret_cast<uint32_t*>(xs + kMaxH);             // [H/32][kQW]
     uint32_t* hq = xq + (kMaxH / 32) * kQW;                             // [k+1][I/32][kQW]
-    // decoded W2 (after the units, over the W1/W3 staging): per (row, slot, sub-block) 8 words
-    // of kvalue + 128 bytes in dp2a pair order, and the sub-block scale d * (ls - 32)
-    uint32_t* w2q = reinterpret_cast<uint32_t*>(st_r);
-    float* w2s = reinterpret_cast<float*>(st_r + kW2Dec);
     __shared__ __align__(8) uint64_t bar_sh, bar_w2, bar_c[kMaxChunks];
     __shared__ unsigned long long s_base;
     __shared__ float red[kDWarps];
@@ -403,7 +396,6 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const __grid_const
     const int task = warp >= 4 ? c + G * (warp - 4) : T;
 
     DEC_TRACE(0);
-    DEC_CLOCK_W(12, kRouteWarp);
     DEC_CLK0(0);
     // ---- every independent load first: x, this warp's router half-row, pointer tables, bias --
     if (tid == 0) {
@@ -462,7 +454,7 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const __grid_const
     }
     const bool x_finite = __syncthreads_and(fin) != 0;  // also: xs, barriers, s_base, tables
     const unsigned long long base = s_base;
-    const uint32_t epoch = static_cast<uint32_t>(base / static_cast<unsigned long long>(G)) + 1u;
+    const uint32_t epoch = static_cast<uint32_t>(base / (static_cast<unsigned long long>(G) * kDWarps)) + 1u;
     if (tid < E) s_bias[tid] = bias_v;
     DEC_TRACE(1);
 
@@ -523,6 +515,7 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const __grid_const
             __nanosleep(64);
         }
         DEC_TRACE_W(3, kRouteWarp);
+        DEC_CLOCK_W(12, kRouteWarp);
         route_warp(v0, v1, g0, g1, s_bias, E, k, a.gate_w != nullptr, a.has_shared != 0, a.status, slot_e, wgt,
                    c == 0 ? a.topk : nullptr);
         __syncwarp();
@@ -573,6 +566,7 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const __grid_const
             // every warp but the routing warp parks on barrier 1 during the routing step (parked
             // warps issue nothing)
             if (q == 1 && warp != kRouteWarp) named_sync(kDThreads);
+            if (q == 1) DEC_CLK0(11);
             const uint8_t *s1, *s3;
             int slot, j;
             if (q == 0) {
@@ -588,6 +582,7 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const __grid_const
                     set_dev_error(a.status, kDevTimeout);
                     if (lane == 0) s_failed = 1;
                 }
+                if (q == 1) DEC_CLK0(12);
                 s1 = st_r + static_cast<size_t>(ch) * 2 * kChunkUnits * kRow13 + iu * rb13;
                 s3 = s1 + kChunkUnits * rb13;
                 slot = (u0 + lu) / I;
@@ -605,39 +600,16 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const __grid_const
             float hv = silu_f(gt) * up;
             if (!x_finite) hv = __int_as_float(0x7fc00000);
             if (lane == 0) __stcg(hx + static_cast<size_t>(slot) * I + j, hv);
+            DEC_CLK0(12 + q);
         }
+        // arrive: every warp of every CTA, after its own h stores (release orders them)
+        __syncwarp();
+        if (lane == 0) asm volatile("red.release.gpu.global.add.u64 [%0], 1;" :: "l"(a.counter) : "memory");
     }
     DEC_CLK0(1);
-    __syncthreads();  // this CTA's h entries are written; the W1/W3 staging is free
-    DEC_TRACE(5);
-    DEC_CLK0(2);
-    if (tid == 0) {   // arrive: the launch's G arrivals complete h
-        asm volatile("fence.acq_rel.gpu;\n\tred.relaxed.gpu.global.add.u64 [%0], 1;" :: "l"(a.counter) : "memory");
-    }
-    DEC_CLK0(3);
-
-    // ---- while h completes: decode this CTA's W2 rows into dp2a operands ---------------------
-    if (!bar_wait(&bar_w2, 0)) { set_dev_error(a.status, kDevTimeout); if (lane == 0) s_failed = 1; }
     const int spr = I / 32;
-#pragma unroll 1
-    for (int q = tid; q < nrows * ns * spr; q += kDThreads) {
-        const int r = q / (ns * spr), rem = q - r * (ns * spr), s = rem / spr, sb = rem - s * spr;
-        const uint8_t* blk = st_2 + static_cast<size_t>(s) * kMaxRows2 * kRow2 + static_cast<size_t>(r) * rb2 +
-                             (sb >> 3) * kBlockBytes;
-        const uint2 hdr = *reinterpret_cast<const uint2*>(blk);
-        const uint32_t* qw = reinterpret_cast<const uint32_t*>(blk + 8 + (sb & 7) * 16);
-        uint2* d = reinterpret_cast<uint2*>(w2q + static_cast<size_t>(q) * 8);
-#pragma unroll 1
-        for (int i = 0; i < 4; ++i) {
-            uint2 o;
-            kv_lookup8(qw[i], o.x, o.y);
-            d[i] = o;
-        }
-        w2s[q] = iq4_subscale(hdr.x, hdr.y, sb & 7);
-    }
-    DEC_CLK0(4);
     if (tid == 0) {  // wait for every CTA's arrival
-        const unsigned long long target = base + static_cast<unsigned long long>(G);
+        const unsigned long long target = base + static_cast<unsigned long long>(G) * kDWarps;
         const uint64_t t0 = tc::globaltimer_ns();
         while (ld_acquire_u64(a.counter) < target) {
             if (tc::globaltimer_ns() - t0 > kSpinLimitNs) {
@@ -676,26 +648,13 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const __grid_const
     const float* resid = a.io ? a.io->resid : a.resid_direct;
     float* out = a.io ? a.io->out : a.out_direct;
     if (warp < nrows) {
+        if (!bar_wait(&bar_w2, 0)) { set_dev_error(a.status, kDevTimeout); if (lane == 0) s_failed = 1; }
         const int n = n0 + warp;
         float y = 0.f;
 #pragma unroll 1
         for (int s = gi; s < ns; s += G2) {
-            const int q = (warp * ns + s) * spr + sb;
-            const uint4* wq = reinterpret_cast<const uint4*>(w2q + static_cast<size_t>(q) * 8);
-            const uint32_t* aq = hq + (s * spr + sb) * kQW;
-            const uint4* a4 = reinterpret_cast<const uint4*>(aq);
-            const uint4 r0 = wq[0], r1 = wq[1];
-            const uint4 av0 = a4[0], av1 = a4[1], av2 = a4[2], av3 = a4[3];
-            int acc = -static_cast<int>(aq[16]);
-            acc = dp2a_lo(av0.x, r0.x, acc); acc = dp2a_hi(av0.y, r0.x, acc);
-            acc = dp2a_lo(av0.z, r0.y, acc); acc = dp2a_hi(av0.w, r0.y, acc);
-            acc = dp2a_lo(av1.x, r0.z, acc); acc = dp2a_hi(av1.y, r0.z, acc);
-            acc = dp2a_lo(av1.z, r0.w, acc); acc = dp2a_hi(av1.w, r0.w, acc);
-            acc = dp2a_lo(av2.x, r1.x, acc); acc = dp2a_hi(av2.y, r1.x, acc);
-            acc = dp2a_lo(av2.z, r1.y, acc); acc = dp2a_hi(av2.w, r1.y, acc);
-            acc = dp2a_lo(av3.x, r1.z, acc); acc = dp2a_hi(av3.y, r1.z, acc);
-            acc = dp2a_lo(av3.z, r1.w, acc); acc = dp2a_hi(av3.w, r1.w, acc);
-            y = fmaf(wgt[s], w2s[q] * __uint_as_float(aq[17]) * static_cast<float>(acc), y);
+            const uint8_t* row = st_2 + static_cast<size_t>(s) * kMaxRows2 * kRow2 + static_cast<size_t>(warp) * rb2;
+            y = fmaf(wgt[s], subblk_dot(row, sb, hq + (s * spr + sb) * kQW), y);
         }
         y = warp_sum(y);
         if (!x_finite) y = __int_as_float(0x7fc00000);

@@ -60,7 +60,7 @@ def test_bucket_static_matches_bucket():
         ranges = ctx.download(outs[0], (E + 2,), np.int32)
         sp = ctx.download(outs[3], (m, k + 1), np.int32)
         assert sp[1, 2] == -1 and (np.delete(sp.ravel(), 1 * (k + 1) + 2) >= 0).all()
-        assert ranges[E + 1] == S - 1 and ranges[2] - ranges[1] == 2  # expert 2 lost token 1
+        assert ranges[E + 1] == S - 1 and ranges[3] - ranges[2] == 2  # expert 2 lost token 1
         # sizes beyond the fixed scratch are refused, not overrun
         assert L.moe_bucket_static(E, k, 1, C.c_void_p(ctx.ptr(topk)), 9000,
                                    *[C.c_void_p(ctx.ptr(o)) for o in got], None) == -4
