@@ -150,24 +150,25 @@ __device__ __forceinline__ SubBlk lds_subblk(const uint8_t* row, int sb) {
 }
 
 // Exact integer dot of one IQ4_XS sub-block (its four qs words) with 32 packed 16-bit
-// activations (kQW layout): sum over j of kv(code_j) * a_j.  Out of line (arguments in
-// registers): the kernel's code size matters more than the call.
-__device__ __noinline__ int dot_subblk_i16(uint32_t w0, uint32_t w1, uint32_t w2, uint32_t w3,
-                                           const uint32_t* aq) {
+// activations (kQW layout): sum over j of kv(code_j) * a_j.  Four independent partial sums keep
+// the dp2a dependency chains short (the pipe is quarter rate; with a handful of warps per
+// sub-partition a single 16-long chain leaves it idle most of the time).
+__device__ __forceinline__ int dot_subblk_i16(uint32_t w0, uint32_t w1, uint32_t w2, uint32_t w3,
+                                              const uint32_t* aq) {
     const uint4* a4 = reinterpret_cast<const uint4*>(aq);
     const uint32_t w[4] = {w0, w1, w2, w3};
-    int acc = -static_cast<int>(aq[16]);
+    int acc[4];
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
         uint32_t r0, r1;
         kv_lookup8(w[i], r0, r1);  // r0 bytes: codes 4i, 16+4i, 4i+1, 17+4i (+128)
         const uint4 av = a4[i];
-        acc = dp2a_lo(av.x, r0, acc);
-        acc = dp2a_hi(av.y, r0, acc);
-        acc = dp2a_lo(av.z, r1, acc);
-        acc = dp2a_hi(av.w, r1, acc);
+        acc[i] = dp2a_lo(av.x, r0, 0);
+        acc[i] = dp2a_hi(av.y, r0, acc[i]);
+        acc[i] = dp2a_lo(av.z, r1, acc[i]);
+        acc[i] = dp2a_hi(av.w, r1, acc[i]);
     }
-    return acc;
+    return ((acc[0] + acc[1]) + (acc[2] + acc[3])) - static_cast<int>(aq[16]);
 }
 
 // f32 contribution of one staged sub-block against packed activations: scale(d, ls) x
@@ -256,6 +257,18 @@ __device__ __forceinline__ void pack_subblocks(const float (&v)[N], uint32_t* ba
     }
 }
 
+// Gathers h (f32 [slots][I] in global memory) and packs it: warp w takes sub-blocks w, w + 16, ...
+__device__ __forceinline__ void gather_pack_h(const float* hx, uint32_t* hq, int nsb, int warp, int lane) {
+    constexpr int kPer = (kMaxTopK + 1) * (kMaxI / 32) / kDWarps;  // 9
+    float hv[kPer];
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+        const int g = warp + kDWarps * i;
+        hv[i] = g < nsb ? __ldcg(hx + g * 32 + lane) : 0.f;
+    }
+    pack_subblocks<kPer>(hv, hq, warp, nsb, lane);
+}
+
 // Order-preserving map of a float onto unsigned integers (NaN: 0, below every number).
 __device__ __forceinline__ uint32_t f2ord(float f) {
     const uint32_t u = __float_as_uint(f);
@@ -284,17 +297,14 @@ __device__ __forceinline__ void cx(uint32_t& ka, uint32_t& ia, uint32_t& kb, uin
 // the lanes' heads (a tie between heads goes to the lower index) and the winning lane pops its
 // head, writing the slot's expert and probability.  Lane k writes the shared expert's slot
 // (gate sigmoid(g . x), or 1 without a gate weight).  CTA 0 also writes the routing record.
-__device__ __forceinline__ void route_warp(const unsigned long long (&v0)[8], const unsigned long long (&v1)[8],
-                                           unsigned long long g0, unsigned long long g1, const float* bias,
-                                           int E, int k, bool has_gate, bool has_shared, int* status,
-                                           int* slot_e, float* wgt, uint2* topk_rec) {
+__device__ __noinline__ void route_warp(const float* lg, float gz, int E, int k, bool has_gate, bool has_shared,
+                                       int* status, int* slot_e, float* wgt, uint2* topk_rec) {
     const int lane = threadIdx.x & 31;
     float pv[8];
     uint32_t om = 0;
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-        const int e = min(lane + 32 * i, E - 1);
-        pv[i] = (__uint_as_float(static_cast<uint32_t>(v0[i])) + __uint_as_float(static_cast<uint32_t>(v1[i]))) + bias[e];
+        pv[i] = lg[min(lane + 32 * i, E - 1)];
         if (lane + 32 * i < E) om = max(om, f2ord(pv[i]));
     }
     const float lmax = ord2f(__reduce_max_sync(0xffffffffu, om));
@@ -327,35 +337,38 @@ __device__ __forceinline__ void route_warp(const unsigned long long (&v0)[8], co
     cx(key[1], idx[1], key[4], idx[4]); cx(key[3], idx[3], key[6], idx[6]);
     cx(key[2], idx[2], key[4], idx[4]); cx(key[3], idx[3], key[5], idx[5]);
     cx(key[3], idx[3], key[4], idx[4]);
-#pragma unroll 1
-    for (int r = 0; r < k; ++r) {
+    uint32_t my_e = 0, my_m = 0;  // lane r: slot r's expert and probability bits
+    // rounds without divergence: the winning lane pops its head by selects; the slot's expert
+    // comes from the winner by a shuffle that is off the rounds' dependency chain
+#pragma unroll
+    for (int r = 0; r < kMaxTopK; ++r) {
+        if (r >= k) break;
         const uint32_t m = __reduce_max_sync(0xffffffffu, key[0]);
         const unsigned tie = __ballot_sync(0xffffffffu, key[0] == m);
-        uint32_t win;
-        if (__popc(tie) == 1) {
-            win = static_cast<uint32_t>(__ffs(tie) - 1);
-        } else {
-            win = __reduce_min_sync(0xffffffffu, key[0] == m ? idx[0] : 0xFFFFu) & 31u;
-        }
-        if (static_cast<uint32_t>(lane) == win) {
-            slot_e[r] = static_cast<int>(idx[0]);
-            wgt[r] = __uint_as_float(m);
-            if (topk_rec) topk_rec[1 + r] = make_uint2(idx[0], m);
+        // equal probabilities in several heads (rare): the lower expert index; computed
+        // alongside, selected without a branch
+        const uint32_t wmin = __reduce_min_sync(0xffffffffu, key[0] == m ? idx[0] : 0xFFFFu) & 31u;
+        const uint32_t win = __popc(tie) == 1 ? static_cast<uint32_t>(__ffs(tie) - 1) : wmin;
+        const uint32_t e = __shfl_sync(0xffffffffu, idx[0], static_cast<int>(win));
+        const bool won = static_cast<uint32_t>(lane) == win;
 #pragma unroll
-            for (int i = 0; i < 7; ++i) {
-                key[i] = key[i + 1];
-                idx[i] = idx[i + 1];
-            }
-            key[7] = 0u;
-            idx[7] = 0xFFFFu;
+        for (int i = 0; i < 7; ++i) {
+            key[i] = won ? key[i + 1] : key[i];
+            idx[i] = won ? idx[i + 1] : idx[i];
         }
+        key[7] = won ? 0u : key[7];
+        idx[7] = won ? 0xFFFFu : idx[7];
+        my_e = lane == r ? e : my_e;
+        my_m = lane == r ? m : my_m;
+    }
+    if (lane < k) {
+        slot_e[lane] = static_cast<int>(my_e);
+        wgt[lane] = __uint_as_float(my_m);
+        if (topk_rec) topk_rec[1 + lane] = make_uint2(my_e, my_m);
     }
     if (lane == 0) {
         float gt = 1.0f;
-        if (has_gate) {
-            const float z = __uint_as_float(static_cast<uint32_t>(g0)) + __uint_as_float(static_cast<uint32_t>(g1));
-            gt = 1.0f / (1.0f + expf(-z));
-        }
+        if (has_gate) gt = 1.0f / (1.0f + expf(-gz));
         if (has_shared) {
             slot_e[k] = E;
             wgt[k] = gt;
@@ -378,6 +391,7 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const __grid_const
     __shared__ float wgt[kMaxTopK + 1];
     __shared__ int slot_e[kMaxTopK + 1];
     __shared__ float s_bias[kMaxExperts];
+    __shared__ float s_lg[kMaxExperts];          // routing logits (bias added)
     __shared__ int s_failed;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int G = static_cast<int>(gridDim.x), c = static_cast<int>(blockIdx.x);
@@ -385,6 +399,7 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const __grid_const
     const int H = a.H, I = a.I, E = a.E, k = a.k;
     const int ns = k + (a.has_shared ? 1 : 0);
     const int rb13 = H / kQK * kBlockBytes, rb2 = I / kQK * kBlockBytes;
+    const int spr = I / 32;  // sub-blocks per h slot
     // this CTA's slices
     const int sh0 = a.has_shared ? c * I / G : 0, sh1 = a.has_shared ? (c + 1) * I / G : 0;
     const int U = k * I;
@@ -516,8 +531,14 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const __grid_const
         }
         DEC_TRACE_W(3, kRouteWarp);
         DEC_CLOCK_W(12, kRouteWarp);
-        route_warp(v0, v1, g0, g1, s_bias, E, k, a.gate_w != nullptr, a.has_shared != 0, a.status, slot_e, wgt,
-                   c == 0 ? a.topk : nullptr);
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+            if (lane + 32 * i < E)
+                s_lg[lane + 32 * i] = (__uint_as_float(static_cast<uint32_t>(v0[i])) +
+                                       __uint_as_float(static_cast<uint32_t>(v1[i]))) + s_bias[lane + 32 * i];
+        __syncwarp();
+        route_warp(s_lg, __uint_as_float(static_cast<uint32_t>(g0)) + __uint_as_float(static_cast<uint32_t>(g1)), E, k,
+                   a.gate_w != nullptr, a.has_shared != 0, a.status, slot_e, wgt, c == 0 ? a.topk : nullptr);
         __syncwarp();
         DEC_CLOCK_W(13, kRouteWarp);
         DEC_TRACE_W(9, kRouteWarp);
@@ -565,7 +586,9 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const __grid_const
             if (q == 0 && !has_sh) continue;
             // every warp but the routing warp parks on barrier 1 during the routing step (parked
             // warps issue nothing)
-            if (q == 1 && warp != kRouteWarp) named_sync(kDThreads);
+            if (q == 1 && warp != kRouteWarp) {
+                named_sync(kDThreads);
+            }
             if (q == 1) DEC_CLK0(11);
             const uint8_t *s1, *s3;
             int slot, j;
@@ -589,7 +612,7 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const __grid_const
                 j = (u0 + lu) % I;
             }
             float gt = 0.f, up = 0.f;
-#pragma unroll 1
+#pragma unroll 2
             for (int sb = lane; sb < H / 32; sb += 32) {
                 const uint32_t* aq = xq + sb * kQW;
                 gt += subblk_dot(s1, sb, aq);
@@ -607,7 +630,6 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const __grid_const
         if (lane == 0) asm volatile("red.release.gpu.global.add.u64 [%0], 1;" :: "l"(a.counter) : "memory");
     }
     DEC_CLK0(1);
-    const int spr = I / 32;
     if (tid == 0) {  // wait for every CTA's arrival
         const unsigned long long target = base + static_cast<unsigned long long>(G) * kDWarps;
         const uint64_t t0 = tc::globaltimer_ns();
@@ -625,40 +647,64 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const __grid_const
     DEC_TRACE(6);
     DEC_CLK0(6);
     // h as 16-bit pairs per sub-block: warp w packs sub-blocks w, w + 16, ... of all slots
-    {
-        const int nsb = ns * spr;
-        constexpr int kPer = (kMaxTopK + 1) * (kMaxI / 32) / kDWarps;  // 9
-        float hv[kPer];
-#pragma unroll
-        for (int i = 0; i < kPer; ++i) {
-            const int g = warp + kDWarps * i;
-            hv[i] = g < nsb ? __ldcg(hx + g * 32 + lane) : 0.f;
-        }
-        DEC_CLK0(7);
-        pack_subblocks<kPer>(hv, hq, warp, nsb, lane);
-        DEC_CLK0(8);
-    }
+    DEC_CLK0(7);
+    gather_pack_h(hx, hq, ns * spr, warp, lane);
+    DEC_CLK0(8);
     __syncthreads();  // hq, slot_e, wgt
     DEC_TRACE(7);
     DEC_CLK0(9);
 
-    // ---- down projection + weighted combine + residual: warp w owns row n0 + w ----------------
-    const int G2 = 32 / spr;
-    const int gi = lane / spr, sb = lane - gi * spr;
+    // ---- down projection + weighted combine + residual --------------------------------------
+    // Thread t takes the (slot, sub-block) pair p = t mod P (P = slots x I/32) for the output
+    // rows r = t / P, t / P + 3, ... : its packed activations stay in registers across the rows,
+    // and the pair partials (each weighted by its slot's routing weight) go to shared memory;
+    // then warp r sums row r's P partials in a fixed order.
     const float* resid = a.io ? a.io->resid : a.resid_direct;
     float* out = a.io ? a.io->out : a.out_direct;
-    if (warp < nrows) {
+    float* part = reinterpret_cast<float*>(st_r);  // [kMaxRows2][P]; the W1/W3 staging is free
+    {
+        const int P = ns * spr;
         if (!bar_wait(&bar_w2, 0)) { set_dev_error(a.status, kDevTimeout); if (lane == 0) s_failed = 1; }
-        const int n = n0 + warp;
-        float y = 0.f;
-#pragma unroll 1
-        for (int s = gi; s < ns; s += G2) {
-            const uint8_t* row = st_2 + static_cast<size_t>(s) * kMaxRows2 * kRow2 + static_cast<size_t>(warp) * rb2;
-            y = fmaf(wgt[s], subblk_dot(row, sb, hq + (s * spr + sb) * kQW), y);
+        if (tid < 3 * P) {
+            const int pp = tid % P, r0 = tid / P, s = pp / spr, sb = pp - s * spr;
+            const uint32_t* aq = hq + pp * kQW;
+            const uint4 a0 = reinterpret_cast<const uint4*>(aq)[0], a1 = reinterpret_cast<const uint4*>(aq)[1];
+            const uint4 a2 = reinterpret_cast<const uint4*>(aq)[2], a3 = reinterpret_cast<const uint4*>(aq)[3];
+            const int corr = static_cast<int>(aq[16]);
+            const float f = wgt[s] * __uint_as_float(aq[17]);
+            const uint8_t* rows = st_2 + static_cast<size_t>(s) * kMaxRows2 * kRow2 + (sb >> 3) * kBlockBytes;
+#pragma unroll 2
+            for (int r = r0; r < nrows; r += 3) {
+                const uint8_t* blk = rows + static_cast<size_t>(r) * rb2;
+                const uint2 hdr = *reinterpret_cast<const uint2*>(blk);
+                // the qs bytes of a sub-block start 8 bytes into a 16-byte unit: two 8-byte loads
+                const uint2 q01 = *reinterpret_cast<const uint2*>(blk + 8 + (sb & 7) * 16);
+                const uint2 q23 = *reinterpret_cast<const uint2*>(blk + 16 + (sb & 7) * 16);
+                const uint32_t w[4] = {q01.x, q01.y, q23.x, q23.y};
+                const uint4 av[4] = {a0, a1, a2, a3};
+                int acc[4];
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    uint32_t k0, k1;
+                    kv_lookup8(w[i], k0, k1);
+                    acc[i] = dp2a_lo(av[i].x, k0, 0);
+                    acc[i] = dp2a_hi(av[i].y, k0, acc[i]);
+                    acc[i] = dp2a_lo(av[i].z, k1, acc[i]);
+                    acc[i] = dp2a_hi(av[i].w, k1, acc[i]);
+                }
+                const int dot = ((acc[0] + acc[1]) + (acc[2] + acc[3])) - corr;
+                part[r * P + pp] = f * iq4_subscale(hdr.x, hdr.y, sb & 7) * static_cast<float>(dot);
+            }
         }
-        y = warp_sum(y);
-        if (!x_finite) y = __int_as_float(0x7fc00000);
-        if (lane == 0) out[n] = (resid ? resid[n] : 0.f) + a.scale * y;
+        __syncthreads();
+        if (warp < nrows) {
+            float y = 0.f;
+#pragma unroll 1
+            for (int i = lane; i < P; i += 32) y += part[warp * P + i];
+            y = warp_sum(y);
+            if (!x_finite) y = __int_as_float(0x7fc00000);
+            if (lane == 0) out[n0 + warp] = (resid ? resid[n0 + warp] : 0.f) + a.scale * y;
+        }
     }
     DEC_CLK0(10);
     DEC_TRACE(8);
@@ -672,6 +718,7 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const __grid_const
             asm volatile("prefetch.global.L2 [%0];" :: "l"(a.pf[r] + static_cast<size_t>(l) * 128));
     }
     __syncthreads();
+    DEC_TRACE(10);
     if (s_failed && tid == 0) {  // drain bulk copies still landing in this CTA's shared memory
         bar_wait(&bar_sh, 0);
         bar_wait(&bar_w2, 0);

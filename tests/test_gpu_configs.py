@@ -10,7 +10,8 @@ ABI against the CPU oracle:
 * config 4: the CUDA-core GEMV expert path forced at M=64 against the oracle.
 
 Tolerances: relative L2 <= 1e-3 and max|d| / max|ref| <= 2e-3 per layer output (the contract's);
-the 40-layer chain's final state within relative L2 1e-2 of the free-running oracle chain.
+the 40-layer chain's final state within relative L2 1e-2 of the free-running oracle chain when
+both chains route every layer alike (a routing flip is allowed only at a near tie).
 """
 import numpy as np
 import pytest
@@ -104,6 +105,7 @@ def test_config2_layer_stack_two_steps():
                 ctx.sync()
                 xs.append(ctx.download(dst, (1, sh.hidden)))
             free = x0.astype(np.float32)
+            flip = None  # first layer whose routing differs between the two chains
             for li in range(n_layers):
                 xin = xs[li]
                 xn = O.rms_norm(xin, eps).astype(np.float32)
@@ -117,11 +119,20 @@ def test_config2_layer_stack_two_steps():
                 hl = sparse_host_layer(seed, li, sh, None, top)
                 ref = coracle.moe_forward(hl, xn, xin, acc64=True)
                 check_close(xs[li + 1], ref["out64"], f"step {t} layer {li}")
-                free = coracle.moe_forward(hl, fn, free, acc64=True)["out64"].astype(np.float32)
+                fr = coracle.moe_forward(hl, fn, free, acc64=True)
+                if flip is None and set(fr["ids"][0].tolist()) != set(ref["ids"][0].tolist()):
+                    flip = li
+                    # the chains' inputs differ by rounding only, so a routing difference must
+                    # come from a near tie between the k-th and (k+1)-th logits
+                    srt = np.sort(lgf[0])[::-1]
+                    assert srt[sh.top_k - 1] - srt[sh.top_k] < 1e-3 * max(abs(srt[0]), 1.0), (t, li)
+                free = fr["out64"].astype(np.float32)
             finals.append(xs[-1])
-            # the free-running oracle chain ends where the stack does: 40 residual layers compound
-            # the per-layer differences, so the stack's bound is looser than one layer's
-            assert O.rel_l2(xs[-1], free) <= STACK_REL_L2, (t, O.rel_l2(xs[-1], free))
+            # without a routing flip, the free-running oracle chain ends where the stack does: 40
+            # residual layers compound the per-layer differences, so the bound is looser than one
+            # layer's (after a flip the chains follow different experts and are not compared)
+            if flip is None:
+                assert O.rel_l2(xs[-1], free) <= STACK_REL_L2, (t, O.rel_l2(xs[-1], free))
         assert not np.array_equal(finals[0], finals[1])
     finally:
         ctx.close()
