@@ -412,6 +412,9 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const __grid_const
 
     DEC_TRACE(0);
     DEC_CLK0(0);
+    // with programmatic dependent launch, wait here for the previous kernel on the stream (its
+    // memory included) before reading anything it may have written
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     // ---- every independent load first: x, this warp's router half-row, pointer tables, bias --
     if (tid == 0) {
         s_failed = 0;
@@ -654,6 +657,9 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const __grid_const
     DEC_TRACE(7);
     DEC_CLK0(9);
 
+    // the next kernel on the stream may start launching (it waits for this grid's completion
+    // in its own griddepcontrol.wait before reading anything)
+    asm volatile("griddepcontrol.launch_dependents;");
     // ---- down projection + weighted combine + residual --------------------------------------
     // Thread t takes the (slot, sub-block) pair p = t mod P (P = slots x I/32) for the output
     // rows r = t / P, t / P + 3, ... : its packed activations stay in registers across the rows,
@@ -786,11 +792,13 @@ int launch_decode(const Layer& L, const Workspace& ws, int* sync, int sm_count, 
     cfg.blockDim = dim3(kDThreads);
     cfg.dynamicSmemBytes = kDecodeSmem;
     cfg.stream = s;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeCooperative;
     attr[0].val.cooperative = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = 2;  // cooperative, and the next kernel on the stream may launch early (PDL)
     return cudaLaunchKernelEx(&cfg, decode_kernel, a) == cudaSuccess ? 0 : -1;
 }
 
