@@ -12,20 +12,22 @@
 //   * a contiguous range of the k * I routed units (slot s = u / I, row j = u % I), ~k I / G;
 //   * a contiguous range of output rows n, over which it computes
 //     out[n] = resid[n] + scale * sum_s w_s (W2_s[n] . h_s) for all k + 1 slots.
-// Work of other CTAs is consumed through two exchanges in global memory whose entries carry the
-// launch's epoch in their high 32 bits (64-bit stores and loads are single-copy atomic): a
-// reader polls the entries it needs until every one shows the current epoch.  The data itself is
-// the barrier, so a consumer starts as soon as the entries it reads are complete, one L2 round
-// trip after the last producer, instead of a counter barrier followed by a second round trip
-// for the data.  Exchanges: the half-row logits (every CTA then computes softmax + top-k itself,
-// identically: fixed reduction order, ties to the lower index) and h (every CTA needs all of h
-// for its output rows).
+// Work of other CTAs is consumed through two exchanges in global memory:
+//   * the half-row logits carry the launch's epoch in their high 32 bits (64-bit stores and
+//     loads are single-copy atomic); one warp per CTA polls them until every entry shows the
+//     current epoch, so the data itself is the barrier (one L2 round trip after the last
+//     producer), then computes softmax + top-k itself, identically in every CTA (fixed reduction
+//     order, ties to the lower index);
+//   * h (every CTA needs all of it for its output rows): every warp stores its h values and
+//     arrives on a 64-bit counter with a release reduction; thread 0 of each CTA polls the
+//     counter (acquire) and the CTA then reads h.
 //
 // Weights move by bulk copies (cp.async.bulk, completion counted on mbarriers): the CTA's
 // shared-expert rows and the shared expert's W2 rows are requested at entry; right after the
-// routing step one warp requests the routed rows (two copies per warp: its units' W1 rows and
-// W3 rows are contiguous) and every routed expert's W2 rows of this CTA's output rows, which are
-// in shared memory long before h is complete.
+// routing step the routing warp requests the routed W1/W3 rows in chunks of 4 units (their rows
+// are contiguous) and every routed expert's W2 rows of this CTA's output rows, which are in
+// shared memory long before h is complete.  Warps waiting for the routing park on a named
+// barrier, so they take no issue slots from the routing warp.
 //
 // Dot products are integer: IQ4_XS codes are exact bytes (kvalue + 128); activations (x, and
 // each slot of h) are rounded to 16-bit fixed point with a power-of-two scale per 32-value
@@ -33,13 +35,14 @@
 // accumulates a sub-block's code x activation products exactly in int32, which is then scaled
 // by d * (ls - 32) / activation scale and accumulated in f32 in a fixed order.
 //
-// Epochs: thread 0 of every CTA reads a 64-bit counter at entry, and increments it by one as
-// the CTA's last act, so a launch of G CTAs adds G.  No CTA can finish before every CTA of its
-// launch has produced its h entries, each of which it does after reading the counter, so all
-// CTAs of a launch read the same value v and use epoch v / G + 1.  Nothing is reset between
-// launches (CUDA-graph replay is safe).  Every wait gives up after 100 ms, records kDevTimeout
-// and lets the CTA finish (in-flight bulk copies are drained first); moe_sync then clears the
-// counter and the exchange entries.
+// Epochs: thread 0 of every CTA reads the counter at entry (v); each of the launch's 16 G warps
+// adds 1 after its h stores, so a launch adds 16 G.  No warp can arrive before every CTA of its
+// launch has read the counter (an arrival needs the routing, which needs every CTA's logits,
+// each published after that CTA's read), so all CTAs read the same v, use epoch v / (16 G) + 1
+// for the logits and wait for v + 16 G.  Nothing is reset between launches (CUDA-graph replay
+// is safe).  Every wait gives up after 100 ms, records kDevTimeout and lets the CTA finish
+// (in-flight bulk copies are drained first); moe_sync then clears the counter and the exchange
+// entries.
 #include <cuda_runtime.h>
 
 #include "moe_common.cuh"
