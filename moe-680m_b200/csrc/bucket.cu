@@ -180,17 +180,149 @@ bucket_scatter_kernel(const uint2* __restrict__ topk, int M, int E, int k, int r
     }
 }
 
+// ---- small batches: count, scan and scatter in one CTA ---------------------------------------
+// For up to kSmallMaxTokens tokens one CTA of 1024 threads does all three steps (one launch
+// instead of three): tokens are taken 1024 at a time, one per thread; per-warp bitmasks give
+// each slot's rank among the chunk's earlier tokens exactly as in the three-launch path, so the
+// results are identical.
+constexpr int kSmallThreads = 1024;
+constexpr int kSmallWarps = kSmallThreads / 32;
+constexpr int kSmallMaxTokens = 2048;
+
+__device__ __forceinline__ void small_masks(uint32_t* masks, int nb, const uint2* topk, int t, int M, int E,
+                                            int k, int routed, int has_shared, int* status) {
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    __syncthreads();  // the previous chunk's masks are no longer read
+    for (int i = tid; i < kSmallWarps * nb; i += kSmallThreads) masks[i] = 0u;
+    __syncthreads();
+    if (t < M) {
+        const uint2* rec = topk + static_cast<size_t>(t) * (k + 1);
+        for (int s = 0; s < (routed ? k : 0); ++s) {
+            if (rec[1 + s].x == kNoExpert) continue;  // empty slot
+            const int e = static_cast<int>(rec[1 + s].x);
+            if (e < 0 || e >= E) { set_dev_error(status, kDevBadExpert); continue; }
+            atomicOr(&masks[warp * nb + e], 1u << lane);
+        }
+        if (has_shared && rec[0].x != kNoExpert) atomicOr(&masks[warp * nb + E], 1u << lane);
+    }
+    __syncthreads();
+}
+
+__global__ void __launch_bounds__(kSmallThreads)
+bucket_small_kernel(const uint2* __restrict__ topk, int M, int E, int k, int routed, int has_shared,
+                    int* __restrict__ ranges, int* __restrict__ sorted_tok, float* __restrict__ sorted_w,
+                    int* __restrict__ slot_pos, Chunk* __restrict__ chunks, int max_chunks, TileLists lists,
+                    int* __restrict__ counters, int* status) {
+    extern __shared__ uint32_t masks[];  // [32][E+1]
+    __shared__ int cnt[kMaxExperts + 1], base[kMaxExperts + 1];
+    __shared__ int4 warp_tot[32];
+    const int nb = E + 1, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    if (tid < nb) cnt[tid] = 0;
+    // 1. counts
+    for (int t0 = 0; t0 < M; t0 += kSmallThreads) {
+        small_masks(masks, nb, topk, t0 + tid, M, E, k, routed, has_shared, status);
+        if (tid < nb) {
+            int c = 0;
+#pragma unroll 4
+            for (int w = 0; w < kSmallWarps; ++w) c += __popc(masks[w * nb + tid]);
+            cnt[tid] += c;
+        }
+    }
+    // 2. scan: ranges, chunk list, tensor-core tile lists
+    const int c_e = tid < nb ? cnt[tid] : 0;
+    const int4 v = make_int4(c_e, (c_e + kGemvTok - 1) / kGemvTok, (c_e + lists.n13 - 1) / lists.n13,
+                             (c_e + lists.n2 - 1) / lists.n2);
+    int4 total;
+    const int4 first = block_exscan4(v, warp_tot, total);
+    if (tid < nb) {
+        ranges[tid] = first.x;
+        base[tid] = first.x;
+        int ci = first.y;
+        for (int q = 0; q < c_e && ci < max_chunks; q += kGemvTok, ++ci)
+            chunks[ci] = Chunk{tid, first.x + q, min(kGemvTok, c_e - q), 0};
+        if (lists.t13) {
+            int ti = first.z;
+            for (int q = 0; q < c_e && ti < lists.max13; q += lists.n13, ++ti)
+                lists.t13[ti] = TcTile{tid, first.x + q, min(lists.n13, c_e - q), 0};
+            ti = first.w;
+            for (int q = 0; q < c_e && ti < lists.max2; q += lists.n2, ++ti)
+                lists.t2[ti] = TcTile{tid, first.x + q, min(lists.n2, c_e - q), 0};
+        }
+    }
+    if (tid == 0) {
+        ranges[nb] = total.x;
+        int c = total.y, a13 = total.z, a2 = total.w;
+        if (c > max_chunks) { set_dev_error(status, kDevOverflow); c = max_chunks; }
+        if (lists.t13) {
+            if (a13 > lists.max13) { set_dev_error(status, kDevOverflow); a13 = lists.max13; }
+            if (a2 > lists.max2) { set_dev_error(status, kDevOverflow); a2 = lists.max2; }
+        } else {
+            a13 = a2 = 0;
+        }
+        counters[0] = c;
+        counters[1] = a13;
+        counters[2] = a2;
+    }
+    __syncthreads();  // base
+    // 3. positions, chunk by chunk in token order
+    const uint32_t lt = (1u << lane) - 1u;
+    const int ns = k + (has_shared ? 1 : 0);
+    for (int t0 = 0; t0 < M; t0 += kSmallThreads) {
+        const int t = t0 + tid;
+        small_masks(masks, nb, topk, t, M, E, k, routed, has_shared, status);
+        if (t < M) {
+            const uint2* rec = topk + static_cast<size_t>(t) * (k + 1);
+            int* sp = slot_pos + static_cast<size_t>(t) * ns;
+            for (int s = 0; s < ns; ++s) {
+                const uint2 r = rec[s == k ? 0 : 1 + s];  // slot k: the shared expert, record entry 0
+                int e;
+                if (s == k) e = r.x == kNoExpert ? -1 : E;
+                else e = (!routed || r.x >= static_cast<uint32_t>(E)) ? -1 : static_cast<int>(r.x);
+                if (e < 0) { sp[s] = -1; continue; }
+                int pos = base[e] + __popc(masks[warp * nb + e] & lt);
+                for (int w = 0; w < warp; ++w) pos += __popc(masks[w * nb + e]);
+                sorted_tok[pos] = t;
+                sorted_w[pos] = __uint_as_float(r.y);
+                sp[s] = pos;
+            }
+        }
+        __syncthreads();  // every slot of the chunk has read base
+        if (tid < nb) {
+            int c = 0;
+#pragma unroll 4
+            for (int w = 0; w < kSmallWarps; ++w) c += __popc(masks[w * nb + tid]);
+            base[tid] += c;
+        }
+    }
+}
+
 }  // namespace
 
 void launch_bucket(int E, int k, bool routed, bool has_shared, const uint2* topk, int M, Workspace& ws,
                    int* ranges, int* sorted_tok, float* sorted_w, int* slot_pos, int* status,
                    cudaStream_t s) {
+    TileLists tl{ws.tiles13, static_cast<int>(ws.max_tiles13), ws.tiles2,
+                 static_cast<int>(ws.max_tiles2), tc_max_n(13), tc_max_n(2)};
+    if (M <= kSmallMaxTokens) {  // one launch
+        const size_t smem_s = static_cast<size_t>(kSmallWarps) * (E + 1) * sizeof(uint32_t);
+        static bool attr_set[64] = {};
+        int dev = 0;
+        cudaGetDevice(&dev);
+        if (dev < 0 || dev >= 64 || !attr_set[dev]) {
+            cudaFuncSetAttribute(bucket_small_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(kSmallWarps * (kMaxExperts + 1) * sizeof(uint32_t)));
+            if (dev >= 0 && dev < 64) attr_set[dev] = true;
+        }
+        bucket_small_kernel<<<1, kSmallThreads, smem_s, s>>>(topk, M, E, k, routed ? 1 : 0, has_shared ? 1 : 0,
+                                                             ranges, sorted_tok, sorted_w, slot_pos, ws.chunks,
+                                                             static_cast<int>(ws.max_chunks), tl, ws.counters,
+                                                             status);
+        return;
+    }
     const int n_tiles = (M + kTile - 1) / kTile;
     const size_t smem = 8 * (E + 1) * sizeof(uint32_t);
     bucket_count_kernel<<<n_tiles, kTile, smem, s>>>(topk, M, E, k, routed ? 1 : 0, has_shared ? 1 : 0,
                                                      ws.tilecnt, status);
-    TileLists tl{ws.tiles13, static_cast<int>(ws.max_tiles13), ws.tiles2,
-                 static_cast<int>(ws.max_tiles2), tc_max_n(13), tc_max_n(2)};
     bucket_scan_kernel<<<1, kScanThreads, 0, s>>>(ws.tilecnt, n_tiles, E, ranges, ws.chunks,
                                           static_cast<int>(ws.max_chunks), tl, ws.counters, status);
     bucket_scatter_kernel<<<n_tiles, kTile, smem, s>>>(topk, M, E, k, routed ? 1 : 0, has_shared ? 1 : 0,

@@ -154,9 +154,9 @@ def test_exact_ties_pick_lower_index(ctx):
     assert (w[:, 0] == w[:, 1]).all() and (w[:, 1] == w[:, 2]).all()
 
 
-def test_bucket_matches_oracle(ctx):
+@pytest.mark.parametrize("m", [700, 1500, 3000])  # one-launch path (<= 2048 tokens), three-launch path
+def test_bucket_matches_oracle(ctx, m):
     lid, hl = model(ctx, 1234, FULL, 1.1)
-    m = 700
     x = synth.tokens(1234, 99, m, FULL.hidden)
     xo = ctx.put(x)
     k, E = FULL.top_k, FULL.n_experts
