@@ -28,6 +28,7 @@ pub const MOE_E_DEVICE: i32 = -5;
 pub const MOE_F_SHARED: u32 = 1;
 pub const MOE_F_SHARED_GATE: u32 = 2;
 pub const MOE_F_EXPERT_SUBSET: u32 = 4;
+pub const MOE_F_REF36: u32 = 8;
 pub const MOE_NO_EXPERT: u32 = 0xFFFF_FFFF;
 
 pub const MOE_FT_NO_SHARED: u32 = 1;

@@ -51,6 +51,13 @@ typedef struct moe_ctx moe_ctx;
                                   and moe_forward_topk, and nothing may be routed to a missing
                                   expert (no counterpart in the single-device reference) */
 
+#define MOE_F_REF36 8u   /* expert weights in the reference's own format: 36-byte blocks of 32 weights
+                            (shaders/common.glsl:59-86), each matrix stored [in][out] with weight
+                            (k, n) at flat index k*out + n (shaders/w1_w3_fused_m1.comp:46-47,
+                            w2_scatter_m1.comp:41): W1/W3 [hidden][inter], W2 [inter][hidden],
+                            hidden*inter/32*36 bytes each.  A compatibility path (CUDA cores, f32,
+                            K-split grouped GEMV); hidden and inter multiples of 512 */
+
 /* Expert id of an empty routed entry in a routing record (skipped by bucketing). */
 #define MOE_NO_EXPERT 0xFFFFFFFFu
 

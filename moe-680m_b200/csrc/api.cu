@@ -159,8 +159,27 @@ int ensure_ws(Ctx* c, uint32_t M, uint32_t E, uint32_t k, uint32_t slots, uint32
 }
 
 int ensure_layer_ws(Ctx* c, const Layer& L, uint32_t M) {
-    return ensure_ws(c, M, L.spec.n_experts, L.spec.top_k, static_cast<uint32_t>(L.slots()),
-                     L.spec.hidden, L.spec.inter);
+    int rc = ensure_ws(c, M, L.spec.n_experts, L.spec.top_k, static_cast<uint32_t>(L.slots()),
+                       L.spec.hidden, L.spec.inter);
+    if (rc || !L.ref36()) return rc;
+    // the reference-format path's K-split partial sums, grown like the workspace
+    const size_t need = moe::ref36_scratch_bytes(static_cast<int>(c->ws.cap_tokens * c->ws.cap_slots),
+                                                 static_cast<int>(c->ws.cap_hidden), static_cast<int>(c->ws.cap_inter));
+    if (need <= c->ref36_scratch_bytes) return MOE_OK;
+    cudaStreamSynchronize(c->stream);
+    if (c->ref36_scratch) cudaFree(c->ref36_scratch);
+    c->ref36_scratch = nullptr;
+    c->ref36_scratch_bytes = 0;
+    void* p = nullptr;
+    const cudaError_t e = cudaMalloc(&p, need);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return fail(c, MOE_E_OOM, "reference-format scratch of %zu bytes: %s", need, cudaGetErrorString(e));
+    }
+    c->ref36_scratch = static_cast<float*>(p);
+    c->ref36_scratch_bytes = need;
+    c->ws_gen += 1;  // captured graphs refer to the old buffer
+    return MOE_OK;
 }
 
 // The decode kernel's grid-synchronisation words in the status block.
@@ -301,7 +320,11 @@ int run_experts(Ctx* c, const Layer& L, uint32_t M, bool routed, bool shared, fl
     const int path = choose_path(c, L, M);
     if (path != moe::kPathGemv && !L.wmaps)
         return fail(c, MOE_E_UNSUPPORTED, "tensor-core path needs hidden and inter multiples of 512");
-    if (path == moe::kPathGemv) {
+    if (path == moe::kPathGemv && L.ref36()) {
+        const int max_chunks = moe::max_chunks_for(static_cast<int>(M), slots, E);
+        moe::launch_ref36_experts(L, ws, static_cast<int>(M), slots, max_chunks, c->ref36_scratch, c->stream);
+        stage(c, "ref36", 4);
+    } else if (path == moe::kPathGemv) {
         const int max_chunks = moe::max_chunks_for(static_cast<int>(M), slots, E);
         moe::launch_gemv13(L, ws.io, ws, static_cast<int>(M), max_chunks, c->sm_count, c->stream);
         stage(c, "gemv13", 1);
@@ -517,6 +540,7 @@ void moe_ctx_destroy(moe_ctx* c) {
     int* status = c->ws.status;
     free_ws(c->ws);
     if (status) cudaFree(status);
+    if (c->ref36_scratch) cudaFree(c->ref36_scratch);
     if (c->owns && c->base) cudaFree(c->base);
     for (cudaEvent_t e : c->ev) cudaEventDestroy(e);
     if (c->own_stream) cudaStreamDestroy(c->own_stream);
@@ -605,7 +629,12 @@ int moe_layer_create(moe_ctx* c, const moe_layer_spec* spec, const uint64_t* w1,
     if (s.flags & MOE_F_SHARED_GATE) {
         if (!off_ok(c, s.shared_gate, H * 4, 16)) return fail(c, MOE_E_INVALID, "shared_gate offset invalid");
     }
-    const uint64_t b13 = I * (H / 256) * 136, b2 = H * (I / 256) * 136;
+    const bool ref36 = (s.flags & MOE_F_REF36) != 0;
+    if (ref36 && !moe::ref36_supported(static_cast<int>(H), static_cast<int>(I)))
+        return fail(c, MOE_E_UNSUPPORTED, "MOE_F_REF36 needs hidden and inter multiples of 512");
+    // GGUF IQ4_XS rows of 136-byte blocks, or the reference's 36-byte blocks of 32 weights
+    const uint64_t b13 = ref36 ? H * I / 32 * 36 : I * (H / 256) * 136;
+    const uint64_t b2 = ref36 ? H * I / 32 * 36 : H * (I / 256) * 136;
     std::vector<const uint8_t*> tab(3 * (E + 1), nullptr);
     const bool subset = (s.flags & MOE_F_EXPERT_SUBSET) != 0;
     for (uint64_t e = 0; e < E; ++e) {
@@ -649,7 +678,7 @@ int moe_layer_create(moe_ctx* c, const moe_layer_spec* spec, const uint64_t* w1,
         else
             cudaFree(wsd);
     }
-    if (moe::tc_supported(static_cast<int>(H), static_cast<int>(I))) {
+    if (!ref36 && moe::tc_supported(static_cast<int>(H), static_cast<int>(I))) {
         // raw IQ4_XS tensor maps for the tensor-core path: [W1 | W3 | W2][E+1]
         std::vector<CUtensorMap> maps(3 * (E + 1));
         bool ok = true;
@@ -808,7 +837,9 @@ int moe_layer_set_next(moe_ctx* c, uint32_t layer_id, int32_t next_id) {
     if (N->has_shared() && N->tab) {
         std::vector<const uint8_t*> t(3 * (E + 1));
         MOE_CUDA(c, cudaMemcpy(t.data(), N->tab, t.size() * sizeof(void*), cudaMemcpyDeviceToHost));
-        const uint64_t b13 = I * (H / 256) * 136, b2 = H * (I / 256) * 136;
+        const bool ref36 = N->ref36();
+        const uint64_t b13 = ref36 ? H * I / 32 * 36 : I * (H / 256) * 136;
+        const uint64_t b2 = ref36 ? H * I / 32 * 36 : H * (I / 256) * 136;
         for (int i = 0; i < 3; ++i) {
             L->next_shared[i] = t[i * (E + 1) + E];
             L->next_shared_bytes[i] = i == 2 ? b2 : b13;

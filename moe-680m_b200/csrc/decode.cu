@@ -746,7 +746,7 @@ bool decode_supported(const Layer& L, int sm_count) {
     // grid large enough for the per-CTA slices of the shared memory plan, and at most one router
     // half-row per warp 4..15
     const int T = 2 * (static_cast<int>(L.spec.n_experts) + 1);
-    return L.tab_aligned16 && L.spec.hidden <= kMaxH && L.spec.hidden % 512 == 0 &&
+    return !L.ref36() && L.tab_aligned16 && L.spec.hidden <= kMaxH && L.spec.hidden % 512 == 0 &&
            L.spec.inter <= kMaxI && L.spec.inter % 512 == 0 && L.spec.n_experts <= kMaxExperts &&
            sm_count >= kMinGrid && T <= (kDWarps - 4) * sm_count;
 }

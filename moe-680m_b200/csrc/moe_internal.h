@@ -60,6 +60,7 @@ struct Layer {
     }
     bool has_shared() const { return (spec.flags & MOE_F_SHARED) != 0; }
     bool subset() const { return (spec.flags & MOE_F_EXPERT_SUBSET) != 0; }
+    bool ref36() const { return (spec.flags & MOE_F_REF36) != 0; }
     int slots() const { return static_cast<int>(spec.top_k) + (has_shared() ? 1 : 0); }
 };
 
@@ -254,6 +255,8 @@ struct Ctx {
     std::string err;
     std::vector<Layer> layers;
     Workspace ws;
+    float* ref36_scratch = nullptr;  // K-split partial sums of MOE_F_REF36 layers
+    size_t ref36_scratch_bytes = 0;
     EpState ep;
 };
 
@@ -334,6 +337,12 @@ void launch_rms_norm(const float* x, float* y, int M, int H, float eps, cudaStre
 void launch_silu_mul(const float* g, const float* u, float* y, uint64_t n, int sm_count, cudaStream_t s);
 void launch_dequant(const uint8_t* src, uint64_t n_blocks, float* dst, cudaStream_t s);
 void launch_dequant_ref36(const uint8_t* src, uint64_t n_blocks, float* dst, cudaStream_t s);
+// Expert products on the reference's 36-byte block format (MOE_F_REF36 layers): writes ws.h
+// and ws.ypart like the GEMV path; scratch holds ref36_scratch_bytes(S, H, I).
+bool ref36_supported(int H, int I);
+size_t ref36_scratch_bytes(int S, int H, int I);
+void launch_ref36_experts(const Layer& L, const Workspace& ws, int M, int slots, int max_chunks, float* scratch,
+                          cudaStream_t s);
 bool vocab_supported(int H, int M);
 // Returns -1 when the shape does not fit the kernel's shared memory (nothing launched).
 int launch_vocab(const uint8_t* w, int V, int H, const float* x, int M, float* logits, uint32_t* ids,

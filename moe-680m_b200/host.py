@@ -23,6 +23,7 @@ MOE_OK = 0
 MOE_F_SHARED = 1
 MOE_F_SHARED_GATE = 2
 MOE_F_EXPERT_SUBSET = 4
+MOE_F_REF36 = 8
 MOE_NO_EXPERT = 0xFFFFFFFF
 MOE_FT_NO_SHARED, MOE_FT_SHARED_ONLY, MOE_FT_UNSCALED = 1, 2, 4
 MOE_EP_TRANSPORT_NCCL, MOE_EP_TRANSPORT_PEER = 0, 1
