@@ -187,7 +187,7 @@ bucket_scatter_kernel(const uint2* __restrict__ topk, int M, int E, int k, int r
 // results are identical.
 constexpr int kSmallThreads = 1024;
 constexpr int kSmallWarps = kSmallThreads / 32;
-constexpr int kSmallMaxTokens = 2048;
+constexpr int kSmallMaxTokens = 1024;
 
 __device__ __forceinline__ void small_masks(uint32_t* masks, int nb, const uint2* topk, int t, int M, int E,
                                             int k, int routed, int has_shared, int* status) {

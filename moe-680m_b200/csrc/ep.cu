@@ -165,33 +165,29 @@ __global__ void ep_combine_kernel(const uint32_t* __restrict__ mask, const int* 
 // partial rows read straight from the expert ranks' output blocks (NVLink loads/stores through
 // CUDA IPC mappings; plain loads and stores only) --------------------------------------------
 
-// Warp per token: its row and reduced record to block my_rank of every rank it visits.
-__global__ void ep_push_kernel(const float* __restrict__ x, const uint2* __restrict__ topk,
-                               const uint32_t* __restrict__ mask, const int* __restrict__ pos, int M, int H,
-                               int k, int epr, int n_ranks, int my_rank, EpPeers P) {
-    const int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
-    if (t < M) {
-        const uint32_t m = mask[t];
-        const float4* src = reinterpret_cast<const float4*>(x + static_cast<size_t>(t) * H);
-        const uint2* rec = topk + static_cast<size_t>(t) * (k + 1);
-        const uint2 r = lane <= k ? rec[lane] : make_uint2(0, 0);
-        for (int d = 0; d < n_ranks; ++d) {
-            if (!((m >> d) & 1u)) continue;
-            const size_t p = static_cast<size_t>(pos[static_cast<size_t>(t) * n_ranks + d]);
-            float4* dst = reinterpret_cast<float4*>(P.x[d] + p * H);
-            for (int i = lane; i < H / 4; i += 32) dst[i] = src[i];
-            if (lane <= k) {
-                uint2 o = r;
-                if (lane > 0) {
-                    const uint32_t e = r.x;
-                    o.x = (e != kNoExpert && e / static_cast<uint32_t>(epr) == static_cast<uint32_t>(d))
-                              ? e : kNoExpert;
-                } else if (d != my_rank) {
-                    o.x = kNoExpert;
-                }
-                P.rec[d][p * (k + 1) + lane] = o;
-            }
+// CTA per (token, destination rank): the token's row and reduced record to block my_rank of
+// rank d when the token visits d.  One CTA per pair (instead of one warp per token looping over
+// its ranks) keeps thousands of NVLink stores in flight from every SM.
+constexpr int kPushThreads = 128;
+
+__global__ void __launch_bounds__(kPushThreads)
+ep_push_kernel(const float* __restrict__ x, const uint2* __restrict__ topk, const uint32_t* __restrict__ mask,
+               const int* __restrict__ pos, int M, int H, int k, int epr, int n_ranks, int my_rank, EpPeers P) {
+    const int t = blockIdx.x, d = blockIdx.y, tid = threadIdx.x;
+    if (t >= M || !((mask[t] >> d) & 1u)) return;
+    const size_t p = static_cast<size_t>(pos[static_cast<size_t>(t) * n_ranks + d]);
+    const float4* src = reinterpret_cast<const float4*>(x + static_cast<size_t>(t) * H);
+    float4* dst = reinterpret_cast<float4*>(P.x[d] + p * H);
+    for (int i = tid; i < H / 4; i += kPushThreads) dst[i] = __ldg(src + i);
+    if (tid <= k) {
+        uint2 o = topk[static_cast<size_t>(t) * (k + 1) + tid];
+        if (tid > 0) {
+            const uint32_t e = o.x;
+            o.x = (e != kNoExpert && e / static_cast<uint32_t>(epr) == static_cast<uint32_t>(d)) ? e : kNoExpert;
+        } else if (d != my_rank) {
+            o.x = kNoExpert;  // the shared expert runs on the token's own rank
         }
+        P.rec[d][p * (k + 1) + tid] = o;
     }
     __threadfence_system();
 }
@@ -247,16 +243,27 @@ __global__ void ep_pull_combine_kernel(const uint32_t* __restrict__ mask, const 
     const int c = (blockIdx.y * blockDim.x + threadIdx.x) * 4;
     if (c >= H) return;
     const uint32_t m = mask[t];
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int d = 0; d < n_ranks; ++d) {
-        if (!((m >> d) & 1u)) continue;
-        const size_t p = static_cast<size_t>(pos[static_cast<size_t>(t) * n_ranks + d]);
-        const float4 y = *reinterpret_cast<const float4*>(P.y[d] + p * H + c);
-        acc.x += y.x; acc.y += y.y; acc.z += y.z; acc.w += y.w;
+    // every remote row is requested before any is added (the NVLink round trips overlap), then
+    // the rows are summed in rank order
+    float4 y[kMaxEpRanks];
+#pragma unroll
+    for (int d = 0; d < kMaxEpRanks; ++d) {
+        y[d] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (d < n_ranks && ((m >> d) & 1u)) {
+            const size_t p = static_cast<size_t>(pos[static_cast<size_t>(t) * n_ranks + d]);
+            y[d] = *reinterpret_cast<const float4*>(P.y[d] + p * H + c);
+        }
     }
     const size_t row = static_cast<size_t>(t) * H + c;
     float4 r = make_float4(0.f, 0.f, 0.f, 0.f);
     if (resid) r = *reinterpret_cast<const float4*>(resid + row);
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int d = 0; d < kMaxEpRanks; ++d) {
+        if (d < n_ranks && ((m >> d) & 1u)) {
+            acc.x += y[d].x; acc.y += y[d].y; acc.z += y[d].z; acc.w += y[d].w;
+        }
+    }
     r.x = fmaf(scale, acc.x, r.x); r.y = fmaf(scale, acc.y, r.y);
     r.z = fmaf(scale, acc.z, r.z); r.w = fmaf(scale, acc.w, r.w);
     *reinterpret_cast<float4*>(out + row) = r;
@@ -267,8 +274,8 @@ __global__ void ep_pull_combine_kernel(const uint32_t* __restrict__ mask, const 
 void launch_ep_push(const float* x, const uint2* topk, EpPlan plan, int M, int H, int k, int epr, int n_ranks,
                     int my_rank, int capacity, const EpPeers& P, cudaStream_t s) {
     if (M > 0)
-        ep_push_kernel<<<(M * 32 + 255) / 256, 256, 0, s>>>(x, topk, plan.mask, plan.pos, M, H, k, epr, n_ranks,
-                                                            my_rank, P);
+        ep_push_kernel<<<dim3(M, n_ranks), kPushThreads, 0, s>>>(x, topk, plan.mask, plan.pos, M, H, k, epr, n_ranks,
+                                                                 my_rank, P);
     ep_fill_kernel<<<32, 256, 0, s>>>(M > 0 ? plan.offsets + n_ranks : nullptr, n_ranks, capacity, k, P);
 }
 

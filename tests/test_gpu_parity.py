@@ -154,7 +154,7 @@ def test_exact_ties_pick_lower_index(ctx):
     assert (w[:, 0] == w[:, 1]).all() and (w[:, 1] == w[:, 2]).all()
 
 
-@pytest.mark.parametrize("m", [700, 1500, 3000])  # one-launch path (<= 2048 tokens), three-launch path
+@pytest.mark.parametrize("m", [700, 1024, 1500, 3000])  # one-launch path (<= 1024 tokens), three-launch path
 def test_bucket_matches_oracle(ctx, m):
     lid, hl = model(ctx, 1234, FULL, 1.1)
     x = synth.tokens(1234, 99, m, FULL.hidden)
