@@ -80,12 +80,11 @@ constexpr uint64_t kSpinLimitNs = 100000000ull;  // 100 ms
 constexpr int kMaxH = 2048;                      // decode_supported limits
 constexpr int kMaxI = 512;
 constexpr int kMinGrid = 144;                    // per-CTA slices below are sized for G >= 144
-constexpr int kMaxShUnits = (kMaxI + kMinGrid - 1) / kMinGrid;                // 4
-constexpr int kMaxRoutedUnits = (kMaxTopK * kMaxI + kMinGrid - 1) / kMinGrid;  // 32 = 2 per warp
-constexpr int kMaxRows2 = (kMaxH + kMinGrid - 1) / kMinGrid;                  // 16 = 1 per warp
-static_assert(kMaxRoutedUnits <= 2 * kDWarps, "two routed units per warp");
+constexpr int kUnits = 32;                        // gate/up units per CTA: one sub-block of h
+constexpr int kMaxRoutedUnits = kUnits;            // 2 per warp
+constexpr int kMaxRows2 = (kMaxH + kMinGrid - 1) / kMinGrid;                  // 15
+static_assert(kUnits == 2 * kDWarps, "two units per warp");
 static_assert(kMaxRows2 <= kDWarps, "one output row per warp");
-static_assert(kMaxRoutedUnits <= 2 * kRouteWarp, "the routing warp itself has no routed units");
 // The routed rows arrive in chunks of 4 units (one bulk copy of 4 W1 rows and one of 4 W3 rows;
 // a chunk that straddles two slots takes two copies per matrix), each chunk on its own mbarrier:
 // few large copies (the bulk-copy unit takes ~70 cycles per request) that still let the warps of
@@ -102,9 +101,8 @@ constexpr int kQW = 20;
 constexpr int kRow13 = kMaxH / kQK * kBlockBytes;  // bytes of one W1/W3 row (1088)
 constexpr int kRow2 = kMaxI / kQK * kBlockBytes;   // bytes of one W2 row (272)
 constexpr size_t kStRouted = size_t(kDWarps) * 4 * kRow13;             // [warp][W1 a, W1 b, W3 a, W3 b]
-constexpr size_t kStShared = size_t(2) * kMaxShUnits * kRow13;         // [W1 rows][W3 rows]
 constexpr size_t kStW2 = size_t(kMaxTopK + 1) * kMaxRows2 * kRow2;      // [slot][row]
-constexpr size_t kDecodeSmem = kStRouted + kStShared + kStW2 + sizeof(float) * kMaxH +
+constexpr size_t kDecodeSmem = kStRouted + kStW2 + sizeof(float) * kMaxH +
                                sizeof(uint32_t) * (kMaxH / 32) * kQW +
                                sizeof(uint32_t) * (kMaxTopK + 1) * (kMaxI / 32) * kQW;
 
@@ -260,18 +258,6 @@ __device__ __forceinline__ void pack_subblocks(const float (&v)[N], uint32_t* ba
     }
 }
 
-// Gathers h (f32 [slots][I] in global memory) and packs it: warp w takes sub-blocks w, w + 16, ...
-__device__ __forceinline__ void gather_pack_h(const float* hx, uint32_t* hq, int nsb, int warp, int lane) {
-    constexpr int kPer = (kMaxTopK + 1) * (kMaxI / 32) / kDWarps;  // 9
-    float hv[kPer];
-#pragma unroll
-    for (int i = 0; i < kPer; ++i) {
-        const int g = warp + kDWarps * i;
-        hv[i] = g < nsb ? __ldcg(hx + g * 32 + lane) : 0.f;
-    }
-    pack_subblocks<kPer>(hv, hq, warp, nsb, lane);
-}
-
 // Order-preserving map of a float onto unsigned integers (NaN: 0, below every number).
 __device__ __forceinline__ uint32_t f2ord(float f) {
     const uint32_t u = __float_as_uint(f);
@@ -382,13 +368,13 @@ __device__ __noinline__ void route_warp(const float* lg, float gz, int E, int k,
 
 __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const __grid_constant__ DecodeArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
-    uint8_t* st_r = smem;                         // routed W1/W3 rows, per warp (then decoded W2)
-    uint8_t* st_s = st_r + kStRouted;             // shared W1 rows, then W3 rows (then decoded W2)
-    uint8_t* st_2 = st_s + kStShared;             // raw W2 rows [slot][row]
+    uint8_t* st_r = smem;                         // W1/W3 rows of this CTA's 32 units, by chunks
+    uint8_t* st_2 = st_r + kStRouted;             // raw W2 rows [slot][row]
     float* xs = reinterpret_cast<float*>(st_2 + kStW2);                 // f32 x (router)
     uint32_t* xq = reinterpret_cast<uint32_t*>(xs + kMaxH);             // [H/32][kQW]
     uint32_t* hq = xq + (kMaxH / 32) * kQW;                             // [k+1][I/32][kQW]
-    __shared__ __align__(8) uint64_t bar_sh, bar_w2, bar_c[kMaxChunks];
+    __shared__ __align__(8) uint64_t bar_w2, bar_c[kMaxChunks];
+    __shared__ float hloc[kUnits];               // this CTA's h values
     __shared__ unsigned long long s_base;
     __shared__ float red[kDWarps];
     __shared__ float wgt[kMaxTopK + 1];
@@ -403,10 +389,13 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const __grid_const
     const int ns = k + (a.has_shared ? 1 : 0);
     const int rb13 = H / kQK * kBlockBytes, rb2 = I / kQK * kBlockBytes;
     const int spr = I / 32;  // sub-blocks per h slot
-    // this CTA's slices
-    const int sh0 = a.has_shared ? c * I / G : 0, sh1 = a.has_shared ? (c + 1) * I / G : 0;
-    const int U = k * I;
-    const int u0 = c * U / G, u1 = (c + 1) * U / G;
+    // this CTA's slices: one 32-value sub-block of h (slot my_slot, values j0 .. j0 + 31; the
+    // shared expert's sub-blocks first), or none; output rows [n0, n1)
+    const int sbid = c;
+    const bool active = sbid < ns * spr;
+    const bool sh_cta = active && a.has_shared && sbid < spr;
+    const int my_slot = !active ? -1 : (a.has_shared ? (sh_cta ? k : sbid / spr - 1) : sbid / spr);
+    const int j0 = (sbid % spr) * kUnits;
     const int n0 = c * H / G, n1 = (c + 1) * H / G;
     const int nrows = n1 - n0;
     const int T = 2 * (E + (a.gate_w ? 1 : 0)), half = H / 2;
@@ -422,17 +411,9 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const __grid_const
     if (tid == 0) {
         s_failed = 0;
         s_base = ld_relaxed_u64(a.counter);
-        tc::mbar_init(&bar_sh, 1);
         tc::mbar_init(&bar_w2, 1);
         for (int i = 0; i < kMaxChunks; ++i) tc::mbar_init(&bar_c[i], 1);
         tc::fence_mbar_init();
-        // the shared expert needs no routing: its rows are requested first
-        if (sh1 > sh0) {
-            const uint32_t nb = static_cast<uint32_t>((sh1 - sh0) * rb13);
-            tc::mbar_arrive_expect_tx(&bar_sh, 2 * nb);
-            tc::bulk_load(st_s, a.tw[0][E] + static_cast<size_t>(sh0) * rb13, nb, &bar_sh);
-            tc::bulk_load(st_s + kMaxShUnits * kRow13, a.tw[1][E] + static_cast<size_t>(sh0) * rb13, nb, &bar_sh);
-        }
         // W2 rows [n0, n1) of every slot land on bar_w2: all bytes expected now, the shared
         // slot's copy issued now, the routed slots' after the routing step
         tc::mbar_arrive_expect_tx(&bar_w2, static_cast<uint32_t>(ns * nrows * rb2));
@@ -475,9 +456,23 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const __grid_const
     }
     const bool x_finite = __syncthreads_and(fin) != 0;  // also: xs, barriers, s_base, tables
     const unsigned long long base = s_base;
-    const uint32_t epoch = static_cast<uint32_t>(base / (static_cast<unsigned long long>(G) * kDWarps)) + 1u;
+    const uint32_t epoch = static_cast<uint32_t>(base / static_cast<unsigned long long>(G)) + 1u;
     if (tid < E) s_bias[tid] = bias_v;
     DEC_TRACE(1);
+    // W1/W3 rows of the CTA's 32 units (rows j0 .. j0 + 31 of one expert) in 8 chunks of 4 units,
+    // each chunk one bulk copy per matrix on its own mbarrier; lanes 0-15 of one warp issue them
+    auto issue_units = [&](const uint8_t* w1e, const uint8_t* w3e) {
+        const int ch = lane >> 1, m = lane & 1;
+        if (lane < 2 * kMaxChunks && m == 0)  // expected bytes posted before any copy is issued
+            tc::mbar_arrive_expect_tx(&bar_c[ch], static_cast<uint32_t>(2 * kChunkUnits * rb13));
+        __syncwarp();
+        if (lane < 2 * kMaxChunks)
+            tc::bulk_load(st_r + static_cast<size_t>(ch) * 2 * kChunkUnits * kRow13 + m * kChunkUnits * rb13,
+                          (m ? w3e : w1e) + static_cast<size_t>(j0 + ch * kChunkUnits) * rb13,
+                          static_cast<uint32_t>(kChunkUnits * rb13), &bar_c[ch]);
+        __syncwarp();
+    };
+    if (sh_cta && warp == 1) issue_units(a.tw[0][E], a.tw[1][E]);  // needs no routing
 
     // ---- router half-row of this warp (f32), published with the launch's epoch --------------
     if (task < T) {
@@ -549,28 +544,9 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const __grid_const
         DEC_CLOCK_W(13, kRouteWarp);
         DEC_TRACE_W(9, kRouteWarp);
         DEC_CLOCK_W(15, kRouteWarp);
-        {
-            // routed W1/W3 rows by chunks: lane (piece, chunk, matrix) = (l >> 4, (l & 15) >> 1,
-            // l & 1); piece 1 is the part of a chunk beyond its first slot
-            const int n_r = u1 - u0, nchk = (n_r + kChunkUnits - 1) / kChunkUnits;
-            const int piece = lane >> 4, ch = (lane & 15) >> 1, m = lane & 1;
-            const bool act = ch < nchk;
-            if (act && piece == 0 && m == 0)  // expected bytes posted before any copy is issued
-                tc::mbar_arrive_expect_tx(&bar_c[ch], static_cast<uint32_t>(2 * min(kChunkUnits, n_r - kChunkUnits * ch) * rb13));
-            __syncwarp();
-            if (act) {
-                const int ca = u0 + kChunkUnits * ch, cb = min(ca + kChunkUnits, u1);
-                const int send = (ca / I + 1) * I;
-                const int pa = piece == 0 ? ca : send, pb = piece == 0 ? min(cb, send) : cb;
-                if (pa < pb)
-                    tc::bulk_load(st_r + static_cast<size_t>(ch) * 2 * kChunkUnits * kRow13 + m * kChunkUnits * rb13 +
-                                      (pa - ca) * rb13,
-                                  a.tw[m][slot_e[pa / I]] + static_cast<size_t>(pa % I) * rb13,
-                                  static_cast<uint32_t>((pb - pa) * rb13), &bar_c[ch]);
-            }
-        }
+        if (active && !sh_cta) issue_units(a.tw[0][slot_e[my_slot]], a.tw[1][slot_e[my_slot]]);
         __syncwarp();
-        named_arrive(kDThreads);  // the parked warps may read the routing now
+        if (!sh_cta) named_arrive(kDThreads);  // the parked warps may read the routing now
         if (lane < k)  // routed W2 rows [n0, n1) of slot `lane`
             tc::bulk_load(st_2 + static_cast<size_t>(lane) * kMaxRows2 * kRow2,
                           a.tw[2][slot_e[lane]] + static_cast<size_t>(n0) * rb2, static_cast<uint32_t>(nrows * rb2),
@@ -579,65 +555,53 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const __grid_const
         DEC_TRACE_W(4, kRouteWarp);
     }
 
-    // ---- gate/up units: the shared unit of warps 8.. (if any), then routed units 2w, 2w + 1 --
-    float* hx = reinterpret_cast<float*>(a.xh);  // h exchange, f32 [k+1][I]
+    // ---- gate/up units: warp w computes units 2w, 2w + 1 (rows j0 + 2w, j0 + 2w + 1) ----------
     {
-        // shared units on warps 8, 9, 10, 12: none on sub-partition 3, the routing warp's
-        const int wsh = warp == 12 ? 3 : (warp >= 8 && warp <= 10 ? warp - 8 : kMaxShUnits);
-        const bool has_sh = wsh < sh1 - sh0;
-        const int ua = u0 + 2 * warp;
-        const int nu = max(0, min(2, u1 - ua));  // routed units of this warp
+        // in a routed CTA every warp but the routing warp parks on barrier 1 during the routing
+        // step (parked warps issue nothing); a shared-expert CTA's data needs no routing
+        if (!sh_cta && warp != kRouteWarp) named_sync(kDThreads);
+        DEC_CLK0(11);
+        if (active) {
+            const int ch = (2 * warp) / kChunkUnits;
+            if (!bar_wait(&bar_c[ch], 0)) { set_dev_error(a.status, kDevTimeout); if (lane == 0) s_failed = 1; }
+            DEC_CLK0(12);
 #pragma unroll 1
-        for (int q = 0; q < 3; ++q) {
-            if (q == 0 && !has_sh) continue;
-            // every warp but the routing warp parks on barrier 1 during the routing step (parked
-            // warps issue nothing)
-            if (q == 1 && warp != kRouteWarp) {
-                named_sync(kDThreads);
-            }
-            if (q == 1) DEC_CLK0(11);
-            const uint8_t *s1, *s3;
-            int slot, j;
-            if (q == 0) {
-                if (!bar_wait(&bar_sh, 0)) { set_dev_error(a.status, kDevTimeout); if (lane == 0) s_failed = 1; }
-                s1 = st_s + wsh * rb13;
-                s3 = st_s + kMaxShUnits * kRow13 + wsh * rb13;
-                slot = k;
-                j = sh0 + wsh;
-            } else {
-                if (q > nu) break;
-                const int lu = 2 * warp + q - 1, ch = lu / kChunkUnits, iu = lu - ch * kChunkUnits;
-                if (q == 1 && !bar_wait(&bar_c[ch], 0)) {
-                    set_dev_error(a.status, kDevTimeout);
-                    if (lane == 0) s_failed = 1;
-                }
-                if (q == 1) DEC_CLK0(12);
-                s1 = st_r + static_cast<size_t>(ch) * 2 * kChunkUnits * kRow13 + iu * rb13;
-                s3 = s1 + kChunkUnits * rb13;
-                slot = (u0 + lu) / I;
-                j = (u0 + lu) % I;
-            }
-            float gt = 0.f, up = 0.f;
+            for (int q = 0; q < 2; ++q) {
+                const int lu = 2 * warp + q, iu = lu - ch * kChunkUnits;
+                const uint8_t* s1 = st_r + static_cast<size_t>(ch) * 2 * kChunkUnits * kRow13 + iu * rb13;
+                const uint8_t* s3 = s1 + kChunkUnits * rb13;
+                float gt = 0.f, up = 0.f;
 #pragma unroll 2
-            for (int sb = lane; sb < H / 32; sb += 32) {
-                const uint32_t* aq = xq + sb * kQW;
-                gt += subblk_dot(s1, sb, aq);
-                up += subblk_dot(s3, sb, aq);
+                for (int sb = lane; sb < H / 32; sb += 32) {
+                    const uint32_t* aq = xq + sb * kQW;
+                    gt += subblk_dot(s1, sb, aq);
+                    up += subblk_dot(s3, sb, aq);
+                }
+                gt = warp_sum(gt);
+                up = warp_sum(up);
+                float hv = silu_f(gt) * up;
+                if (!x_finite) hv = __int_as_float(0x7fc00000);
+                if (lane == 0) hloc[lu] = hv;
+                DEC_CLK0(13 + q);
             }
-            gt = warp_sum(gt);
-            up = warp_sum(up);
-            float hv = silu_f(gt) * up;
-            if (!x_finite) hv = __int_as_float(0x7fc00000);
-            if (lane == 0) __stcg(hx + static_cast<size_t>(slot) * I + j, hv);
-            DEC_CLK0(12 + q);
         }
-        // arrive: every warp of every CTA, after its own h stores (release orders them)
+    }
+    __syncthreads();  // hloc complete
+    uint32_t* hx = reinterpret_cast<uint32_t*>(a.xh);  // packed h exchange: [slots x I/32][kQW]
+    if (warp == 0) {
+        // publish this CTA's sub-block packed (16-bit pairs, its own power-of-two scale), then
+        // arrive: one arrival per CTA, after the stores (release orders the warp's stores, which
+        // __syncwarp has made visible to lane 0)
+        if (active) {
+            float v[1] = {hloc[lane]};
+            pack_subblocks<1>(v, hx + static_cast<size_t>(sbid) * kQW, 0, 1, lane);
+        }
         __syncwarp();
         if (lane == 0) asm volatile("red.release.gpu.global.add.u64 [%0], 1;" :: "l"(a.counter) : "memory");
     }
     DEC_CLK0(1);
     if (tid == 0) {  // wait for every CTA's arrival
-        const unsigned long long target = base + static_cast<unsigned long long>(G) * kDWarps;
+        const unsigned long long target = base + static_cast<unsigned long long>(G);
         const uint64_t t0 = tc::globaltimer_ns();
         while (ld_acquire_u64(a.counter) < target) {
             if (tc::globaltimer_ns() - t0 > kSpinLimitNs) {
@@ -652,9 +616,13 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const __grid_const
     __syncthreads();
     DEC_TRACE(6);
     DEC_CLK0(6);
-    // h as 16-bit pairs per sub-block: warp w packs sub-blocks w, w + 16, ... of all slots
-    DEC_CLK0(7);
-    gather_pack_h(hx, hq, ns * spr, warp, lane);
+    // every CTA's packed sub-block of h into shared memory (the slots' sub-blocks in order: the
+    // shared expert's first when there is one)
+    {
+        const int P = ns * spr;
+        for (int i = tid; i < P * kQW / 4; i += kDThreads)
+            reinterpret_cast<uint4*>(hq)[i] = __ldcg(reinterpret_cast<const uint4*>(hx) + i);
+    }
     DEC_CLK0(8);
     __syncthreads();  // hq, slot_e, wgt
     DEC_TRACE(7);
@@ -675,7 +643,9 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const __grid_const
         const int P = ns * spr;
         if (!bar_wait(&bar_w2, 0)) { set_dev_error(a.status, kDevTimeout); if (lane == 0) s_failed = 1; }
         if (tid < 3 * P) {
-            const int pp = tid % P, r0 = tid / P, s = pp / spr, sb = pp - s * spr;
+            // pair pp is exchange sub-block pp: the shared expert's sub-blocks come first
+            const int pp = tid % P, r0 = tid / P, sb = pp % spr;
+            const int s = a.has_shared ? (pp < spr ? k : pp / spr - 1) : pp / spr;
             const uint32_t* aq = hq + pp * kQW;
             const uint4 a0 = reinterpret_cast<const uint4*>(aq)[0], a1 = reinterpret_cast<const uint4*>(aq)[1];
             const uint4 a2 = reinterpret_cast<const uint4*>(aq)[2], a3 = reinterpret_cast<const uint4*>(aq)[3];
@@ -729,9 +699,9 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const __grid_const
     __syncthreads();
     DEC_TRACE(10);
     if (s_failed && tid == 0) {  // drain bulk copies still landing in this CTA's shared memory
-        bar_wait(&bar_sh, 0);
         bar_wait(&bar_w2, 0);
-        for (int ch = 0; ch < (u1 - u0 + kChunkUnits - 1) / kChunkUnits; ++ch) bar_wait(&bar_c[ch], 0);
+        if (active)
+            for (int ch = 0; ch < kMaxChunks; ++ch) bar_wait(&bar_c[ch], 0);
     }
 }
 
@@ -746,9 +716,11 @@ bool decode_supported(const Layer& L, int sm_count) {
     // grid large enough for the per-CTA slices of the shared memory plan, and at most one router
     // half-row per warp 4..15
     const int T = 2 * (static_cast<int>(L.spec.n_experts) + 1);
+    const int ns = static_cast<int>(L.spec.top_k) + (L.has_shared() ? 1 : 0);
     return !L.ref36() && L.tab_aligned16 && L.spec.hidden <= kMaxH && L.spec.hidden % 512 == 0 &&
            L.spec.inter <= kMaxI && L.spec.inter % 512 == 0 && L.spec.n_experts <= kMaxExperts &&
-           sm_count >= kMinGrid && T <= (kDWarps - 4) * sm_count;
+           sm_count >= kMinGrid && T <= (kDWarps - 4) * sm_count &&
+           ns * static_cast<int>(L.spec.inter / 32) <= sm_count;  // one h sub-block per CTA
 }
 
 int launch_decode(const Layer& L, const Workspace& ws, int* sync, int sm_count, cudaStream_t s,
