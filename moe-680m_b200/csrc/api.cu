@@ -65,9 +65,8 @@ void free_ws(Workspace& ws) {
 }
 
 // Grow the workspace to hold a forward of M tokens for (E, k, slots, H, I).
-int ensure_ws(Ctx* c, uint32_t M, uint32_t E, uint32_t k, uint32_t slots, uint32_t H,
-              uint32_t I) {
-    Workspace& ws = c->ws;
+int ensure_ws_of(Ctx* c, Workspace& ws, uint32_t M, uint32_t E, uint32_t k, uint32_t slots, uint32_t H,
+                 uint32_t I) {
     if (ws.base && M <= ws.cap_tokens && E <= ws.cap_experts && slots <= ws.cap_slots &&
         H <= ws.cap_hidden && I <= ws.cap_inter)
         return MOE_OK;
@@ -158,10 +157,26 @@ int ensure_ws(Ctx* c, uint32_t M, uint32_t E, uint32_t k, uint32_t slots, uint32
     return MOE_OK;
 }
 
+int ensure_ws(Ctx* c, uint32_t M, uint32_t E, uint32_t k, uint32_t slots, uint32_t H, uint32_t I) {
+    return ensure_ws_of(c, c->ws, M, E, k, slots, H, I);
+}
+
+bool use_shared_split(const Ctx* c, const Layer& L, uint32_t M);
+
 int ensure_layer_ws(Ctx* c, const Layer& L, uint32_t M) {
     int rc = ensure_ws(c, M, L.spec.n_experts, L.spec.top_k, static_cast<uint32_t>(L.slots()),
                        L.spec.hidden, L.spec.inter);
-    if (rc || !L.ref36()) return rc;
+    if (rc) return rc;
+    if (use_shared_split(c, L, M)) {
+        c->ws_sh.status = c->ws.status;
+        if ((rc = ensure_ws_of(c, c->ws_sh, M, L.spec.n_experts, 0, 1, L.spec.hidden, L.spec.inter))) return rc;
+        if (!c->side_stream) {
+            MOE_CUDA(c, cudaStreamCreateWithFlags(&c->side_stream, cudaStreamNonBlocking));
+            MOE_CUDA(c, cudaEventCreateWithFlags(&c->ev_fork, cudaEventDisableTiming));
+            MOE_CUDA(c, cudaEventCreateWithFlags(&c->ev_join, cudaEventDisableTiming));
+        }
+    }
+    if (!L.ref36()) return MOE_OK;
     // the reference-format path's K-split partial sums, grown like the workspace
     const size_t need = moe::ref36_scratch_bytes(static_cast<int>(c->ws.cap_tokens * c->ws.cap_slots),
                                                  static_cast<int>(c->ws.cap_hidden), static_cast<int>(c->ws.cap_inter));
@@ -297,6 +312,20 @@ int choose_path(const Ctx* c, const Layer& L, uint32_t M) {
     return (M <= 8 || !L.wmaps) ? moe::kPathGemv : moe::kPathTcTmemA;
 }
 
+// Batches of at least kSplitMinTokens on the tensor-core path run the shared expert as a separate
+// pass on a second stream, concurrently with the router, top-k and bucketing (it needs no
+// routing); the combine adds its rows after the routed slots, in the order of a single pass, so
+// the result is bit-identical.  MOE_B200_SHARED_SPLIT=0 keeps the single pass.
+constexpr uint32_t kSplitMinTokens = 64;
+
+bool use_shared_split(const Ctx* c, const Layer& L, uint32_t M) {
+    static const bool enabled = [] {
+        const char* e = std::getenv("MOE_B200_SHARED_SPLIT");
+        return !(e && e[0] == '0');
+    }();
+    return enabled && M >= kSplitMinTokens && L.has_shared() && L.wmaps && choose_path(c, L, M) != moe::kPathGemv;
+}
+
 int ensure_tmap(Ctx* c, moe::BMaps* m, const void** base, uint64_t* rows, uint64_t* cols,
                 const void* p, uint64_t r, uint64_t cl) {
     if (*base == p && *rows == r && *cols == cl) return MOE_OK;
@@ -307,10 +336,39 @@ int ensure_tmap(Ctx* c, moe::BMaps* m, const void** base, uint64_t* rows, uint64
     return MOE_OK;
 }
 
+// The shared expert over all M tokens on the side stream with its own workspace: unweighted rows
+// in ws_sh.ypart [M][H].  Forked from the context's stream after set_io; joined before the
+// combine (run_experts with split).
+int fork_shared_pass(Ctx* c, const Layer& L, uint32_t M) {
+    Workspace& w = c->ws_sh;
+    const int E = static_cast<int>(L.spec.n_experts), H = static_cast<int>(L.spec.hidden);
+    const int I = static_cast<int>(L.spec.inter);
+    cudaStream_t s = c->side_stream;
+    int rc = ensure_tmap(c, &w.xmap, &w.xmap_base, &w.xmap_rows, &w.xmap_cols, w.x16, M, H);
+    if (rc) return rc;
+    rc = ensure_tmap(c, &w.hmap, &w.hmap_base, &w.hmap_rows, &w.hmap_cols, w.h16, M, I);
+    if (rc) return rc;
+    MOE_CUDA(c, cudaEventRecord(c->ev_fork, c->stream));
+    MOE_CUDA(c, cudaStreamWaitEvent(s, c->ev_fork, 0));
+    moe::launch_shared_plan(E, static_cast<int>(M), w, s);
+    moe::launch_convert_x(c->ws.io, w.slot_pos, static_cast<int>(M), 1, H, w.x16, w.xexp, s);
+    const int tiles13 = (static_cast<int>(M) + moe::tc_max_n(13) - 1) / moe::tc_max_n(13);
+    const int tiles2 = (static_cast<int>(M) + moe::tc_max_n(2) - 1) / moe::tc_max_n(2);
+    const bool a_tmem = choose_path(c, L, M) == moe::kPathTcTmemA;
+    moe::launch_tc13(L, w.xmap, w, tiles13 * (2 * I / 128), c->sm_count, a_tmem, s);
+    moe::launch_convert_h(w.h, static_cast<int>(M), w.ranges + E + 1, I, w.h16, w.hexp, s);
+    moe::launch_tc2(L, w.hmap, w, tiles2 * (H / 128), c->sm_count, a_tmem, s);
+    c->launches += 5;
+    MOE_CUDA(c, cudaEventRecord(c->ev_join, s));
+    return check_launch(c, "shared pass");
+}
+
 // routed: use the routed entries of the records; shared: add the shared expert's slot; scale:
-// the combine scale (the layer's, or 1 for expert-parallel partial rows).
-int run_experts(Ctx* c, const Layer& L, uint32_t M, bool routed, bool shared, float scale) {
+// the combine scale (the layer's, or 1 for expert-parallel partial rows); split: the shared
+// expert's rows come from fork_shared_pass instead of a slot.
+int run_experts(Ctx* c, const Layer& L, uint32_t M, bool routed, bool shared, float scale, bool split = false) {
     Workspace& ws = c->ws;
+    if (split) shared = false;
     const int slots = static_cast<int>(L.spec.top_k) + (shared ? 1 : 0);
     const int E = static_cast<int>(L.spec.n_experts);
     moe::launch_bucket(E, static_cast<int>(L.spec.top_k), routed, shared, ws.topk,
@@ -349,7 +407,9 @@ int run_experts(Ctx* c, const Layer& L, uint32_t M, bool routed, bool shared, fl
         moe::launch_tc2(L, ws.hmap, ws, items2, c->sm_count, a_tmem, c->stream);
         stage(c, "tc2", 1);
     }
-    moe::launch_combine(L, ws, ws.io, static_cast<int>(M), slots, scale, c->stream);
+    if (split) MOE_CUDA(c, cudaStreamWaitEvent(c->stream, c->ev_join, 0));
+    moe::launch_combine(L, ws, ws.io, static_cast<int>(M), slots, scale, c->stream,
+                        split ? c->ws_sh.ypart : nullptr);
     stage(c, "combine", 1);
     return check_launch(c, "experts");
 }
@@ -378,9 +438,12 @@ int record_forward(Ctx* c, const Layer& L, uint32_t M, const float* x, const flo
         return check_launch(c, "decode");
     }
     run_set_io(c, x, resid, out);
-    int rc = run_route(c, L, M);
+    const bool split = use_shared_split(c, L, M) && c->ws_sh.cap_tokens >= M && c->side_stream;
+    int rc = split ? fork_shared_pass(c, L, M) : MOE_OK;
     if (rc) return rc;
-    return run_experts(c, L, M, true, L.has_shared(), L.spec.scale);
+    rc = run_route(c, L, M);
+    if (rc) return rc;
+    return run_experts(c, L, M, true, L.has_shared(), L.spec.scale, split);
 }
 
 // Replay (capturing on first use) the forward of (layer, M, path) with new activation pointers:
@@ -541,6 +604,11 @@ void moe_ctx_destroy(moe_ctx* c) {
     free_ws(c->ws);
     if (status) cudaFree(status);
     if (c->ref36_scratch) cudaFree(c->ref36_scratch);
+    c->ws_sh.status = nullptr;
+    free_ws(c->ws_sh);
+    if (c->ev_fork) cudaEventDestroy(c->ev_fork);
+    if (c->ev_join) cudaEventDestroy(c->ev_join);
+    if (c->side_stream) cudaStreamDestroy(c->side_stream);
     if (c->owns && c->base) cudaFree(c->base);
     for (cudaEvent_t e : c->ev) cudaEventDestroy(e);
     if (c->own_stream) cudaStreamDestroy(c->own_stream);

@@ -19,6 +19,8 @@
 #include "moe_common.cuh"
 #include "moe_internal.h"
 
+#include <algorithm>
+
 namespace moe {
 
 namespace {
@@ -296,7 +298,40 @@ bucket_small_kernel(const uint2* __restrict__ topk, int M, int E, int k, int rou
     }
 }
 
+// The bucketing of a shared-expert-only pass (no routing needed): bucket E holds every token
+// in order, so slot position = token; tensor-core tiles of up to n13 / n2 tokens.
+__global__ void shared_plan_kernel(int M, int E, int* __restrict__ ranges, int* __restrict__ sorted_tok,
+                                   float* __restrict__ sorted_w, int* __restrict__ slot_pos, TileLists lists,
+                                   int* __restrict__ counters) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < M) {
+        sorted_tok[i] = i;
+        sorted_w[i] = 1.0f;
+        slot_pos[i] = i;
+    }
+    if (i <= E) ranges[i] = 0;
+    if (i == 0) {
+        ranges[E + 1] = M;
+        int a13 = 0, a2 = 0;
+        for (int q = 0; q < M && a13 < lists.max13; q += lists.n13, ++a13)
+            lists.t13[a13] = TcTile{E, q, min(lists.n13, M - q), 0};
+        for (int q = 0; q < M && a2 < lists.max2; q += lists.n2, ++a2)
+            lists.t2[a2] = TcTile{E, q, min(lists.n2, M - q), 0};
+        counters[0] = 0;
+        counters[1] = a13;
+        counters[2] = a2;
+    }
+}
+
 }  // namespace
+
+void launch_shared_plan(int E, int M, Workspace& ws, cudaStream_t s) {
+    TileLists tl{ws.tiles13, static_cast<int>(ws.max_tiles13), ws.tiles2,
+                 static_cast<int>(ws.max_tiles2), tc_max_n(13), tc_max_n(2)};
+    const int n = std::max(M, E + 1);
+    shared_plan_kernel<<<(n + 255) / 256, 256, 0, s>>>(M, E, ws.ranges, ws.sorted_tok, ws.sorted_w, ws.slot_pos,
+                                                       tl, ws.counters);
+}
 
 void launch_bucket(int E, int k, bool routed, bool has_shared, const uint2* topk, int M, Workspace& ws,
                    int* ranges, int* sorted_tok, float* sorted_w, int* slot_pos, int* status,

@@ -587,6 +587,7 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const __grid_const
         }
     }
     __syncthreads();  // hloc complete
+    DEC_TRACE(5);
     uint32_t* hx = reinterpret_cast<uint32_t*>(a.xh);  // packed h exchange: [slots x I/32][kQW]
     if (warp == 0) {
         // publish this CTA's sub-block packed (16-bit pairs, its own power-of-two scale), then

@@ -195,7 +195,8 @@ gemv2_kernel(int H, int I, ExpertTables tabs, const Chunk* __restrict__ chunks,
 __global__ void __launch_bounds__(256)
 combine_kernel(const float* __restrict__ ypart, const int* __restrict__ slot_pos,
                const float* __restrict__ sorted_w, int ns, int H, float scale,
-               const IoArgs* __restrict__ io) {
+               const IoArgs* __restrict__ io, const float* __restrict__ ysh, const uint2* __restrict__ topk,
+               int k) {
     const float* __restrict__ resid = io->resid;
     float* __restrict__ out = io->out;
     const int t = blockIdx.x;
@@ -210,6 +211,15 @@ combine_kernel(const float* __restrict__ ypart, const int* __restrict__ slot_pos
         const float4 y = *reinterpret_cast<const float4*>(ypart + static_cast<size_t>(p) * H + c);
         acc.x = fmaf(w, y.x, acc.x); acc.y = fmaf(w, y.y, acc.y);
         acc.z = fmaf(w, y.z, acc.z); acc.w = fmaf(w, y.w, acc.w);
+    }
+    if (ysh) {  // the shared expert's row of a separate shared pass, weighted by its gate, last
+        const uint2 r0 = topk[static_cast<size_t>(t) * (k + 1)];
+        if (r0.x != kNoExpert) {
+            const float w = __uint_as_float(r0.y);
+            const float4 y = *reinterpret_cast<const float4*>(ysh + static_cast<size_t>(t) * H + c);
+            acc.x = fmaf(w, y.x, acc.x); acc.y = fmaf(w, y.y, acc.y);
+            acc.z = fmaf(w, y.z, acc.z); acc.w = fmaf(w, y.w, acc.w);
+        }
     }
     float4 r = make_float4(0.f, 0.f, 0.f, 0.f);
     if (resid) r = *reinterpret_cast<const float4*>(resid + static_cast<size_t>(t) * H + c);
@@ -276,10 +286,11 @@ void launch_gemv2(const Layer& L, const Workspace& ws, int M, int max_chunks, in
 }
 
 void launch_combine(const Layer& L, const Workspace& ws, const IoArgs* io, int M, int ns, float scale,
-                    cudaStream_t s) {
+                    cudaStream_t s, const float* ysh) {
     const int H = L.spec.hidden;
     dim3 grid(M, (H / 4 + 255) / 256);
-    combine_kernel<<<grid, 256, 0, s>>>(ws.ypart, ws.slot_pos, ws.sorted_w, ns, H, scale, io);
+    combine_kernel<<<grid, 256, 0, s>>>(ws.ypart, ws.slot_pos, ws.sorted_w, ns, H, scale, io, ysh, ws.topk,
+                                        static_cast<int>(L.spec.top_k));
 }
 
 }  // namespace moe

@@ -255,6 +255,11 @@ struct Ctx {
     std::string err;
     std::vector<Layer> layers;
     Workspace ws;
+    // the shared expert's pass of a large-batch forward, on a second stream concurrently with
+    // the routing (its own workspace; created on first use)
+    Workspace ws_sh;
+    cudaStream_t side_stream = nullptr;
+    cudaEvent_t ev_fork = nullptr, ev_join = nullptr;
     float* ref36_scratch = nullptr;  // K-split partial sums of MOE_F_REF36 layers
     size_t ref36_scratch_bytes = 0;
     EpState ep;
@@ -301,8 +306,12 @@ size_t decode_exchange_words(int E, int k, int I);
 int launch_decode(const Layer& L, const Workspace& ws, int* sync, int sm_count, cudaStream_t s,
                    const float* x = nullptr, const float* resid = nullptr, float* out = nullptr,
                    float norm_eps = -1.0f);
+// ysh: unweighted shared-expert rows [M][H] of a separate shared pass (weighted by the gate in
+// entry 0 of each routing record, added after the ns slots of ws), or null.
 void launch_combine(const Layer& L, const Workspace& ws, const IoArgs* io, int M, int ns,
-                    float scale, cudaStream_t s);
+                    float scale, cudaStream_t s, const float* ysh = nullptr);
+// Bucketing of a shared-expert-only pass: bucket E = every token in order, tiles of it.
+void launch_shared_plan(int E, int M, Workspace& ws, cudaStream_t s);
 // Expert-parallel dispatch plan (arena or workspace memory): mask[M], pos[M][n_ranks],
 // offsets[2 * n_ranks] (block starts, rows used per block).
 constexpr int kMaxEpRanks = 8;
