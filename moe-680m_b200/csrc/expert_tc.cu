@@ -14,15 +14,20 @@
 //               row) per tensor-map load, into a 2-deep shared-memory ring;
 //   producer warps (16, or 8 with MOE_B200_TC_PRODUCER_WARPS=8) dequantise from that ring
 //               (kvalues_iq4nl lookup by byte permutes, fp16 scale per 32-weight sub-block) and
-//               store the fp16 A operand, 64 K per stage, into TMEM (tcgen05.st) or 128-byte-
-//               swizzled shared memory; the warps of one 32-row quarter take turns by stage;
+//               store the fp16 A operand into TMEM (tcgen05.st; 128 K per pipeline stage) or
+//               128-byte-swizzled shared memory (64 K per stage); the warps of one 32-row
+//               quarter take turns by stage;
 //   TMA-B warp  fp16 activations of the tile's slots (pre-scaled per slot by a power of two, K
-//               permuted as below), one 16/32/64/128-row box per stage, 6 stages in flight;
+//               permuted as below), one 16/32/64/128-row box per 64 K, 4 stages in flight;
 //   MMA warp    allocates TMEM; one elected lane issues tcgen05.mma (M=128, N=16..kNMax, K=16)
 //               and tcgen05.commit;
 //   8 epilogue warps (two per TMEM lane quarter): TMEM -> registers, undo the activation
 //               scale, store f32 out[slot][feature] (gate/up pre-activations, or the unweighted
 //               down output).
+// Every stage costs one handshake per role (full / empty barriers, one arrival per warp), and
+// that fixed cost, not memory or the tensor pipe, paced the 64-K stages (measured: with the
+// dequantisation, MMAs and operand loads all stubbed out the kernel kept most of its time), so
+// a stage covers 128 K: two 64-K sub-slots in TMEM and two B boxes.
 // The accumulators are double-buffered in TMEM so the epilogue of one item overlaps the main
 // loop of the next.  Every mbarrier wait is bounded: on timeout the CTA records an error
 // status, stops issuing work, lets in-flight operations drain and frees its TMEM.
@@ -93,21 +98,27 @@ constexpr int kStagesPerChunk = 8;                 // 512 K / 64 K
 constexpr int kBStageBytes = kNMax * 128;
 constexpr int kAStageBytes = 128 * 128;            // smem-A variant
 
-// MMA stages (64 K each) in flight and depth of the raw A ring (512-K chunks).  With A in TMEM
-// (TMEM columns 256..) the default is 6 stages and a 2-chunk raw ring (measured: raw rings of 2,
-// 3 and 4 chunks perform alike, 6 stages ~1 % faster than 4); with A in shared memory, 4 and 2.
+// Pipeline depth.  With A in TMEM (columns 256..511): 4 stages of 128 K (MOE_TC_SUB = 2 sub-slots
+// of 64 K; MOE_TC_SUB=1 gives MOE_TC_STAGES stages of 64 K) and a 2-chunk raw ring (raw rings of
+// 2, 3 and 4 chunks measured alike); with A in shared memory, 4 stages of 64 K and 2 chunks.
 #ifndef MOE_TC_STAGES
 #define MOE_TC_STAGES 6
 #endif
 #ifndef MOE_TC_RAW
 #define MOE_TC_RAW 2
 #endif
+#ifndef MOE_TC_SUB
+#define MOE_TC_SUB 2
+#endif
 template <bool A_TMEM>
 struct Layout {
-    static constexpr int kStages = A_TMEM ? MOE_TC_STAGES : 4;
+    // 64-K sub-slots per pipeline stage (one barrier handshake per stage)
+    static constexpr int kSub = A_TMEM ? MOE_TC_SUB : 1;
+    static constexpr int kStages = A_TMEM ? (kSub == 2 ? 4 : MOE_TC_STAGES) : 4;
     static constexpr int kRaw = A_TMEM ? MOE_TC_RAW : 2;
+    static constexpr size_t kBSt = static_cast<size_t>(kSub) * kBStageBytes;  // B bytes per stage
     static constexpr size_t kB = 0;
-    static constexpr size_t kA = kB + static_cast<size_t>(kStages) * kBStageBytes;
+    static constexpr size_t kA = kB + static_cast<size_t>(kStages) * kBSt;
     static constexpr size_t kR = kA + (A_TMEM ? 0 : static_cast<size_t>(kStages) * kAStageBytes);
     static constexpr size_t kBars = kR + static_cast<size_t>(kRaw) * kRawBytes;
     static constexpr size_t kTotal = kBars + 256 + 1024;  // + barriers, + alignment slack
@@ -179,6 +190,9 @@ expert_tc_kernel(const __grid_constant__ BMaps bmap, const TcArgs a) {
     using Lay = Layout<A_TMEM>;
     constexpr int kRaw = Lay::kRaw;
     constexpr int kStages = Lay::kStages;
+    constexpr int kSub = Lay::kSub;
+    constexpr int kSPC = kStagesPerChunk / kSub;  // pipeline stages per raw chunk
+    static_assert(kSub == 1 || A_TMEM, "multi-slot stages need A in TMEM");
     // A producer warp waits on the slot of its own previous stage; with fewer slots than warps
     // per row quarter it would wait on a slot another warp has not filled yet and the barrier
     // parity would alias.
@@ -202,20 +216,20 @@ expert_tc_kernel(const __grid_constant__ BMaps bmap, const TcArgs a) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n_items = a.counters[a.counter_idx] * a.n_rt;
     const int nchunk = a.K / 512;
-    const int nst = nchunk * kStagesPerChunk;
+    const int nst = nchunk * kSPC;
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < kStages; ++i) {
-            mbar_init(&full[i], 128 + 1);  // one producer warp per row quarter + TMA-B
+            mbar_init(&full[i], 4 + 1);  // one arrival per row-quarter producer warp + TMA-B
             mbar_init(&empty[i], 1);
         }
         for (int i = 0; i < kRaw; ++i) {
             mbar_init(&rfull[i], 1);
-            mbar_init(&rempty[i], kProdWarps * 32);
+            mbar_init(&rempty[i], kProdWarps);  // one arrival per producer warp
         }
         for (int i = 0; i < 2; ++i) {
             mbar_init(&accf[i], 1);
-            mbar_init(&acce[i], R::kEpiWarps * 32);
+            mbar_init(&acce[i], R::kEpiWarps);  // one arrival per epilogue warp
         }
         *abort = 0;
         fence_mbar_init();
@@ -238,7 +252,7 @@ expert_tc_kernel(const __grid_constant__ BMaps bmap, const TcArgs a) {
         const int row = q * 32 + lane;
         // dequantise one 64-K stage (header + 32 qs bytes of this thread's row), wait for the
         // slot, store the fp16 A operand, signal the MMA warp
-        auto produce = [&](int g, uint2 hdr, const uint32_t (&qw)[8], int ib0) -> bool {
+        auto produce = [&](int g, int h, uint2 hdr, const uint32_t (&qw)[8], int ib0) -> bool {
             const int slot = g % kStages;
             uint32_t v[32];
             const __half2 s0 = subscale_h2(hdr.x, hdr.y, ib0);
@@ -246,10 +260,11 @@ expert_tc_kernel(const __grid_constant__ BMaps bmap, const TcArgs a) {
 #pragma unroll
             for (int i = 0; i < 8; ++i) word_f16(qw[i], i < 4 ? s0 : s1, v + 4 * i);
             if (warp == 0 && lane == 0) TC_TRACE(7, g);
-            if (!mbar_wait(&empty[slot], ((g / kStages) & 1) ^ 1, abort)) return false;
+            if (h == 0 && !mbar_wait_warp(&empty[slot], ((g / kStages) & 1) ^ 1, abort)) return false;
             if (warp == 0 && lane == 0) TC_TRACE(1, g);
             if constexpr (A_TMEM) {
-                tmem_st32(tmem + (static_cast<uint32_t>(q * 32) << 16) + kACol0 + slot * 32, v);
+                tmem_st32(tmem + (static_cast<uint32_t>(q * 32) << 16) + kACol0 + (slot * kSub + h) * 32, v);
+                if (h != kSub - 1) return true;
                 tmem_wait_st();
                 tc_fence_before();
             } else if constexpr (!A_TMEM) {
@@ -260,7 +275,8 @@ expert_tc_kernel(const __grid_constant__ BMaps bmap, const TcArgs a) {
                         make_uint4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
                 fence_proxy_async_smem();
             }
-            mbar_arrive(&full[slot]);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&full[slot]);
             return true;
         };
         int g = 0, rc = 0;
@@ -268,24 +284,28 @@ expert_tc_kernel(const __grid_constant__ BMaps bmap, const TcArgs a) {
             bool ok = true;
             for (int kc = 0; kc < nchunk && ok; ++kc, ++rc) {
                 const int rs = rc % kRaw;
-                if (!mbar_wait(&rfull[rs], (rc / kRaw) & 1, abort)) { ok = false; break; }
+                if (!mbar_wait_warp(&rfull[rs], (rc / kRaw) & 1, abort)) { ok = false; break; }
                 if (warp == 0 && lane == 0) TC_TRACE(5, 512 + rc);
                 const uint8_t* raw = rst + rs * kRawBytes + row * kRawRowBytes;
-                for (int sc = 0; sc < kStagesPerChunk; ++sc, ++g) {
+                for (int sc = 0; sc < kSPC && ok; ++sc, ++g) {
                     if (g % kParts != part) continue;
-                    const uint8_t* blk = raw + (sc >> 2) * kBlockBytes;
-                    const int ib0 = (sc & 3) * 2;
-                    const uint2 hdr = lds64(blk);
-                    uint32_t qw[8];
+                    for (int h = 0; h < kSub; ++h) {
+                        const int os = sc * kSub + h;  // 64-K sub-stage within the chunk
+                        const uint8_t* blk = raw + (os >> 2) * kBlockBytes;
+                        const int ib0 = (os & 3) * 2;
+                        const uint2 hdr = lds64(blk);
+                        uint32_t qw[8];
 #pragma unroll
-                    for (int i = 0; i < 8; i += 2) {
-                        const uint2 qq = lds64(blk + 8 + ib0 * 16 + i * 4);
-                        qw[i] = qq.x;
-                        qw[i + 1] = qq.y;
+                        for (int i = 0; i < 8; i += 2) {
+                            const uint2 qq = lds64(blk + 8 + ib0 * 16 + i * 4);
+                            qw[i] = qq.x;
+                            qw[i + 1] = qq.y;
+                        }
+                        if (!produce(g, h, hdr, qw, ib0)) { ok = false; break; }
                     }
-                    if (!produce(g, hdr, qw, ib0)) { ok = false; break; }
                 }
-                if (ok) mbar_arrive(&rempty[rs]);
+                __syncwarp();
+                if (ok && lane == 0) mbar_arrive(&rempty[rs]);
             }
             if (!ok) break;
         }
@@ -306,14 +326,14 @@ expert_tc_kernel(const __grid_constant__ BMaps bmap, const TcArgs a) {
                 if (!mbar_wait_warp(&full[slot], (g / kStages) & 1, abort)) { ok = false; break; }
                 if (lane == 0) TC_TRACE(0, g);
                 tc_fence_after();
-                const uint32_t bbase = smem_u32(bst + slot * kBStageBytes);
+                const uint32_t bbase = smem_u32(bst + slot * Lay::kBSt);
                 if (elect_one()) {
 #pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        const uint64_t bdesc = sw128_desc(bbase + 32 * j);
+                    for (int j = 0; j < 4 * kSub; ++j) {
+                        const uint64_t bdesc = sw128_desc(bbase + (j >> 2) * kBStageBytes + 32 * (j & 3));
                         const uint32_t accum = (s | j) != 0;
                         if constexpr (A_TMEM) {
-                            mma_ts(d, tmem + kACol0 + slot * 32 + 8 * j, bdesc, idesc, accum);
+                            mma_ts(d, tmem + kACol0 + slot * 32 * kSub + 8 * j, bdesc, idesc, accum);
                         } else {
                             const uint32_t aa = smem_u32(ast + slot * kAStageBytes) + 32 * j;
                             mma_ss(d, sw128_desc(aa), bdesc, idesc, accum);
@@ -342,8 +362,10 @@ expert_tc_kernel(const __grid_constant__ BMaps bmap, const TcArgs a) {
                     const int slot = g % kStages;
                     if (!mbar_wait(&empty[slot], ((g / kStages) & 1) ^ 1, abort)) { ok = false; break; }
                     TC_TRACE(2, g);
-                    mbar_arrive_expect_tx(&full[slot], bbytes);
-                    tma_load_2d(bst + slot * kBStageBytes, bm, s * 64, x.p0, &full[slot]);
+                    mbar_arrive_expect_tx(&full[slot], bbytes * kSub);
+                    for (int h = 0; h < kSub; ++h)
+                        tma_load_2d(bst + slot * Lay::kBSt + h * kBStageBytes, bm, (s * kSub + h) * 64, x.p0,
+                                    &full[slot]);
                 }
                 if (!ok) break;
             }
@@ -401,7 +423,7 @@ expert_tc_kernel(const __grid_constant__ BMaps bmap, const TcArgs a) {
         for (int item = blockIdx.x; item < n_items; item += gridDim.x, ++it) {
             const Item x = get_item(a, item);
             const int b = it & 1;
-            if (!mbar_wait(&accf[b], (it >> 1) & 1, abort)) break;
+            if (!mbar_wait_warp(&accf[b], (it >> 1) & 1, abort)) break;
             if (ew == 0 && lane == 0) TC_TRACE(4, it);
             tc_fence_after();
             const int feat = x.rt * 128 + row;
@@ -422,7 +444,8 @@ expert_tc_kernel(const __grid_constant__ BMaps bmap, const TcArgs a) {
                 }
             }
             tc_fence_before();
-            mbar_arrive(&acce[b]);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acce[b]);
             if (ew == 0 && lane == 0) TC_TRACE(5, it);
         }
     }
