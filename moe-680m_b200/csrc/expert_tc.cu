@@ -13,12 +13,13 @@
 //   TMA-A warp  raw IQ4_XS bytes of the item's 128 weight rows, 512 K (two 136-byte blocks per
 //               row) per tensor-map load, into a 2-deep shared-memory ring;
 //   producer warps (16, or 8 with MOE_B200_TC_PRODUCER_WARPS=8) dequantise from that ring
-//               (kvalues_iq4nl lookup by byte permutes, fp16 scale per 32-weight sub-block) and
+//               (a shared-memory table of kvalues_iq4nl half2 per qs byte, fp16 scale per
+//               32-weight sub-block) and
 //               store the fp16 A operand into TMEM (tcgen05.st; 128 K per pipeline stage) or
 //               128-byte-swizzled shared memory (64 K per stage); the warps of one 32-row
 //               quarter take turns by stage;
 //   TMA-B warp  fp16 activations of the tile's slots (pre-scaled per slot by a power of two, K
-//               permuted as below), one 16/32/64/128-row box per 64 K, 4 stages in flight;
+//               permuted as below), one 16/32/64/112-row box per 64 K, 4 stages in flight;
 //   MMA warp    allocates TMEM; one elected lane issues tcgen05.mma (M=128, N=16..kNMax, K=16)
 //               and tcgen05.commit;
 //   8 epilogue warps (two per TMEM lane quarter): TMEM -> registers, undo the activation
@@ -68,17 +69,21 @@ namespace {
 
 using namespace tc;
 
+#ifndef MOE_TC_EPI_WARPS
+#define MOE_TC_EPI_WARPS 8
+#endif
 // Warp roles: producers 0..PW-1, then MMA, TMA-B, TMA-A, and eight epilogue warps.
 template <int PW>
 struct Roles {
     static constexpr int kProd = PW;
     static constexpr int kMma = PW, kTmaB = PW + 1, kTmaA = PW + 2, kEpi0 = PW + 3;
-    static constexpr int kEpiWarps = 8;               // two per 32-lane TMEM quarter
+    static constexpr int kEpiWarps = MOE_TC_EPI_WARPS;  // 4: one per 32-lane TMEM quarter; 8: two
     static constexpr int kThreads = (PW + 3 + kEpiWarps) * 32;
     static constexpr int kParts = PW / 4;          // producer warps per 32-row quarter
 };
 constexpr int kTmemCols = 512;
-constexpr int kNMax = 128;          // tokens per tile
+constexpr int kNMax = 112;          // tokens per tile (B stages of 112 rows leave shared memory for the
+                                    // dequantisation table)
 constexpr int kAccStride = 128;     // TMEM columns per accumulator buffer
 constexpr int kACol0 = 256;         // TMEM column of A stage 0 (32 columns per stage)
 constexpr int kRawRowBytes = 2 * kBlockBytes;      // 512 K of one weight row
@@ -96,7 +101,10 @@ constexpr int kRawElem = MOE_TC_RAW_ELEM;          // bytes per element of the r
 constexpr int kRawBytes = 128 * kRawRowBytes;      // one raw A chunk (34,816 bytes)
 constexpr int kStagesPerChunk = 8;                 // 512 K / 64 K
 constexpr int kBStageBytes = kNMax * 128;
+// rows of B box i (16, 32, 64, kNMax): the smallest covering the tile is loaded
+__host__ __device__ constexpr int box_rows(int i) { return i < 3 ? 16 << i : kNMax; }
 constexpr int kAStageBytes = 128 * 128;            // smem-A variant
+constexpr int kKvTabBytes = 256 * 32 * 4;          // kv half2 per qs byte, one copy per lane (bank)
 
 // Pipeline depth.  With A in TMEM (columns 256..511): 4 stages of 128 K (MOE_TC_SUB = 2 sub-slots
 // of 64 K; MOE_TC_SUB=1 gives MOE_TC_STAGES stages of 64 K) and a 2-chunk raw ring (raw rings of
@@ -106,6 +114,9 @@ constexpr int kAStageBytes = 128 * 128;            // smem-A variant
 #endif
 #ifndef MOE_TC_RAW
 #define MOE_TC_RAW 2
+#endif
+#ifndef MOE_TC_EPI_SLEEP
+#define MOE_TC_EPI_SLEEP 0
 #endif
 #ifndef MOE_TC_SUB
 #define MOE_TC_SUB 2
@@ -120,7 +131,8 @@ struct Layout {
     static constexpr size_t kB = 0;
     static constexpr size_t kA = kB + static_cast<size_t>(kStages) * kBSt;
     static constexpr size_t kR = kA + (A_TMEM ? 0 : static_cast<size_t>(kStages) * kAStageBytes);
-    static constexpr size_t kBars = kR + static_cast<size_t>(kRaw) * kRawBytes;
+    static constexpr size_t kT = kR + static_cast<size_t>(kRaw) * kRawBytes;  // dequantisation table
+    static constexpr size_t kBars = kT + kKvTabBytes;
     static constexpr size_t kTotal = kBars + 256 + 1024;  // + barriers, + alignment slack
 };
 
@@ -143,23 +155,26 @@ struct TcArgs {
 };
 
 // ---- dequantisation ---------------------------------------------------------------------------
-// Two fp16 weights (lo/hi nibble of one qs byte) from kv+128 bytes: build 1024+u halves with a
-// byte permute, subtract 1152 (exact), multiply by the sub-block scale.
-__device__ __forceinline__ uint32_t pair_f16(uint32_t r, uint32_t sel, __half2 scale) {
-    const uint32_t m = prmt(r, 0x64646464u, sel);
-    __half2 v = *reinterpret_cast<const __half2*>(&m);
-    v = __hmul2(__hsub2(v, __half2half2(__ushort_as_half(0x6480))), scale);  // 0x6480 = 1152
-    return *reinterpret_cast<uint32_t*>(&v);
+// kvalues_iq4nl[n] from the packed kv+128 byte tables.
+__device__ __forceinline__ int kv_value(uint32_t n) {
+    const uint32_t w = n < 4 ? kKvT0 : n < 8 ? kKvT1 : n < 12 ? kKvT2 : kKvT3;
+    return static_cast<int>((w >> (8 * (n & 3))) & 0xFFu) - 128;
 }
 
-// One qs word -> 4 packed fp16x2 (8 weights in permuted K order).
-__device__ __forceinline__ void word_f16(uint32_t q, __half2 scale, uint32_t* o) {
-    uint32_t r0, r1;
-    kv_lookup8(q, r0, r1);
-    o[0] = pair_f16(r0, 0x4140u, scale);
-    o[1] = pair_f16(r0, 0x4342u, scale);
-    o[2] = pair_f16(r1, 0x4140u, scale);
-    o[3] = pair_f16(r1, 0x4342u, scale);
+// One qs word -> 4 packed fp16x2 by table: word (b * 32 + lane) of the table holds the half2
+// {kv[b & 15], kv[b >> 4]} of qs byte b, one copy per lane so that the 32 lanes of a warp read
+// 32 different banks whatever their bytes; tl = table address + 4 * lane.  The same values as
+// word_f16 (kv * scale, rounded once), with most of the work on the load and FMA pipes instead
+// of the byte-permute (ALU) pipe, which bounded the dequantisation.
+__device__ __forceinline__ void word_tab(uint32_t q, __half2 scale, uint32_t tl, uint32_t* o) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const uint32_t off = i == 0 ? (q << 7) & 0x7F80u : (q >> (8 * i - 7)) & 0x7F80u;
+        uint32_t m;
+        asm volatile("ld.shared.b32 %0, [%1];" : "=r"(m) : "r"(tl + off));
+        __half2 v = __hmul2(*reinterpret_cast<const __half2*>(&m), scale);
+        o[i] = *reinterpret_cast<uint32_t*>(&v);
+    }
 }
 
 __device__ __forceinline__ __half2 subscale_h2(uint32_t h0, uint32_t h1, int ib) {
@@ -204,6 +219,7 @@ expert_tc_kernel(const __grid_constant__ BMaps bmap, const TcArgs a) {
     uint8_t* ast = smem + Lay::kA;
     uint8_t* rst = smem + Lay::kR;
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Lay::kBars);
+    uint32_t* kvtab = reinterpret_cast<uint32_t*>(smem + Lay::kT);
     uint64_t* full = bars;                    // [kStages]  A stored + B landed
     uint64_t* empty = full + kStages;         // [kStages]  MMAs of the stage done
     uint64_t* rfull = empty + kStages;        // [kRaw]     raw A chunk landed
@@ -234,6 +250,12 @@ expert_tc_kernel(const __grid_constant__ BMaps bmap, const TcArgs a) {
         *abort = 0;
         fence_mbar_init();
     }
+    for (int i = threadIdx.x; i < kKvTabBytes / 4; i += blockDim.x) {
+        const uint32_t b = static_cast<uint32_t>(i) >> 5;
+        const __half lo = __int2half_rn(kv_value(b & 15u)), hi = __int2half_rn(kv_value(b >> 4));
+        const __half2 h = __halves2half2(lo, hi);
+        kvtab[i] = *reinterpret_cast<const uint32_t*>(&h);
+    }
     if (warp == kMmaWarp) tmem_alloc(tmem_base_p, kTmemCols);
     if (warp == kTmaBWarp && lane < 4) tma_prefetch_desc(&bmap.m[lane]);
     tc_fence_before();
@@ -250,6 +272,7 @@ expert_tc_kernel(const __grid_constant__ BMaps bmap, const TcArgs a) {
         const int q = warp & 3;
         const int part = warp >> 2;
         const int row = q * 32 + lane;
+        const uint32_t ktab = smem_u32(kvtab) + 4u * lane;
         // dequantise one 64-K stage (header + 32 qs bytes of this thread's row), wait for the
         // slot, store the fp16 A operand, signal the MMA warp
         auto produce = [&](int g, int h, uint2 hdr, const uint32_t (&qw)[8], int ib0) -> bool {
@@ -258,7 +281,7 @@ expert_tc_kernel(const __grid_constant__ BMaps bmap, const TcArgs a) {
             const __half2 s0 = subscale_h2(hdr.x, hdr.y, ib0);
             const __half2 s1 = subscale_h2(hdr.x, hdr.y, ib0 + 1);
 #pragma unroll
-            for (int i = 0; i < 8; ++i) word_f16(qw[i], i < 4 ? s0 : s1, v + 4 * i);
+            for (int i = 0; i < 8; ++i) word_tab(qw[i], i < 4 ? s0 : s1, ktab, v + 4 * i);
             if (warp == 0 && lane == 0) TC_TRACE(7, g);
             if (h == 0 && !mbar_wait_warp(&empty[slot], ((g / kStages) & 1) ^ 1, abort)) return false;
             if (warp == 0 && lane == 0) TC_TRACE(1, g);
@@ -356,7 +379,7 @@ expert_tc_kernel(const __grid_constant__ BMaps bmap, const TcArgs a) {
                 // one box per stage: 16, 32, 64 or 128 rows, the smallest covering the tile
                 const int bsel = x.n <= 16 ? 0 : x.n <= 32 ? 1 : x.n <= 64 ? 2 : 3;
                 const CUtensorMap* bm = &bmap.m[bsel];
-                const uint32_t bbytes = (16u << bsel) * 128u;
+                const uint32_t bbytes = static_cast<uint32_t>(box_rows(bsel)) * 128u;
                 bool ok = true;
                 for (int s = 0; s < nst; ++s, ++g) {
                     const int slot = g % kStages;
@@ -420,27 +443,47 @@ expert_tc_kernel(const __grid_constant__ BMaps bmap, const TcArgs a) {
         const int sub = ew >> 2;
         const int row = q * 32 + lane;
         int it = 0;
+        constexpr int kStep = 16 * (R::kEpiWarps / 4);  // columns between a warp's chunks
         for (int item = blockIdx.x; item < n_items; item += gridDim.x, ++it) {
             const Item x = get_item(a, item);
             const int b = it & 1;
-            if (!mbar_wait_warp(&accf[b], (it >> 1) & 1, abort)) break;
+            // activation exponents of the tile's tokens, read before the accumulator is ready:
+            // lane j holds token j + 32 i in ex[i]; a chunk's 16 tokens lie in one group of 32
+            int ex[(kNMax + 31) / 32];
+#pragma unroll
+            for (int i = 0; i < (kNMax + 31) / 32; ++i) {
+                const int t = lane + 32 * i;
+                ex[i] = t < x.n ? __ldg(a.sexp + x.p0 + t) : 0;
+            }
+            if (!mbar_wait_warp(&accf[b], (it >> 1) & 1, abort, MOE_TC_EPI_SLEEP)) break;
             if (ew == 0 && lane == 0) TC_TRACE(4, it);
             tc_fence_after();
             const int feat = x.rt * 128 + row;
             const uint32_t tl = tmem + (static_cast<uint32_t>(q * 32) << 16) + b * kAccStride;
             float* __restrict__ out = a.out + feat;
-            for (int c0 = sub * 16; c0 < x.n; c0 += 32) {
-                uint32_t v[16];
-                tmem_ld16(tl + c0, v);
-                int e[16];
-#pragma unroll
-                for (int t = 0; t < 16; ++t) e[t] = c0 + t < x.n ? __ldg(a.sexp + x.p0 + c0 + t) : 0;
+            for (int c0 = sub * 16; c0 < x.n; c0 += 2 * kStep) {
+                // two chunks per TMEM wait: c0 and c0 + kStep
+                const int c1 = c0 + kStep;
+                uint32_t v[2][16];
+                tmem_ld16(tl + c0, v[0]);
+                if (c1 < x.n) tmem_ld16(tl + c1, v[1]);
                 tmem_wait_ld();
 #pragma unroll
-                for (int t = 0; t < 16; ++t) {
-                    if (c0 + t < x.n)
-                        out[static_cast<size_t>(x.p0 + c0 + t) * a.out_ld] =
-                            __uint_as_float(v[t]) * __int_as_float((127 + e[t]) << 23);  // * 2^e
+                for (int h = 0; h < 2; ++h) {
+                    const int cc = h == 0 ? c0 : c1;
+                    if (cc >= x.n) break;
+                    const int gi = cc >> 5;
+                    int eg = ex[0];
+#pragma unroll
+                    for (int i = 1; i < (kNMax + 31) / 32; ++i)
+                        if (gi == i) eg = ex[i];
+#pragma unroll
+                    for (int t = 0; t < 16; ++t) {
+                        const int e = __shfl_sync(0xffffffffu, eg, (cc & 31) + t);
+                        if (cc + t < x.n)
+                            out[static_cast<size_t>(x.p0 + cc + t) * a.out_ld] =
+                                __uint_as_float(v[h][t]) * __int_as_float((127 + e) << 23);  // * 2^e
+                    }
                 }
             }
             tc_fence_before();
@@ -635,7 +678,7 @@ static PFN_cuTensorMapEncodeTiled_v12000 tmap_encoder() {
     return encode;
 }
 
-// 2D tensor maps over an fp16 [rows][cols] row-major matrix, boxes of 16/32/64/128 rows x 64
+// 2D tensor maps over an fp16 [rows][cols] row-major matrix, boxes of 16/32/64/112 rows x 64
 // cols, 128B swizzle.
 bool make_fp16_tmaps(BMaps* m, const void* base, uint64_t rows, uint64_t cols) {
     auto encode = tmap_encoder();
@@ -643,7 +686,7 @@ bool make_fp16_tmaps(BMaps* m, const void* base, uint64_t rows, uint64_t cols) {
     for (int i = 0; i < 4; ++i) {
         const cuuint64_t dims[2] = {cols, rows};
         const cuuint64_t strides[1] = {cols * 2};
-        const cuuint32_t box[2] = {64, 16u << i};
+        const cuuint32_t box[2] = {64, static_cast<cuuint32_t>(box_rows(i))};
         const cuuint32_t estr[2] = {1, 1};
         if (encode(&m->m[i], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides,
                    box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,

@@ -51,11 +51,12 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
 // so that every role of the CTA stops issuing work.  Returns false on timeout or when another
 // role has aborted.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort,
-                                          uint64_t limit_ns = 1000000000ull) {
+                                          uint64_t limit_ns = 1000000000ull, uint32_t sleep_ns = 0) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = globaltimer_ns();
     for (uint32_t i = 1;; ++i) {
         if (mbar_try_wait(bar, parity)) return true;
+        if (sleep_ns) __nanosleep(sleep_ns);
         if ((i & 63u) == 0u) {
             if (*abort) return false;
             if (globaltimer_ns() - t0 > limit_ns) {
@@ -78,8 +79,9 @@ __device__ __forceinline__ bool elect_one() {
 }
 
 // Warp-wide bounded wait: every lane polls, and all lanes agree on the outcome.
-__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, volatile int* abort) {
-    const bool ok = mbar_wait(bar, parity, abort);
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, volatile int* abort,
+                                               uint32_t sleep_ns = 0) {
+    const bool ok = mbar_wait(bar, parity, abort, 1000000000ull, sleep_ns);
     return __all_sync(0xffffffffu, ok) != 0;
 }
 
