@@ -184,31 +184,13 @@ bucket_scatter_kernel(const uint2* __restrict__ topk, int M, int E, int k, int r
 
 // ---- small batches: count, scan and scatter in one CTA ---------------------------------------
 // For up to kSmallMaxTokens tokens one CTA of 1024 threads does all three steps (one launch
-// instead of three): tokens are taken 1024 at a time, one per thread; per-warp bitmasks give
-// each slot's rank among the chunk's earlier tokens exactly as in the three-launch path, so the
-// results are identical.
+// instead of three), one token per thread: the token's routing record is read once into
+// registers; per-warp bitmasks give each slot's rank among the earlier tokens exactly as in the
+// three-launch path, so the results are identical.  The chunk and tile lists are written by all
+// threads in parallel (entry -> bucket by binary search over the per-bucket list offsets).
 constexpr int kSmallThreads = 1024;
 constexpr int kSmallWarps = kSmallThreads / 32;
-constexpr int kSmallMaxTokens = 1024;
-
-__device__ __forceinline__ void small_masks(uint32_t* masks, int nb, const uint2* topk, int t, int M, int E,
-                                            int k, int routed, int has_shared, int* status) {
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    __syncthreads();  // the previous chunk's masks are no longer read
-    for (int i = tid; i < kSmallWarps * nb; i += kSmallThreads) masks[i] = 0u;
-    __syncthreads();
-    if (t < M) {
-        const uint2* rec = topk + static_cast<size_t>(t) * (k + 1);
-        for (int s = 0; s < (routed ? k : 0); ++s) {
-            if (rec[1 + s].x == kNoExpert) continue;  // empty slot
-            const int e = static_cast<int>(rec[1 + s].x);
-            if (e < 0 || e >= E) { set_dev_error(status, kDevBadExpert); continue; }
-            atomicOr(&masks[warp * nb + e], 1u << lane);
-        }
-        if (has_shared && rec[0].x != kNoExpert) atomicOr(&masks[warp * nb + E], 1u << lane);
-    }
-    __syncthreads();
-}
+constexpr int kSmallMaxTokens = kSmallThreads;
 
 __global__ void __launch_bounds__(kSmallThreads)
 bucket_small_kernel(const uint2* __restrict__ topk, int M, int E, int k, int routed, int has_shared,
@@ -216,43 +198,59 @@ bucket_small_kernel(const uint2* __restrict__ topk, int M, int E, int k, int rou
                     int* __restrict__ slot_pos, Chunk* __restrict__ chunks, int max_chunks, TileLists lists,
                     int* __restrict__ counters, int* status) {
     extern __shared__ uint32_t masks[];  // [32][E+1]
-    __shared__ int cnt[kMaxExperts + 1], base[kMaxExperts + 1];
+    // per bucket: first slot, first chunk, first gate/up tile, first down tile (+ totals at nb)
+    __shared__ int4 first_s[kMaxExperts + 2];
     __shared__ int4 warp_tot[32];
     const int nb = E + 1, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    if (tid < nb) cnt[tid] = 0;
-    // 1. counts
-    for (int t0 = 0; t0 < M; t0 += kSmallThreads) {
-        small_masks(masks, nb, topk, t0 + tid, M, E, k, routed, has_shared, status);
-        if (tid < nb) {
-            int c = 0;
-#pragma unroll 4
-            for (int w = 0; w < kSmallWarps; ++w) c += __popc(masks[w * nb + tid]);
-            cnt[tid] += c;
+    const int t = tid;
+    // the token's slots: bucket (or -1) and gate weight, read once
+    int eb[kMaxTopK + 1];
+    uint32_t wb[kMaxTopK + 1];
+    {
+        uint2 rec[kMaxTopK + 1];
+#pragma unroll
+        for (int i = 0; i <= kMaxTopK; ++i)
+            rec[i] = (t < M && i <= k) ? topk[static_cast<size_t>(t) * (k + 1) + i] : make_uint2(kNoExpert, 0u);
+#pragma unroll
+        for (int s = 0; s <= kMaxTopK; ++s) {
+            // slot s < k: routed entry 1 + s; slot k: the shared expert (record entry 0)
+            const uint2 r = s < k ? rec[(1 + s) <= kMaxTopK ? 1 + s : kMaxTopK] : rec[0];
+            int e = -1;
+            if (s < k) {
+                if (routed && r.x != kNoExpert) {
+                    if (r.x >= static_cast<uint32_t>(E)) set_dev_error(status, kDevBadExpert);
+                    else e = static_cast<int>(r.x);
+                }
+            } else if (s == k) {
+                e = (has_shared && r.x != kNoExpert) ? E : -1;
+            }
+            eb[s] = t < M ? e : -1;
+            wb[s] = r.y;
         }
     }
-    // 2. scan: ranges, chunk list, tensor-core tile lists
-    const int c_e = tid < nb ? cnt[tid] : 0;
+    for (int i = tid; i < kSmallWarps * nb; i += kSmallThreads) masks[i] = 0u;
+    __syncthreads();
+#pragma unroll
+    for (int s = 0; s <= kMaxTopK; ++s)
+        if (eb[s] >= 0) atomicOr(&masks[warp * nb + eb[s]], 1u << lane);
+    __syncthreads();
+    // 1. counts and 2. scan
+    int c_e = 0;
+    if (tid < nb) {
+#pragma unroll 4
+        for (int w = 0; w < kSmallWarps; ++w) c_e += __popc(masks[w * nb + tid]);
+    }
     const int4 v = make_int4(c_e, (c_e + kGemvTok - 1) / kGemvTok, (c_e + lists.n13 - 1) / lists.n13,
                              (c_e + lists.n2 - 1) / lists.n2);
     int4 total;
     const int4 first = block_exscan4(v, warp_tot, total);
     if (tid < nb) {
         ranges[tid] = first.x;
-        base[tid] = first.x;
-        int ci = first.y;
-        for (int q = 0; q < c_e && ci < max_chunks; q += kGemvTok, ++ci)
-            chunks[ci] = Chunk{tid, first.x + q, min(kGemvTok, c_e - q), 0};
-        if (lists.t13) {
-            int ti = first.z;
-            for (int q = 0; q < c_e && ti < lists.max13; q += lists.n13, ++ti)
-                lists.t13[ti] = TcTile{tid, first.x + q, min(lists.n13, c_e - q), 0};
-            ti = first.w;
-            for (int q = 0; q < c_e && ti < lists.max2; q += lists.n2, ++ti)
-                lists.t2[ti] = TcTile{tid, first.x + q, min(lists.n2, c_e - q), 0};
-        }
+        first_s[tid] = first;
     }
     if (tid == 0) {
         ranges[nb] = total.x;
+        first_s[nb] = total;
         int c = total.y, a13 = total.z, a2 = total.w;
         if (c > max_chunks) { set_dev_error(status, kDevOverflow); c = max_chunks; }
         if (lists.t13) {
@@ -265,35 +263,50 @@ bucket_small_kernel(const uint2* __restrict__ topk, int M, int E, int k, int rou
         counters[1] = a13;
         counters[2] = a2;
     }
-    __syncthreads();  // base
-    // 3. positions, chunk by chunk in token order
-    const uint32_t lt = (1u << lane) - 1u;
-    const int ns = k + (has_shared ? 1 : 0);
-    for (int t0 = 0; t0 < M; t0 += kSmallThreads) {
-        const int t = t0 + tid;
-        small_masks(masks, nb, topk, t, M, E, k, routed, has_shared, status);
-        if (t < M) {
-            const uint2* rec = topk + static_cast<size_t>(t) * (k + 1);
-            int* sp = slot_pos + static_cast<size_t>(t) * ns;
-            for (int s = 0; s < ns; ++s) {
-                const uint2 r = rec[s == k ? 0 : 1 + s];  // slot k: the shared expert, record entry 0
-                int e;
-                if (s == k) e = r.x == kNoExpert ? -1 : E;
-                else e = (!routed || r.x >= static_cast<uint32_t>(E)) ? -1 : static_cast<int>(r.x);
-                if (e < 0) { sp[s] = -1; continue; }
-                int pos = base[e] + __popc(masks[warp * nb + e] & lt);
-                for (int w = 0; w < warp; ++w) pos += __popc(masks[w * nb + e]);
-                sorted_tok[pos] = t;
-                sorted_w[pos] = __uint_as_float(r.y);
-                sp[s] = pos;
-            }
+    __syncthreads();
+    // chunk and tile lists, one entry per thread
+    const int* fs = reinterpret_cast<const int*>(first_s);  // field f of bucket b at fs[4 * b + f]
+    auto bucket_of = [&](int f, int i) {
+        int lo = 0, hi = nb - 1;
+        while (lo < hi) {
+            const int mid = (lo + hi + 1) >> 1;
+            if (fs[4 * mid + f] <= i) lo = mid;
+            else hi = mid - 1;
         }
-        __syncthreads();  // every slot of the chunk has read base
-        if (tid < nb) {
-            int c = 0;
-#pragma unroll 4
-            for (int w = 0; w < kSmallWarps; ++w) c += __popc(masks[w * nb + tid]);
-            base[tid] += c;
+        return lo;
+    };
+    for (int ci = tid; ci < min(total.y, max_chunks); ci += kSmallThreads) {
+        const int e = bucket_of(1, ci);
+        const int q = (ci - fs[4 * e + 1]) * kGemvTok, cnt = fs[4 * (e + 1)] - fs[4 * e];
+        chunks[ci] = Chunk{e, fs[4 * e] + q, min(kGemvTok, cnt - q), 0};
+    }
+    if (lists.t13) {
+        for (int ti = tid; ti < min(total.z, lists.max13); ti += kSmallThreads) {
+            const int e = bucket_of(2, ti);
+            const int q = (ti - fs[4 * e + 2]) * lists.n13, cnt = fs[4 * (e + 1)] - fs[4 * e];
+            lists.t13[ti] = TcTile{e, fs[4 * e] + q, min(lists.n13, cnt - q), 0};
+        }
+        for (int ti = tid; ti < min(total.w, lists.max2); ti += kSmallThreads) {
+            const int e = bucket_of(3, ti);
+            const int q = (ti - fs[4 * e + 3]) * lists.n2, cnt = fs[4 * (e + 1)] - fs[4 * e];
+            lists.t2[ti] = TcTile{e, fs[4 * e] + q, min(lists.n2, cnt - q), 0};
+        }
+    }
+    // 3. positions in token order
+    if (t < M) {
+        const uint32_t lt = (1u << lane) - 1u;
+        const int ns = k + (has_shared ? 1 : 0);
+        int* sp = slot_pos + static_cast<size_t>(t) * ns;
+#pragma unroll
+        for (int s = 0; s <= kMaxTopK; ++s) {
+            if (s >= ns) break;
+            const int e = eb[s];
+            if (e < 0) { sp[s] = -1; continue; }
+            int pos = fs[4 * e] + __popc(masks[warp * nb + e] & lt);
+            for (int w = 0; w < warp; ++w) pos += __popc(masks[w * nb + e]);
+            sorted_tok[pos] = t;
+            sorted_w[pos] = __uint_as_float(wb[s]);
+            sp[s] = pos;
         }
     }
 }

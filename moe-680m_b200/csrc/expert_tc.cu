@@ -611,7 +611,7 @@ void launch_tc_pw(const BMaps& bmap, const TcArgs& args, int n_cta, cudaStream_t
 int producer_warps() {
     static int pw = [] {
         const char* e = std::getenv("MOE_B200_TC_PRODUCER_WARPS");
-        return (e && std::atoi(e) == 8) ? 8 : 16;
+        return (e && std::atoi(e) == 8) ? 8 : (e && std::atoi(e) == 12) ? 12 : 16;
     }();
     return pw;
 }
@@ -619,6 +619,7 @@ int producer_warps() {
 template <bool A_TMEM>
 void launch_tc(const BMaps& bmap, const TcArgs& args, int n_cta, cudaStream_t s) {
     if (producer_warps() == 8) launch_tc_pw<A_TMEM, 8>(bmap, args, n_cta, s);
+    else if (producer_warps() == 12) launch_tc_pw<A_TMEM, 12>(bmap, args, n_cta, s);
     else launch_tc_pw<A_TMEM, 16>(bmap, args, n_cta, s);
 }
 
