@@ -546,8 +546,11 @@ def main():
     n_mats = statistics.mean(distinct) + 1  # + shared expert
     hbm, tfl, peak_kind = peaks()
     stage_ms = {k: v[1] / max(v[0], 1) for k, v in stages.items()}
+    # the tensor-core launches on the timed stream carry the routed experts only when the library
+    # runs the shared expert as its own concurrent pass (batches of 64+ tokens, the default)
+    tc_mats = n_mats - (1 if os.environ.get("MOE_B200_SHARED_SPLIT", "1") != "0" and not ep_mode else 0)
     alg_bytes = {"gemv13": n_mats * 2 * sh.w13_bytes, "gemv2": n_mats * sh.w2_bytes,
-                 "tc13": n_mats * 2 * sh.w13_bytes, "tc2": n_mats * sh.w2_bytes,
+                 "tc13": tc_mats * 2 * sh.w13_bytes, "tc2": tc_mats * sh.w2_bytes,
                  "router": E * H * 4 + H * 4 + PREFILL_M * H * 4}
     dom = max(stage_ms, key=stage_ms.get)
     layer_bytes = n_mats * sh.expert_bytes

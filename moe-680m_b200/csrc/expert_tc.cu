@@ -125,7 +125,7 @@ template <bool A_TMEM>
 struct Layout {
     // 64-K sub-slots per pipeline stage (one barrier handshake per stage)
     static constexpr int kSub = A_TMEM ? MOE_TC_SUB : 1;
-    static constexpr int kStages = A_TMEM ? (kSub == 2 ? 4 : MOE_TC_STAGES) : 4;
+    static constexpr int kStages = A_TMEM ? (kSub == 4 ? 2 : kSub == 2 ? 4 : MOE_TC_STAGES) : 4;
     static constexpr int kRaw = A_TMEM ? MOE_TC_RAW : 2;
     static constexpr size_t kBSt = static_cast<size_t>(kSub) * kBStageBytes;  // B bytes per stage
     static constexpr size_t kB = 0;
@@ -618,9 +618,13 @@ int producer_warps() {
 
 template <bool A_TMEM>
 void launch_tc(const BMaps& bmap, const TcArgs& args, int n_cta, cudaStream_t s) {
+#if MOE_TC_SUB == 4
+    launch_tc_pw<A_TMEM, 8>(bmap, args, n_cta, s);
+#else
     if (producer_warps() == 8) launch_tc_pw<A_TMEM, 8>(bmap, args, n_cta, s);
     else if (producer_warps() == 12) launch_tc_pw<A_TMEM, 12>(bmap, args, n_cta, s);
     else launch_tc_pw<A_TMEM, 16>(bmap, args, n_cta, s);
+#endif
 }
 
 static_assert(Layout<true>::kTotal <= 227 * 1024, "smem budget (A in TMEM)");
