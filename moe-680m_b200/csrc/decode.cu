@@ -3,31 +3,30 @@
 // moe-680m's router.comp + router_topk.comp + do_route + the 18 w1_w3_fused / w2_scatter
 // dispatches of record_and_submit_moe's decode branch (src/inference.rs:734-762).
 //
-// One CTA per SM (cooperative launch, so every CTA is resident), 16 warps.  Each CTA owns fixed
-// slices of the work:
+// One CTA per SM (cooperative launch, so every CTA is resident; programmatic dependent launch
+// lets a layer's prologue overlap the previous launch's tail), 16 warps.  Each CTA owns:
 //   * router half-rows t = c, c + G, ... of the 2 (E + 1) halves (row E: the shared-expert gate
-//     g . x), f32 dot products of the f32 router weight with x;
-//   * a contiguous range of the shared expert's gate/up units (unit j: rows j of W1 and W3,
-//     h[j] = silu(W1[j] . x) * (W3[j] . x)), ~I/G units;
-//   * a contiguous range of the k * I routed units (slot s = u / I, row j = u % I), ~k I / G;
-//   * a contiguous range of output rows n, over which it computes
+//     g . x), f32 dot products of the f32 router weight with x, on warps 4..15;
+//   * one 32-value sub-block of h: CTA c < (k + 1) I / 32 computes units j0..j0+31 of one slot
+//     (unit j: rows j of W1 and W3, h[j] = silu(W1[j] . x) * (W3[j] . x)); the shared expert's
+//     sub-blocks come first, so those CTAs start without waiting for the routing;
+//   * a set of output rows n, over which it computes
 //     out[n] = resid[n] + scale * sum_s w_s (W2_s[n] . h_s) for all k + 1 slots.
 // Work of other CTAs is consumed through two exchanges in global memory:
 //   * the half-row logits carry the launch's epoch in their high 32 bits (64-bit stores and
-//     loads are single-copy atomic); one warp per CTA polls them until every entry shows the
-//     current epoch, so the data itself is the barrier (one L2 round trip after the last
-//     producer), then computes softmax + top-k itself, identically in every CTA (fixed reduction
-//     order, ties to the lower index);
-//   * h (every CTA needs all of it for its output rows): every warp stores its h values and
-//     arrives on a 64-bit counter with a release reduction; thread 0 of each CTA polls the
-//     counter (acquire) and the CTA then reads h.
+//     loads are single-copy atomic); the routing warp of each CTA polls them until every entry
+//     shows the current epoch, so the data itself is the barrier (one L2 round trip after the
+//     last producer), then computes softmax + top-k itself, identically in every CTA (fixed
+//     reduction order, ties to the lower index);
+//   * h: each active CTA publishes its sub-block already packed (16-bit fixed point with its
+//     power-of-two scale) and arrives once on a 64-bit counter with a release reduction; thread 0
+//     of each CTA polls the counter (acquire) and the CTA then reads all of packed h.
 //
-// Weights move by bulk copies (cp.async.bulk, completion counted on mbarriers): the CTA's
-// shared-expert rows and the shared expert's W2 rows are requested at entry; right after the
-// routing step the routing warp requests the routed W1/W3 rows in chunks of 4 units (their rows
-// are contiguous) and every routed expert's W2 rows of this CTA's output rows, which are in
-// shared memory long before h is complete.  Warps waiting for the routing park on a named
-// barrier, so they take no issue slots from the routing warp.
+// Weights move by bulk copies (cp.async.bulk, completion counted on mbarriers): a shared-expert
+// CTA requests its W1/W3 rows at entry, a routed CTA right after the routing step (chunks of 4
+// units; the rows are contiguous); W2 rows of this CTA's output rows follow and are in shared
+// memory long before h is complete.  Warps waiting for the routing park on a named barrier, so
+// they take no issue slots from the routing warp.
 //
 // Dot products are integer: IQ4_XS codes are exact bytes (kvalue + 128); activations (x, and
 // each slot of h) are rounded to 16-bit fixed point with a power-of-two scale per 32-value
@@ -35,14 +34,15 @@
 // accumulates a sub-block's code x activation products exactly in int32, which is then scaled
 // by d * (ls - 32) / activation scale and accumulated in f32 in a fixed order.
 //
-// Epochs: thread 0 of every CTA reads the counter at entry (v); each of the launch's 16 G warps
-// adds 1 after its h stores, so a launch adds 16 G.  No warp can arrive before every CTA of its
-// launch has read the counter (an arrival needs the routing, which needs every CTA's logits,
-// each published after that CTA's read), so all CTAs read the same v, use epoch v / (16 G) + 1
-// for the logits and wait for v + 16 G.  Nothing is reset between launches (CUDA-graph replay
-// is safe).  Every wait gives up after 100 ms, records kDevTimeout and lets the CTA finish
-// (in-flight bulk copies are drained first); moe_sync then clears the counter and the exchange
-// entries.
+// Epochs: thread 0 of every CTA reads the counter at entry (v); each of the launch's G CTAs
+// adds 1 after publishing its h sub-block (CTAs without one add 1 as well), so a launch adds G.
+// No CTA can arrive before every CTA of its launch has read the counter (an arrival follows a
+// CTA-wide barrier that the routing warp reaches only after the logits exchange of its launch,
+// which needs every CTA's logits, each published after that CTA's read), so all CTAs read the same v, use
+// epoch v / G + 1 for the logits and wait for v + G.  Nothing is reset between launches
+// (CUDA-graph replay is safe).  Every wait gives up after 100 ms, records kDevTimeout and lets
+// the CTA finish (in-flight bulk copies are drained first); moe_sync then clears the counter
+// and the exchange entries.
 #include <cuda_runtime.h>
 
 #include "moe_common.cuh"
