@@ -513,15 +513,6 @@ __device__ __forceinline__ int row_exp(float mx) {
 
 __device__ __forceinline__ float pow2f(int e) { return __int_as_float((127 + e) << 23); }
 
-// Write the 8 halves of permuted chunk c from f32 values at k = kb.. (lo) and kb+16.. (hi).
-__device__ __forceinline__ void put_chunk(__half* d, int c, float4 lo, float4 hi, float sc) {
-    __half2 o[4];
-    o[0] = __floats2half2_rn(lo.x * sc, hi.x * sc);
-    o[1] = __floats2half2_rn(lo.y * sc, hi.y * sc);
-    o[2] = __floats2half2_rn(lo.z * sc, hi.z * sc);
-    o[3] = __floats2half2_rn(lo.w * sc, hi.w * sc);
-    *reinterpret_cast<uint4*>(d + 8 * c) = *reinterpret_cast<uint4*>(o);
-}
 
 // chunk c (8 halves): stage c/8, sub-block (c%8)/4, word c%4 -> k = 64*(c/8)+32*((c%8)/4)+4*(c%4)
 __device__ __forceinline__ int chunk_k(int c) { return 64 * (c >> 3) + 32 * ((c & 7) >> 2) + 4 * (c & 3); }
@@ -530,74 +521,101 @@ __device__ __forceinline__ float4 swiglu4(float4 g, float4 u) {
     return make_float4(silu_f(g.x) * u.x, silu_f(g.y) * u.y, silu_f(g.z) * u.z, silu_f(g.w) * u.w);
 }
 
-// One warp per token: x[t] -> fp16(x * 2^-e) in the permuted K order, written to the rows of
-// all the token's slots (slot_pos[t][0..ns)); sexp[p] = e for those slots.
-__global__ void __launch_bounds__(256)
+// Two permuted chunks of 8 halves (chunks c0, c1) from four float4 (lo, hi of each), scaled.
+__device__ __forceinline__ uint4 pack_chunk(float4 lo, float4 hi, float sc) {
+    __half2 o[4];
+    o[0] = __floats2half2_rn(lo.x * sc, hi.x * sc);
+    o[1] = __floats2half2_rn(lo.y * sc, hi.y * sc);
+    o[2] = __floats2half2_rn(lo.z * sc, hi.z * sc);
+    o[3] = __floats2half2_rn(lo.w * sc, hi.w * sc);
+    return *reinterpret_cast<uint4*>(o);
+}
+
+__device__ __forceinline__ float absmax4(float4 v) {
+    return fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+}
+
+// Largest value of v over a group of `warps` consecutive warps starting at warp w0 (red: one
+// float per warp of the block).  Every thread of the group gets the result.
+__device__ __forceinline__ float group_max(float v, float* red, int w0, int warps) {
+    v = warp_max(v);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (warps == 1) return v;
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    float m = 0.f;
+    for (int w = 0; w < warps; ++w) m = fmaxf(m, red[w0 + w]);
+    return m;
+}
+
+// One CTA of len/16 threads per token: x[t] -> fp16(x * 2^-e) in the permuted K order, written
+// to the rows of all the token's slots (slot_pos[t][0..ns)); sexp[p] = e for those slots.
+// Each thread holds its two chunks (16 values) in registers: the row is read once.
+__global__ void __launch_bounds__(1024)
 convert_x_kernel(const IoArgs* __restrict__ io, const int* __restrict__ slot_pos, int M, int ns,
                  int len, __half* __restrict__ dst, int* __restrict__ sexp) {
-    const int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    __shared__ int pos[kMaxTopK + 1];
+    __shared__ float red[32];
+    const int t = blockIdx.x, tid = threadIdx.x, nt = blockDim.x;
     if (t >= M) return;
-    const float* s = io->x + static_cast<size_t>(t) * len;
-    int pos[kMaxTopK + 1];
+    if (tid <= kMaxTopK) pos[tid] = tid < ns ? slot_pos[static_cast<size_t>(t) * ns + tid] : -1;
+    __syncthreads();
     bool any = false;
 #pragma unroll
-    for (int j = 0; j < kMaxTopK + 1; ++j) {
-        pos[j] = j < ns ? slot_pos[static_cast<size_t>(t) * ns + j] : -1;
-        any |= pos[j] >= 0;
-    }
+    for (int j = 0; j <= kMaxTopK; ++j) any |= pos[j] >= 0;
     if (!any) return;  // a token without slots (expert-parallel padding rows): row not read
-    float mx = 0.f;
-    for (int i = lane * 4; i < len; i += 128) {
-        const float4 v = *reinterpret_cast<const float4*>(s + i);
-        mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
-    }
-    const int e = row_exp(warp_max(mx));
+    const float* s = io->x + static_cast<size_t>(t) * len;
+    const int c0 = tid, c1 = tid + nt;
+    const float4 l0 = *reinterpret_cast<const float4*>(s + chunk_k(c0));
+    const float4 h0 = *reinterpret_cast<const float4*>(s + chunk_k(c0) + 16);
+    const float4 l1 = *reinterpret_cast<const float4*>(s + chunk_k(c1));
+    const float4 h1 = *reinterpret_cast<const float4*>(s + chunk_k(c1) + 16);
+    const float mx = group_max(fmaxf(fmaxf(absmax4(l0), absmax4(h0)), fmaxf(absmax4(l1), absmax4(h1))), red, 0,
+                               nt >> 5);
+    const int e = row_exp(mx);
     const float sc = pow2f(-e);
-    if (lane < ns && pos[lane] >= 0) sexp[pos[lane]] = e;
-    for (int c = lane; c < len / 8; c += 32) {
-        const int kb = chunk_k(c);
-        const float4 lo = *reinterpret_cast<const float4*>(s + kb);
-        const float4 hi = *reinterpret_cast<const float4*>(s + kb + 16);
-        __half2 o[4];
-        o[0] = __floats2half2_rn(lo.x * sc, hi.x * sc);
-        o[1] = __floats2half2_rn(lo.y * sc, hi.y * sc);
-        o[2] = __floats2half2_rn(lo.z * sc, hi.z * sc);
-        o[3] = __floats2half2_rn(lo.w * sc, hi.w * sc);
-        const uint4 val = *reinterpret_cast<uint4*>(o);
+    if (tid < ns && pos[tid] >= 0) sexp[pos[tid]] = e;
+    const uint4 v0 = pack_chunk(l0, h0, sc), v1 = pack_chunk(l1, h1, sc);
 #pragma unroll
-        for (int j = 0; j < kMaxTopK + 1; ++j)
-            if (j < ns && pos[j] >= 0)
-                *reinterpret_cast<uint4*>(dst + static_cast<size_t>(pos[j]) * len + 8 * c) = val;
+    for (int j = 0; j <= kMaxTopK; ++j) {
+        if (pos[j] < 0) continue;
+        __half* d = dst + static_cast<size_t>(pos[j]) * len;
+        *reinterpret_cast<uint4*>(d + 8 * c0) = v0;
+        *reinterpret_cast<uint4*>(d + 8 * c1) = v1;
     }
 }
 
 // gu[p] = [g (I) | u (I)] f32 -> h = silu(g) * u -> dst[p][perm(k)] = fp16(h * 2^-e); sexp[p] = e.
-// One warp per slot; h is staged in shared memory (I <= 1024).
+// I/16 threads per slot row (rows per CTA: 256 / (I/16)), two chunks each, held in registers.
 __global__ void __launch_bounds__(256)
 convert_h_kernel(const float* __restrict__ gu, int n_rows, const int* __restrict__ n_used, int I,
                  __half* __restrict__ dst, int* __restrict__ sexp) {
-    __shared__ __align__(16) float hs[8][1024];
-    const int wib = threadIdx.x >> 5;
-    const int p = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
-    if (p >= n_rows || p >= *n_used) return;  // slot rows past the buckets' total are unused
-    const float* g = gu + static_cast<size_t>(p) * 2 * I;
+    __shared__ float red[8];
+    const int T = I / 16, tid = threadIdx.x;
+    const int r = tid / T, c0 = tid - r * T, c1 = c0 + T;
+    const int p = blockIdx.x * (blockDim.x / T) + r;
+    const int used = min(n_rows, *n_used);  // slot rows past the buckets' total are unused
+    const bool live = p < used;
+    const float* g = gu + static_cast<size_t>(live ? p : 0) * 2 * I;
     const float* u = g + I;
-    float* h = hs[wib];
-    float mx = 0.f;
-    for (int i = lane * 4; i < I; i += 128) {
-        const float4 v = swiglu4(*reinterpret_cast<const float4*>(g + i), *reinterpret_cast<const float4*>(u + i));
-        *reinterpret_cast<float4*>(h + i) = v;
-        mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+    float4 l0 = make_float4(0.f, 0.f, 0.f, 0.f), h0 = l0, l1 = l0, h1 = l0;
+    if (live) {
+        const int k0 = chunk_k(c0), k1 = chunk_k(c1);
+        l0 = swiglu4(*reinterpret_cast<const float4*>(g + k0), *reinterpret_cast<const float4*>(u + k0));
+        h0 = swiglu4(*reinterpret_cast<const float4*>(g + k0 + 16), *reinterpret_cast<const float4*>(u + k0 + 16));
+        l1 = swiglu4(*reinterpret_cast<const float4*>(g + k1), *reinterpret_cast<const float4*>(u + k1));
+        h1 = swiglu4(*reinterpret_cast<const float4*>(g + k1 + 16), *reinterpret_cast<const float4*>(u + k1 + 16));
     }
-    __syncwarp();
-    const int e = row_exp(warp_max(mx));
-    if (lane == 0) sexp[p] = e;
+    const int wpr = T >> 5;  // warps per row
+    const float mx = group_max(fmaxf(fmaxf(absmax4(l0), absmax4(h0)), fmaxf(absmax4(l1), absmax4(h1))), red,
+                               r * wpr, wpr);
+    if (!live) return;
+    const int e = row_exp(mx);
+    if (c0 == 0) sexp[p] = e;
     const float sc = pow2f(-e);
     __half* d = dst + static_cast<size_t>(p) * I;
-    for (int c = lane; c < I / 8; c += 32) {
-        const int kb = chunk_k(c);
-        put_chunk(d, c, *reinterpret_cast<const float4*>(h + kb), *reinterpret_cast<const float4*>(h + kb + 16), sc);
-    }
+    *reinterpret_cast<uint4*>(d + 8 * c0) = pack_chunk(l0, h0, sc);
+    *reinterpret_cast<uint4*>(d + 8 * c1) = pack_chunk(l1, h1, sc);
 }
 
 template <bool A_TMEM, int PW>
@@ -636,16 +654,21 @@ static_assert(Layout<false>::kTotal > 114 * 1024, "one CTA (and TMEM owner) per 
 
 int tc_max_n(int) { return kNMax; }
 
-bool tc_supported(int hidden, int inter) { return hidden % 512 == 0 && inter % 512 == 0; }
+bool tc_supported(int hidden, int inter) {
+    // conversion kernels: hidden / 16 threads per token (<= 1024), inter / 16 per slot row (<= 256)
+    return hidden % 512 == 0 && inter % 512 == 0 && hidden <= 16384 && inter <= 4096;
+}
 
 void launch_convert_x(const IoArgs* x, const int* slot_pos, int M, int ns, int len, __half* dst,
                       int* sexp, cudaStream_t s) {
-    convert_x_kernel<<<(M * 32 + 255) / 256, 256, 0, s>>>(x, slot_pos, M, ns, len, dst, sexp);
+    convert_x_kernel<<<M, len / 16, 0, s>>>(x, slot_pos, M, ns, len, dst, sexp);
 }
 
 void launch_convert_h(const float* gu, int n_rows, const int* n_used, int inter, __half* dst, int* sexp,
                       cudaStream_t s) {
-    convert_h_kernel<<<(n_rows * 32 + 255) / 256, 256, 0, s>>>(gu, n_rows, n_used, inter, dst, sexp);
+    const int per_cta = 256 / (inter / 16);
+    convert_h_kernel<<<(n_rows + per_cta - 1) / per_cta, per_cta * (inter / 16), 0, s>>>(gu, n_rows, n_used, inter,
+                                                                                        dst, sexp);
 }
 
 void launch_tc13(const Layer& L, const BMaps& xmap, const Workspace& ws, int max_items,
