@@ -587,20 +587,34 @@ def main():
         xin = ctx.alloc(PREFILL_M * H * 4)
         nbytes = PREFILL_M * H * 4
 
-        def e2e_step(i):
-            ctx.upload_ptr(xin, hx[i % 4].data_ptr(), nbytes)
-            step(xin, i)
-            ctx.download_ptr(out_off, hout.data_ptr(), nbytes)
+        hout2 = [hout, torch.empty((PREFILL_M, H), dtype=torch.float32).pin_memory()]
+
+        if ep_mode:
+            # expert parallel: upload, the exchange step, blocking read-back of the result
+            def e2e_step(i):
+                ctx.upload_ptr(xin, hx[i % 4].data_ptr(), nbytes)
+                step(xin, i)
+                ctx.download_ptr(out_off, hout.data_ptr(), nbytes)
+        else:
+            # moe_forward_host: each step's rows go up on a copy stream, the layer runs, the result
+            # comes back on another copy stream; successive steps overlap (the serving pattern)
+            def e2e_step(i):
+                ctx.forward_host(pre_ids[i % PREFILL_LAYERS], hx[i % 4].data_ptr(), hout2[i % 2].data_ptr(),
+                                 PREFILL_M)
         for i in range(2):
             e2e_step(i)
+        ctx.sync()
         torch.cuda.synchronize()
         _barrier(world)
         t0 = time.perf_counter()
         for i in range(K):
             e2e_step(i)
+        ctx.sync()
         e2e_s = _max_over_ranks((time.perf_counter() - t0) / K, world)
         e2e = {"value": world * PREFILL_M / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": nbytes,
-               "d2h_bytes_per_step": nbytes}
+               "d2h_bytes_per_step": nbytes,
+               "api": "moe_arena_upload + moe_forward_ep + moe_arena_download per step" if ep_mode else
+                      "moe_forward_host per step (pinned host rows in and out), one moe_sync after the K steps"}
 
         # ---- config 3: 8192 tokens in total over the N GPUs (strong scaling), uniform router
         # logits and the config-1 Zipf skew ------------------------------------------------------

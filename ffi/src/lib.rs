@@ -104,6 +104,8 @@ pub mod sys {
                                  ranges: *mut i32, tokens: *mut i32, weights: *mut f32, slot_pos: *mut i32,
                                  stream: *mut c_void) -> i32;
         pub fn moe_forward(ctx: *mut MoeCtx, layer_id: u32, x_off: u64, resid_off: u64, out_off: u64, m: u32) -> i32;
+        pub fn moe_forward_host(ctx: *mut MoeCtx, layer_id: u32, x_host: *const f32, out_host: *mut f32, m: u32,
+                                add_residual: i32) -> i32;
         pub fn moe_layer_set_next(ctx: *mut MoeCtx, layer_id: u32, next_id: i32) -> i32;
         pub fn moe_forward_norm(ctx: *mut MoeCtx, layer_id: u32, x_off: u64, out_off: u64, m: u32, eps: f32) -> i32;
         pub fn moe_forward_routed(ctx: *mut MoeCtx, layer_id: u32, x_off: u64, resid_off: u64, out_off: u64,

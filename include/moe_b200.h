@@ -164,6 +164,20 @@ int moe_bucket_static(uint32_t n_experts, uint32_t top_k, int has_shared, const 
 int moe_forward(moe_ctx* ctx, uint32_t layer_id, uint64_t x_off, uint64_t resid_off,
                 uint64_t out_off, uint32_t M);
 
+/* moe_forward from and to host memory, asynchronously: x_host[M][H] f32 goes to the device on a
+ * copy stream, the layer runs on the context's stream, out_host[M][H] comes back on a second
+ * copy stream; out = (add_residual ? x : 0) + MoE(x).  The call returns before any of it has
+ * run, so a caller serving successive batches overlaps one batch's copies with another's layer:
+ * the library keeps two device staging slots and orders every copy and launch with events
+ * (a slot is reused only after its previous layer call and result copy are done).  x_host must
+ * stay unchanged and out_host unread until moe_sync returns; pinned host memory (cudaHostAlloc /
+ * cudaHostRegister) is needed for the copies to overlap anything.  Not capturable in a CUDA
+ * graph (it launches the layer's own graph).  Replaces the reference's upload / submit / fence /
+ * read-back sequence around record_and_submit_moe (src/inference.rs:663-766 with the staging
+ * copies of src/memory.rs:297). */
+int moe_forward_host(moe_ctx* ctx, uint32_t layer_id, const float* x_host, float* out_host, uint32_t M,
+                     int add_residual);
+
 /* Declare that layer next_id runs after layer_id (-1: none).  The single-token kernel of
  * layer_id then prefetches next_id's router weight and shared expert into L2 while it finishes,
  * so a layer stack decodes with those reads served from L2 (no counterpart in the reference,

@@ -606,6 +606,15 @@ void moe_ctx_destroy(moe_ctx* c) {
     if (c->ref36_scratch) cudaFree(c->ref36_scratch);
     c->ws_sh.status = nullptr;
     free_ws(c->ws_sh);
+    if (c->h2d_stream) cudaStreamSynchronize(c->h2d_stream);
+    if (c->d2h_stream) cudaStreamSynchronize(c->d2h_stream);
+    for (int b = 0; b < 2; ++b) {
+        if (c->host_stage[b]) cudaFree(c->host_stage[b]);
+        for (cudaEvent_t e : {c->ev_in[b], c->ev_done[b], c->ev_out[b]})
+            if (e) cudaEventDestroy(e);
+    }
+    if (c->h2d_stream) cudaStreamDestroy(c->h2d_stream);
+    if (c->d2h_stream) cudaStreamDestroy(c->d2h_stream);
     if (c->ev_fork) cudaEventDestroy(c->ev_fork);
     if (c->ev_join) cudaEventDestroy(c->ev_join);
     if (c->side_stream) cudaStreamDestroy(c->side_stream);
@@ -660,6 +669,8 @@ int moe_sync(moe_ctx* c) {
     if (!c) return fail(c, MOE_E_INVALID, "NULL context");
     DeviceGuard g(c->device);
     MOE_CUDA(c, cudaStreamSynchronize(c->stream));
+    if (c->h2d_stream) MOE_CUDA(c, cudaStreamSynchronize(c->h2d_stream));
+    if (c->d2h_stream) MOE_CUDA(c, cudaStreamSynchronize(c->d2h_stream));
     int st = 0;
     MOE_CUDA(c, cudaMemcpy(&st, c->ws.status, sizeof(int), cudaMemcpyDeviceToHost));
     if (st != 0) {
@@ -861,6 +872,84 @@ int moe_bucket(moe_ctx* c, uint32_t n_experts, uint32_t top_k, int has_shared, u
                        c->ws.status, c->stream);
     stage(c, "bucket", 3);
     return check_launch(c, "bucket");
+}
+
+// Staging slots and streams of moe_forward_host, grown to hold M tokens of width H.
+static int ensure_host_stage(Ctx* c, uint32_t M, uint32_t H) {
+    if (!c->h2d_stream) {
+        MOE_CUDA(c, cudaStreamCreateWithFlags(&c->h2d_stream, cudaStreamNonBlocking));
+        MOE_CUDA(c, cudaStreamCreateWithFlags(&c->d2h_stream, cudaStreamNonBlocking));
+        for (int b = 0; b < 2; ++b) {
+            MOE_CUDA(c, cudaEventCreateWithFlags(&c->ev_in[b], cudaEventDisableTiming));
+            MOE_CUDA(c, cudaEventCreateWithFlags(&c->ev_done[b], cudaEventDisableTiming));
+            MOE_CUDA(c, cudaEventCreateWithFlags(&c->ev_out[b], cudaEventDisableTiming));
+        }
+    }
+    const size_t need = 2 * static_cast<size_t>(M) * H * sizeof(float);
+    if (need <= c->host_stage_bytes) return MOE_OK;
+    // earlier calls may still use the old slots
+    MOE_CUDA(c, cudaStreamSynchronize(c->stream));
+    MOE_CUDA(c, cudaStreamSynchronize(c->h2d_stream));
+    MOE_CUDA(c, cudaStreamSynchronize(c->d2h_stream));
+    for (int b = 0; b < 2; ++b) {
+        if (c->host_stage[b]) cudaFree(c->host_stage[b]);
+        c->host_stage[b] = nullptr;
+    }
+    c->host_stage_bytes = 0;
+    for (int b = 0; b < 2; ++b) {
+        void* p = nullptr;
+        const cudaError_t e = cudaMalloc(&p, need);
+        if (e != cudaSuccess) {
+            cudaGetLastError();
+            return fail(c, MOE_E_OOM, "host staging of %zu bytes: %s", need, cudaGetErrorString(e));
+        }
+        c->host_stage[b] = static_cast<float*>(p);
+    }
+    c->host_stage_bytes = need;
+    return MOE_OK;
+}
+
+int moe_forward_host(moe_ctx* c, uint32_t layer_id, const float* x_host, float* out_host, uint32_t M,
+                     int add_residual) {
+    if (!c || !x_host || !out_host) return fail(c, MOE_E_INVALID, "NULL argument");
+    Layer* L;
+    int rc = get_layer(c, layer_id, &L);
+    if (rc) return rc;
+    if (L->subset())
+        return fail(c, MOE_E_UNSUPPORTED, "expert-subset layer: route with moe_route and run moe_forward_topk");
+    if (M == 0) return MOE_OK;
+    if (stream_capturing(c)) return fail(c, MOE_E_INVALID, "moe_forward_host cannot be captured");
+    DeviceGuard g(c->device);
+    const uint32_t H = L->spec.hidden;
+    if ((rc = ensure_layer_ws(c, *L, M))) return rc;
+    if ((rc = ensure_host_stage(c, M, H))) return rc;
+    const int b = c->host_next;
+    c->host_next ^= 1;
+    const size_t bytes = static_cast<size_t>(M) * H * sizeof(float);
+    float* xs = c->host_stage[b];
+    float* os = xs + static_cast<size_t>(M) * H;
+    // host -> slot b once the layer call two calls back has finished reading it
+    MOE_CUDA(c, cudaStreamWaitEvent(c->h2d_stream, c->ev_done[b], 0));
+    MOE_CUDA(c, cudaMemcpyAsync(xs, x_host, bytes, cudaMemcpyHostToDevice, c->h2d_stream));
+    MOE_CUDA(c, cudaEventRecord(c->ev_in[b], c->h2d_stream));
+    // the layer, once its rows are in and slot b's previous result has been read out
+    MOE_CUDA(c, cudaStreamWaitEvent(c->stream, c->ev_in[b], 0));
+    MOE_CUDA(c, cudaStreamWaitEvent(c->stream, c->ev_out[b], 0));
+    const float* resid = add_residual ? xs : nullptr;
+    if (c->use_graphs && !c->prof && !use_decode(c, *L, M))
+        rc = graph_forward(c, layer_id, *L, M, xs, resid, os);
+    else {
+        prof_begin(c);
+        rc = record_forward(c, *L, M, xs, resid, os);
+        prof_end(c);
+    }
+    if (rc) return rc;
+    MOE_CUDA(c, cudaEventRecord(c->ev_done[b], c->stream));
+    // result -> host
+    MOE_CUDA(c, cudaStreamWaitEvent(c->d2h_stream, c->ev_done[b], 0));
+    MOE_CUDA(c, cudaMemcpyAsync(out_host, os, bytes, cudaMemcpyDeviceToHost, c->d2h_stream));
+    MOE_CUDA(c, cudaEventRecord(c->ev_out[b], c->d2h_stream));
+    return MOE_OK;
 }
 
 int moe_forward(moe_ctx* c, uint32_t layer_id, uint64_t x_off, uint64_t resid_off,

@@ -33,7 +33,7 @@ EXPORTS = (
     "moe_abi_version", "moe_ctx_create", "moe_ctx_create_external", "moe_ctx_destroy",
     "moe_arena_upload", "moe_arena_download", "moe_arena_ptr", "moe_set_stream", "moe_sync",
     "moe_last_error", "moe_layer_create", "moe_reserve", "moe_route", "moe_do_route",
-    "moe_bucket", "moe_forward", "moe_forward_routed", "moe_rms_norm", "moe_dequant_iq4xs",
+    "moe_bucket", "moe_forward", "moe_forward_host", "moe_forward_routed", "moe_rms_norm", "moe_dequant_iq4xs",
     "moe_synth_iq4xs", "moe_profile", "moe_profile_read", "moe_launch_count", "moe_set_path",
     "moe_bucket_static", "moe_forward_topk", "moe_ep_plan_bytes", "moe_ep_dispatch",
     "moe_ep_combine", "moe_dequant_ref36", "moe_forward_norm", "moe_vocab_logits",
@@ -99,6 +99,7 @@ def lib():
         "moe_do_route": (i32, [vp, u32, u64, u32, P(C.c_uint16), P(f32), P(f32)]),
         "moe_bucket": (i32, [vp, u32, u32, i32, u64, u32, u64, u64, u64, u64]),
         "moe_forward": (i32, [vp, u32, u64, u64, u64, u32]),
+        "moe_forward_host": (i32, [vp, u32, vp, vp, u32, C.c_int]),
         "moe_forward_routed": (i32, [vp, u32, u64, u64, u64, u32, P(C.c_uint16), P(f32), P(f32)]),
         "moe_rms_norm": (i32, [vp, u64, u64, u32, u32, f32]),
         "moe_dequant_iq4xs": (i32, [vp, u64, u64, u64]),
@@ -258,6 +259,12 @@ class Context:
 
     def forward(self, layer: int, x_off: int, resid_off: int, out_off: int, m: int):
         self._check(lib().moe_forward(self.h, layer, x_off, resid_off, out_off, m))
+
+    def forward_host(self, layer: int, x_host_ptr: int, out_host_ptr: int, m: int, add_residual: bool = True):
+        """Asynchronous forward from / to host memory (pointers to f32 [m][H]); results are in
+        out_host after sync()."""
+        self._check(lib().moe_forward_host(self.h, layer, C.c_void_p(x_host_ptr), C.c_void_p(out_host_ptr), m,
+                                           int(add_residual)))
 
     def forward_norm(self, layer: int, x_off: int, out_off: int, m: int, eps: float = 1e-6):
         """out = x + MoE(RMSNorm(x)) (one step of the layer stack)."""
