@@ -168,7 +168,7 @@ int moe_forward(moe_ctx* ctx, uint32_t layer_id, uint64_t x_off, uint64_t resid_
  * copy stream, the layer runs on the context's stream, out_host[M][H] comes back on a second
  * copy stream; out = (add_residual ? x : 0) + MoE(x).  The call returns before any of it has
  * run, so a caller serving successive batches overlaps one batch's copies with another's layer:
- * the library keeps two device staging slots and orders every copy and launch with events
+ * the library keeps three device staging slots and orders every copy and launch with events
  * (a slot is reused only after its previous layer call and result copy are done).  x_host must
  * stay unchanged and out_host unread until moe_sync returns; pinned host memory (cudaHostAlloc /
  * cudaHostRegister) is needed for the copies to overlap anything.  Not capturable in a CUDA

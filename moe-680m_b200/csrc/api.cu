@@ -608,7 +608,7 @@ void moe_ctx_destroy(moe_ctx* c) {
     free_ws(c->ws_sh);
     if (c->h2d_stream) cudaStreamSynchronize(c->h2d_stream);
     if (c->d2h_stream) cudaStreamSynchronize(c->d2h_stream);
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < Ctx::kHostSlots; ++b) {
         if (c->host_stage[b]) cudaFree(c->host_stage[b]);
         for (cudaEvent_t e : {c->ev_in[b], c->ev_done[b], c->ev_out[b]})
             if (e) cudaEventDestroy(e);
@@ -879,7 +879,7 @@ static int ensure_host_stage(Ctx* c, uint32_t M, uint32_t H) {
     if (!c->h2d_stream) {
         MOE_CUDA(c, cudaStreamCreateWithFlags(&c->h2d_stream, cudaStreamNonBlocking));
         MOE_CUDA(c, cudaStreamCreateWithFlags(&c->d2h_stream, cudaStreamNonBlocking));
-        for (int b = 0; b < 2; ++b) {
+        for (int b = 0; b < Ctx::kHostSlots; ++b) {
             MOE_CUDA(c, cudaEventCreateWithFlags(&c->ev_in[b], cudaEventDisableTiming));
             MOE_CUDA(c, cudaEventCreateWithFlags(&c->ev_done[b], cudaEventDisableTiming));
             MOE_CUDA(c, cudaEventCreateWithFlags(&c->ev_out[b], cudaEventDisableTiming));
@@ -891,12 +891,12 @@ static int ensure_host_stage(Ctx* c, uint32_t M, uint32_t H) {
     MOE_CUDA(c, cudaStreamSynchronize(c->stream));
     MOE_CUDA(c, cudaStreamSynchronize(c->h2d_stream));
     MOE_CUDA(c, cudaStreamSynchronize(c->d2h_stream));
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < Ctx::kHostSlots; ++b) {
         if (c->host_stage[b]) cudaFree(c->host_stage[b]);
         c->host_stage[b] = nullptr;
     }
     c->host_stage_bytes = 0;
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < Ctx::kHostSlots; ++b) {
         void* p = nullptr;
         const cudaError_t e = cudaMalloc(&p, need);
         if (e != cudaSuccess) {
@@ -924,11 +924,11 @@ int moe_forward_host(moe_ctx* c, uint32_t layer_id, const float* x_host, float* 
     if ((rc = ensure_layer_ws(c, *L, M))) return rc;
     if ((rc = ensure_host_stage(c, M, H))) return rc;
     const int b = c->host_next;
-    c->host_next ^= 1;
+    c->host_next = (b + 1) % Ctx::kHostSlots;
     const size_t bytes = static_cast<size_t>(M) * H * sizeof(float);
     float* xs = c->host_stage[b];
     float* os = xs + static_cast<size_t>(M) * H;
-    // host -> slot b once the layer call two calls back has finished reading it
+    // host -> slot b once the layer call that last used it has finished reading it
     MOE_CUDA(c, cudaStreamWaitEvent(c->h2d_stream, c->ev_done[b], 0));
     MOE_CUDA(c, cudaMemcpyAsync(xs, x_host, bytes, cudaMemcpyHostToDevice, c->h2d_stream));
     MOE_CUDA(c, cudaEventRecord(c->ev_in[b], c->h2d_stream));

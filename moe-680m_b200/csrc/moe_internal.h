@@ -260,13 +260,14 @@ struct Ctx {
     Workspace ws_sh;
     cudaStream_t side_stream = nullptr;
     cudaEvent_t ev_fork = nullptr, ev_join = nullptr;
-    // moe_forward_host: two device staging slots (x rows then out rows), copy streams and the
-    // events that order them with the layer on `stream` (created on first use)
-    float* host_stage[2] = {nullptr, nullptr};
+    // moe_forward_host: kHostSlots device staging slots (x rows then out rows), copy streams and
+    // the events that order them with the layer on `stream` (created on first use)
+    static constexpr int kHostSlots = 3;
+    float* host_stage[kHostSlots] = {};
     size_t host_stage_bytes = 0;  // per slot (x + out)
     int host_next = 0;
     cudaStream_t h2d_stream = nullptr, d2h_stream = nullptr;
-    cudaEvent_t ev_in[2] = {nullptr, nullptr}, ev_done[2] = {nullptr, nullptr}, ev_out[2] = {nullptr, nullptr};
+    cudaEvent_t ev_in[kHostSlots] = {}, ev_done[kHostSlots] = {}, ev_out[kHostSlots] = {};
     float* ref36_scratch = nullptr;  // K-split partial sums of MOE_F_REF36 layers
     size_t ref36_scratch_bytes = 0;
     EpState ep;
