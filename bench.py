@@ -616,7 +616,7 @@ def main():
         e2e = {"value": world * PREFILL_M / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": nbytes,
                "d2h_bytes_per_step": nbytes, "steps": k_e2e,
                "api": "moe_arena_upload + moe_forward_ep + moe_arena_download per step" if ep_mode else
-                      "moe_forward_host per step (pinned host rows in and out), one moe_sync after the K steps"}
+                      "moe_forward_host per step (pinned host rows in and out), one moe_sync after the timed steps"}
 
         # ---- config 3: 8192 tokens in total over the N GPUs (strong scaling), uniform router
         # logits and the config-1 Zipf skew ------------------------------------------------------
