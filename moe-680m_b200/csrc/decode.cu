@@ -653,8 +653,11 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const __grid_const
             const int corr = static_cast<int>(aq[16]);
             const float f = wgt[s] * __uint_as_float(aq[17]);
             const uint8_t* rows = st_2 + static_cast<size_t>(s) * kMaxRows2 * kRow2 + (sb >> 3) * kBlockBytes;
-#pragma unroll 2
-            for (int r = r0; r < nrows; r += 3) {
+            // the thread's rows unrolled completely, so that their loads and lookups interleave
+#pragma unroll
+            for (int i = 0; i < (kMaxRows2 + 2) / 3; ++i) {
+                const int r = r0 + 3 * i;
+                if (r >= nrows) break;
                 const uint8_t* blk = rows + static_cast<size_t>(r) * rb2;
                 const uint2 hdr = *reinterpret_cast<const uint2*>(blk);
                 // the qs bytes of a sub-block start 8 bytes into a 16-byte unit: two 8-byte loads
