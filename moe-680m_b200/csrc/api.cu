@@ -289,12 +289,16 @@ int run_route(Ctx* c, const Layer& L, uint32_t M) {
                 return fail(c, MOE_E_CUDA, "cuTensorMapEncodeTiled failed for the router operands");
             ws.xh_base = ws.xh; ws.xh_rows = M; ws.xh_cols = static_cast<uint64_t>(H);
         }
-        moe::launch_split_x(ws.io, static_cast<size_t>(M) * H, ws.xh, ws.xl, c->stream);
+        // the split kernel also computes the shared gate logit (column E of the logit planes)
+        const bool gate = (L.spec.flags & MOE_F_SHARED_GATE) != 0 && L.gate_ptr;
+        const int n_split = moe::router_tc_split(static_cast<int>(M), E, H);
+        moe::launch_split_x(ws.io, static_cast<int>(M), H, ws.xh, ws.xl,
+                            gate ? reinterpret_cast<const float*>(L.gate_ptr) : nullptr, ws.logits, n_split, E,
+                            c->stream);
         stage(c, "router_split", 1);
         moe::launch_router_tc(L, ws.xhmap, ws.xlmap, static_cast<int>(M), ws.logits, ws.status, c->stream);
         stage(c, "router", 1);
-        moe::launch_topk(L, ws.logits, moe::router_tc_split(static_cast<int>(M), E, H), false, ws.io,
-                         static_cast<int>(M), ws.topk, ws.status, c->stream);
+        moe::launch_topk(L, ws.logits, n_split, gate, ws.io, static_cast<int>(M), ws.topk, ws.status, c->stream);
     } else {
         moe::launch_router_logits(L, ws.io, static_cast<int>(M), ws.logits, c->stream);
         stage(c, "router", 1);

@@ -296,7 +296,9 @@ void launch_convert_h(const float* gu, int n_rows, const int* n_used, int inter,
 bool make_iq4_tmap(CUtensorMap* m, const void* base, uint64_t rows, uint64_t row_bytes);
 bool make_f32_tmap(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows);
 void launch_split_tf32(const float* src, size_t n, float* hi, float* lo, cudaStream_t s);
-void launch_split_x(const IoArgs* io, size_t n, float* hi, float* lo, cudaStream_t s);
+// x -> TF32 parts; with gate_w, also the shared gate logit into column E of the logit planes.
+void launch_split_x(const IoArgs* io, int M, int H, float* hi, float* lo, const float* gate_w, float* logits,
+                    int n_split, int E, cudaStream_t s);
 int router_tc_split(int M, int E, int H);
 void launch_router_tc(const Layer& L, const CUtensorMap& xh, const CUtensorMap& xl, int M,
                       float* partial, int* status, cudaStream_t s);

@@ -151,17 +151,43 @@ __global__ void split_tf32_kernel(const float* __restrict__ src, size_t n, float
     }
 }
 
-__global__ void split_x_kernel(const IoArgs* __restrict__ io, size_t n, float* __restrict__ hi,
-                               float* __restrict__ lo) {
-    const float* src = io->x;
-    for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n;
-         i += static_cast<size_t>(gridDim.x) * blockDim.x) {
-        const float v = src[i];
-        uint32_t h;
-        asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(h) : "f"(v));
-        const float hf = __uint_as_float(h);
-        hi[i] = hf;
-        lo[i] = v - hf;
+// One CTA (128 threads) per token: x[t] -> (TF32 part, remainder) for the router operands and,
+// when the layer has a shared-expert gate, the gate logit g . x[t] (f32, fixed-order reduction)
+// into column E of the first logit plane, with zeros in column E of the other n_split - 1
+// planes, so that the top-k kernel's in-order sum of the planes returns it unchanged.
+__global__ void __launch_bounds__(128)
+split_x_kernel(const IoArgs* __restrict__ io, int M, int H, float* __restrict__ hi, float* __restrict__ lo,
+               const float* __restrict__ gate_w, float* __restrict__ logits, int n_split, int E) {
+    __shared__ float red[4];
+    const int t = blockIdx.x, tid = threadIdx.x;
+    const float4* src = reinterpret_cast<const float4*>(io->x + static_cast<size_t>(t) * H);
+    float4* h4 = reinterpret_cast<float4*>(hi + static_cast<size_t>(t) * H);
+    float4* l4 = reinterpret_cast<float4*>(lo + static_cast<size_t>(t) * H);
+    float z = 0.f;
+    for (int i = tid; i < H / 4; i += 128) {
+        const float4 v = src[i];
+        float vv[4] = {v.x, v.y, v.z, v.w}, hh[4], ll[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            uint32_t h;
+            asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(h) : "f"(vv[j]));
+            hh[j] = __uint_as_float(h);
+            ll[j] = vv[j] - hh[j];
+        }
+        h4[i] = make_float4(hh[0], hh[1], hh[2], hh[3]);
+        l4[i] = make_float4(ll[0], ll[1], ll[2], ll[3]);
+        if (gate_w) {
+            const float4 g = reinterpret_cast<const float4*>(gate_w)[i];
+            z = fmaf(v.x, g.x, z); z = fmaf(v.y, g.y, z); z = fmaf(v.z, g.z, z); z = fmaf(v.w, g.w, z);
+        }
+    }
+    if (!gate_w) return;
+    z = warp_sum(z);
+    if ((tid & 31) == 0) red[tid >> 5] = z;
+    __syncthreads();
+    if (tid < n_split) {
+        const float zz = tid == 0 ? ((red[0] + red[1]) + (red[2] + red[3])) : 0.f;
+        logits[(static_cast<size_t>(tid) * M + t) * (E + 1) + E] = zz;
     }
 }
 
@@ -174,9 +200,9 @@ void launch_split_tf32(const float* src, size_t n, float* hi, float* lo, cudaStr
     split_tf32_kernel<<<1184, 256, 0, s>>>(src, n, hi, lo);
 }
 
-void launch_split_x(const IoArgs* io, size_t n, float* hi, float* lo, cudaStream_t s) {
-    const int blocks = static_cast<int>(std::min<size_t>((n + 255) / 256, 4096));
-    split_x_kernel<<<blocks, 256, 0, s>>>(io, n, hi, lo);
+void launch_split_x(const IoArgs* io, int M, int H, float* hi, float* lo, const float* gate_w, float* logits,
+                    int n_split, int E, cudaStream_t s) {
+    split_x_kernel<<<M, 128, 0, s>>>(io, M, H, hi, lo, gate_w, logits, n_split, E);
 }
 
 int router_tc_split(int M, int E, int H) {
