@@ -76,7 +76,16 @@ static int forward_and_check(uint32_t id, uint32_t m) {
     CHECK(moe_forward(g_ctx, id, x, x, out, m));
     CHECK(moe_sync(g_ctx));
     CHECK(moe_arena_download(g_ctx, out, b, n * sizeof(float)));
+    /* the same rows from host memory through the asynchronous entry point */
+    float* xh = malloc(n * sizeof(float));
+    float* c = malloc(n * sizeof(float));
+    CHECK(moe_arena_download(g_ctx, x, xh, n * sizeof(float)));
+    CHECK(moe_forward_host(g_ctx, id, xh, c, m, 1));
+    CHECK(moe_sync(g_ctx));
     int bad = 0;
+    if (memcmp(a, c, n * sizeof(float)) != 0) bad = 1;
+    free(xh);
+    free(c);
     double s = 0.0;
     for (size_t i = 0; i < n; ++i) {
         if (!isfinite(a[i])) bad = 1;
