@@ -191,6 +191,35 @@ bucket_scatter_kernel(const uint2* __restrict__ topk, int M, int E, int k, int r
 constexpr int kSmallThreads = 1024;
 constexpr int kSmallWarps = kSmallThreads / 32;
 constexpr int kSmallMaxTokens = kSmallThreads;
+constexpr int kSortMax = kSmallThreads;  // tile lists longer than this keep bucket order
+
+// Stable sort of a tile list by token count, descending (one CTA; n <= kSortMax entries, else
+// left as is): each entry's rank is the number of entries that precede it in the new order.
+__device__ void sort_tiles(TcTile* list, int n, TcTile* buf, int* nbuf) {
+    if (n > kSortMax) return;
+    const int i = threadIdx.x;
+    if (i < n) {
+        buf[i] = list[i];
+        nbuf[i] = list[i].n;
+    }
+    __syncthreads();
+    if (i < n) {
+        const int ni = nbuf[i];
+        int r[8] = {0, 0, 0, 0, 0, 0, 0, 0};  // independent partial counts
+        int j = 0;
+        for (; j + 8 <= n; j += 8) {
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                const int nj = nbuf[j + u];
+                r[u] += (nj > ni || (nj == ni && j + u < i)) ? 1 : 0;
+            }
+        }
+        for (; j < n; ++j) r[0] += (nbuf[j] > ni || (nbuf[j] == ni && j < i)) ? 1 : 0;
+        const int rank = ((r[0] + r[1]) + (r[2] + r[3])) + ((r[4] + r[5]) + (r[6] + r[7]));
+        list[rank] = buf[i];
+    }
+    __syncthreads();
+}
 
 __global__ void __launch_bounds__(kSmallThreads)
 bucket_small_kernel(const uint2* __restrict__ topk, int M, int E, int k, int routed, int has_shared,
@@ -201,6 +230,8 @@ bucket_small_kernel(const uint2* __restrict__ topk, int M, int E, int k, int rou
     // per bucket: first slot, first chunk, first gate/up tile, first down tile (+ totals at nb)
     __shared__ int4 first_s[kMaxExperts + 2];
     __shared__ int4 warp_tot[32];
+    __shared__ TcTile tsort[kSortMax];
+    __shared__ int tsort_n[kSortMax];
     const int nb = E + 1, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int t = tid;
     // the token's slots: bucket (or -1) and gate weight, read once
@@ -291,6 +322,14 @@ bucket_small_kernel(const uint2* __restrict__ topk, int M, int E, int k, int rou
             const int q = (ti - fs[4 * e + 3]) * lists.n2, cnt = fs[4 * (e + 1)] - fs[4 * e];
             lists.t2[ti] = TcTile{e, fs[4 * e] + q, min(lists.n2, cnt - q), 0};
         }
+    }
+    // the down-projection tile list largest first: that kernel deals items round robin and its
+    // short items cost in proportion to their tile's token count (its epilogue), so the largest
+    // tiles are spread over the first rounds (stable: equal sizes keep their order; the results
+    // do not depend on it).  The gate/up list gained nothing from the same order (measured).
+    if (lists.t2) {
+        __syncthreads();  // the lists above are complete
+        sort_tiles(lists.t2, min(total.w, lists.max2), tsort, tsort_n);
     }
     // 3. positions in token order
     if (t < M) {
